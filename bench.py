@@ -1,0 +1,516 @@
+"""Benchmark: B-KV/s of find + insert_or_assign (dim 32, load factor 1.0).
+
+Workload (BASELINE config 2 at LF 1.0, one shard per GPU): uint64 keys,
+float32 values of dim 32, 64 Mi slots per GPU, EvictStrategy::kLru, the
+table filled to load factor 1.0. One step = find of 1 Mi keys (100% hits)
++ insert_or_assign of 1 Mi keys (50% resident keys, 50% new keys that evict
+the least recently used). value = keys of all steps on all GPUs / time.
+
+N = 1 runs the table directly. N > 1 runs the sharded table: every rank
+submits its own batches; keys travel to their owner GPU and results come
+back over NCCL all-to-all (weak scaling: per-GPU table and batch fixed).
+
+`--impl reference` times the reference's algorithm on the host CPU instead
+(the reference needs an Ascend NPU and CANN, neither exists here, so its CPU
+restatement in oracle/ stands in for it), with every host thread.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "hierarchicalkv-ascend_b200")
+ORACLE = os.path.join(ROOT, "oracle")
+for _p in (PKG, ORACLE):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "B-KV/s for find & insert_or_assign (dim 32, LF 1.0) at 1/2/4/8 B200; %HBM peak"
+UNIT = "B-KV/s"
+DIM = 32
+VALUE_BYTES = DIM * 4
+CAPACITY = 64 << 20          # slots per GPU
+BATCH = 1 << 20              # keys per call
+PREFILL_FACTOR = 1.6         # inserted keys / capacity to reach LF 1.0 under LRU
+HOT = 4 << 20                # most recent prefill keys, source of hits
+# algorithmic bytes per key (SURVEY 8d model, 128-byte digest line per bucket)
+FIND_HIT_BYTES = 145 + 2 * VALUE_BYTES                 # 401
+INSERT_HIT_BYTES = 160 + 2 * VALUE_BYTES               # 416
+INSERT_EVICT_BYTES = 1185 + 2 * VALUE_BYTES            # 1441
+INSERT_MIX_BYTES = 0.5 * (INSERT_HIT_BYTES + INSERT_EVICT_BYTES)  # 928.5
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# --------------------------------------------------------------------------
+# key generation on the device: key = Murmur3 finalizer(counter), a bijection
+# of uint64, so keys are distinct by construction (int64 bit patterns).
+# --------------------------------------------------------------------------
+def fmix_t(x):
+    import torch
+
+    def srl(v, s):
+        return (v >> s) & ((1 << (64 - s)) - 1)
+
+    c1 = 0xFF51AFD7ED558CCD - (1 << 64)
+    c2 = 0xC4CEB9FE1A85EC53 - (1 << 64)
+    x = x ^ srl(x, 33)
+    x = x * c1
+    x = x ^ srl(x, 33)
+    x = x * c2
+    x = x ^ srl(x, 33)
+    return x
+
+
+def key_of(counters):
+    import torch
+
+    k = fmix_t(counters)
+    # the four reserved keys are -4..-1 as int64; move the (p = 2^-62) hits
+    return torch.where(k >= -4, k - 8, k)
+
+
+def keys_from_counters(start, n, device):
+    import torch
+
+    return key_of(torch.arange(start, start + n, dtype=torch.int64, device=device))
+
+
+def owner_t(keys, world):
+    """Owner rank as the sharded table computes it: (Murmur3(key) >> 40) % W."""
+    h = fmix_t(keys)
+    return ((h >> 40) & ((1 << 24) - 1)) % world
+
+
+# --------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed
+    region (read-only queries)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,"
+              "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"hkv_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "20"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 10:
+                rows.append(parts)
+        try:
+            os.remove(self.path)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [r for r in rows if r[4].isdigit() and int(r[4]) > 0] or rows
+        sm = [float(r[1]) for r in loaded if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[j] for r in loaded for j in range(4)
+                          if r[6 + j].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows), "samples_under_load": len(loaded)}
+
+
+# --------------------------------------------------------------------------
+def dist_setup(n_gpus):
+    import torch
+    import torch.distributed as dist
+
+    if n_gpus <= 1:
+        return 0, 1, 0, None
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    from datetime import timedelta
+
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=300),
+                            device_id=torch.device("cuda", local))
+    return rank, world, local, dist
+
+
+def build_table(world, rank, dist):
+    import torch
+
+    import hkv_b200 as H
+
+    opts = H.HashTableOptions(init_capacity=CAPACITY, max_capacity=CAPACITY,
+                              max_hbm_for_vectors=CAPACITY * VALUE_BYTES * 2,
+                              dim=DIM, max_load_factor=1.0)
+    if world == 1:
+        t = H.HashTable(H.EvictStrategy.kLru)
+        t.init(opts)
+        return t, t
+    uid = [H.ShardedHashTable.unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    opts.device_id = torch.cuda.current_device()
+    s = H.ShardedHashTable(opts, rank, world, uid[0], H.EvictStrategy.kLru)
+    return s, H.HashTable.borrow(H.lib().hkv_sharded_local(s._h), H.EvictStrategy.kLru)
+
+
+def prefill(local, rank, world, device):
+    """Fill each shard to load factor 1.0 with the keys it owns (every rank
+    generates the same global key stream and keeps its own keys)."""
+    import torch
+
+    total = int(CAPACITY * world * PREFILL_FACTOR)
+    chunk = 4 << 20
+    vals = torch.randn((chunk, DIM), device=device)
+    start = 0
+    while start < total:
+        n = min(chunk, total - start)
+        k = keys_from_counters(start, n, device)
+        if world > 1:
+            k = k[owner_t(k, world) == rank]
+        m = k.numel()
+        local.insert_or_assign(m, k, vals[:m])
+        start += n
+    torch.cuda.synchronize()
+    return total
+
+
+def prepare_batches(steps, rank, world, total_prefill, device, seed):
+    """Per step: a find batch of resident (hot) keys and an insert batch of
+    half hot keys, half never-seen keys. Hot keys are the most recent prefill
+    keys of the global stream."""
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed + rank)
+    hot_start = total_prefill - HOT * world
+    fresh_base = total_prefill + rank * (steps + 1) * BATCH
+    finds, inserts, vals = [], [], []
+    for s in range(steps):
+        idx = torch.randint(0, HOT * world, (BATCH,), generator=g, device=device)
+        finds.append(key_of(hot_start + idx))
+        perm = torch.randperm(HOT * world, generator=g, device=device)[: BATCH // 2]
+        hot = key_of(hot_start + perm)
+        fresh = keys_from_counters(fresh_base + s * BATCH // 2, BATCH // 2, device)
+        ins = torch.cat([hot, fresh])
+        ins = ins[torch.randperm(BATCH, generator=g, device=device)]
+        inserts.append(ins)
+        vals.append(torch.rand((BATCH, DIM), generator=g, device=device))
+    torch.cuda.synchronize()
+    return finds, inserts, vals
+
+
+def run_gpu(args):
+    import numpy as np
+    import torch
+
+    rank, world, local_rank, dist = dist_setup(args.gpus)
+    device = torch.device("cuda", torch.cuda.current_device())
+    table, local = build_table(world, rank, dist)
+    total = prefill(local, rank, world, device)
+    lf = local.load_factor()
+    steps, warm = args.steps, args.warmup
+    finds, inserts, vals = prepare_batches(steps + warm, rank, world, total, device, 1234)
+    out_vals = torch.empty((BATCH, DIM), device=device)
+    founds = [torch.zeros(BATCH, dtype=torch.bool, device=device) for _ in range(steps + warm)]
+    stream = torch.cuda.current_stream()
+
+    def step(i, ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        table.find(BATCH, finds[i], out_vals, founds[i])
+        if ev is not None:
+            ev[1].record(stream)
+        table.insert_or_assign(BATCH, inserts[i], vals[i])
+        if ev is not None:
+            ev[2].record(stream)
+
+    for i in range(warm):
+        step(i)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.05)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t0.record(stream)
+    for i in range(steps):
+        step(warm + i, evs[i])
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = t0.elapsed_time(t1)
+    find_ms = sum(e[0].elapsed_time(e[1]) for e in evs)
+    ins_ms = sum(e[1].elapsed_time(e[2]) for e in evs)
+    hit = float(torch.stack(founds[warm:]).float().mean().item())
+    if dist:
+        tt = torch.tensor([ms, find_ms, ins_ms], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms, find_ms, ins_ms = [float(x) for x in tt.tolist()]
+    keys_total = 2 * BATCH * steps * world
+    value = keys_total / (ms * 1e-3) / 1e9
+
+    result = {
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
+        "steps": steps, "warmup": warm, "ms_per_step": round(ms / steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "u64 keys / f32 values", "data": "synthetic (seeded device keys)",
+        "config": {"workload": "BASELINE config 2 at load factor 1.0: find 1 Mi keys "
+                               "(100% hits) + insert_or_assign 1 Mi keys (50% hits, "
+                               "50% new keys evicting LRU) per step",
+                   "capacity_per_gpu": CAPACITY, "dim": DIM, "batch": BATCH,
+                   "strategy": "kLru", "load_factor": round(lf, 4),
+                   "find_hit_rate": round(hit, 4),
+                   "parallelism": "single table" if world == 1 else
+                   f"sharded x{world} (NCCL all-to-all)",
+                   "l2": "table 9.2 GB/GPU >> 126 MB L2; every step uses its own input batches"},
+    }
+    if rank == 0:
+        find_keys_s = BATCH * steps / (find_ms * 1e-3)
+        ins_keys_s = BATCH * steps / (ins_ms * 1e-3)
+        result["ops"] = {
+            "find": {"bkvs": round(find_keys_s / 1e9, 4),
+                     "bkvs_2^30": round(find_keys_s / 2 ** 30, 4),
+                     "ms_per_call": round(find_ms / steps, 4)},
+            "insert_or_assign": {"bkvs": round(ins_keys_s / 1e9, 4),
+                                 "bkvs_2^30": round(ins_keys_s / 2 ** 30, 4),
+                                 "ms_per_call": round(ins_ms / steps, 4)}}
+        peak, kind = peaks()
+        rf = {}
+        for name, per_key, t_ms in (("find", FIND_HIT_BYTES, find_ms),
+                                    ("insert_or_assign", INSERT_MIX_BYTES, ins_ms)):
+            ach = per_key * BATCH / (t_ms / steps * 1e-3) / 1e9
+            rf[name] = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak,
+                        "unit": "GB/s", "frac": round(ach / peak, 4),
+                        "algorithmic_bytes_per_key": per_key, "peak_kind": kind}
+        dom = "insert_or_assign" if ins_ms >= find_ms else "find"
+        roof = dict(rf[dom])
+        roof["kernel"] = dom
+        roof["traffic"] = traffic_from_profiles(dom)
+        result["roofline"] = roof
+        result["roofline_by_op"] = rf
+        result["clocks"] = clocks
+        result["gpu_launches"] = 2 * steps if world == 1 else None
+        if world == 1:
+            result["e2e"] = e2e(table, finds, inserts, vals, warm, min(steps, 20))
+            if not args.no_cpu_baseline:
+                result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        table.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def traffic_from_profiles(kernel):
+    p = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    if not os.path.exists(p):
+        return None
+    d = json.load(open(p))
+    v = d.get(kernel)
+    return None if v is None else v.get("bytes_per_launch")
+
+
+def e2e(table, finds, inserts, vals, warm, steps):
+    """Same step through the public API with host buffers: H2D of the keys
+    and values from pinned memory, find + insert_or_assign, D2H of the found
+    values and flags, all inside the timed region."""
+    import torch
+
+    hk = [f.cpu().pin_memory() for f in finds[warm:warm + steps]]
+    hi = [f.cpu().pin_memory() for f in inserts[warm:warm + steps]]
+    hv = [v.cpu().pin_memory() for v in vals[warm:warm + steps]]
+    out_h = torch.empty((BATCH, DIM)).pin_memory()
+    fnd_h = torch.empty(BATCH, dtype=torch.bool).pin_memory()
+    dk = torch.empty(BATCH, dtype=torch.int64, device="cuda")
+    di = torch.empty(BATCH, dtype=torch.int64, device="cuda")
+    dv = torch.empty((BATCH, DIM), device="cuda")
+    do = torch.empty((BATCH, DIM), device="cuda")
+    df = torch.empty(BATCH, dtype=torch.bool, device="cuda")
+    stream = torch.cuda.current_stream()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record(stream)
+    for i in range(steps):
+        dk.copy_(hk[i], non_blocking=True)
+        di.copy_(hi[i], non_blocking=True)
+        dv.copy_(hv[i], non_blocking=True)
+        table.find(BATCH, dk, do, df)
+        table.insert_or_assign(BATCH, di, dv)
+        out_h.copy_(do, non_blocking=True)
+        fnd_h.copy_(df, non_blocking=True)
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    h2d = BATCH * 8 * 2 + BATCH * VALUE_BYTES
+    d2h = BATCH * VALUE_BYTES + BATCH
+    return {"value": round(2 * BATCH * steps / (ms * 1e-3) / 1e9, 4), "unit": UNIT,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps}
+
+
+# --------------------------------------------------------------------------
+# CPU arm: the reference's algorithm (oracle/ restatement) on host threads.
+# --------------------------------------------------------------------------
+def cpu_run(capacity, steps, warm, threads):
+    import numpy as np
+
+    import hkv_oracle as O
+
+    rng = np.random.default_rng(77)
+    t = O.OracleTable(capacity, capacity, dim=DIM, strategy=O.LRU,
+                      max_load_factor=1.0, threads=threads)
+    total = int(capacity * PREFILL_FACTOR)
+    chunk = 1 << 22
+    clock = 1
+    ctr = np.arange(total + (steps + warm + 1) * BATCH, dtype=np.uint64)
+
+    def fmix(x):
+        x = x.copy()
+        with np.errstate(over="ignore"):
+            x ^= x >> np.uint64(33)
+            x *= np.uint64(0xFF51AFD7ED558CCD)
+            x ^= x >> np.uint64(33)
+            x *= np.uint64(0xC4CEB9FE1A85EC53)
+            x ^= x >> np.uint64(33)
+        return x
+
+    vals = rng.random((chunk, DIM)).astype(np.float32)
+    for s in range(0, total, chunk):
+        k = fmix(ctr[s:min(s + chunk, total)])
+        t.set_clock(clock)
+        clock += 1
+        t.insert_or_assign(k, vals[:len(k)])
+    hot = fmix(ctr[max(0, total - min(HOT, capacity // 4)):total])
+    batches = []
+    for s in range(steps + warm):
+        f = hot[rng.integers(0, len(hot), BATCH)]
+        ins = np.concatenate([rng.choice(hot, BATCH // 2, replace=False),
+                              fmix(ctr[total + s * BATCH // 2: total + (s + 1) * BATCH // 2])])
+        batches.append((f, ins, rng.random((BATCH, DIM)).astype(np.float32)))
+    out = np.empty((BATCH, DIM), np.float32)
+    for s in range(warm):
+        t.set_clock(clock)
+        clock += 1
+        t.find(batches[s][0], values=out)
+        t.insert_or_assign(batches[s][1], batches[s][2])
+    t0 = time.perf_counter()
+    for s in range(warm, warm + steps):
+        t.set_clock(clock)
+        clock += 1
+        t.find(batches[s][0], values=out)
+        t.insert_or_assign(batches[s][1], batches[s][2])
+    dt = time.perf_counter() - t0
+    return 2 * BATCH * steps / dt / 1e9, dt, t.load_factor()
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(seconds_hint):
+    cap = 8 << 20
+    threads = cpu_threads()
+    v, dt, lf = cpu_run(cap, 3, 1, threads)
+    return {"value": round(v, 5), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"oracle/ restatement, {cap >> 20} Mi slots (1/8 of the GPU table), "
+                      f"dim 32, kLru, LF {lf:.3f}, 3 steps x (1 Mi find + 1 Mi "
+                      f"insert_or_assign), {dt:.2f} s timed"}
+
+
+def run_reference(args):
+    """`--impl reference`: the reference's CPU algorithm on all host threads."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = cpu_threads()
+    mem_gb = 0
+    try:
+        for line in open("/proc/meminfo"):
+            if line.startswith("MemAvailable"):
+                mem_gb = int(line.split()[1]) / (1 << 20)
+    except OSError:
+        pass
+    cap = CAPACITY if mem_gb > 64 else 8 << 20
+    steps = max(1, min(args.steps, 5))
+    v, dt, lf = cpu_run(cap, steps, min(args.warmup, 1), threads)
+    out = {"metric": METRIC, "value": round(v, 5), "unit": UNIT, "impl": "reference",
+           "n_gpus": args.gpus, "steps": steps, "warmup": min(args.warmup, 1),
+           "ms_per_step": round(dt / steps * 1e3, 3), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "u64 keys / f32 values",
+           "data": "synthetic (seeded)",
+           "config": {"workload": "BASELINE config 2 at load factor 1.0 (find 1 Mi hits "
+                                  "+ insert_or_assign 1 Mi 50/50 per step)",
+                      "capacity": cap, "dim": DIM, "strategy": "kLru",
+                      "load_factor": round(lf, 4)},
+           "cpu_baseline": {"value": round(v, 5), "unit": UNIT, "cores": threads,
+                            "kind": "port",
+                            "sample": f"oracle/ CPU restatement (the reference needs an "
+                                      f"Ascend NPU + CANN), {cap >> 20} Mi slots, "
+                                      f"{steps} steps, {dt:.2f} s"},
+           "e2e": {"value": round(v, 5), "unit": UNIT, "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=40)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

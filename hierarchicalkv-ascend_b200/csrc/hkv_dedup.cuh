@@ -1,0 +1,285 @@
+// hkv_dedup.cuh -- merging duplicate keys of one batch.
+//
+// Insert-like calls with unique_key=false, and the sharded table, first
+// collapse each batch to one representative per distinct key. The scratch
+// is an open-addressing set of 2^k >= 2n slots (key, smallest input index).
+// Representatives are numbered in order of first occurrence (a prefix sum),
+// so the merged batch is deterministic.
+#pragma once
+
+#include "hkv_device.cuh"
+
+namespace hkvb {
+
+constexpr uint32_t kNoIndex = 0xFFFFFFFFu;
+
+struct DedupView {
+  uint64_t* set_keys;   // [cap] EMPTY_KEY when free
+  uint32_t* set_first;  // [cap] smallest input index holding that key
+  uint32_t* set_last;   // [cap] largest input index holding that key
+  uint32_t* set_uid;    // [cap] representative number of that key
+  uint64_t cap;         // power of two
+};
+
+// Stage 1: insert every non-reserved key; slot_of[i] = its set slot
+// (kNoIndex for reserved keys, which the table ignores anyway).
+__global__ void dedup_insert_kernel(DedupView d, const uint64_t* __restrict__ keys,
+                                    uint64_t n, uint32_t* __restrict__ slot_of,
+                                    int* error) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t key = keys[i];
+    if (is_reserved(key)) {
+      slot_of[i] = kNoIndex;
+      continue;
+    }
+    uint64_t s = murmur3(key ^ 0x9E3779B97F4A7C15ull) & (d.cap - 1);
+    uint32_t res = kNoIndex;
+    for (uint64_t probe = 0; probe < d.cap; probe++) {
+      const uint64_t old = cas_u64(d.set_keys + s, kEmptyKey, key);
+      if (old == kEmptyKey || old == key) {
+        atomicMin(d.set_first + s, static_cast<uint32_t>(i));
+        atomicMax(d.set_last + s, static_cast<uint32_t>(i));
+        res = static_cast<uint32_t>(s);
+        break;
+      }
+      s = (s + 1) & (d.cap - 1);
+    }
+    if (res == kNoIndex) atomicOr(error, kErrSpinTimeout);  // set full: cannot happen at 2x
+    slot_of[i] = res;
+  }
+}
+
+// Stage 2: flag[i] = 1 iff input i is the first occurrence of its key.
+__global__ void dedup_flag_kernel(DedupView d, const uint32_t* __restrict__ slot_of,
+                                  uint64_t n, uint32_t* __restrict__ flag) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t s = slot_of[i];
+    flag[i] = (s != kNoIndex && d.set_first[s] == static_cast<uint32_t>(i)) ? 1u : 0u;
+  }
+}
+
+// ---- exclusive prefix sum of uint32 (three passes) -------------------------
+constexpr int kScanThreads = 256;
+constexpr int kScanItems = 8;
+constexpr int kScanTile = kScanThreads * kScanItems;
+
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v,
+                                                         uint32_t* total) {
+  __shared__ uint32_t warp_sums[kScanThreads / 32];
+  const uint32_t lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  uint32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, x, o);
+    if (lane >= static_cast<uint32_t>(o)) x += y;
+  }
+  if (lane == 31) warp_sums[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    uint32_t s = lane < kScanThreads / 32 ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, s, o);
+      if (lane >= static_cast<uint32_t>(o)) s += y;
+    }
+    if (lane < kScanThreads / 32) warp_sums[lane] = s;
+  }
+  __syncthreads();
+  const uint32_t before = (w > 0 ? warp_sums[w - 1] : 0) + x - v;
+  *total = warp_sums[kScanThreads / 32 - 1];
+  __syncthreads();
+  return before;
+}
+
+// pass 1: per-tile exclusive scan in place, tile totals to sums[]
+__global__ void __launch_bounds__(kScanThreads)
+    scan_tiles_kernel(uint32_t* __restrict__ data, uint64_t n,
+                      uint32_t* __restrict__ sums) {
+  const uint64_t base = blockIdx.x * (uint64_t)kScanTile + threadIdx.x * kScanItems;
+  uint32_t v[kScanItems], acc = 0;
+#pragma unroll
+  for (int j = 0; j < kScanItems; j++) {
+    v[j] = (base + j < n) ? data[base + j] : 0u;
+    acc += v[j];
+  }
+  uint32_t total;
+  uint32_t run = block_exclusive_scan(acc, &total);
+#pragma unroll
+  for (int j = 0; j < kScanItems; j++) {
+    if (base + j < n) data[base + j] = run;
+    run += v[j];
+  }
+  if (threadIdx.x == 0) sums[blockIdx.x] = total;
+}
+
+// pass 2: exclusive scan of the tile totals (one block); grand total in *total
+__global__ void __launch_bounds__(kScanThreads)
+    scan_sums_kernel(uint32_t* __restrict__ sums, uint64_t nt,
+                     uint32_t* __restrict__ total_out) {
+  uint32_t carry = 0;
+  for (uint64_t b = 0; b < nt; b += kScanThreads) {
+    const uint64_t i = b + threadIdx.x;
+    const uint32_t v = i < nt ? sums[i] : 0u;
+    uint32_t tot;
+    const uint32_t ex = block_exclusive_scan(v, &tot);
+    if (i < nt) sums[i] = carry + ex;
+    carry += tot;
+  }
+  if (threadIdx.x == 0) *total_out = carry;
+}
+
+// pass 3: add tile offsets
+__global__ void __launch_bounds__(kScanThreads)
+    scan_add_kernel(uint32_t* __restrict__ data, uint64_t n,
+                    const uint32_t* __restrict__ sums) {
+  const uint64_t base = blockIdx.x * (uint64_t)kScanTile;
+  const uint32_t add = sums[blockIdx.x];
+  for (int j = threadIdx.x; j < kScanTile; j += kScanThreads)
+    if (base + j < n) data[base + j] += add;
+}
+
+// Stage 3: representatives. For first occurrence i with rank u:
+// ukeys[u] = key, set_uid[slot] = u, rep_first[u] = i.
+__global__ void dedup_emit_kernel(DedupView d, const uint64_t* __restrict__ keys,
+                                  const uint32_t* __restrict__ slot_of,
+                                  const uint32_t* __restrict__ rank, uint64_t n,
+                                  uint64_t* __restrict__ ukeys,
+                                  uint32_t* __restrict__ rep_first,
+                                  uint32_t* __restrict__ rep_last) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t s = slot_of[i];
+    if (s == kNoIndex || d.set_first[s] != static_cast<uint32_t>(i)) continue;
+    const uint32_t u = rank[i];
+    ukeys[u] = keys[i];
+    d.set_uid[s] = u;
+    rep_first[u] = static_cast<uint32_t>(i);
+    if (rep_last) rep_last[u] = d.set_last[s];
+  }
+}
+
+// Stage 4: inverse map uid_of[i] (kNoIndex for reserved inputs).
+__global__ void dedup_inverse_kernel(DedupView d,
+                                     const uint32_t* __restrict__ slot_of,
+                                     uint64_t n, uint32_t* __restrict__ uid_of) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t s = slot_of[i];
+    uid_of[i] = s == kNoIndex ? kNoIndex : d.set_uid[s];
+  }
+}
+
+// Merged input score of each representative. Lfu: sum of all occurrences
+// (a hit adds every occurrence's score, score_functor.h:157-160); EpochLfu:
+// saturating sum of the low 32 bits (:297-309); others: the last
+// occurrence's score (each later occurrence overwrites, :431-455).
+__global__ void dedup_scores_kernel(int strategy, const uint64_t* __restrict__ scores,
+                                    const uint32_t* __restrict__ uid_of,
+                                    const uint32_t* __restrict__ rep_last,
+                                    uint64_t n, uint64_t* __restrict__ uscores) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t u = uid_of[i];
+    if (u == kNoIndex) continue;
+    if (strategy == kLfu) {
+      atomicAdd(reinterpret_cast<unsigned long long*>(uscores + u), scores[i]);
+    } else if (strategy == kEpochLfu) {
+      atomicAdd(reinterpret_cast<unsigned long long*>(uscores + u),
+                scores[i] & 0xFFFFFFFFull);
+    } else if (rep_last[u] == static_cast<uint32_t>(i)) {
+      uscores[u] = scores[i];
+    }
+  }
+}
+
+__global__ void clamp_low32_kernel(uint64_t* __restrict__ s, uint64_t m) {
+  for (uint64_t u = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; u < m;
+       u += (uint64_t)gridDim.x * blockDim.x)
+    if (s[u] > 0xFFFFFFFFull) s[u] = 0xFFFFFFFFull;
+}
+
+// Gather rows: dst[u] = src[idx[u]].
+template <int VW>
+__global__ void gather_rows_kernel(uint8_t* __restrict__ dst,
+                                   const uint8_t* __restrict__ src,
+                                   const uint32_t* __restrict__ idx, uint64_t m,
+                                   uint32_t vb) {
+  const Tile tile;
+  const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / kTile);
+  for (uint64_t u = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / kTile;
+       u < m; u += ntiles)
+    copy_row<VW>(dst + u * vb, src + static_cast<uint64_t>(idx[u]) * vb, vb,
+                 tile.lane, kTile);
+}
+
+// find_or_insert scatter: every non-representative occurrence whose
+// representative was found or inserted reads the representative's row.
+template <int VW>
+__global__ void scatter_found_rows_kernel(uint8_t* __restrict__ values,
+                                          const uint8_t* __restrict__ urows,
+                                          const uint32_t* __restrict__ uid_of,
+                                          const uint32_t* __restrict__ rep_first,
+                                          const uint8_t* __restrict__ ustatus,
+                                          uint64_t n, uint32_t vb) {
+  const Tile tile;
+  const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / kTile);
+  for (uint64_t i = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / kTile;
+       i < n; i += ntiles) {
+    const uint32_t u = uid_of[i];
+    if (u == kNoIndex) continue;
+    const uint8_t st = ustatus[u];
+    if (st == kRefused || st == kIllegal || st == kTimedOut) continue;
+    copy_row<VW>(values + i * vb, urows + static_cast<uint64_t>(u) * vb, vb,
+                 tile.lane, kTile);
+  }
+}
+
+// insert_and_evict scatter: every occurrence of a refused representative is
+// reported with its own key, value and desired score (each duplicate is
+// refused on its own in the reference, insert_and_evict_kernel.h:291-303).
+template <int S, int VW>
+__global__ void scatter_refused_kernel(const uint64_t* __restrict__ keys,
+                                       const uint8_t* __restrict__ values,
+                                       const uint64_t* __restrict__ scores,
+                                       const uint32_t* __restrict__ uid_of,
+                                       const uint8_t* __restrict__ ustatus,
+                                       uint64_t n, uint32_t vb, uint64_t epoch,
+                                       uint64_t* __restrict__ ev_keys,
+                                       uint8_t* __restrict__ ev_values,
+                                       uint64_t* __restrict__ ev_scores,
+                                       unsigned long long* __restrict__ counter) {
+  __shared__ uint64_t s_clock;
+  if (threadIdx.x == 0) s_clock = global_timer_ns();
+  __syncthreads();
+  const Tile tile;
+  const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / kTile);
+  for (uint64_t i = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / kTile;
+       i < n; i += ntiles) {
+    const uint32_t u = uid_of[i];
+    if (u == kNoIndex || ustatus[u] != kRefused) continue;
+    unsigned long long o = 0;
+    if (tile.lane == 0) {
+      o = atomicAdd(counter, 1ull);
+      ev_keys[o] = keys[i];
+      if (ev_scores)
+        ev_scores[o] = desired_when_missed<S>(scores, i, epoch, s_clock);
+    }
+    o = tile.shfl(o, 0);
+    copy_row<VW>(ev_values + o * vb, values + i * vb, vb, tile.lane, kTile);
+  }
+}
+
+// status[i] = ustatus[uid_of[i]] (kIllegal for reserved inputs).
+__global__ void expand_status_kernel(const uint8_t* __restrict__ ustatus,
+                                     const uint32_t* __restrict__ uid_of,
+                                     uint64_t n, uint8_t* __restrict__ status) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t u = uid_of[i];
+    status[i] = u == kNoIndex ? static_cast<uint8_t>(kIllegal) : ustatus[u];
+  }
+}
+
+}  // namespace hkvb

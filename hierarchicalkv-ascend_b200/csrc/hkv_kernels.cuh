@@ -1,0 +1,961 @@
+// hkv_kernels.cuh -- sm_100a kernels of the HierarchicalKV hot path.
+//
+// One key is handled by a tile of 8 lanes. Each lane loads 16 of the bucket's
+// 128 digests (one 16-byte load, the tile reads the whole 128-byte line),
+// compares them with __vcmpeq4, and the tile picks slots with ballots and
+// shuffles. Values move in VW-byte vectors (16 bytes for float rows whose
+// byte size is a multiple of 16). Locks are the key words themselves: a slot
+// is owned by whoever swapped its key to LOCKED_KEY (reference types.h:65).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "hkv_device.cuh"
+
+namespace hkvb {
+
+// ============================================================================
+// Table initialisation and clear
+// ============================================================================
+
+// initialize_buckets key/digest/score fill (reference init_table_kernel.h
+// :81-104), one launch for any bucket range. Each thread owns 16 slots.
+__global__ void init_buckets_kernel(TableView t, uint64_t b0, uint64_t b1,
+                                    int reset_scores) {
+  const uint64_t chunks = (b1 - b0) * (kBucket / 16);
+  const uint4 ek = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu,
+                              0xFFFFFFFFu);
+  const uint32_t ed = kEmptyDigest * 0x01010101u;
+  const uint4 ed4 = make_uint4(ed, ed, ed, ed);
+  for (uint64_t c = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; c < chunks;
+       c += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t s = b0 * kBucket + c * 16;
+    reinterpret_cast<uint4*>(t.digests + s)[0] = ed4;
+    uint4* k4 = reinterpret_cast<uint4*>(t.keys + s);
+#pragma unroll
+    for (int j = 0; j < 8; j++) k4[j] = ek;
+    if (reset_scores) {
+      uint4* s4 = reinterpret_cast<uint4*>(t.scores + s);
+#pragma unroll
+      for (int j = 0; j < 8; j++) s4[j] = make_uint4(0, 0, 0, 0);
+    }
+    if ((s & (kBucket - 1)) == 0) t.sizes[s >> kBucketShift] = 0;
+  }
+}
+
+// ============================================================================
+// Reductions for size() and fast_load_factor()
+// ============================================================================
+// Sum of sizes[0, nb) into *out (out zeroed by the caller).
+__global__ void sum_sizes_kernel(const int32_t* __restrict__ sizes, uint64_t nb,
+                                 unsigned long long* out) {
+  int64_t s = 0;
+  for (uint64_t b = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; b < nb;
+       b += (uint64_t)gridDim.x * blockDim.x)
+    s += sizes[b];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+  __shared__ int64_t part[32];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    int64_t v = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    if (threadIdx.x == 0) atomicAdd(out, static_cast<unsigned long long>(v));
+  }
+}
+
+// ============================================================================
+// Digest probe shared by the lookup kernels
+// ============================================================================
+struct Locate {
+  uint64_t bkt;
+  uint32_t pos;
+  uint32_t d4;  // digest replicated into 4 bytes
+};
+
+__device__ __forceinline__ Locate locate(const TableView& t, uint64_t key) {
+  const uint64_t h = murmur3(key);
+  const uint64_t g = global_index(t, h);
+  Locate l;
+  l.bkt = g >> kBucketShift;
+  l.pos = static_cast<uint32_t>(g & (kBucket - 1));
+  l.d4 = static_cast<uint32_t>(digest_of_hash(h)) * 0x01010101u;
+  return l;
+}
+
+// Exact find rule of the reference (find_utils.h:31-86) on one tile: the key
+// is found at the digest hit p holding it, unless a digest-empty slot holding
+// EMPTY_KEY comes before p in the group walk. Returns p or -1. `dv` is this
+// lane's 16 digests; keys are read with L1-bypassing loads when `coherent`.
+template <bool kCoherent>
+__device__ __forceinline__ int tile_find(const TableView& t, const Tile& tile,
+                                         const Locate& l, uint4 dv,
+                                         uint64_t key) {
+  const uint64_t* bk = t.keys + l.bkt * kBucket;
+  uint32_t hits = bytes_eq16(dv, l.d4);
+  uint32_t best = 0xFFFFFFFFu;
+  while (hits) {
+    const uint32_t j = __ffs(hits) - 1;
+    hits &= hits - 1;
+    const uint32_t q = tile.lane * kDigestsPerLane + j;
+    const uint64_t k = kCoherent ? ld_cg_u64(bk + q) : __ldg(bk + q);
+    if (k == key) best = min(best, (hit_rank(q, l.pos) << 8) | q);
+  }
+#pragma unroll
+  for (int o = kTile / 2; o > 0; o >>= 1) best = min(best, tile.shfl_xor(best, o));
+  if (best == 0xFFFFFFFFu) return -1;
+  const uint32_t prank = best >> 8;
+  uint32_t empt = bytes_eq16(dv, kEmptyDigest * 0x01010101u);
+  bool stop = false;
+  while (empt) {
+    const uint32_t j = __ffs(empt) - 1;
+    empt &= empt - 1;
+    const uint32_t q = tile.lane * kDigestsPerLane + j;
+    if (empty_rank(q, l.pos) < prank) {
+      const uint64_t k = kCoherent ? ld_cg_u64(bk + q) : __ldg(bk + q);
+      if (k == kEmptyKey) stop = true;
+    }
+  }
+  if (tile.ballot(stop)) return -1;
+  return static_cast<int>(best & 0xFF);
+}
+
+// ============================================================================
+// find / contains (reference find_with_digest_kernel.h:33-108,
+// contains_kernel.h:31-64)
+// ============================================================================
+template <int VW>
+__global__ void __launch_bounds__(256)
+    find_kernel(TableView t, const uint64_t* __restrict__ keys,
+                uint8_t* __restrict__ values, bool* __restrict__ founds,
+                uint64_t* __restrict__ scores, uint64_t n) {
+  const Tile tile;
+  const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / kTile);
+  const uint32_t vb = t.value_bytes;
+  for (uint64_t i = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / kTile;
+       i < n; i += ntiles) {
+    const uint64_t key = __ldg(keys + i);
+    int p = -1;
+    Locate l;
+    if (!is_reserved(key)) {
+      l = locate(t, key);
+      const uint4 dv = __ldg(reinterpret_cast<const uint4*>(
+                                 t.digests + l.bkt * kBucket) +
+                             tile.lane);
+      p = tile_find<false>(t, tile, l, dv, key);
+    }
+    if (tile.lane == 0 && founds != nullptr) founds[i] = p >= 0;
+    if (p >= 0) {
+      if (tile.lane == 0 && scores != nullptr)
+        scores[i] = __ldg(t.scores + l.bkt * kBucket + p);
+      if (values != nullptr)
+        copy_row_nc_cs<VW>(values + i * vb, value_ptr(t, l.bkt, p), vb,
+                           tile.lane, kTile);
+    }
+  }
+}
+
+// ============================================================================
+// Upsert family: insert_or_assign, find_or_insert, insert_and_evict
+// ============================================================================
+enum UpsertMode : int {
+  kModeInsertOrAssign = 0,
+  kModeFindOrInsert = 1,
+  kModeInsertAndEvict = 2
+};
+
+struct UpsertArgs {
+  const uint64_t* keys;
+  const uint8_t* values_in;  // insert_or_assign / insert_and_evict input rows
+  uint8_t* values_io;        // find_or_insert rows (in on a miss, out on a hit)
+  const uint64_t* scores;    // input scores (nullable per strategy)
+  uint64_t n;
+  uint64_t epoch;
+  uint64_t* ev_keys;         // insert_and_evict outputs
+  uint8_t* ev_values;
+  uint64_t* ev_scores;
+  unsigned long long* ev_counter;
+  uint8_t* status;           // optional Occupy code per key
+  const uint32_t* dn;        // optional device-side key count (overrides n)
+  int report_refused;        // insert_and_evict: report refused inputs
+};
+
+// Per-key probe of the unique-key insert kernels (reference
+// insert_or_assign_kernel.h:105-271). On return the tile owns `slot` (its key
+// word is LOCKED_KEY) unless the result is kRefused or kTimedOut.
+//  1. digest hits: CAS(key -> LOCKED); a hit slot that another tile holds
+//     LOCKED is waited for, since it may be this very key being updated.
+//  2. bucket not full: claim the first EMPTY_KEY slot in linear order from
+//     pos with CAS(EMPTY -> LOCKED) (the reference's group walk visits empty
+//     slots in this same order).
+//  3. otherwise evict: the minimum score over the bucket, chosen with the
+//     reference's 16-lane butterfly so ties resolve exactly as there
+//     (lane = owner_idx % 16); refuse iff desired < min; lock the victim with
+//     CAS and re-check its score, retrying on any interference.
+template <int S>
+__device__ __forceinline__ int upsert_probe(const TableView& t, const Tile& tile,
+                                            const Locate& l, uint64_t key,
+                                            uint64_t desired, uint64_t owner_idx,
+                                            uint32_t& slot, uint64_t& vkey,
+                                            uint64_t& vscore) {
+  uint64_t* bk = t.keys + l.bkt * kBucket;
+  const uint64_t* bs = t.scores + l.bkt * kBucket;
+  const uint4 dv =
+      __ldcg(reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) +
+             tile.lane);
+  const int32_t bsize = __ldcg(t.sizes + l.bkt);
+  uint64_t t0 = 0;
+
+  // ---- 1. digest hits ------------------------------------------------------
+  uint32_t hits = bytes_eq16(dv, l.d4);
+  int mine = -1;
+  int timed_out = 0;
+  while (hits) {
+    const uint32_t j = __ffs(hits) - 1;
+    const uint32_t q = tile.lane * kDigestsPerLane + j;
+    const uint64_t old = cas_u64(bk + q, key, kLockedKey);
+    if (old == key) {
+      mine = static_cast<int>(q);
+      break;
+    }
+    if (old == kLockedKey) {
+      if (t0 == 0) t0 = global_timer_ns();
+      if (global_timer_ns() - t0 > kSpinLimitNs) {
+        timed_out = 1;
+        break;
+      }
+      __nanosleep(64);
+      continue;  // retry the same slot
+    }
+    hits &= hits - 1;
+  }
+  const uint32_t fm = tile.ballot(mine >= 0);
+  if (fm) {
+    const int src = __ffs(fm) - 1;
+    // A key can sit in one slot only; release any other lock defensively.
+    if (mine >= 0 && static_cast<int>(tile.lane) != src) exch_u64(bk + mine, key);
+    slot = tile.shfl(static_cast<uint32_t>(mine), src);
+    return kDuplicate;
+  }
+  if (tile.ballot(timed_out)) {
+    if (tile.lane == 0) atomicOr(t.error, kErrSpinTimeout);
+    return kTimedOut;
+  }
+
+  // ---- 2. first EMPTY slot in linear order from pos ------------------------
+  if (bsize < static_cast<int32_t>(kBucket)) {
+    uint32_t empt = bytes_eq16(dv, kEmptyDigest * 0x01010101u);
+    const uint32_t lo = tile.lane * kDigestsPerLane;
+    const uint32_t sh =
+        (l.pos >= lo && l.pos < lo + kDigestsPerLane) ? l.pos - lo : 0;
+    while (true) {
+      uint32_t best = 0xFFFFFFFFu;
+      if (empt) {
+        const uint32_t hi = empt & (0xFFFFu << sh);
+        const uint32_t j = __ffs(hi ? hi : empt) - 1;
+        const uint32_t q = lo + j;
+        best = (linear_rank(q, l.pos) << 8) | q;
+      }
+#pragma unroll
+      for (int o = kTile / 2; o > 0; o >>= 1)
+        best = min(best, tile.shfl_xor(best, o));
+      if (best == 0xFFFFFFFFu) break;
+      const uint32_t q = best & 0xFF;
+      const uint32_t owner = q / kDigestsPerLane;
+      uint64_t old = 0;
+      if (tile.lane == owner) {
+        old = cas_u64(bk + q, kEmptyKey, kLockedKey);
+        empt &= ~(1u << (q - lo));
+      }
+      old = tile.shfl(old, owner);
+      if (old == kEmptyKey) {
+        slot = q;
+        return kOccupiedEmpty;
+      }
+    }
+  }
+
+  // ---- 3. evict the minimum score ------------------------------------------
+  for (int round = 0;; round++) {
+    // lane L scans positions L + 8m: even m belong to virtual lane L, odd m
+    // to virtual lane L+8 of the reference's 16-lane scan (positions c+16j).
+    uint64_t s0 = kMaxScore, s1 = kMaxScore;
+    uint32_t p0 = l.pos, p1 = l.pos;
+#pragma unroll
+    for (int m = 0; m < 16; m++) {
+      const uint32_t q = tile.lane + 8 * m;
+      const uint64_t sc = ld_cg_u64(bs + q);
+      if (m & 1) {
+        if (sc < s1) { s1 = sc; p1 = q; }
+      } else {
+        if (sc < s0) { s0 = sc; p0 = q; }
+      }
+    }
+    // butterfly offset 8: virtual lanes L and L+8 live in this lane
+    {
+      const uint64_t a = s0, b = s1;
+      const uint32_t pa = p0, pb = p1;
+      if (b < a) { s0 = b; p0 = pb; }
+      if (a < b) { s1 = a; p1 = pa; }
+    }
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+      const uint64_t os0 = tile.shfl_xor(s0, o), os1 = tile.shfl_xor(s1, o);
+      const uint32_t op0 = tile.shfl_xor(p0, o), op1 = tile.shfl_xor(p1, o);
+      if (os0 < s0) { s0 = os0; p0 = op0; }
+      if (os1 < s1) { s1 = os1; p1 = op1; }
+    }
+    const uint32_t owner = static_cast<uint32_t>(owner_idx & 15);
+    const uint64_t ms = tile.shfl(owner >= 8 ? s1 : s0, owner & 7);
+    const uint32_t mp = tile.shfl(owner >= 8 ? p1 : p0, owner & 7);
+    if (desired < ms) return kRefused;
+    int r = 0;
+    uint64_t k = 0;
+    if (tile.lane == 0) {
+      k = ld_volatile_u64(bk + mp);
+      if (k != kLockedKey && k != kEmptyKey) {
+        if (cas_u64(bk + mp, k, kLockedKey) == k) {
+          if (ld_volatile_u64(bs + mp) <= ms) {
+            r = (k == kReclaimKey) ? kOccupiedReclaimed : kEvict;
+          } else {
+            exch_u64(bk + mp, k);
+          }
+        }
+      }
+      if (r == 0) {
+        if (t0 == 0) t0 = global_timer_ns();
+        if (global_timer_ns() - t0 > kSpinLimitNs) r = kTimedOut;
+      }
+    }
+    r = tile.shfl(r, 0);
+    if (r == kTimedOut) {
+      if (tile.lane == 0) atomicOr(t.error, kErrSpinTimeout);
+      return kTimedOut;
+    }
+    if (r) {
+      slot = mp;
+      vkey = tile.shfl(k, 0);
+      vscore = ms;
+      return r;
+    }
+    backoff(round);
+  }
+}
+
+// Writes of a locked slot after the probe; releases the lock last.
+template <int Mode, int S, int VW>
+__device__ __forceinline__ void upsert_commit(const TableView& t,
+                                              const Tile& tile,
+                                              const UpsertArgs& a, uint64_t i,
+                                              const Locate& l, uint64_t key,
+                                              uint64_t desired, int res,
+                                              uint32_t slot, uint64_t vkey,
+                                              uint64_t vscore, uint64_t ev_idx) {
+  const uint32_t vb = t.value_bytes;
+  uint64_t* bk = t.keys + l.bkt * kBucket;
+  const uint64_t s = l.bkt * kBucket + slot;
+  if (res == kRefused) {
+    if constexpr (Mode == kModeInsertAndEvict) {
+      if (!a.report_refused) return;
+      // reference insert_and_evict_kernel.h:553-557, :675-683
+      if (tile.lane == 0) {
+        a.ev_keys[ev_idx] = key;
+        if (a.ev_scores) a.ev_scores[ev_idx] = desired;
+      }
+      copy_row<VW>(a.ev_values + ev_idx * vb, a.values_in + i * vb, vb,
+                   tile.lane, kTile);
+    }
+    return;
+  }
+  uint8_t* row = value_ptr(t, l.bkt, slot);
+  if (tile.lane == 0) {
+    const bool ins = res != kDuplicate;
+    uint64_t ns;
+    const uint64_t old = ins ? 0 : ld_volatile_u64(t.scores + s);
+    if (score_on_write<S>(old, a.scores, i, desired, ins, &ns)) {
+      if (ins) t.digests[s] = static_cast<uint8_t>(l.d4);
+      t.scores[s] = ns;
+    }
+    if (res == kOccupiedEmpty || res == kOccupiedReclaimed)
+      atomicAdd(t.sizes + l.bkt, 1);
+    if constexpr (Mode == kModeInsertAndEvict) {
+      if (res == kEvict) {
+        a.ev_keys[ev_idx] = vkey;
+        if (a.ev_scores) a.ev_scores[ev_idx] = vscore;
+      }
+    }
+  }
+  if constexpr (Mode == kModeInsertAndEvict) {
+    if (res == kEvict)
+      copy_row<VW>(a.ev_values + ev_idx * vb, row, vb, tile.lane, kTile);
+  }
+  if constexpr (Mode == kModeFindOrInsert) {
+    if (res == kDuplicate)
+      copy_row<VW>(a.values_io + i * vb, row, vb, tile.lane, kTile);
+    else
+      copy_row<VW>(row, a.values_io + i * vb, vb, tile.lane, kTile);
+  } else {
+    copy_row<VW>(row, a.values_in + i * vb, vb, tile.lane, kTile);
+  }
+  __threadfence();
+  tile.sync();
+  if (tile.lane == 0) exch_u64(bk + slot, key);
+}
+
+template <int Mode, int S, int VW>
+__global__ void __launch_bounds__(256) upsert_kernel(TableView t, UpsertArgs a) {
+  __shared__ uint64_t s_clock;
+  if (threadIdx.x == 0) s_clock = global_timer_ns();
+  __syncthreads();
+  const uint64_t clk = s_clock;
+  const Tile tile;
+  const uint32_t wl = threadIdx.x & 31;
+  const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x / 32);
+  const uint64_t warp = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / 32;
+  const uint64_t n = a.dn != nullptr ? *a.dn : a.n;
+  for (uint64_t base = warp * 4; base < n; base += nwarps * 4) {
+    const uint64_t i = base + (wl >> 3);
+    int res = kIllegal;
+    uint32_t slot = 0;
+    uint64_t vkey = 0, vscore = 0, desired = 0, key = 0;
+    Locate l;
+    l.bkt = 0;
+    l.pos = 0;
+    l.d4 = 0;
+    if (i < n) {
+      key = a.keys[i];
+      if (!is_reserved(key)) {
+        desired = desired_when_missed<S>(a.scores, i, a.epoch, clk);
+        l = locate(t, key);
+        res = upsert_probe<S>(t, tile, l, key, desired, i, slot, vkey, vscore);
+      }
+      if (a.status != nullptr && tile.lane == 0) a.status[i] = res;
+    }
+    uint64_t ev_idx = 0;
+    if constexpr (Mode == kModeInsertAndEvict) {
+      // warp-aggregated compaction: one atomic per warp (reference uses a
+      // prefix sum plus block and global atomics, insert_and_evict_kernel.h
+      // :594-642)
+      const bool need =
+          (res == kEvict || (res == kRefused && a.report_refused)) &&
+          tile.lane == 0;
+      const uint32_t vote = __ballot_sync(0xFFFFFFFFu, need);
+      unsigned long long wbase = 0;
+      if (wl == 0 && vote) wbase = atomicAdd(a.ev_counter, __popc(vote));
+      wbase = __shfl_sync(0xFFFFFFFFu, wbase, 0);
+      ev_idx = wbase + __popc(vote & ((1u << tile.shift) - 1u));
+    }
+    if (res != kIllegal && res != kTimedOut)
+      upsert_commit<Mode, S, VW>(t, tile, a, i, l, key, desired, res, slot,
+                                 vkey, vscore, ev_idx);
+  }
+}
+
+// ============================================================================
+// accum_or_assign (reference accum_or_assign_kernel.h:55-155 with
+// find_and_lock, find_utils.h:94-228): one warp per key, 32-slot windows
+// from pos. Waits on LOCKED slots (bounded), so duplicate keys in one batch
+// serialise on the key word.
+// ============================================================================
+struct AccumArgs {
+  const uint64_t* keys;
+  const uint8_t* values;
+  const bool* accum_or_assigns;
+  const uint64_t* scores;
+  uint64_t n;
+  uint64_t epoch;
+  uint8_t* status;
+};
+
+template <class VT>
+struct AccumOps;
+template <>
+struct AccumOps<float> {
+  static __device__ __forceinline__ float add(float a, float b) { return a + b; }
+};
+template <>
+struct AccumOps<__half> {
+  static __device__ __forceinline__ __half add(__half a, __half b) {
+    return __float2half_rn(__half2float(a) + __half2float(b));
+  }
+};
+template <>
+struct AccumOps<__nv_bfloat16> {
+  static __device__ __forceinline__ __nv_bfloat16 add(__nv_bfloat16 a,
+                                                      __nv_bfloat16 b) {
+    return __float2bfloat16_rn(__bfloat162float(a) + __bfloat162float(b));
+  }
+};
+
+// Returns Occupy; on success the warp owns `slot` and `evk` holds the key it
+// displaced (EMPTY_KEY / RECLAIM_KEY / victim).
+__device__ __forceinline__ int warp_find_and_lock(const TableView& t,
+                                                  const Locate& l, uint64_t key,
+                                                  uint64_t desired,
+                                                  uint32_t& slot,
+                                                  uint64_t& evk) {
+  const uint32_t lane = threadIdx.x & 31;
+  uint64_t* bk = t.keys + l.bkt * kBucket;
+  const uint64_t* bs = t.scores + l.bkt * kBucket;
+  const uint64_t t0 = global_timer_ns();
+  auto expired = [&]() { return global_timer_ns() - t0 > kSpinLimitNs; };
+restart:
+  if (expired()) return kTimedOut;
+  for (uint32_t w = 0; w < kBucket; w += 32) {
+    const uint32_t q = (l.pos + w + lane) & (kBucket - 1);
+    while (true) {
+      const uint64_t k = ld_volatile_u64(bk + q);
+      const uint32_t hit = __ballot_sync(0xFFFFFFFFu, k == key);
+      if (hit) {
+        const int src = __ffs(hit) - 1;
+        uint64_t old = 0;
+        if (static_cast<int>(lane) == src) old = cas_u64(bk + q, key, kLockedKey);
+        old = __shfl_sync(0xFFFFFFFFu, old, src);
+        if (old == key) {
+          slot = __shfl_sync(0xFFFFFFFFu, q, src);
+          evk = key;
+          return kDuplicate;
+        }
+        if (expired()) return kTimedOut;
+        __nanosleep(64);
+        continue;
+      }
+      if (__ballot_sync(0xFFFFFFFFu, k == kLockedKey)) {
+        if (expired()) return kTimedOut;
+        __nanosleep(64);
+        continue;
+      }
+      uint32_t em = __ballot_sync(0xFFFFFFFFu, k == kEmptyKey);
+      while (em) {
+        const int src = __ffs(em) - 1;
+        uint64_t old = 0;
+        if (static_cast<int>(lane) == src)
+          old = cas_u64(bk + q, kEmptyKey, kLockedKey);
+        old = __shfl_sync(0xFFFFFFFFu, old, src);
+        if (old == kEmptyKey) {
+          slot = __shfl_sync(0xFFFFFFFFu, q, src);
+          evk = kEmptyKey;
+          return kOccupiedEmpty;
+        }
+        if (old == key || old == kLockedKey) goto restart;
+        em &= ~(1u << src);
+      }
+      break;
+    }
+  }
+  // eviction: each lane the first strictly-smallest score over its slots
+  uint64_t lm = kMaxScore, lk = kEmptyKey;
+  uint32_t lp = 0;
+  for (uint32_t w = 0; w < kBucket; w += 32) {
+    const uint32_t q = (l.pos + w + lane) & (kBucket - 1);
+    const uint64_t sc = ld_volatile_u64(bs + q);
+    if (sc < lm) {
+      uint64_t k;
+      bool gave_up = false;
+      while ((k = ld_volatile_u64(bk + q)) == kLockedKey) {
+        if (expired()) {
+          gave_up = true;
+          break;
+        }
+        __nanosleep(64);
+      }
+      if (!gave_up && k != kEmptyKey) {
+        lm = sc;
+        lp = q;
+        lk = k;
+      }
+    }
+  }
+  uint64_t gm = lm;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) gm = min(gm, __shfl_xor_sync(0xFFFFFFFFu, gm, o));
+  if (desired < gm) return kRefused;
+  const uint32_t vote = __ballot_sync(0xFFFFFFFFu, lm <= gm);
+  if (vote) {
+    const int src = __ffs(vote) - 1;
+    int ok = 0;
+    if (static_cast<int>(lane) == src) {
+      if (cas_u64(bk + lp, lk, kLockedKey) == lk) {
+        if (ld_volatile_u64(bs + lp) <= gm)
+          ok = 1;
+        else
+          exch_u64(bk + lp, lk);
+      }
+    }
+    ok = __shfl_sync(0xFFFFFFFFu, ok, src);
+    if (ok) {
+      slot = __shfl_sync(0xFFFFFFFFu, lp, src);
+      evk = __shfl_sync(0xFFFFFFFFu, lk, src);
+      return evk == kReclaimKey ? kOccupiedReclaimed : kEvict;
+    }
+  }
+  __nanosleep(128);
+  goto restart;
+}
+
+template <int S, class VT>
+__global__ void __launch_bounds__(256) accum_kernel(TableView t, AccumArgs a) {
+  __shared__ uint64_t s_clock;
+  if (threadIdx.x == 0) s_clock = global_timer_ns();
+  __syncthreads();
+  const uint64_t clk = s_clock;
+  const uint32_t lane = threadIdx.x & 31;
+  const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x / 32);
+  const uint32_t vb = t.value_bytes;
+  const uint32_t ne = vb / sizeof(VT);
+  for (uint64_t i = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / 32;
+       i < a.n; i += nwarps) {
+    const uint64_t key = a.keys[i];
+    int res = kIllegal;
+    if (!is_reserved(key)) {
+      const uint64_t desired = desired_when_missed<S>(a.scores, i, a.epoch, clk);
+      const bool is_accum = a.accum_or_assigns[i];
+      const Locate l = locate(t, key);
+      uint32_t slot = 0;
+      uint64_t evk = 0;
+      res = warp_find_and_lock(t, l, key, desired, slot, evk);
+      if (res == kTimedOut) {
+        if (lane == 0) atomicOr(t.error, kErrSpinTimeout);
+      } else if (res != kRefused) {
+        uint64_t* bk = t.keys + l.bkt * kBucket;
+        const uint64_t s = l.bkt * kBucket + slot;
+        if ((is_accum && res != kDuplicate) || (!is_accum && res == kDuplicate)) {
+          // reference :114-128: undo the lock and skip
+          if (lane == 0) exch_u64(bk + slot, res == kDuplicate ? key : evk);
+          res = kIllegal;
+        } else {
+          VT* dst = reinterpret_cast<VT*>(value_ptr(t, l.bkt, slot));
+          const VT* src = reinterpret_cast<const VT*>(a.values + i * vb);
+          for (uint32_t e = lane; e < ne; e += 32)
+            dst[e] = is_accum ? AccumOps<VT>::add(src[e], dst[e]) : src[e];
+          if (lane == 0) {
+            if (res == kOccupiedEmpty || res == kOccupiedReclaimed)
+              atomicAdd(t.sizes + l.bkt, 1);
+            const bool ins = res != kDuplicate;
+            uint64_t ns;
+            if (score_on_write<S>(ld_volatile_u64(t.scores + s), a.scores, i,
+                                  desired, ins, &ns)) {
+              t.digests[s] = static_cast<uint8_t>(l.d4);
+              t.scores[s] = ns;
+            }
+          }
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) exch_u64(bk + slot, key);
+        }
+      }
+    }
+    if (a.status != nullptr && lane == 0) a.status[i] = res;
+  }
+}
+
+// ============================================================================
+// assign_scores (reference assign_scores_kernel_with_filter.h:38-141) and
+// erase (reference remove_kernel.h:33-113)
+// ============================================================================
+// Locks the slot holding `key` (found with the find rule when kStopRule);
+// waits on LOCKED hits. Returns slot or -1; -2 on timeout.
+template <bool kStopRule>
+__device__ __forceinline__ int tile_lock_existing(const TableView& t,
+                                                  const Tile& tile,
+                                                  const Locate& l, uint64_t key,
+                                                  uint4 dv) {
+  uint64_t* bk = t.keys + l.bkt * kBucket;
+  uint32_t hits = bytes_eq16(dv, l.d4);
+  int mine = -1, to = 0;
+  uint64_t t0 = 0;
+  while (hits) {
+    const uint32_t j = __ffs(hits) - 1;
+    const uint32_t q = tile.lane * kDigestsPerLane + j;
+    const uint64_t old = cas_u64(bk + q, key, kLockedKey);
+    if (old == key) {
+      mine = static_cast<int>(q);
+      break;
+    }
+    if (old == kLockedKey) {
+      if (t0 == 0) t0 = global_timer_ns();
+      if (global_timer_ns() - t0 > kSpinLimitNs) {
+        to = 1;
+        break;
+      }
+      __nanosleep(64);
+      continue;
+    }
+    hits &= hits - 1;
+  }
+  const uint32_t fm = tile.ballot(mine >= 0);
+  if (!fm) return tile.ballot(to) ? -2 : -1;
+  const int src = __ffs(fm) - 1;
+  if (mine >= 0 && static_cast<int>(tile.lane) != src) exch_u64(bk + mine, key);
+  const uint32_t p = tile.shfl(static_cast<uint32_t>(mine), src);
+  if constexpr (kStopRule) {
+    // a digest-empty EMPTY_KEY slot before p in the walk hides the key
+    uint32_t empt = bytes_eq16(dv, kEmptyDigest * 0x01010101u);
+    const uint32_t pr = hit_rank(p, l.pos);
+    bool stop = false;
+    while (empt) {
+      const uint32_t j = __ffs(empt) - 1;
+      empt &= empt - 1;
+      const uint32_t q = tile.lane * kDigestsPerLane + j;
+      if (empty_rank(q, l.pos) < pr && ld_volatile_u64(bk + q) == kEmptyKey)
+        stop = true;
+    }
+    if (tile.ballot(stop)) {
+      if (tile.lane == 0) exch_u64(bk + p, key);
+      return -1;
+    }
+  }
+  return static_cast<int>(p);
+}
+
+template <int S>
+__global__ void __launch_bounds__(256)
+    assign_scores_kernel(TableView t, const uint64_t* __restrict__ keys,
+                         const uint64_t* __restrict__ scores, uint64_t n,
+                         uint64_t epoch) {
+  __shared__ uint64_t s_clock;
+  if (threadIdx.x == 0) s_clock = global_timer_ns();
+  __syncthreads();
+  const uint64_t clk = s_clock;
+  const Tile tile;
+  const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / kTile);
+  for (uint64_t i = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / kTile;
+       i < n; i += ntiles) {
+    const uint64_t key = keys[i];
+    if (is_reserved(key)) continue;
+    const Locate l = locate(t, key);
+    const uint4 dv =
+        __ldcg(reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) +
+               tile.lane);
+    const int p = tile_lock_existing<true>(t, tile, l, key, dv);
+    if (p == -2) {
+      if (tile.lane == 0) atomicOr(t.error, kErrSpinTimeout);
+      continue;
+    }
+    if (p < 0) continue;
+    if (tile.lane == 0) {
+      const uint64_t s = l.bkt * kBucket + p;
+      uint64_t ns;
+      if (score_without_missed<S>(ld_volatile_u64(t.scores + s), scores, i,
+                                  epoch, clk, &ns))
+        t.scores[s] = ns;
+      __threadfence();
+      exch_u64(t.keys + s, key);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    erase_kernel(TableView t, const uint64_t* __restrict__ keys, uint64_t n) {
+  const Tile tile;
+  const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / kTile);
+  for (uint64_t i = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / kTile;
+       i < n; i += ntiles) {
+    const uint64_t key = keys[i];
+    if (is_reserved(key)) continue;
+    const Locate l = locate(t, key);
+    const uint4 dv =
+        __ldcg(reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) +
+               tile.lane);
+    const int p = tile_lock_existing<false>(t, tile, l, key, dv);
+    if (p == -2) {
+      if (tile.lane == 0) atomicOr(t.error, kErrSpinTimeout);
+      continue;
+    }
+    if (p < 0) continue;
+    if (tile.lane == 0) {
+      const uint64_t s = l.bkt * kBucket + p;
+      t.scores[s] = 0;
+      t.digests[s] = kReclaimDigest;
+      atomicSub(t.sizes + l.bkt, 1);
+      __threadfence();
+      exch_u64(t.keys + s, kReclaimKey);
+    }
+  }
+}
+
+// clear (reference clear_kernel.h:29-60) is init_buckets_kernel without the
+// score reset.
+
+// ============================================================================
+// export_batch (reference dump_kernel.h:37-123): slots [offset, offset+len);
+// each warp takes 32 consecutive slots, ballot-compacts the live ones and
+// reserves its output range with one atomic. Output order is not
+// deterministic (same as the reference).
+// ============================================================================
+template <int VW>
+__global__ void __launch_bounds__(256)
+    export_kernel(TableView t, uint64_t offset, uint64_t len,
+                  unsigned long long* __restrict__ counter,
+                  uint64_t* __restrict__ out_keys, uint8_t* __restrict__ out_values,
+                  uint64_t* __restrict__ out_scores) {
+  const uint32_t lane = threadIdx.x & 31;
+  const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x / 32);
+  const uint32_t vb = t.value_bytes;
+  const Tile tile;
+  for (uint64_t w = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / 32;
+       w * 32 < len; w += nwarps) {
+    const uint64_t r = w * 32 + lane;
+    const uint64_t s = offset + r;
+    uint64_t k = kEmptyKey;
+    if (r < len) k = t.keys[s];
+    const bool live = !is_reserved(k);
+    const uint32_t vote = __ballot_sync(0xFFFFFFFFu, live);
+    if (!vote) continue;
+    unsigned long long base = 0;
+    if (lane == 0) base = atomicAdd(counter, __popc(vote));
+    base = __shfl_sync(0xFFFFFFFFu, base, 0);
+    if (live) {
+      const uint64_t o = base + __popc(vote & ((1u << lane) - 1u));
+      out_keys[o] = k;
+      if (out_scores != nullptr) out_scores[o] = t.scores[s];
+    }
+    if (out_values == nullptr) continue;
+    // tile j copies the live slots with rank j, j+4, ...
+    const uint32_t cnt = __popc(vote);
+    uint32_t rest = vote;
+    for (uint32_t rank = 0; rank < cnt; rank++) {
+      const uint32_t src = __ffs(rest) - 1;
+      rest &= rest - 1;
+      if ((rank & 3) != (lane >> 3)) continue;
+      const uint64_t ss = offset + w * 32 + src;
+      copy_row<VW>(out_values + (base + rank) * vb,
+                   value_ptr(t, ss >> kBucketShift,
+                             static_cast<uint32_t>(ss & (kBucket - 1))),
+                   vb, tile.lane, kTile);
+    }
+  }
+}
+
+// ============================================================================
+// Rehash after the bucket count doubles (reference rehash_kernel.h:30-207).
+// One warp per old bucket. The bucket and its new sibling are staged in
+// shared memory; every lane runs the reference's sequential algorithm on the
+// staged copy (identical decisions, warp-uniform control flow), lane 0
+// writes the staged state, and the whole warp moves each value row as the
+// algorithm moves its key. The final layout is the reference's, slot for
+// slot.
+// ============================================================================
+struct RehashStage {
+  uint64_t okeys[kBucket];
+  uint64_t oscores[kBucket];
+  uint64_t nkeys[kBucket];
+  uint64_t nscores[kBucket];
+  uint8_t ohome[kBucket];
+};
+
+template <int VW>
+__device__ __forceinline__ void warp_move_value(const TableView& t,
+                                                uint64_t sb, uint32_t sp,
+                                                uint64_t db, uint32_t dp,
+                                                uint32_t lane) {
+  copy_row<VW>(value_ptr(t, db, dp), value_ptr(t, sb, sp), t.value_bytes,
+               lane, 32);
+}
+
+template <int VW>
+__global__ void __launch_bounds__(256)
+    rehash_kernel(TableView t, uint64_t old_nb) {
+  __shared__ RehashStage stage[8];
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t wi = threadIdx.x >> 5;
+  RehashStage& st = stage[wi];
+  const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x / 32);
+  const uint64_t new_cap = t.capacity;  // power of two after doubling
+  for (uint64_t b = blockIdx.x * (uint64_t)(blockDim.x / 32) + wi; b < old_nb;
+       b += nwarps) {
+    const uint64_t nbk = b + old_nb;
+    for (uint32_t q = lane; q < kBucket; q += 32) {
+      const uint64_t k = t.keys[b * kBucket + q];
+      st.okeys[q] = k;
+      st.oscores[q] = t.scores[b * kBucket + q];
+      st.nkeys[q] = kEmptyKey;
+      st.nscores[q] = 0;
+      st.ohome[q] = static_cast<uint8_t>(murmur3(k) & (kBucket - 1));
+    }
+    __syncwarp();
+    int32_t moved = 0, removed = 0;
+    uint32_t kp = 0;
+    while (kp < kBucket) {
+      const uint64_t k = st.okeys[kp];
+      if (k == kEmptyKey || k == kReclaimKey) {
+        kp++;
+        continue;
+      }
+      const uint64_t g = murmur3(k) & (new_cap - 1);
+      if ((g >> kBucketShift) == b) {
+        kp++;
+        continue;
+      }
+      // copy_key_to_new_bucket, rehash_kernel.h:30-67
+      const uint32_t npos = static_cast<uint32_t>(g & (kBucket - 1));
+      uint32_t dst = kBucket;
+      for (uint32_t off = 0; off < kBucket; off++) {
+        const uint32_t p = (npos + off) & (kBucket - 1);
+        if (st.nkeys[p] == kEmptyKey) {
+          dst = p;
+          break;
+        }
+      }
+      if (dst < kBucket) {
+        warp_move_value<VW>(t, b, kp, nbk, dst, lane);
+        __syncwarp();
+        if (lane == 0) {
+          st.nkeys[dst] = k;
+          st.nscores[dst] = st.oscores[kp];
+        }
+        moved++;
+      }
+      removed++;
+      if (lane == 0) st.okeys[kp] = kEmptyKey;
+      __syncwarp();
+      // defragmentation_for_rehash, rehash_kernel.h:77-135
+      uint32_t rm = kp, off = 1;
+      while (off < kBucket) {
+        const uint32_t cur = (rm + off) & (kBucket - 1);
+        const uint64_t ck = st.okeys[cur];
+        if (ck == kEmptyKey) break;
+        const uint32_t start = st.ohome[cur];
+        if ((start <= rm && rm < cur) || (cur < start && start <= rm) ||
+            (rm < cur && cur < start)) {
+          warp_move_value<VW>(t, b, cur, b, rm, lane);
+          __syncwarp();
+          if (lane == 0) {
+            st.okeys[rm] = ck;
+            st.oscores[rm] = st.oscores[cur];
+            st.ohome[rm] = st.ohome[cur];
+            st.okeys[cur] = kEmptyKey;
+          }
+          __syncwarp();
+          rm = cur;
+          off = 1;
+        } else {
+          off++;
+        }
+      }
+      kp = 0;
+    }
+    __syncwarp();
+    for (uint32_t q = lane; q < kBucket; q += 32) {
+      const uint64_t ok = st.okeys[q], nk = st.nkeys[q];
+      t.keys[b * kBucket + q] = ok;
+      t.scores[b * kBucket + q] = st.oscores[q];
+      t.digests[b * kBucket + q] =
+          ok == kEmptyKey ? kEmptyDigest : digest_of_hash(murmur3(ok));
+      t.keys[nbk * kBucket + q] = nk;
+      t.scores[nbk * kBucket + q] = st.nscores[q];
+      t.digests[nbk * kBucket + q] =
+          nk == kEmptyKey ? kEmptyDigest : digest_of_hash(murmur3(nk));
+    }
+    if (lane == 0) {
+      t.sizes[b] -= removed;
+      t.sizes[nbk] = moved;
+    }
+    __syncwarp();
+  }
+}
+
+}  // namespace hkvb

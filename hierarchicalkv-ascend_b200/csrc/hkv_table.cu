@@ -1,0 +1,1083 @@
+// hkv_table.cu -- host logic of the B200 HierarchicalKV table and its C ABI.
+//
+// Mirrors the reference host class (include/hkv_hashtable.h) and table core
+// (include/table.h): option checks, bucket-count rule, value slices split
+// between HBM and mapped pinned host memory, auto-grow before insert-like
+// calls, reserve by doubling plus rehash. All device work is in
+// hkv_kernels.cuh / hkv_dedup.cuh; there is no CPU fallback.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cstring>
+#include <string>
+
+#include "hkv_dedup.cuh"
+#include "hkv_kernels.cuh"
+#include "hkv_table.cuh"
+
+namespace hkvb {
+
+namespace {
+
+thread_local std::string g_last_error;
+
+uint32_t elem_size(int vt) {
+  switch (vt) {
+    case HKV_VALUE_F32: return 4;
+    case HKV_VALUE_F16: return 2;
+    case HKV_VALUE_BF16: return 2;
+    case HKV_VALUE_F64: return 8;
+    case HKV_VALUE_U32: return 4;
+    case HKV_VALUE_U16: return 2;
+    case HKV_VALUE_I8: return 1;
+    case HKV_VALUE_U64: return 8;
+    default: return 0;
+  }
+}
+
+bool is_pow2(uint64_t x) { return x && !(x & (x - 1)); }
+
+uint32_t log2_floor(uint64_t x) {
+  uint32_t r = 0;
+  while ((2ull << r) <= x) r++;
+  return r;
+}
+
+uint64_t ceil_div(uint64_t a, uint64_t b) { return (a + b - 1) / b; }
+
+constexpr uint64_t MB(uint64_t n) { return n << 20; }
+constexpr uint64_t GB(uint64_t n) { return n << 30; }
+
+// get_slice_size, reference table.h:244-268.
+uint64_t slice_size_rule(uint64_t max_size, uint32_t value_bytes) {
+  const uint64_t min_slice = kBucket * static_cast<uint64_t>(value_bytes);
+  const uint64_t max_table = max_size * value_bytes;
+  uint64_t s;
+  if (max_table >= GB(128))
+    s = GB(16);
+  else if (max_table >= GB(16))
+    s = GB(2);
+  else if (max_table >= GB(2))
+    s = MB(128);
+  else if (max_table >= MB(128))
+    s = MB(16);
+  else if (max_table >= MB(16))
+    s = MB(1);
+  else
+    s = min_slice;
+  return std::max(std::max(min_slice, s), MB(2));
+}
+
+// precomputation_for_kernel_div, reference table.h:106-127.
+void magic_for(uint64_t d, uint64_t* magic, uint32_t* shift) {
+  unsigned __int128 one = 1;
+  uint64_t s = 0;
+  for (; s < 64; s++)
+    if ((one << s) >= d) break;
+  const unsigned __int128 m = ((one << 64) * ((one << s) - d)) / d + 1;
+  *magic = static_cast<uint64_t>(m);
+  *shift = static_cast<uint32_t>(s - 1);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+TableImpl::TableImpl(const hkv_options& o, int key_type, int value_type,
+                     int strategy)
+    : opt_(o), key_type_(key_type), value_type_(value_type),
+      strategy_(strategy) {
+  // option checks, reference hkv_hashtable.h:962-1042
+  HKV_REQUIRE(key_type == HKV_KEY_U64 || key_type == HKV_KEY_I64,
+              HKV_ERR_INVALID, "The key_type must be int64_t or uint64_t.");
+  HKV_REQUIRE(strategy >= HKV_LRU && strategy <= HKV_CUSTOMIZED,
+              HKV_ERR_INVALID, "unknown evict strategy");
+  elem_bytes_ = elem_size(value_type);
+  HKV_REQUIRE(elem_bytes_ != 0, HKV_ERR_INVALID, "unknown value type");
+  HKV_REQUIRE(o.dim > 0, HKV_ERR_INVALID, "dim must be positive");
+  HKV_REQUIRE(o.reserved_key_start_bit >= 0 && o.reserved_key_start_bit <= 62,
+              HKV_ERR_INVALID,
+              "options.reserved_key_start_bit should >= 0 and <= 62.");
+  HKV_REQUIRE(o.reserved_key_start_bit == 0, HKV_ERR_UNSUPPORTED,
+              "only the default reserved keys (reserved_key_start_bit = 0) "
+              "are supported");
+  HKV_REQUIRE(o.max_bucket_size >= 16, HKV_ERR_INVALID,
+              "Bucket size should be greater than or equal to 16");
+  HKV_REQUIRE(is_pow2(o.max_bucket_size), HKV_ERR_INVALID,
+              "Bucket size should be the pow of 2");
+  HKV_REQUIRE(o.max_bucket_size == kBucket, HKV_ERR_UNSUPPORTED,
+              "this build supports max_bucket_size = 128 only");
+  HKV_REQUIRE(is_pow2(o.num_of_buckets_per_alloc), HKV_ERR_INVALID,
+              "Then `num_of_buckets_per_alloc` should be the pow of 2");
+  HKV_REQUIRE(o.init_capacity >= o.num_of_buckets_per_alloc * o.max_bucket_size,
+              HKV_ERR_INVALID,
+              "Then `num_of_buckets_per_alloc` must be equal or less than "
+              "initial required buckets number");
+  HKV_REQUIRE(!(o.io_by_cpu && o.max_hbm_for_vectors != 0), HKV_ERR_INVALID,
+              "[HierarchicalKV] `io_by_cpu` should not be true when "
+              "`max_hbm_for_vectors` is not 0!");
+  HKV_REQUIRE(!o.io_by_cpu, HKV_ERR_UNSUPPORTED,
+              "io_by_cpu is not supported: values are read zero-copy");
+  HKV_REQUIRE(!o.api_lock, HKV_ERR_UNSUPPORTED, "api_lock is not supported");
+  value_bytes_ = static_cast<uint32_t>(o.dim * elem_bytes_);
+
+  if (o.device_id >= 0) {
+    CUDA_TRY(cudaSetDevice(o.device_id));
+    device_ = o.device_id;
+  } else {
+    CUDA_TRY(cudaGetDevice(&device_));
+    opt_.device_id = device_;
+  }
+  CUDA_TRY(cudaDeviceGetAttribute(&sm_count_, cudaDevAttrMultiProcessorCount,
+                                  device_));
+
+  // bucket count rule, reference table.h:299-309
+  max_size_ = std::max(o.init_capacity, o.max_capacity);
+  if (o.init_capacity * 2 > max_size_) {
+    num_buckets_ = 1 + (max_size_ - 1) / kBucket;
+  } else {
+    num_buckets_ = 1;
+    while (num_buckets_ * kBucket < o.init_capacity) num_buckets_ *= 2;
+  }
+  capacity_ = num_buckets_ * kBucket;
+  magic_for(capacity_, &div_magic_, &div_shift_);
+  reach_max_ = o.init_capacity * 2 > o.max_capacity;  // hkv_hashtable.h:1021
+  remaining_hbm_ = o.max_hbm_for_vectors;
+
+  // slice geometry: 2^slice_shift buckets per slice, never more than the
+  // initial bucket count so that doubling appends whole slices.
+  const uint64_t bucket_bytes = kBucket * static_cast<uint64_t>(value_bytes_);
+  const uint64_t rule = std::max<uint64_t>(
+      1, slice_size_rule(max_size_, value_bytes_) / bucket_bytes);
+  slice_shift_ = std::min(log2_floor(rule), log2_floor(num_buckets_));
+
+  const size_t slots = capacity_;
+  CUDA_TRY(cudaMalloc(&keys_, slots * 8));
+  CUDA_TRY(cudaMalloc(&scores_, slots * 8));
+  CUDA_TRY(cudaMalloc(&digests_, slots));
+  CUDA_TRY(cudaMalloc(&sizes_, num_buckets_ * 4));
+  CUDA_TRY(cudaMalloc(&d_error_, sizeof(int)));
+  CUDA_TRY(cudaMemset(d_error_, 0, sizeof(int)));
+  CUDA_TRY(cudaMalloc(&d_scratch_, 4 * sizeof(unsigned long long)));
+  CUDA_TRY(cudaHostAlloc(&h_scratch_, 4 * sizeof(unsigned long long),
+                         cudaHostAllocDefault));
+  const uint64_t max_buckets = std::max<uint64_t>(
+      num_buckets_, ceil_div(std::max<uint64_t>(max_size_, capacity_), kBucket));
+  d_slices_cap_ = ceil_div(max_buckets, 1ull << slice_shift_) + 1;
+  CUDA_TRY(cudaMalloc(&d_slices_, d_slices_cap_ * sizeof(uint8_t*)));
+  allocate_slices(0, num_buckets_);
+  upload_slices();
+  const TableView v = view();
+  init_buckets_kernel<<<std::max(1, warp_grid(num_buckets_)), 256>>>(
+      v, 0, num_buckets_, 1);
+  CUDA_TRY(cudaGetLastError());
+  CUDA_TRY(cudaDeviceSynchronize());
+}
+
+TableImpl::~TableImpl() {
+  cudaDeviceSynchronize();
+  for (auto& s : slices_) {
+    if (s.host)
+      cudaFreeHost(s.host);
+    else
+      cudaFree(s.dev);
+  }
+  cudaFree(keys_);
+  cudaFree(scores_);
+  cudaFree(digests_);
+  cudaFree(sizes_);
+  cudaFree(d_error_);
+  cudaFree(d_scratch_);
+  cudaFree(d_slices_);
+  cudaFreeHost(h_scratch_);
+}
+
+// initialize_buckets slice placement, reference table.h:143-184: slices go to
+// HBM while the remaining budget holds a whole slice, then to pinned host
+// memory mapped into the device address space.
+void TableImpl::allocate_slices(uint64_t b0, uint64_t b1) {
+  const uint64_t bps = 1ull << slice_shift_;
+  const uint64_t bucket_bytes = kBucket * static_cast<uint64_t>(value_bytes_);
+  for (uint64_t b = b0; b < b1; b += bps) {
+    const uint64_t cnt = std::min(bps, b1 - b);
+    const size_t bytes = cnt * bucket_bytes;
+    Slice s{nullptr, nullptr, bytes};
+    if (remaining_hbm_ >= bytes) {
+      CUDA_TRY(cudaMalloc(&s.dev, bytes));
+      remaining_hbm_ -= bytes;
+    } else {
+      pure_hbm_ = false;
+      CUDA_TRY(cudaHostAlloc(&s.host, bytes,
+                             cudaHostAllocMapped | cudaHostAllocPortable));
+      CUDA_TRY(cudaHostGetDevicePointer(reinterpret_cast<void**>(&s.dev),
+                                        s.host, 0));
+    }
+    slices_.push_back(s);
+  }
+}
+
+void TableImpl::upload_slices() {
+  HKV_REQUIRE(slices_.size() <= d_slices_cap_, HKV_ERR_RUNTIME,
+              "slice table overflow");
+  std::vector<uint8_t*> p(slices_.size());
+  for (size_t i = 0; i < slices_.size(); i++) p[i] = slices_[i].dev;
+  CUDA_TRY(cudaMemcpy(d_slices_, p.data(), p.size() * sizeof(uint8_t*),
+                      cudaMemcpyHostToDevice));
+}
+
+TableView TableImpl::view() const {
+  TableView v;
+  v.keys = keys_;
+  v.scores = scores_;
+  v.digests = digests_;
+  v.sizes = sizes_;
+  v.slices = d_slices_;
+  v.values0 = slices_.empty() ? nullptr : slices_[0].dev;
+  v.error = d_error_;
+  v.capacity = capacity_;
+  v.num_buckets = num_buckets_;
+  v.div_magic = div_magic_;
+  v.div_shift = div_shift_;
+  v.cap_pow2 = is_pow2(capacity_) ? 1 : 0;
+  v.slice_shift = slice_shift_;
+  v.single_slice = slices_.size() == 1 ? 1 : 0;
+  v.value_bytes = value_bytes_;
+  v.pad = 0;
+  return v;
+}
+
+int TableImpl::tile_grid(size_t n) const {
+  const uint64_t blocks = ceil_div(std::max<size_t>(n, 1), 256 / kTile);
+  return static_cast<int>(std::min<uint64_t>(blocks, sm_count_ * 64ull));
+}
+
+int TableImpl::warp_grid(size_t nwarps) const {
+  const uint64_t blocks = ceil_div(std::max<size_t>(nwarps, 1), 8);
+  return static_cast<int>(std::min<uint64_t>(blocks, sm_count_ * 64ull));
+}
+
+// Vector width for value rows: the largest of 16/4/1 bytes dividing the row
+// size and the alignment of every row base pointer.
+int TableImpl::value_width(std::initializer_list<const void*> ptrs) const {
+  int w = 16;
+  auto fits = [&](int x) {
+    if (value_bytes_ % x) return false;
+    for (const void* p : ptrs)
+      if (p && reinterpret_cast<uintptr_t>(p) % x) return false;
+    return true;
+  };
+  while (w > 1 && !fits(w)) w = (w == 16) ? 4 : 1;
+  return w;
+}
+
+#define DISPATCH_VW(vw, ...)            \
+  do {                                  \
+    if ((vw) == 16) {                   \
+      constexpr int VW = 16;            \
+      __VA_ARGS__;                      \
+    } else if ((vw) == 4) {             \
+      constexpr int VW = 4;             \
+      __VA_ARGS__;                      \
+    } else {                            \
+      constexpr int VW = 1;             \
+      __VA_ARGS__;                      \
+    }                                   \
+  } while (0)
+
+#define DISPATCH_STRATEGY(st, ...)      \
+  do {                                  \
+    switch (st) {                       \
+      case kLru: {                      \
+        constexpr int S = kLru;         \
+        __VA_ARGS__;                    \
+        break;                          \
+      }                                 \
+      case kLfu: {                      \
+        constexpr int S = kLfu;         \
+        __VA_ARGS__;                    \
+        break;                          \
+      }                                 \
+      case kEpochLru: {                 \
+        constexpr int S = kEpochLru;    \
+        __VA_ARGS__;                    \
+        break;                          \
+      }                                 \
+      case kEpochLfu: {                 \
+        constexpr int S = kEpochLfu;    \
+        __VA_ARGS__;                    \
+        break;                          \
+      }                                 \
+      default: {                        \
+        constexpr int S = kCustomized;  \
+        __VA_ARGS__;                    \
+        break;                          \
+      }                                 \
+    }                                   \
+  } while (0)
+
+// check_evict_strategy, reference hkv_hashtable.h:3270-3298.
+void TableImpl::check_strategy(const uint64_t* scores, bool ignore) const {
+  if (ignore) return;
+  if (strategy_ == kLru || strategy_ == kEpochLru)
+    HKV_REQUIRE(scores == nullptr, HKV_ERR_INVALID,
+                "the scores should not be specified when running on LRU or "
+                "Epoch LRU mode.");
+  if (strategy_ == kLfu || strategy_ == kEpochLfu)
+    HKV_REQUIRE(scores != nullptr, HKV_ERR_INVALID,
+                "the scores should be specified when running on LFU or Epoch "
+                "LFU mode.");
+  if (strategy_ == kCustomized)
+    HKV_REQUIRE(scores != nullptr, HKV_ERR_INVALID,
+                "the scores should be specified when running on customized "
+                "mode.");
+  if (strategy_ == kEpochLru || strategy_ == kEpochLfu)
+    HKV_REQUIRE(epoch_ != kIgnoredEpoch, HKV_ERR_INVALID,
+                "the global_epoch is invalid and should be assigned by calling "
+                "`set_global_epoch` when running on Epoch LRU or Epoch LFU "
+                "mode.");
+}
+
+uint64_t TableImpl::sum_sizes(uint64_t nb, cudaStream_t s) {
+  CUDA_TRY(cudaMemsetAsync(d_scratch_, 0, sizeof(unsigned long long), s));
+  const int blocks = static_cast<int>(
+      std::min<uint64_t>(ceil_div(nb, 256 * 4), sm_count_ * 4ull));
+  sum_sizes_kernel<<<std::max(blocks, 1), 256, 0, s>>>(sizes_, nb, d_scratch_);
+  CUDA_TRY(cudaGetLastError());
+  CUDA_TRY(cudaMemcpyAsync(h_scratch_, d_scratch_, sizeof(unsigned long long),
+                           cudaMemcpyDeviceToHost, s));
+  CUDA_TRY(cudaStreamSynchronize(s));
+  return h_scratch_[0];
+}
+
+// fast_load_factor, reference hkv_hashtable.h:3229-3268.
+float TableImpl::fast_load_factor(size_t delta, cudaStream_t s) {
+  const uint64_t N = std::min<uint64_t>(num_buckets_, 1024);
+  const uint64_t total = sum_sizes(N, s);
+  return static_cast<float>((delta * 1.0) / (capacity_ * 1.0) +
+                            (total * 1.0) / (opt_.max_bucket_size * N * 1.0));
+}
+
+// auto-grow before insert-like calls, reference hkv_hashtable.h:1103-1106.
+void TableImpl::auto_grow(size_t n, cudaStream_t s) {
+  while (!reach_max_ && fast_load_factor(n, s) > opt_.max_load_factor)
+    reserve(capacity_ * 2, s);
+}
+
+size_t TableImpl::size(cudaStream_t s) { return sum_sizes(num_buckets_, s); }
+
+float TableImpl::load_factor(cudaStream_t s) {
+  return static_cast<float>((size(s) * 1.0) / (capacity_ * 1.0));
+}
+
+// ---------------------------------------------------------------------------
+// Upsert family
+// ---------------------------------------------------------------------------
+void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
+                       const uint8_t* values_in, uint8_t* values_io,
+                       const uint64_t* scores, uint64_t* ev_keys,
+                       uint8_t* ev_values, uint64_t* ev_scores,
+                       uint64_t* d_counter, cudaStream_t s, bool unique,
+                       bool ignore, uint8_t* status) {
+  const int st = ignore ? kCustomized : strategy_;
+  const TableView v = view();
+  UpsertArgs a;
+  std::memset(&a, 0, sizeof a);
+  a.epoch = epoch_;
+  a.ev_keys = ev_keys;
+  a.ev_values = ev_values;
+  a.ev_scores = ev_scores;
+  a.ev_counter = reinterpret_cast<unsigned long long*>(d_counter);
+  a.report_refused = 1;
+  a.status = status;
+  const uint8_t* rows = mode == kModeFindOrInsert ? values_io : values_in;
+
+  if (unique) {
+    a.keys = keys;
+    a.values_in = values_in;
+    a.values_io = values_io;
+    a.scores = scores;
+    a.n = n;
+    const int vw = value_width({rows, ev_values});
+    const int grid = warp_grid(ceil_div(n, 4));
+    DISPATCH_STRATEGY(st, DISPATCH_VW(vw, {
+      if (mode == kModeInsertOrAssign)
+        upsert_kernel<kModeInsertOrAssign, S, VW><<<grid, 256, 0, s>>>(v, a);
+      else if (mode == kModeFindOrInsert)
+        upsert_kernel<kModeFindOrInsert, S, VW><<<grid, 256, 0, s>>>(v, a);
+      else
+        upsert_kernel<kModeInsertAndEvict, S, VW><<<grid, 256, 0, s>>>(v, a);
+    }));
+    CUDA_TRY(cudaGetLastError());
+    return;
+  }
+
+  // ---- duplicate keys: merge to one representative per key ---------------
+  Workspace ws(s);
+  const DedupResult d =
+      dedup_batch(n, keys, scores, st, ws, s, sm_count_, d_error_);
+  uint8_t* ustatus = ws.get<uint8_t>(n);
+  uint8_t* urows = ws.get<uint8_t>(n * static_cast<size_t>(value_bytes_));
+  const uint32_t* rep_first = d.rep_first;
+  const uint32_t* rep_last = d.rep_last;
+  const uint32_t* uid_of = d.uid_of;
+  const int vwr = value_width({rows});
+  // insert value: last occurrence (insert_or_assign, insert_and_evict: each
+  // later duplicate overwrites) or first occurrence (find_or_insert: the
+  // first inserts, the rest hit and read it back)
+  DISPATCH_VW(vwr, gather_rows_kernel<VW><<<tile_grid(n), 256, 0, s>>>(
+                       urows, rows, mode == kModeFindOrInsert ? rep_first
+                                                              : rep_last,
+                       n, value_bytes_));
+  CUDA_TRY(cudaGetLastError());
+
+  a.keys = d.ukeys;
+  a.values_in = urows;
+  a.values_io = urows;
+  a.scores = d.uscores;
+  a.n = n;
+  a.dn = d.dm;
+  a.status = ustatus;
+  a.report_refused = 0;
+  CUDA_TRY(cudaMemsetAsync(ustatus, kIllegal, n, s));
+  const int vw = value_width({urows, ev_values});
+  const int grid = warp_grid(ceil_div(n, 4));
+  DISPATCH_STRATEGY(st, DISPATCH_VW(vw, {
+    if (mode == kModeInsertOrAssign)
+      upsert_kernel<kModeInsertOrAssign, S, VW><<<grid, 256, 0, s>>>(v, a);
+    else if (mode == kModeFindOrInsert)
+      upsert_kernel<kModeFindOrInsert, S, VW><<<grid, 256, 0, s>>>(v, a);
+    else
+      upsert_kernel<kModeInsertAndEvict, S, VW><<<grid, 256, 0, s>>>(v, a);
+  }));
+  CUDA_TRY(cudaGetLastError());
+  if (mode == kModeFindOrInsert) {
+    DISPATCH_VW(vwr, scatter_found_rows_kernel<VW><<<tile_grid(n), 256, 0, s>>>(
+                         values_io, urows, uid_of, rep_first, ustatus, n,
+                         value_bytes_));
+  } else if (mode == kModeInsertAndEvict) {
+    const int vwe = value_width({rows, ev_values});
+    DISPATCH_STRATEGY(st, DISPATCH_VW(vwe, {
+      scatter_refused_kernel<S, VW><<<tile_grid(n), 256, 0, s>>>(
+          keys, rows, scores, uid_of, ustatus, n, value_bytes_, epoch_,
+          ev_keys, ev_values, ev_scores,
+          reinterpret_cast<unsigned long long*>(d_counter));
+    }));
+  }
+  if (status != nullptr) {
+    // per-input status: each occurrence reports its representative's result
+    expand_status_kernel<<<static_cast<int>(std::min<uint64_t>(
+                               ceil_div(n, 256), sm_count_ * 32ull)),
+                           256, 0, s>>>(ustatus, uid_of, n, status);
+  }
+  CUDA_TRY(cudaGetLastError());
+}
+
+DedupResult dedup_batch(size_t n, const uint64_t* keys, const uint64_t* scores,
+                        int strategy, Workspace& ws, cudaStream_t s,
+                        int sm_count, int* d_error) {
+  uint64_t cap = 1024;
+  while (cap < 2 * static_cast<uint64_t>(n)) cap <<= 1;
+  DedupView d;
+  d.cap = cap;
+  d.set_keys = ws.get<uint64_t>(cap);
+  d.set_first = ws.get<uint32_t>(cap);
+  d.set_last = ws.get<uint32_t>(cap);
+  d.set_uid = ws.get<uint32_t>(cap);
+  CUDA_TRY(cudaMemsetAsync(d.set_keys, 0xFF, cap * 8, s));
+  CUDA_TRY(cudaMemsetAsync(d.set_first, 0xFF, cap * 4, s));
+  CUDA_TRY(cudaMemsetAsync(d.set_last, 0, cap * 4, s));
+  DedupResult r;
+  uint32_t* slot_of = ws.get<uint32_t>(n);
+  uint32_t* rank = ws.get<uint32_t>(n);
+  r.uid_of = ws.get<uint32_t>(n);
+  const uint64_t ntiles = ceil_div(n, kScanTile);
+  uint32_t* sums = ws.get<uint32_t>(ntiles + 1);
+  r.dm = ws.get<uint32_t>(1);
+  r.ukeys = ws.get<uint64_t>(n);
+  r.rep_first = ws.get<uint32_t>(n);
+  r.rep_last = ws.get<uint32_t>(n);
+  r.uscores = scores ? ws.get<uint64_t>(n) : nullptr;
+  const int g1 = static_cast<int>(
+      std::min<uint64_t>(ceil_div(n, 256), sm_count * 32ull));
+  dedup_insert_kernel<<<g1, 256, 0, s>>>(d, keys, n, slot_of, d_error);
+  dedup_flag_kernel<<<g1, 256, 0, s>>>(d, slot_of, n, rank);
+  scan_tiles_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, s>>>(rank, n,
+                                                                       sums);
+  scan_sums_kernel<<<1, kScanThreads, 0, s>>>(sums, ntiles, r.dm);
+  scan_add_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, s>>>(rank, n,
+                                                                     sums);
+  dedup_emit_kernel<<<g1, 256, 0, s>>>(d, keys, slot_of, rank, n, r.ukeys,
+                                       r.rep_first, r.rep_last);
+  dedup_inverse_kernel<<<g1, 256, 0, s>>>(d, slot_of, n, r.uid_of);
+  if (scores) {
+    CUDA_TRY(cudaMemsetAsync(r.uscores, 0, n * 8, s));
+    dedup_scores_kernel<<<g1, 256, 0, s>>>(strategy, scores, r.uid_of,
+                                           r.rep_last, n, r.uscores);
+    if (strategy == kEpochLfu)
+      clamp_low32_kernel<<<g1, 256, 0, s>>>(r.uscores, n);
+  }
+  CUDA_TRY(cudaGetLastError());
+  return r;
+}
+
+void TableImpl::insert_or_assign(size_t n, const uint64_t* keys,
+                                 const uint8_t* values, const uint64_t* scores,
+                                 cudaStream_t s, bool unique, bool ignore) {
+  if (n == 0) return;
+  auto_grow(n, s);
+  check_strategy(scores, ignore);
+  HKV_REQUIRE(keys != nullptr && values != nullptr, HKV_ERR_INVALID,
+              "keys and values must not be null");
+  upsert(kModeInsertOrAssign, n, keys, values, nullptr, scores, nullptr,
+         nullptr, nullptr, nullptr, s, unique, ignore, nullptr);
+}
+
+void TableImpl::insert_and_evict(size_t n, const uint64_t* keys,
+                                 const uint8_t* values, const uint64_t* scores,
+                                 uint64_t* ev_keys, uint8_t* ev_values,
+                                 uint64_t* ev_scores, uint64_t* d_counter,
+                                 cudaStream_t s, bool unique, bool ignore) {
+  if (n == 0) return;
+  // reference hkv_hashtable.h:1273-1276: null buffers return silently
+  if (keys == nullptr || values == nullptr || ev_keys == nullptr ||
+      ev_values == nullptr || d_counter == nullptr)
+    return;
+  auto_grow(n, s);
+  check_strategy(scores, ignore);
+  if (!pure_hbm_)
+    throw HkvError{HKV_ERR_RUNTIME,
+                   "Only allow insert_and_evict in pure HBM mode."};
+  upsert(kModeInsertAndEvict, n, keys, values, nullptr, scores, ev_keys,
+         ev_values, ev_scores, d_counter, s, unique, ignore, nullptr);
+}
+
+void TableImpl::find_or_insert(size_t n, const uint64_t* keys, uint8_t* values,
+                               const uint64_t* scores, cudaStream_t s,
+                               bool unique, bool ignore, uint8_t* status) {
+  if (n == 0) return;
+  auto_grow(n, s);
+  check_strategy(scores, ignore);
+  HKV_REQUIRE(keys != nullptr && values != nullptr, HKV_ERR_INVALID,
+              "keys and values must not be null");
+  upsert(kModeFindOrInsert, n, keys, nullptr, values, scores, nullptr, nullptr,
+         nullptr, nullptr, s, unique, ignore, status);
+}
+
+void TableImpl::accum_or_assign(size_t n, const uint64_t* keys,
+                                const uint8_t* values, const bool* accum,
+                                const uint64_t* scores, cudaStream_t s,
+                                bool ignore) {
+  // reference hkv_hashtable.h:1445-1450
+  if (value_type_ == HKV_VALUE_F64 || value_type_ == HKV_VALUE_U16 ||
+      value_type_ == HKV_VALUE_U32)
+    throw HkvError{HKV_ERR_RUNTIME,
+                   "[accum_or_assign] Does not support double/uint16_t/"
+                   "uint32_t value_type."};
+  HKV_REQUIRE(value_type_ == HKV_VALUE_F32 || value_type_ == HKV_VALUE_F16 ||
+                  value_type_ == HKV_VALUE_BF16,
+              HKV_ERR_UNSUPPORTED,
+              "accum_or_assign supports float, half and bfloat16 values");
+  if (n == 0) return;
+  auto_grow(n, s);
+  check_strategy(scores, ignore);
+  if (keys == nullptr || values == nullptr || accum == nullptr) return;
+  const int st = ignore ? kCustomized : strategy_;
+  const TableView v = view();
+  AccumArgs a{keys, values, accum, scores, n, epoch_, nullptr};
+  const int grid = warp_grid(n);
+  DISPATCH_STRATEGY(st, {
+    if (value_type_ == HKV_VALUE_F32)
+      accum_kernel<S, float><<<grid, 256, 0, s>>>(v, a);
+    else if (value_type_ == HKV_VALUE_F16)
+      accum_kernel<S, __half><<<grid, 256, 0, s>>>(v, a);
+    else
+      accum_kernel<S, __nv_bfloat16><<<grid, 256, 0, s>>>(v, a);
+  });
+  CUDA_TRY(cudaGetLastError());
+}
+
+void TableImpl::assign_scores(size_t n, const uint64_t* keys,
+                              const uint64_t* scores, cudaStream_t s) {
+  if (n == 0) return;
+  check_strategy(scores, false);
+  const TableView v = view();
+  DISPATCH_STRATEGY(strategy_, {
+    assign_scores_kernel<S><<<tile_grid(n), 256, 0, s>>>(v, keys, scores, n,
+                                                         epoch_);
+  });
+  CUDA_TRY(cudaGetLastError());
+}
+
+void TableImpl::find(size_t n, const uint64_t* keys, uint8_t* values,
+                     bool* founds, uint64_t* scores, cudaStream_t s) {
+  if (n == 0) return;
+  // reference find_with_digest_kernel.h:42-44: null values -> nothing written
+  if (keys == nullptr || values == nullptr) return;
+  const TableView v = view();
+  const int vw = value_width({values});
+  DISPATCH_VW(vw, find_kernel<VW><<<tile_grid(n), 256, 0, s>>>(
+                      v, keys, values, founds, scores, n));
+  CUDA_TRY(cudaGetLastError());
+}
+
+void TableImpl::contains(size_t n, const uint64_t* keys, bool* founds,
+                         cudaStream_t s) {
+  if (n == 0) return;
+  if (keys == nullptr || founds == nullptr) return;
+  const TableView v = view();
+  find_kernel<16><<<tile_grid(n), 256, 0, s>>>(v, keys, nullptr, founds,
+                                               nullptr, n);
+  CUDA_TRY(cudaGetLastError());
+}
+
+void TableImpl::erase(size_t n, const uint64_t* keys, cudaStream_t s) {
+  if (n == 0 || keys == nullptr) return;
+  erase_kernel<<<tile_grid(n), 256, 0, s>>>(view(), keys, n);
+  CUDA_TRY(cudaGetLastError());
+}
+
+void TableImpl::clear(cudaStream_t s) {
+  init_buckets_kernel<<<warp_grid(num_buckets_), 256, 0, s>>>(
+      view(), 0, num_buckets_, 0);
+  CUDA_TRY(cudaGetLastError());
+}
+
+void TableImpl::export_batch(size_t n, size_t offset, uint64_t* d_counter,
+                             uint64_t* keys, uint8_t* values, uint64_t* scores,
+                             cudaStream_t s) {
+  HKV_REQUIRE(d_counter != nullptr, HKV_ERR_INVALID, "d_counter is null");
+  CUDA_TRY(cudaMemsetAsync(d_counter, 0, sizeof(uint64_t), s));
+  if (offset >= capacity_) return;
+  n = std::min<size_t>(capacity_ - offset, n);
+  if (n == 0) return;
+  const int vw = value_width({values});
+  DISPATCH_VW(vw, export_kernel<VW><<<warp_grid(ceil_div(n, 32)), 256, 0, s>>>(
+                      view(), offset, n,
+                      reinterpret_cast<unsigned long long*>(d_counter), keys,
+                      values, scores));
+  CUDA_TRY(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------------------
+// reserve, reference hkv_hashtable.h:2873-2935 and table.h:360-377
+// ---------------------------------------------------------------------------
+void TableImpl::double_capacity(cudaStream_t s) {
+  const uint64_t old_nb = num_buckets_, new_nb = old_nb * 2;
+  const size_t old_slots = old_nb * kBucket, new_slots = new_nb * kBucket;
+  uint64_t *nk = nullptr, *ns = nullptr;
+  uint8_t* nd = nullptr;
+  int32_t* nz = nullptr;
+  CUDA_TRY(cudaMalloc(&nk, new_slots * 8));
+  CUDA_TRY(cudaMalloc(&ns, new_slots * 8));
+  CUDA_TRY(cudaMalloc(&nd, new_slots));
+  CUDA_TRY(cudaMalloc(&nz, new_nb * 4));
+  CUDA_TRY(cudaMemcpyAsync(nk, keys_, old_slots * 8, cudaMemcpyDeviceToDevice, s));
+  CUDA_TRY(cudaMemcpyAsync(ns, scores_, old_slots * 8, cudaMemcpyDeviceToDevice, s));
+  CUDA_TRY(cudaMemcpyAsync(nd, digests_, old_slots, cudaMemcpyDeviceToDevice, s));
+  CUDA_TRY(cudaMemcpyAsync(nz, sizes_, old_nb * 4, cudaMemcpyDeviceToDevice, s));
+  CUDA_TRY(cudaStreamSynchronize(s));
+  cudaFree(keys_);
+  cudaFree(scores_);
+  cudaFree(digests_);
+  cudaFree(sizes_);
+  keys_ = nk;
+  scores_ = ns;
+  digests_ = nd;
+  sizes_ = nz;
+  allocate_slices(old_nb, new_nb);
+  upload_slices();
+  num_buckets_ = new_nb;
+  capacity_ = new_slots;
+  magic_for(capacity_, &div_magic_, &div_shift_);
+  const TableView v = view();
+  init_buckets_kernel<<<warp_grid(old_nb), 256, 0, s>>>(v, old_nb, new_nb, 1);
+  const int vw = value_width({});
+  const int grid = static_cast<int>(
+      std::min<uint64_t>(ceil_div(old_nb, 8), sm_count_ * 16ull));
+  DISPATCH_VW(vw, rehash_kernel<VW><<<grid, 256, 0, s>>>(v, old_nb));
+  CUDA_TRY(cudaGetLastError());
+  CUDA_TRY(cudaStreamSynchronize(s));
+}
+
+void TableImpl::reserve(size_t new_capacity, cudaStream_t s) {
+  if (reach_max_ || new_capacity > opt_.max_capacity) {
+    reach_max_ = capacity_ * 2 > opt_.max_capacity;
+    return;
+  }
+  CUDA_TRY(cudaStreamSynchronize(s));
+  while (capacity_ < new_capacity && capacity_ * 2 <= opt_.max_capacity)
+    double_capacity(s);
+  reach_max_ = capacity_ * 2 > opt_.max_capacity;
+}
+
+void TableImpl::check_device_error(cudaStream_t s) {
+  CUDA_TRY(cudaStreamSynchronize(s));
+  int e = 0;
+  CUDA_TRY(cudaMemcpy(&e, d_error_, sizeof(int), cudaMemcpyDeviceToHost));
+  if (e) {
+    CUDA_TRY(cudaMemset(d_error_, 0, sizeof(int)));
+    throw HkvError{HKV_ERR_TIMEOUT,
+                   "a device lock wait exceeded its time limit; the keys "
+                   "involved were not processed"};
+  }
+}
+
+void TableImpl::get_state(uint64_t* keys, uint64_t* scores, uint8_t* digests,
+                          int32_t* sizes, uint8_t* values) {
+  CUDA_TRY(cudaDeviceSynchronize());
+  if (keys) CUDA_TRY(cudaMemcpy(keys, keys_, capacity_ * 8, cudaMemcpyDeviceToHost));
+  if (scores) CUDA_TRY(cudaMemcpy(scores, scores_, capacity_ * 8, cudaMemcpyDeviceToHost));
+  if (digests) CUDA_TRY(cudaMemcpy(digests, digests_, capacity_, cudaMemcpyDeviceToHost));
+  if (sizes) CUDA_TRY(cudaMemcpy(sizes, sizes_, num_buckets_ * 4, cudaMemcpyDeviceToHost));
+  if (values) {
+    size_t off = 0;
+    for (auto& sl : slices_) {
+      CUDA_TRY(cudaMemcpy(values + off, sl.dev, sl.bytes, cudaMemcpyDefault));
+      off += sl.bytes;
+    }
+  }
+}
+
+void TableImpl::set_state(const uint64_t* keys, const uint64_t* scores,
+                          const uint8_t* digests, const int32_t* sizes,
+                          const uint8_t* values) {
+  CUDA_TRY(cudaDeviceSynchronize());
+  if (keys) CUDA_TRY(cudaMemcpy(keys_, keys, capacity_ * 8, cudaMemcpyHostToDevice));
+  if (scores) CUDA_TRY(cudaMemcpy(scores_, scores, capacity_ * 8, cudaMemcpyHostToDevice));
+  if (digests) CUDA_TRY(cudaMemcpy(digests_, digests, capacity_, cudaMemcpyHostToDevice));
+  if (sizes) CUDA_TRY(cudaMemcpy(sizes_, sizes, num_buckets_ * 4, cudaMemcpyHostToDevice));
+  if (values) {
+    size_t off = 0;
+    for (auto& sl : slices_) {
+      CUDA_TRY(cudaMemcpy(sl.dev, values + off, sl.bytes, cudaMemcpyDefault));
+      off += sl.bytes;
+    }
+  }
+  CUDA_TRY(cudaDeviceSynchronize());
+}
+
+void set_last_error(const std::string& m) { g_last_error = m; }
+const char* last_error() { return g_last_error.c_str(); }
+
+}  // namespace hkvb
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+using hkvb::HkvError;
+using hkvb::TableImpl;
+
+#define HKV_API_BEGIN try {
+#define HKV_API_END                                     \
+  return HKV_OK;                                        \
+  }                                                     \
+  catch (const HkvError& e) {                           \
+    hkvb::set_last_error(e.msg);                        \
+    return e.code;                                      \
+  }                                                     \
+  catch (const std::exception& e) {                     \
+    hkvb::set_last_error(e.what());                     \
+    return HKV_ERR_RUNTIME;                             \
+  }
+
+#define HKV_TABLE(t)                                                      \
+  HKV_REQUIRE((t) != nullptr && (t)->impl != nullptr, HKV_ERR_INVALID,    \
+              "null table");                                              \
+  TableImpl* T = (t)->impl
+
+static inline cudaStream_t as_stream(void* s) {
+  return reinterpret_cast<cudaStream_t>(s);
+}
+
+extern "C" {
+
+void hkv_options_init(hkv_options* o) {
+  std::memset(o, 0, sizeof(*o));
+  o->max_bucket_size = 128;
+  o->dim = 64;
+  o->max_load_factor = 0.5f;
+  o->block_size = 128;
+  o->io_block_size = 1024;
+  o->device_id = -1;
+  o->num_of_buckets_per_alloc = 1;
+}
+
+const char* hkv_last_error(void) { return hkvb::last_error(); }
+
+int hkv_table_create(const hkv_options* options, int key_type, int value_type,
+                     int evict_strategy, hkv_table** out) {
+  HKV_API_BEGIN
+  HKV_REQUIRE(options != nullptr && out != nullptr, HKV_ERR_INVALID,
+              "null argument");
+  *out = nullptr;
+  auto* t = new hkv_table;
+  try {
+    t->impl = new TableImpl(*options, key_type, value_type, evict_strategy);
+  } catch (...) {
+    delete t;
+    throw;
+  }
+  *out = t;
+  HKV_API_END
+}
+
+int hkv_table_destroy(hkv_table* table) {
+  HKV_API_BEGIN
+  if (table) {
+    delete table->impl;
+    delete table;
+  }
+  HKV_API_END
+}
+
+int hkv_insert_or_assign(hkv_table* table, size_t n, const void* keys,
+                         const void* values, const uint64_t* scores,
+                         void* stream, bool unique_key,
+                         bool ignore_evict_strategy) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  T->insert_or_assign(n, static_cast<const uint64_t*>(keys),
+                      static_cast<const uint8_t*>(values), scores,
+                      as_stream(stream), unique_key, ignore_evict_strategy);
+  HKV_API_END
+}
+
+int hkv_insert_and_evict(hkv_table* table, size_t n, const void* keys,
+                         const void* values, const uint64_t* scores,
+                         void* evicted_keys, void* evicted_values,
+                         uint64_t* evicted_scores, uint64_t* d_evicted_counter,
+                         void* stream, bool unique_key,
+                         bool ignore_evict_strategy) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  T->insert_and_evict(n, static_cast<const uint64_t*>(keys),
+                      static_cast<const uint8_t*>(values), scores,
+                      static_cast<uint64_t*>(evicted_keys),
+                      static_cast<uint8_t*>(evicted_values), evicted_scores,
+                      d_evicted_counter, as_stream(stream), unique_key,
+                      ignore_evict_strategy);
+  HKV_API_END
+}
+
+int hkv_insert_and_evict_count(hkv_table* table, size_t n, const void* keys,
+                               const void* values, const uint64_t* scores,
+                               void* evicted_keys, void* evicted_values,
+                               uint64_t* evicted_scores, void* stream,
+                               bool unique_key, bool ignore_evict_strategy,
+                               size_t* h_evicted_count) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  HKV_REQUIRE(h_evicted_count != nullptr, HKV_ERR_INVALID, "null count");
+  *h_evicted_count = 0;
+  if (n == 0) return HKV_OK;
+  cudaStream_t s = as_stream(stream);
+  uint64_t* d = nullptr;
+  CUDA_TRY(cudaMallocAsync(&d, sizeof(uint64_t), s));
+  CUDA_TRY(cudaMemsetAsync(d, 0, sizeof(uint64_t), s));
+  try {
+    T->insert_and_evict(n, static_cast<const uint64_t*>(keys),
+                        static_cast<const uint8_t*>(values), scores,
+                        static_cast<uint64_t*>(evicted_keys),
+                        static_cast<uint8_t*>(evicted_values), evicted_scores,
+                        d, s, unique_key, ignore_evict_strategy);
+  } catch (...) {
+    cudaFreeAsync(d, s);
+    throw;
+  }
+  uint64_t h = 0;
+  CUDA_TRY(cudaMemcpyAsync(&h, d, sizeof(uint64_t), cudaMemcpyDeviceToHost, s));
+  CUDA_TRY(cudaFreeAsync(d, s));
+  CUDA_TRY(cudaStreamSynchronize(s));
+  *h_evicted_count = h;
+  HKV_API_END
+}
+
+int hkv_accum_or_assign(hkv_table* table, size_t n, const void* keys,
+                        const void* value_or_deltas,
+                        const bool* accum_or_assigns, const uint64_t* scores,
+                        void* stream, bool ignore_evict_strategy) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  T->accum_or_assign(n, static_cast<const uint64_t*>(keys),
+                     static_cast<const uint8_t*>(value_or_deltas),
+                     accum_or_assigns, scores, as_stream(stream),
+                     ignore_evict_strategy);
+  HKV_API_END
+}
+
+int hkv_find_or_insert(hkv_table* table, size_t n, const void* keys,
+                       void* values, const uint64_t* scores, void* stream,
+                       bool unique_key, bool ignore_evict_strategy) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  T->find_or_insert(n, static_cast<const uint64_t*>(keys),
+                    static_cast<uint8_t*>(values), scores, as_stream(stream),
+                    unique_key, ignore_evict_strategy);
+  HKV_API_END
+}
+
+int hkv_assign_scores(hkv_table* table, size_t n, const void* keys,
+                      const uint64_t* scores, void* stream, bool unique_key) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  (void)unique_key;  // duplicates serialise on the key lock either way
+  T->assign_scores(n, static_cast<const uint64_t*>(keys), scores,
+                   as_stream(stream));
+  HKV_API_END
+}
+
+int hkv_find(hkv_table* table, size_t n, const void* keys, void* values,
+             bool* founds, uint64_t* scores, void* stream) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  T->find(n, static_cast<const uint64_t*>(keys), static_cast<uint8_t*>(values),
+          founds, scores, as_stream(stream));
+  HKV_API_END
+}
+
+int hkv_contains(hkv_table* table, size_t n, const void* keys, bool* founds,
+                 void* stream) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  T->contains(n, static_cast<const uint64_t*>(keys), founds, as_stream(stream));
+  HKV_API_END
+}
+
+int hkv_erase(hkv_table* table, size_t n, const void* keys, void* stream) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  T->erase(n, static_cast<const uint64_t*>(keys), as_stream(stream));
+  HKV_API_END
+}
+
+int hkv_clear(hkv_table* table, void* stream) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  T->clear(as_stream(stream));
+  HKV_API_END
+}
+
+int hkv_export_batch(hkv_table* table, size_t n, size_t offset,
+                     uint64_t* d_counter, void* keys, void* values,
+                     uint64_t* scores, void* stream) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  T->export_batch(n, offset, d_counter, static_cast<uint64_t*>(keys),
+                  static_cast<uint8_t*>(values), scores, as_stream(stream));
+  HKV_API_END
+}
+
+int hkv_export_batch_count(hkv_table* table, size_t n, size_t offset,
+                           void* keys, void* values, uint64_t* scores,
+                           void* stream, size_t* h_count) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  HKV_REQUIRE(h_count != nullptr, HKV_ERR_INVALID, "null count");
+  cudaStream_t s = as_stream(stream);
+  uint64_t* d = nullptr;
+  CUDA_TRY(cudaMallocAsync(&d, sizeof(uint64_t), s));
+  try {
+    T->export_batch(n, offset, d, static_cast<uint64_t*>(keys),
+                    static_cast<uint8_t*>(values), scores, s);
+  } catch (...) {
+    cudaFreeAsync(d, s);
+    throw;
+  }
+  uint64_t h = 0;
+  CUDA_TRY(cudaMemcpyAsync(&h, d, sizeof(uint64_t), cudaMemcpyDeviceToHost, s));
+  CUDA_TRY(cudaFreeAsync(d, s));
+  CUDA_TRY(cudaStreamSynchronize(s));
+  *h_count = h;
+  HKV_API_END
+}
+
+int hkv_size(hkv_table* table, void* stream, size_t* out) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  *out = T->size(as_stream(stream));
+  HKV_API_END
+}
+
+int hkv_capacity(hkv_table* table, size_t* out) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  *out = T->capacity();
+  HKV_API_END
+}
+
+int hkv_load_factor(hkv_table* table, void* stream, float* out) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  *out = T->load_factor(as_stream(stream));
+  HKV_API_END
+}
+
+int hkv_dim(hkv_table* table, size_t* out) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  *out = T->dim();
+  HKV_API_END
+}
+
+int hkv_max_bucket_size(hkv_table* table, size_t* out) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  (void)T;
+  *out = hkvb::kBucket;
+  HKV_API_END
+}
+
+int hkv_bucket_count(hkv_table* table, size_t* out) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  *out = T->bucket_count();
+  HKV_API_END
+}
+
+int hkv_is_pure_hbm_mode(hkv_table* table, bool* out) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  *out = T->pure_hbm();
+  HKV_API_END
+}
+
+int hkv_reserve(hkv_table* table, size_t new_capacity, void* stream) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  T->reserve(new_capacity, as_stream(stream));
+  HKV_API_END
+}
+
+int hkv_set_global_epoch(hkv_table* table, uint64_t epoch) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  T->set_global_epoch(epoch);
+  HKV_API_END
+}
+
+int hkv_check_device_error(hkv_table* table, void* stream) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  T->check_device_error(as_stream(stream));
+  HKV_API_END
+}
+
+int hkv_debug_get_state(hkv_table* table, uint64_t* keys, uint64_t* scores,
+                        uint8_t* digests, int32_t* sizes, void* values) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  T->get_state(keys, scores, digests, sizes, static_cast<uint8_t*>(values));
+  HKV_API_END
+}
+
+int hkv_debug_set_state(hkv_table* table, const uint64_t* keys,
+                        const uint64_t* scores, const uint8_t* digests,
+                        const int32_t* sizes, const void* values) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  T->set_state(keys, scores, digests, sizes,
+               static_cast<const uint8_t*>(values));
+  HKV_API_END
+}
+
+}  // extern "C"

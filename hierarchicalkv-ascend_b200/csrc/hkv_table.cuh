@@ -1,0 +1,173 @@
+// hkv_table.cuh -- host-side table object behind the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/hkv_b200.h"
+#include "hkv_device.cuh"
+
+namespace hkvb {
+
+struct HkvError {
+  int code;
+  std::string msg;
+};
+
+#define HKV_REQUIRE(cond, code, msg)              \
+  do {                                            \
+    if (!(cond)) throw ::hkvb::HkvError{(code), (msg)}; \
+  } while (0)
+
+#define CUDA_TRY(expr)                                                     \
+  do {                                                                     \
+    cudaError_t e_ = (expr);                                               \
+    if (e_ != cudaSuccess)                                                 \
+      throw ::hkvb::HkvError{HKV_ERR_CUDA, std::string(#expr) + ": " +     \
+                                               cudaGetErrorString(e_)};    \
+  } while (0)
+
+struct Slice {
+  uint8_t* dev;   // device-visible address
+  uint8_t* host;  // host address when the slice is pinned host memory
+  size_t bytes;
+};
+
+// Stream-ordered scratch (cudaMallocAsync / cudaFreeAsync).
+class Workspace {
+ public:
+  explicit Workspace(cudaStream_t s) : stream_(s) {}
+  ~Workspace() {
+    for (void* p : ptrs_) cudaFreeAsync(p, stream_);
+  }
+  template <class T>
+  T* get(size_t count) {
+    void* p = nullptr;
+    CUDA_TRY(cudaMallocAsync(&p, count * sizeof(T) + 16, stream_));
+    ptrs_.push_back(p);
+    return static_cast<T*>(p);
+  }
+
+ private:
+  cudaStream_t stream_;
+  std::vector<void*> ptrs_;
+};
+
+// Duplicate-key merge of one batch (hkv_dedup.cuh). All arrays live in the
+// workspace; `dm` is the device-side count of representatives.
+struct DedupResult {
+  uint64_t* ukeys;
+  uint32_t* rep_first;
+  uint32_t* rep_last;
+  uint32_t* uid_of;
+  uint64_t* uscores;  // merged scores, nullptr when scores == nullptr
+  uint32_t* dm;
+};
+DedupResult dedup_batch(size_t n, const uint64_t* keys, const uint64_t* scores,
+                        int strategy, Workspace& ws, cudaStream_t s,
+                        int sm_count, int* d_error);
+
+class TableImpl {
+ public:
+  TableImpl(const hkv_options& o, int key_type, int value_type, int strategy);
+  ~TableImpl();
+
+  TableView view() const;
+
+  void insert_or_assign(size_t n, const uint64_t* keys, const uint8_t* values,
+                        const uint64_t* scores, cudaStream_t s, bool unique,
+                        bool ignore);
+  void insert_and_evict(size_t n, const uint64_t* keys, const uint8_t* values,
+                        const uint64_t* scores, uint64_t* ev_keys,
+                        uint8_t* ev_values, uint64_t* ev_scores,
+                        uint64_t* d_counter, cudaStream_t s, bool unique,
+                        bool ignore);
+  void find_or_insert(size_t n, const uint64_t* keys, uint8_t* values,
+                      const uint64_t* scores, cudaStream_t s, bool unique,
+                      bool ignore, uint8_t* status = nullptr);
+  void accum_or_assign(size_t n, const uint64_t* keys, const uint8_t* values,
+                       const bool* accum, const uint64_t* scores,
+                       cudaStream_t s, bool ignore);
+  void assign_scores(size_t n, const uint64_t* keys, const uint64_t* scores,
+                     cudaStream_t s);
+  void find(size_t n, const uint64_t* keys, uint8_t* values, bool* founds,
+            uint64_t* scores, cudaStream_t s);
+  void contains(size_t n, const uint64_t* keys, bool* founds, cudaStream_t s);
+  void erase(size_t n, const uint64_t* keys, cudaStream_t s);
+  void clear(cudaStream_t s);
+  void export_batch(size_t n, size_t offset, uint64_t* d_counter,
+                    uint64_t* keys, uint8_t* values, uint64_t* scores,
+                    cudaStream_t s);
+  size_t size(cudaStream_t s);
+  float load_factor(cudaStream_t s);
+  void reserve(size_t new_capacity, cudaStream_t s);
+  void check_device_error(cudaStream_t s);
+  void get_state(uint64_t* keys, uint64_t* scores, uint8_t* digests,
+                 int32_t* sizes, uint8_t* values);
+  void set_state(const uint64_t* keys, const uint64_t* scores,
+                 const uint8_t* digests, const int32_t* sizes,
+                 const uint8_t* values);
+
+  uint64_t capacity() const { return capacity_; }
+  uint64_t bucket_count() const { return num_buckets_; }
+  uint64_t dim() const { return opt_.dim; }
+  uint32_t value_bytes() const { return value_bytes_; }
+  bool pure_hbm() const { return pure_hbm_; }
+  int strategy() const { return strategy_; }
+  int value_type() const { return value_type_; }
+  int device() const { return device_; }
+  int* error_word() const { return d_error_; }
+  int value_width(std::initializer_list<const void*> ptrs) const;
+  void set_global_epoch(uint64_t e) { epoch_ = e; }
+  uint64_t global_epoch() const { return epoch_; }
+
+  // grid size for kernels that use one 8-lane tile per key
+  int tile_grid(size_t n) const;
+  int warp_grid(size_t nwarps) const;
+
+ private:
+  void check_strategy(const uint64_t* scores, bool ignore) const;
+  void auto_grow(size_t n, cudaStream_t s);
+  float fast_load_factor(size_t delta, cudaStream_t s);
+  uint64_t sum_sizes(uint64_t nb, cudaStream_t s);
+  void allocate_slices(uint64_t b0, uint64_t b1);
+  void upload_slices();
+  void double_capacity(cudaStream_t s);
+  void upsert(int mode, size_t n, const uint64_t* keys,
+              const uint8_t* values_in, uint8_t* values_io,
+              const uint64_t* scores, uint64_t* ev_keys, uint8_t* ev_values,
+              uint64_t* ev_scores, uint64_t* d_counter, cudaStream_t s,
+              bool unique, bool ignore, uint8_t* status);
+
+  hkv_options opt_;
+  int key_type_, value_type_, strategy_;
+  uint32_t elem_bytes_, value_bytes_;
+  int device_ = 0;
+  int sm_count_ = 148;
+  uint64_t* keys_ = nullptr;
+  uint64_t* scores_ = nullptr;
+  uint8_t* digests_ = nullptr;
+  int32_t* sizes_ = nullptr;
+  int* d_error_ = nullptr;
+  unsigned long long* d_scratch_ = nullptr;  // small device counters
+  unsigned long long* h_scratch_ = nullptr;  // pinned host mirror
+  std::vector<Slice> slices_;
+  uint8_t** d_slices_ = nullptr;
+  size_t d_slices_cap_ = 0;
+  uint64_t capacity_ = 0, num_buckets_ = 0, max_size_ = 0;
+  uint64_t div_magic_ = 0;
+  uint32_t div_shift_ = 0;
+  uint32_t slice_shift_ = 0;
+  uint64_t remaining_hbm_ = 0;
+  bool reach_max_ = false;
+  bool pure_hbm_ = true;
+  uint64_t epoch_ = kIgnoredEpoch;
+};
+
+}  // namespace hkvb
+
+struct hkv_table {
+  hkvb::TableImpl* impl;
+};

@@ -1,0 +1,466 @@
+"""Python binding of the B200 HierarchicalKV table (libhkv_b200.so, C ABI in
+include/hkv_b200.h).
+
+`HashTable` mirrors the reference's `HashTable<K, V, S, Strategy>`
+(include/hkv_hashtable.h of yangzhen92/HierarchicalKV-ascend): same method
+names, argument order and defaults, with torch tensors (or raw device
+addresses) in place of device pointers and a torch CUDA stream in place of
+the ACL stream. Errors raise `HkvException` (configuration / argument,
+the reference's HKV_CHECK), `CudaException` (runtime API), `HkvTimeout`
+(a device lock wait ran out) or `RuntimeError` (std::runtime_error).
+
+The library is loaded from this directory. There is no fallback: if the
+shared library is missing or cannot be loaded, importing this module fails.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libhkv_b200.so")
+
+HKV_OK = 0
+HKV_ERR_INVALID = 1
+HKV_ERR_CUDA = 2
+HKV_ERR_TIMEOUT = 3
+HKV_ERR_UNSUPPORTED = 4
+HKV_ERR_RUNTIME = 5
+
+
+class EvictStrategy:
+    """EvictStrategy::EvictStrategyEnum, reference hkv_hashtable.h:111-119."""
+
+    kLru = 0
+    kLfu = 1
+    kEpochLru = 2
+    kEpochLfu = 3
+    kCustomized = 4
+
+
+KEY_U64 = 0
+KEY_I64 = 1
+VALUE_TYPES = {"float32": 0, "float16": 1, "bfloat16": 2, "float64": 3,
+               "uint32": 4, "uint16": 5, "int8": 6, "uint64": 7}
+IGNORED_GLOBAL_EPOCH = 0xFFFFFFFFFFFFFFFF
+
+
+class HkvException(ValueError):
+    """HKV_CHECK failures (reference debug.h:53-74)."""
+
+
+class CudaException(RuntimeError):
+    """CUDA runtime failures (the reference's NpuException, debug.h:30-51)."""
+
+
+class HkvTimeout(RuntimeError):
+    """A device-side lock wait exceeded its bound."""
+
+
+class HkvUnsupported(NotImplementedError):
+    """Valid in the reference, not supported by this build."""
+
+
+class _Options(ctypes.Structure):
+    _fields_ = [
+        ("init_capacity", ctypes.c_uint64),
+        ("max_capacity", ctypes.c_uint64),
+        ("max_hbm_for_vectors", ctypes.c_uint64),
+        ("max_bucket_size", ctypes.c_uint64),
+        ("dim", ctypes.c_uint64),
+        ("max_load_factor", ctypes.c_float),
+        ("block_size", ctypes.c_int),
+        ("io_block_size", ctypes.c_int),
+        ("device_id", ctypes.c_int),
+        ("io_by_cpu", ctypes.c_int),
+        ("use_constant_memory", ctypes.c_int),
+        ("reserved_key_start_bit", ctypes.c_int),
+        ("num_of_buckets_per_alloc", ctypes.c_uint64),
+        ("api_lock", ctypes.c_int),
+    ]
+
+
+@dataclass
+class HashTableOptions:
+    """HashTableOptions, reference hashtable_options.h:534-566."""
+
+    init_capacity: int = 0
+    max_capacity: int = 0
+    max_hbm_for_vectors: int = 0
+    max_bucket_size: int = 128
+    dim: int = 64
+    max_load_factor: float = 0.5
+    block_size: int = 128
+    io_block_size: int = 1024
+    device_id: int = -1
+    io_by_cpu: bool = False
+    use_constant_memory: bool = False
+    reserved_key_start_bit: int = 0
+    num_of_buckets_per_alloc: int = 1
+    api_lock: bool = False
+
+    def _c(self) -> _Options:
+        o = _Options()
+        for f, _ in _Options._fields_:
+            v = getattr(self, f)
+            setattr(o, f, float(v) if f == "max_load_factor" else int(v))
+        return o
+
+
+# C ABI symbols and their signatures (include/hkv_b200.h)
+_P = ctypes.c_void_p
+_SZ = ctypes.c_size_t
+_B = ctypes.c_bool
+_U64 = ctypes.c_uint64
+SIGNATURES = {
+    "hkv_options_init": (None, [ctypes.POINTER(_Options)]),
+    "hkv_last_error": (ctypes.c_char_p, []),
+    "hkv_table_create": (ctypes.c_int, [ctypes.POINTER(_Options), ctypes.c_int,
+                                        ctypes.c_int, ctypes.c_int, ctypes.POINTER(_P)]),
+    "hkv_table_destroy": (ctypes.c_int, [_P]),
+    "hkv_insert_or_assign": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _B, _B]),
+    "hkv_insert_and_evict": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _P, _P, _P, _P, _B, _B]),
+    "hkv_insert_and_evict_count": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _P, _P, _P,
+                                                  _B, _B, ctypes.POINTER(_SZ)]),
+    "hkv_accum_or_assign": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _P, _B]),
+    "hkv_find_or_insert": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _B, _B]),
+    "hkv_assign_scores": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _B]),
+    "hkv_find": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _P]),
+    "hkv_contains": (ctypes.c_int, [_P, _SZ, _P, _P, _P]),
+    "hkv_erase": (ctypes.c_int, [_P, _SZ, _P, _P]),
+    "hkv_clear": (ctypes.c_int, [_P, _P]),
+    "hkv_export_batch": (ctypes.c_int, [_P, _SZ, _SZ, _P, _P, _P, _P, _P]),
+    "hkv_export_batch_count": (ctypes.c_int, [_P, _SZ, _SZ, _P, _P, _P, _P,
+                                              ctypes.POINTER(_SZ)]),
+    "hkv_size": (ctypes.c_int, [_P, _P, ctypes.POINTER(_SZ)]),
+    "hkv_capacity": (ctypes.c_int, [_P, ctypes.POINTER(_SZ)]),
+    "hkv_load_factor": (ctypes.c_int, [_P, _P, ctypes.POINTER(ctypes.c_float)]),
+    "hkv_dim": (ctypes.c_int, [_P, ctypes.POINTER(_SZ)]),
+    "hkv_max_bucket_size": (ctypes.c_int, [_P, ctypes.POINTER(_SZ)]),
+    "hkv_bucket_count": (ctypes.c_int, [_P, ctypes.POINTER(_SZ)]),
+    "hkv_is_pure_hbm_mode": (ctypes.c_int, [_P, ctypes.POINTER(_B)]),
+    "hkv_reserve": (ctypes.c_int, [_P, _SZ, _P]),
+    "hkv_set_global_epoch": (ctypes.c_int, [_P, _U64]),
+    "hkv_check_device_error": (ctypes.c_int, [_P, _P]),
+    "hkv_debug_get_state": (ctypes.c_int, [_P, _P, _P, _P, _P, _P]),
+    "hkv_debug_set_state": (ctypes.c_int, [_P, _P, _P, _P, _P, _P]),
+    "hkv_nccl_unique_id": (ctypes.c_int, [_P]),
+    "hkv_sharded_create": (ctypes.c_int, [ctypes.POINTER(_Options), ctypes.c_int,
+                                          ctypes.c_int, ctypes.c_int, _P, ctypes.c_int,
+                                          ctypes.c_int, ctypes.POINTER(_P)]),
+    "hkv_sharded_destroy": (ctypes.c_int, [_P]),
+    "hkv_sharded_local": (_P, [_P]),
+    "hkv_sharded_find_or_insert": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P]),
+    "hkv_sharded_find": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _P]),
+    "hkv_sharded_insert_or_assign": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P]),
+    "hkv_sharded_size": (ctypes.c_int, [_P, _P, ctypes.POINTER(_SZ)]),
+}
+
+
+def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Loads libhkv_b200.so and declares every C ABI signature."""
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+_LIB = None
+
+
+def lib() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is None:
+        _LIB = load_library()
+    return _LIB
+
+
+def _check(status: int) -> None:
+    if status == HKV_OK:
+        return
+    msg = (lib().hkv_last_error() or b"").decode()
+    if status == HKV_ERR_INVALID:
+        raise HkvException(msg)
+    if status == HKV_ERR_CUDA:
+        raise CudaException(msg)
+    if status == HKV_ERR_TIMEOUT:
+        raise HkvTimeout(msg)
+    if status == HKV_ERR_UNSUPPORTED:
+        raise HkvUnsupported(msg)
+    raise RuntimeError(msg)
+
+
+def _ptr(x):
+    """Device address of a tensor (or an int address, or None)."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    return x.data_ptr()
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+class HashTable:
+    """Mirror of the reference's HashTable<K, V, S, Strategy>.
+
+    key_dtype: "uint64" or "int64"; value_dtype: a name in VALUE_TYPES.
+    """
+
+    def __init__(self, evict_strategy: int = EvictStrategy.kLru,
+                 key_dtype: str = "uint64", value_dtype: str = "float32"):
+        self.evict_strategy = evict_strategy
+        self.key_dtype = key_dtype
+        self.value_dtype = value_dtype
+        self._h = None
+        self._options = None
+        self._borrowed = False
+
+    @classmethod
+    def borrow(cls, handle, evict_strategy, key_dtype="uint64", value_dtype="float32"):
+        """Wraps a table handle owned elsewhere (e.g. a sharded table's local
+        shard); closing the wrapper does not destroy it."""
+        t = cls(evict_strategy, key_dtype, value_dtype)
+        t._h = handle
+        t._borrowed = True
+        return t
+
+    # -- lifecycle ---------------------------------------------------------
+    def init(self, options: HashTableOptions) -> None:
+        """HashTable::init, reference hkv_hashtable.h:962-1042."""
+        if self._h is not None:
+            return
+        h = ctypes.c_void_p()
+        o = options._c()
+        _check(lib().hkv_table_create(ctypes.byref(o),
+                                      KEY_I64 if self.key_dtype == "int64" else KEY_U64,
+                                      VALUE_TYPES[self.value_dtype],
+                                      self.evict_strategy, ctypes.byref(h)))
+        self._h = h.value
+        self._options = options
+
+    def close(self) -> None:
+        if self._h is not None and not self._borrowed:
+            _check(lib().hkv_table_destroy(self._h))
+        self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._h
+
+    # -- insert-like ---------------------------------------------------------
+    def insert_or_assign(self, n, keys, values, scores=None, stream=None,
+                         unique_key=True, ignore_evict_strategy=False):
+        _check(lib().hkv_insert_or_assign(self._h, n, _ptr(keys), _ptr(values),
+                                          _ptr(scores), _stream(stream),
+                                          unique_key, ignore_evict_strategy))
+
+    def insert_and_evict(self, n, keys, values, scores, evicted_keys,
+                         evicted_values, evicted_scores=None,
+                         d_evicted_counter=None, stream=None, unique_key=True,
+                         ignore_evict_strategy=False):
+        """With d_evicted_counter: the device-counter overload (caller zeroes
+        it). Without: the overload that returns the count (synchronises)."""
+        if d_evicted_counter is not None:
+            _check(lib().hkv_insert_and_evict(
+                self._h, n, _ptr(keys), _ptr(values), _ptr(scores),
+                _ptr(evicted_keys), _ptr(evicted_values), _ptr(evicted_scores),
+                _ptr(d_evicted_counter), _stream(stream), unique_key,
+                ignore_evict_strategy))
+            return None
+        cnt = ctypes.c_size_t(0)
+        _check(lib().hkv_insert_and_evict_count(
+            self._h, n, _ptr(keys), _ptr(values), _ptr(scores),
+            _ptr(evicted_keys), _ptr(evicted_values), _ptr(evicted_scores),
+            _stream(stream), unique_key, ignore_evict_strategy,
+            ctypes.byref(cnt)))
+        return cnt.value
+
+    def accum_or_assign(self, n, keys, value_or_deltas, accum_or_assigns,
+                        scores=None, stream=None, ignore_evict_strategy=False):
+        _check(lib().hkv_accum_or_assign(self._h, n, _ptr(keys),
+                                         _ptr(value_or_deltas),
+                                         _ptr(accum_or_assigns), _ptr(scores),
+                                         _stream(stream), ignore_evict_strategy))
+
+    def find_or_insert(self, n, keys, values, scores=None, stream=None,
+                       unique_key=True, ignore_evict_strategy=False):
+        _check(lib().hkv_find_or_insert(self._h, n, _ptr(keys), _ptr(values),
+                                        _ptr(scores), _stream(stream),
+                                        unique_key, ignore_evict_strategy))
+
+    def assign_scores(self, n, keys, scores=None, stream=None, unique_key=True):
+        _check(lib().hkv_assign_scores(self._h, n, _ptr(keys), _ptr(scores),
+                                       _stream(stream), unique_key))
+
+    assign = assign_scores
+
+    # -- lookups -------------------------------------------------------------
+    def find(self, n, keys, values, founds, scores=None, stream=None):
+        _check(lib().hkv_find(self._h, n, _ptr(keys), _ptr(values),
+                              _ptr(founds), _ptr(scores), _stream(stream)))
+
+    def contains(self, n, keys, founds, stream=None):
+        _check(lib().hkv_contains(self._h, n, _ptr(keys), _ptr(founds),
+                                  _stream(stream)))
+
+    def erase(self, n, keys, stream=None):
+        _check(lib().hkv_erase(self._h, n, _ptr(keys), _stream(stream)))
+
+    def clear(self, stream=None):
+        _check(lib().hkv_clear(self._h, _stream(stream)))
+
+    def export_batch(self, n, offset, keys, values, scores=None, stream=None,
+                     d_counter=None):
+        """Without d_counter returns the exported count (synchronises)."""
+        if d_counter is not None:
+            _check(lib().hkv_export_batch(self._h, n, offset, _ptr(d_counter),
+                                          _ptr(keys), _ptr(values),
+                                          _ptr(scores), _stream(stream)))
+            return None
+        cnt = ctypes.c_size_t(0)
+        _check(lib().hkv_export_batch_count(self._h, n, offset, _ptr(keys),
+                                            _ptr(values), _ptr(scores),
+                                            _stream(stream), ctypes.byref(cnt)))
+        return cnt.value
+
+    # -- properties ------------------------------------------------------------
+    def size(self, stream=None) -> int:
+        out = ctypes.c_size_t(0)
+        _check(lib().hkv_size(self._h, _stream(stream), ctypes.byref(out)))
+        return out.value
+
+    def empty(self, stream=None) -> bool:
+        return self.size(stream) == 0
+
+    def capacity(self) -> int:
+        out = ctypes.c_size_t(0)
+        _check(lib().hkv_capacity(self._h, ctypes.byref(out)))
+        return out.value
+
+    def load_factor(self, stream=None) -> float:
+        out = ctypes.c_float(0)
+        _check(lib().hkv_load_factor(self._h, _stream(stream), ctypes.byref(out)))
+        return out.value
+
+    def dim(self) -> int:
+        out = ctypes.c_size_t(0)
+        _check(lib().hkv_dim(self._h, ctypes.byref(out)))
+        return out.value
+
+    def max_bucket_size(self) -> int:
+        out = ctypes.c_size_t(0)
+        _check(lib().hkv_max_bucket_size(self._h, ctypes.byref(out)))
+        return out.value
+
+    def bucket_count(self) -> int:
+        out = ctypes.c_size_t(0)
+        _check(lib().hkv_bucket_count(self._h, ctypes.byref(out)))
+        return out.value
+
+    def is_pure_hbm_mode(self) -> bool:
+        out = ctypes.c_bool(False)
+        _check(lib().hkv_is_pure_hbm_mode(self._h, ctypes.byref(out)))
+        return out.value
+
+    def reserve(self, new_capacity, stream=None):
+        _check(lib().hkv_reserve(self._h, new_capacity, _stream(stream)))
+
+    def set_global_epoch(self, epoch: int):
+        _check(lib().hkv_set_global_epoch(self._h, epoch))
+
+    def check_device_error(self, stream=None):
+        _check(lib().hkv_check_device_error(self._h, _stream(stream)))
+
+    # -- test support ------------------------------------------------------
+    def get_state(self):
+        """Raw slot state as numpy arrays (keys, scores, digests, sizes, values)."""
+        import numpy as np
+
+        cap, nb, dim = self.capacity(), self.bucket_count(), self.dim()
+        keys = np.empty(cap, np.uint64)
+        scores = np.empty(cap, np.uint64)
+        digests = np.empty(cap, np.uint8)
+        sizes = np.empty(nb, np.int32)
+        vt = np.dtype(self.value_dtype) if self.value_dtype != "bfloat16" else np.uint16
+        values = np.empty(cap * dim, vt)
+        _check(lib().hkv_debug_get_state(self._h, keys.ctypes.data, scores.ctypes.data,
+                                         digests.ctypes.data, sizes.ctypes.data,
+                                         values.ctypes.data))
+        return keys, scores, digests, sizes, values.reshape(cap, dim)
+
+    def set_state(self, keys=None, scores=None, digests=None, sizes=None, values=None):
+        def p(a):
+            return None if a is None else a.ctypes.data
+
+        _check(lib().hkv_debug_set_state(self._h, p(keys), p(scores), p(digests),
+                                         p(sizes), p(values)))
+
+
+class ShardedHashTable:
+    """One table shard per rank; collective calls route keys to their owner
+    over NCCL all-to-all (no reference counterpart)."""
+
+    def __init__(self, options: HashTableOptions, rank: int, world_size: int,
+                 nccl_id: bytes, evict_strategy: int = EvictStrategy.kLru,
+                 key_dtype: str = "uint64", value_dtype: str = "float32"):
+        h = ctypes.c_void_p()
+        o = options._c()
+        buf = ctypes.create_string_buffer(bytes(nccl_id), 128)
+        _check(lib().hkv_sharded_create(ctypes.byref(o),
+                                        KEY_I64 if key_dtype == "int64" else KEY_U64,
+                                        VALUE_TYPES[value_dtype], evict_strategy,
+                                        buf, rank, world_size, ctypes.byref(h)))
+        self._h = h.value
+        self.rank, self.world_size = rank, world_size
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(128)
+        _check(lib().hkv_nccl_unique_id(buf))
+        return buf.raw
+
+    def close(self):
+        if self._h is not None:
+            _check(lib().hkv_sharded_destroy(self._h))
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def find_or_insert(self, n, keys, values, scores=None, stream=None):
+        _check(lib().hkv_sharded_find_or_insert(self._h, n, _ptr(keys), _ptr(values),
+                                                _ptr(scores), _stream(stream)))
+
+    def find(self, n, keys, values, founds, scores=None, stream=None):
+        _check(lib().hkv_sharded_find(self._h, n, _ptr(keys), _ptr(values),
+                                      _ptr(founds), _ptr(scores), _stream(stream)))
+
+    def insert_or_assign(self, n, keys, values, scores=None, stream=None):
+        _check(lib().hkv_sharded_insert_or_assign(self._h, n, _ptr(keys), _ptr(values),
+                                                  _ptr(scores), _stream(stream)))
+
+    def size(self, stream=None) -> int:
+        out = ctypes.c_size_t(0)
+        _check(lib().hkv_sharded_size(self._h, _stream(stream), ctypes.byref(out)))
+        return out.value

@@ -1,0 +1,233 @@
+/*
+ * hkv_b200.h -- C ABI of the B200 HierarchicalKV hash table.
+ *
+ * This is the drop-in boundary for the reference's HashTable<K,V,S,Strategy>
+ * (yangzhen92/HierarchicalKV-ascend, include/hkv_hashtable.h). Every entry
+ * point takes plain pointers and sizes; device pointers are CUDA device (or
+ * mapped/managed) memory, `stream` is a cudaStream_t passed as void*. The C++
+ * mirror in include/hkv_hashtable.h, the Python binding and any cgo/JNI/ctypes
+ * caller bind exactly these symbols.
+ *
+ * Every function returns an hkv_status. On failure hkv_last_error() gives the
+ * message of the calling thread's last error. Status codes mirror the
+ * reference's exceptions: HKV_ERR_INVALID for HkvException (HKV_CHECK,
+ * debug.h:53-74), HKV_ERR_CUDA for NpuException (NPU_CHECK, debug.h:30-51),
+ * HKV_ERR_RUNTIME for std::runtime_error.
+ *
+ * Key type: 64-bit integers (uint64 or int64, same bit patterns). The four
+ * reserved keys 0xFFFFFFFFFFFFFFFC..0xFFFFFFFFFFFFFFFF are ignored by every
+ * operation (reference types.h:63-70, :153-156). Score type: uint64.
+ * Values: rows of `dim` elements of `value_type`.
+ */
+#ifndef HKV_B200_H_
+#define HKV_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+#include <stdbool.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+typedef enum {
+  HKV_OK = 0,
+  HKV_ERR_INVALID = 1,     /* bad argument or configuration (HkvException) */
+  HKV_ERR_CUDA = 2,        /* CUDA runtime failure (NpuException) */
+  HKV_ERR_TIMEOUT = 3,     /* a device lock wait ran out (device error word) */
+  HKV_ERR_UNSUPPORTED = 4, /* valid in the reference, not supported here */
+  HKV_ERR_RUNTIME = 5      /* std::runtime_error in the reference */
+} hkv_status;
+
+/* EvictStrategy::EvictStrategyEnum, hkv_hashtable.h:111-119. */
+typedef enum {
+  HKV_LRU = 0,
+  HKV_LFU = 1,
+  HKV_EPOCH_LRU = 2,
+  HKV_EPOCH_LFU = 3,
+  HKV_CUSTOMIZED = 4
+} hkv_evict_strategy;
+
+typedef enum { HKV_KEY_U64 = 0, HKV_KEY_I64 = 1 } hkv_key_type;
+
+typedef enum {
+  HKV_VALUE_F32 = 0,
+  HKV_VALUE_F16 = 1,
+  HKV_VALUE_BF16 = 2,
+  HKV_VALUE_F64 = 3,
+  HKV_VALUE_U32 = 4,
+  HKV_VALUE_U16 = 5,
+  HKV_VALUE_I8 = 6,
+  HKV_VALUE_U64 = 7
+} hkv_value_type;
+
+/* HashTableOptions, hashtable_options.h:534-566 (field for field; the pool
+ * options of MemoryPoolOptions are not needed by this build). */
+typedef struct {
+  uint64_t init_capacity;
+  uint64_t max_capacity;
+  uint64_t max_hbm_for_vectors; /* bytes of HBM for values; the rest goes to
+                                   mapped pinned host memory */
+  uint64_t max_bucket_size;     /* 128 */
+  uint64_t dim;
+  float max_load_factor;        /* 0.5 */
+  int block_size;               /* accepted, unused */
+  int io_block_size;            /* accepted, unused */
+  int device_id;                /* -1: current device */
+  int io_by_cpu;                /* must be 0 */
+  int use_constant_memory;      /* reserved */
+  int reserved_key_start_bit;   /* 0 only */
+  uint64_t num_of_buckets_per_alloc;
+  int api_lock;                 /* must be 0 */
+} hkv_options;
+
+typedef struct hkv_table hkv_table;
+
+/* Fills `o` with the reference's defaults (hashtable_options.h:535-562). */
+void hkv_options_init(hkv_options* o);
+
+/* Message of the calling thread's last failed call. */
+const char* hkv_last_error(void);
+
+/* HashTable::HashTable + init(options), hkv_hashtable.h:938-1042. */
+int hkv_table_create(const hkv_options* options, int key_type, int value_type,
+                     int evict_strategy, hkv_table** out);
+
+/* HashTable::~HashTable, hkv_hashtable.h:944-960. */
+int hkv_table_destroy(hkv_table* table);
+
+/* insert_or_assign, hkv_hashtable.h:1077-1215. */
+int hkv_insert_or_assign(hkv_table* table, size_t n, const void* keys,
+                         const void* values, const uint64_t* scores,
+                         void* stream, bool unique_key,
+                         bool ignore_evict_strategy);
+
+/* insert_and_evict (device counter), hkv_hashtable.h:1260-1310. The caller
+ * zeroes *d_evicted_counter before the call. */
+int hkv_insert_and_evict(hkv_table* table, size_t n, const void* keys,
+                         const void* values, const uint64_t* scores,
+                         void* evicted_keys, void* evicted_values,
+                         uint64_t* evicted_scores, uint64_t* d_evicted_counter,
+                         void* stream, bool unique_key,
+                         bool ignore_evict_strategy);
+
+/* insert_and_evict returning the count (synchronises the stream),
+ * hkv_hashtable.h:1368-1396. */
+int hkv_insert_and_evict_count(hkv_table* table, size_t n, const void* keys,
+                               const void* values, const uint64_t* scores,
+                               void* evicted_keys, void* evicted_values,
+                               uint64_t* evicted_scores, void* stream,
+                               bool unique_key, bool ignore_evict_strategy,
+                               size_t* h_evicted_count);
+
+/* accum_or_assign, hkv_hashtable.h:1438-1507. */
+int hkv_accum_or_assign(hkv_table* table, size_t n, const void* keys,
+                        const void* value_or_deltas,
+                        const bool* accum_or_assigns, const uint64_t* scores,
+                        void* stream, bool ignore_evict_strategy);
+
+/* find_or_insert, hkv_hashtable.h:1526-1632. */
+int hkv_find_or_insert(hkv_table* table, size_t n, const void* keys,
+                       void* values, const uint64_t* scores, void* stream,
+                       bool unique_key, bool ignore_evict_strategy);
+
+/* assign_scores (and its alias assign), hkv_hashtable.h:1943-1995. */
+int hkv_assign_scores(hkv_table* table, size_t n, const void* keys,
+                      const uint64_t* scores, void* stream, bool unique_key);
+
+/* find, hkv_hashtable.h:2113-2152. Misses leave values/scores untouched. */
+int hkv_find(hkv_table* table, size_t n, const void* keys, void* values,
+             bool* founds, uint64_t* scores, void* stream);
+
+/* contains, hkv_hashtable.h:2330-2348. */
+int hkv_contains(hkv_table* table, size_t n, const void* keys, bool* founds,
+                 void* stream);
+
+/* erase, hkv_hashtable.h:2358-2376. */
+int hkv_erase(hkv_table* table, size_t n, const void* keys, void* stream);
+
+/* clear, hkv_hashtable.h:2482-2493. */
+int hkv_clear(hkv_table* table, void* stream);
+
+/* export_batch (device counter, set not accumulated), hkv_hashtable.h
+ * :2519-2549. */
+int hkv_export_batch(hkv_table* table, size_t n, size_t offset,
+                     uint64_t* d_counter, void* keys, void* values,
+                     uint64_t* scores, void* stream);
+
+/* export_batch returning the count (synchronises), hkv_hashtable.h
+ * :2557-2577. */
+int hkv_export_batch_count(hkv_table* table, size_t n, size_t offset,
+                           void* keys, void* values, uint64_t* scores,
+                           void* stream, size_t* h_count);
+
+/* size / empty / capacity / load_factor / dim / max_bucket_size /
+ * bucket_count / is_pure_hbm_mode, hkv_hashtable.h:2784-2819, :2849, :2945,
+ * :2984-3008. size and load_factor synchronise the stream. */
+int hkv_size(hkv_table* table, void* stream, size_t* out);
+int hkv_capacity(hkv_table* table, size_t* out);
+int hkv_load_factor(hkv_table* table, void* stream, float* out);
+int hkv_dim(hkv_table* table, size_t* out);
+int hkv_max_bucket_size(hkv_table* table, size_t* out);
+int hkv_bucket_count(hkv_table* table, size_t* out);
+int hkv_is_pure_hbm_mode(hkv_table* table, bool* out);
+
+/* reserve, hkv_hashtable.h:2873-2935. */
+int hkv_reserve(hkv_table* table, size_t new_capacity, void* stream);
+
+/* set_global_epoch, hkv_hashtable.h:3197. */
+int hkv_set_global_epoch(hkv_table* table, uint64_t epoch);
+
+/* No reference counterpart: synchronises `stream` and reports a device lock
+ * wait that ran out during earlier calls (HKV_ERR_TIMEOUT), then clears it.
+ * The reference's device waits have no bound (find_utils.h:169-173). */
+int hkv_check_device_error(hkv_table* table, void* stream);
+
+/* No reference counterpart (test support): copies the raw slot state to /
+ * from HOST buffers, slot-major (capacity entries; sizes has bucket_count
+ * entries; values capacity*dim elements). Any pointer may be NULL. */
+int hkv_debug_get_state(hkv_table* table, uint64_t* keys, uint64_t* scores,
+                        uint8_t* digests, int32_t* sizes, void* values);
+int hkv_debug_set_state(hkv_table* table, const uint64_t* keys,
+                        const uint64_t* scores, const uint8_t* digests,
+                        const int32_t* sizes, const void* values);
+
+/* ---- sharded table (no reference counterpart: the reference is one device)
+ * One table shard per GPU; keys are routed to shard owner(key) =
+ * Murmur3(key) % world_size and exchanged with NCCL all-to-all. ---------- */
+typedef struct hkv_sharded hkv_sharded;
+
+/* NCCL unique id (128 bytes) for rank 0 to broadcast to the others. */
+int hkv_nccl_unique_id(uint8_t out[128]);
+
+int hkv_sharded_create(const hkv_options* local_options, int key_type,
+                       int value_type, int evict_strategy,
+                       const uint8_t nccl_id[128], int rank, int world_size,
+                       hkv_sharded** out);
+int hkv_sharded_destroy(hkv_sharded* s);
+hkv_table* hkv_sharded_local(hkv_sharded* s);
+
+/* Collective: every rank calls with its own batch (sizes may differ).
+ * Semantics per key are those of the local op on the owner shard;
+ * duplicate keys are merged as for unique_key=false. */
+int hkv_sharded_find_or_insert(hkv_sharded* s, size_t n, const void* keys,
+                               void* values, const uint64_t* scores,
+                               void* stream);
+int hkv_sharded_find(hkv_sharded* s, size_t n, const void* keys, void* values,
+                     bool* founds, uint64_t* scores, void* stream);
+int hkv_sharded_insert_or_assign(hkv_sharded* s, size_t n, const void* keys,
+                                 const void* values, const uint64_t* scores,
+                                 void* stream);
+/* Collective sum of the shard sizes. */
+int hkv_sharded_size(hkv_sharded* s, void* stream, size_t* out);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+#endif /* HKV_B200_H_ */
