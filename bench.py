@@ -46,6 +46,13 @@ INSERT_EVICT_BYTES = 1185 + 2 * VALUE_BYTES            # 1441
 INSERT_MIX_BYTES = 0.5 * (INSERT_HIT_BYTES + INSERT_EVICT_BYTES)  # 928.5
 
 
+_T0 = time.time()
+
+
+def log(msg):
+    print(f"[bench {time.time() - _T0:7.1f}s] {msg}", file=sys.stderr, flush=True)
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -168,13 +175,13 @@ def dist_setup(n_gpus):
     return rank, world, local, dist
 
 
-def build_table(world, rank, dist):
+def build_table(world, rank, dist, capacity):
     import torch
 
     import hkv_b200 as H
 
-    opts = H.HashTableOptions(init_capacity=CAPACITY, max_capacity=CAPACITY,
-                              max_hbm_for_vectors=CAPACITY * VALUE_BYTES * 2,
+    opts = H.HashTableOptions(init_capacity=capacity, max_capacity=capacity,
+                              max_hbm_for_vectors=capacity * VALUE_BYTES * 2,
                               dim=DIM, max_load_factor=1.0)
     if world == 1:
         t = H.HashTable(H.EvictStrategy.kLru)
@@ -187,12 +194,12 @@ def build_table(world, rank, dist):
     return s, H.HashTable.borrow(H.lib().hkv_sharded_local(s._h), H.EvictStrategy.kLru)
 
 
-def prefill(local, rank, world, device):
+def prefill(local, rank, world, device, capacity):
     """Fill each shard to load factor 1.0 with the keys it owns (every rank
     generates the same global key stream and keeps its own keys)."""
     import torch
 
-    total = int(CAPACITY * world * PREFILL_FACTOR)
+    total = int(capacity * world * PREFILL_FACTOR)
     chunk = 4 << 20
     vals = torch.randn((chunk, DIM), device=device)
     start = 0
@@ -204,11 +211,14 @@ def prefill(local, rank, world, device):
         m = k.numel()
         local.insert_or_assign(m, k, vals[:m])
         start += n
+        if (start // chunk) % 8 == 0 or start >= total:
+            torch.cuda.synchronize()
+            log(f"prefill {start}/{total} keys")
     torch.cuda.synchronize()
     return total
 
 
-def prepare_batches(steps, rank, world, total_prefill, device, seed):
+def prepare_batches(steps, rank, world, total_prefill, device, seed, capacity):
     """Per step: a find batch of resident (hot) keys and an insert batch of
     half hot keys, half never-seen keys. Hot keys are the most recent prefill
     keys of the global stream."""
@@ -216,16 +226,17 @@ def prepare_batches(steps, rank, world, total_prefill, device, seed):
 
     g = torch.Generator(device=device)
     g.manual_seed(seed + rank)
-    hot_start = total_prefill - HOT * world
+    nhot = min(HOT, capacity // 8) * world
+    hot_start = total_prefill - nhot
     fresh_base = total_prefill + rank * (steps + 1) * BATCH
     finds, inserts, vals = [], [], []
     for s in range(steps):
-        idx = torch.randint(0, HOT * world, (BATCH,), generator=g, device=device)
+        idx = torch.randint(0, nhot, (BATCH,), generator=g, device=device)
         finds.append(key_of(hot_start + idx))
-        perm = torch.randperm(HOT * world, generator=g, device=device)[: BATCH // 2]
-        hot = key_of(hot_start + perm)
+        perm = torch.randperm(nhot, generator=g, device=device)[: BATCH // 2]
+        hot_keys = key_of(hot_start + perm)
         fresh = keys_from_counters(fresh_base + s * BATCH // 2, BATCH // 2, device)
-        ins = torch.cat([hot, fresh])
+        ins = torch.cat([hot_keys, fresh])
         ins = ins[torch.randperm(BATCH, generator=g, device=device)]
         inserts.append(ins)
         vals.append(torch.rand((BATCH, DIM), generator=g, device=device))
@@ -239,11 +250,15 @@ def run_gpu(args):
 
     rank, world, local_rank, dist = dist_setup(args.gpus)
     device = torch.device("cuda", torch.cuda.current_device())
-    table, local = build_table(world, rank, dist)
-    total = prefill(local, rank, world, device)
+    cap = args.capacity
+    log(f"rank {rank}/{world}: table of {cap} slots")
+    table, local = build_table(world, rank, dist, cap)
+    total = prefill(local, rank, world, device, cap)
     lf = local.load_factor()
+    log(f"prefill done, load factor {lf:.4f}")
     steps, warm = args.steps, args.warmup
-    finds, inserts, vals = prepare_batches(steps + warm, rank, world, total, device, 1234)
+    finds, inserts, vals = prepare_batches(steps + warm, rank, world, total, device, 1234, cap)
+    log("batches ready")
     out_vals = torch.empty((BATCH, DIM), device=device)
     founds = [torch.zeros(BATCH, dtype=torch.bool, device=device) for _ in range(steps + warm)]
     stream = torch.cuda.current_stream()
@@ -261,6 +276,7 @@ def run_gpu(args):
     for i in range(warm):
         step(i)
     torch.cuda.synchronize()
+    log("warmup done")
     if dist:
         dist.barrier()
     sampler = ClockSampler(local_rank)
@@ -281,6 +297,7 @@ def run_gpu(args):
         dist.barrier()
     clocks = sampler.stop()
     ms = t0.elapsed_time(t1)
+    log(f"timed {steps} steps: {ms:.3f} ms")
     find_ms = sum(e[0].elapsed_time(e[1]) for e in evs)
     ins_ms = sum(e[1].elapsed_time(e[2]) for e in evs)
     hit = float(torch.stack(founds[warm:]).float().mean().item())
@@ -299,7 +316,7 @@ def run_gpu(args):
         "config": {"workload": "BASELINE config 2 at load factor 1.0: find 1 Mi keys "
                                "(100% hits) + insert_or_assign 1 Mi keys (50% hits, "
                                "50% new keys evicting LRU) per step",
-                   "capacity_per_gpu": CAPACITY, "dim": DIM, "batch": BATCH,
+                   "capacity_per_gpu": cap, "dim": DIM, "batch": BATCH,
                    "strategy": "kLru", "load_factor": round(lf, 4),
                    "find_hit_rate": round(hit, 4),
                    "parallelism": "single table" if world == 1 else
@@ -334,8 +351,10 @@ def run_gpu(args):
         result["gpu_launches"] = 2 * steps if world == 1 else None
         if world == 1:
             result["e2e"] = e2e(table, finds, inserts, vals, warm, min(steps, 20))
+            log("e2e done")
             if not args.no_cpu_baseline:
                 result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+                log("cpu baseline done")
         print(json.dumps(result), flush=True)
     if world > 1:
         table.close()
@@ -505,6 +524,8 @@ def main():
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--capacity", type=int, default=CAPACITY,
+                    help="slots per GPU (diagnostics; the metric uses the default)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

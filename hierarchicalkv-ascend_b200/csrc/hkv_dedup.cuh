@@ -200,13 +200,15 @@ __global__ void clamp_low32_kernel(uint64_t* __restrict__ s, uint64_t m) {
     if (s[u] > 0xFFFFFFFFull) s[u] = 0xFFFFFFFFull;
 }
 
-// Gather rows: dst[u] = src[idx[u]].
+// Gather rows: dst[u] = src[idx[u]] for u < *dm (representatives only).
 template <int VW>
 __global__ void gather_rows_kernel(uint8_t* __restrict__ dst,
                                    const uint8_t* __restrict__ src,
-                                   const uint32_t* __restrict__ idx, uint64_t m,
+                                   const uint32_t* __restrict__ idx,
+                                   const uint32_t* __restrict__ dm,
                                    uint32_t vb) {
   const Tile tile;
+  const uint64_t m = *dm;
   const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / kTile);
   for (uint64_t u = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / kTile;
        u < m; u += ntiles)

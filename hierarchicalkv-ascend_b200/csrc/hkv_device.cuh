@@ -44,6 +44,7 @@ enum Occupy : int {
 
 // Device error word bits.
 constexpr int kErrSpinTimeout = 1;
+constexpr int kErrBounds = 2;  // only raised by builds with HKV_CHECK_BOUNDS
 
 // Murmur3 64-bit finalizer (reference utils.h:64-72).
 __host__ __device__ constexpr uint64_t murmur3(uint64_t k) {
@@ -84,8 +85,20 @@ struct TableView {
   uint32_t slice_shift;    // log2(buckets per slice)
   uint32_t single_slice;
   uint32_t value_bytes;    // dim * sizeof(V)
-  uint32_t pad;
+  uint32_t num_slices;
 };
+
+// Self-checking builds (-DHKV_CHECK_BOUNDS) verify every table index before
+// use; a bad index raises kErrBounds, records a site code in error[1] and the
+// access is redirected to slot 0 of bucket 0 instead of faulting.
+#ifdef HKV_CHECK_BOUNDS
+#define HKV_BOUND(t, cond, site)                   \
+  ((cond) ? true                                   \
+          : (atomicOr((t).error, kErrBounds),      \
+             atomicExch((t).error + 1, (site)), false))
+#else
+#define HKV_BOUND(t, cond, site) true
+#endif
 
 // hashed % capacity by the round-up magic-number method the reference uses
 // (Granlund & Montgomery; reference utils.h:85-97, table.h:106-127).
@@ -99,6 +112,13 @@ __device__ __forceinline__ uint64_t global_index(const TableView& t,
 
 __device__ __forceinline__ uint8_t* value_ptr(const TableView& t, uint64_t bkt,
                                               uint32_t pos) {
+  if (!HKV_BOUND(t, bkt < t.num_buckets && pos < kBucket, 11)) {
+    bkt = 0;
+    pos = 0;
+  }
+  if (!t.single_slice &&
+      !HKV_BOUND(t, (bkt >> t.slice_shift) < t.num_slices, 12))
+    bkt = 0;
   uint8_t* base;
   uint64_t local;
   if (t.single_slice) {

@@ -81,6 +81,7 @@ __device__ __forceinline__ Locate locate(const TableView& t, uint64_t key) {
   const uint64_t g = global_index(t, h);
   Locate l;
   l.bkt = g >> kBucketShift;
+  if (!HKV_BOUND(t, l.bkt < t.num_buckets, 1)) l.bkt = 0;
   l.pos = static_cast<uint32_t>(g & (kBucket - 1));
   l.d4 = static_cast<uint32_t>(digest_of_hash(h)) * 0x01010101u;
   return l;
@@ -183,194 +184,74 @@ struct UpsertArgs {
   int report_refused;        // insert_and_evict: report refused inputs
 };
 
-// Per-key probe of the unique-key insert kernels (reference
-// insert_or_assign_kernel.h:105-271). On return the tile owns `slot` (its key
-// word is LOCKED_KEY) unless the result is kRefused or kTimedOut.
-//  1. digest hits: CAS(key -> LOCKED); a hit slot that another tile holds
-//     LOCKED is waited for, since it may be this very key being updated.
-//  2. bucket not full: claim the first EMPTY_KEY slot in linear order from
-//     pos with CAS(EMPTY -> LOCKED) (the reference's group walk visits empty
-//     slots in this same order).
-//  3. otherwise evict: the minimum score over the bucket, chosen with the
-//     reference's 16-lane butterfly so ties resolve exactly as there
-//     (lane = owner_idx % 16); refuse iff desired < min; lock the victim with
-//     CAS and re-check its score, retrying on any interference.
-template <int S>
-__device__ __forceinline__ int upsert_probe(const TableView& t, const Tile& tile,
-                                            const Locate& l, uint64_t key,
-                                            uint64_t desired, uint64_t owner_idx,
-                                            uint32_t& slot, uint64_t& vkey,
-                                            uint64_t& vscore) {
-  uint64_t* bk = t.keys + l.bkt * kBucket;
-  const uint64_t* bs = t.scores + l.bkt * kBucket;
-  const uint4 dv =
-      __ldcg(reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) +
-             tile.lane);
-  const int32_t bsize = __ldcg(t.sizes + l.bkt);
-  uint64_t t0 = 0;
+// ---------------------------------------------------------------------------
+// Lock discipline. A slot is owned by whoever swapped its key word to
+// LOCKED_KEY. The four tiles of a warp work in warp-uniform rounds: in a
+// round each tile takes its decision with plain loads while holding
+// nothing, makes one CAS attempt, and if it wins it writes the slot and
+// releases it before the round ends; a tile that meets a lock simply tries
+// again next round. No tile therefore ever waits, inside a round, for a
+// lock held by a tile of its own warp (whose release could sit behind a
+// reconvergence point), and tiles of other warps always finish the round
+// that holds their lock. A key gives up after kSpinLimitNs of failed rounds
+// and raises kErrSpinTimeout.
+// ---------------------------------------------------------------------------
+constexpr int kRetry = 7;  // a round's result when a lock was in the way
 
-  // ---- 1. digest hits ------------------------------------------------------
-  uint32_t hits = bytes_eq16(dv, l.d4);
-  int mine = -1;
-  int timed_out = 0;
-  while (hits) {
-    const uint32_t j = __ffs(hits) - 1;
-    const uint32_t q = tile.lane * kDigestsPerLane + j;
-    const uint64_t old = cas_u64(bk + q, key, kLockedKey);
-    if (old == key) {
-      mine = static_cast<int>(q);
-      break;
-    }
-    if (old == kLockedKey) {
-      if (t0 == 0) t0 = global_timer_ns();
-      if (global_timer_ns() - t0 > kSpinLimitNs) {
-        timed_out = 1;
-        break;
-      }
-      __nanosleep(64);
-      continue;  // retry the same slot
-    }
-    hits &= hits - 1;
-  }
-  const uint32_t fm = tile.ballot(mine >= 0);
-  if (fm) {
-    const int src = __ffs(fm) - 1;
-    // A key can sit in one slot only; release any other lock defensively.
-    if (mine >= 0 && static_cast<int>(tile.lane) != src) exch_u64(bk + mine, key);
-    slot = tile.shfl(static_cast<uint32_t>(mine), src);
-    return kDuplicate;
-  }
-  if (tile.ballot(timed_out)) {
-    if (tile.lane == 0) atomicOr(t.error, kErrSpinTimeout);
-    return kTimedOut;
-  }
-
-  // ---- 2. first EMPTY slot in linear order from pos ------------------------
-  if (bsize < static_cast<int32_t>(kBucket)) {
-    uint32_t empt = bytes_eq16(dv, kEmptyDigest * 0x01010101u);
-    const uint32_t lo = tile.lane * kDigestsPerLane;
-    const uint32_t sh =
-        (l.pos >= lo && l.pos < lo + kDigestsPerLane) ? l.pos - lo : 0;
-    while (true) {
-      uint32_t best = 0xFFFFFFFFu;
-      if (empt) {
-        const uint32_t hi = empt & (0xFFFFu << sh);
-        const uint32_t j = __ffs(hi ? hi : empt) - 1;
-        const uint32_t q = lo + j;
-        best = (linear_rank(q, l.pos) << 8) | q;
-      }
+// Victim of a full bucket with the reference's 16-lane scan and xor
+// butterfly (insert_or_assign_kernel.h:193-238), so ties resolve exactly as
+// there: virtual lane c takes the first strictly smallest score among
+// positions c, c+16, ...; lane L of the tile holds virtual lanes L and L+8
+// (positions L+8m, even and odd m); the key's own lane is owner_idx % 16.
+__device__ __forceinline__ void min_score_butterfly(const Tile& tile,
+                                                    const uint64_t* bs,
+                                                    uint32_t pos,
+                                                    uint64_t owner_idx,
+                                                    uint64_t& ms, uint32_t& mp) {
+  uint64_t s0 = kMaxScore, s1 = kMaxScore;
+  uint32_t p0 = pos, p1 = pos;
 #pragma unroll
-      for (int o = kTile / 2; o > 0; o >>= 1)
-        best = min(best, tile.shfl_xor(best, o));
-      if (best == 0xFFFFFFFFu) break;
-      const uint32_t q = best & 0xFF;
-      const uint32_t owner = q / kDigestsPerLane;
-      uint64_t old = 0;
-      if (tile.lane == owner) {
-        old = cas_u64(bk + q, kEmptyKey, kLockedKey);
-        empt &= ~(1u << (q - lo));
-      }
-      old = tile.shfl(old, owner);
-      if (old == kEmptyKey) {
-        slot = q;
-        return kOccupiedEmpty;
-      }
+  for (int m = 0; m < 16; m++) {
+    const uint32_t q = tile.lane + 8 * m;
+    const uint64_t sc = ld_cg_u64(bs + q);
+    if (m & 1) {
+      if (sc < s1) { s1 = sc; p1 = q; }
+    } else {
+      if (sc < s0) { s0 = sc; p0 = q; }
     }
   }
-
-  // ---- 3. evict the minimum score ------------------------------------------
-  for (int round = 0;; round++) {
-    // lane L scans positions L + 8m: even m belong to virtual lane L, odd m
-    // to virtual lane L+8 of the reference's 16-lane scan (positions c+16j).
-    uint64_t s0 = kMaxScore, s1 = kMaxScore;
-    uint32_t p0 = l.pos, p1 = l.pos;
-#pragma unroll
-    for (int m = 0; m < 16; m++) {
-      const uint32_t q = tile.lane + 8 * m;
-      const uint64_t sc = ld_cg_u64(bs + q);
-      if (m & 1) {
-        if (sc < s1) { s1 = sc; p1 = q; }
-      } else {
-        if (sc < s0) { s0 = sc; p0 = q; }
-      }
-    }
-    // butterfly offset 8: virtual lanes L and L+8 live in this lane
-    {
-      const uint64_t a = s0, b = s1;
-      const uint32_t pa = p0, pb = p1;
-      if (b < a) { s0 = b; p0 = pb; }
-      if (a < b) { s1 = a; p1 = pa; }
-    }
-#pragma unroll
-    for (int o = 4; o > 0; o >>= 1) {
-      const uint64_t os0 = tile.shfl_xor(s0, o), os1 = tile.shfl_xor(s1, o);
-      const uint32_t op0 = tile.shfl_xor(p0, o), op1 = tile.shfl_xor(p1, o);
-      if (os0 < s0) { s0 = os0; p0 = op0; }
-      if (os1 < s1) { s1 = os1; p1 = op1; }
-    }
-    const uint32_t owner = static_cast<uint32_t>(owner_idx & 15);
-    const uint64_t ms = tile.shfl(owner >= 8 ? s1 : s0, owner & 7);
-    const uint32_t mp = tile.shfl(owner >= 8 ? p1 : p0, owner & 7);
-    if (desired < ms) return kRefused;
-    int r = 0;
-    uint64_t k = 0;
-    if (tile.lane == 0) {
-      k = ld_volatile_u64(bk + mp);
-      if (k != kLockedKey && k != kEmptyKey) {
-        if (cas_u64(bk + mp, k, kLockedKey) == k) {
-          if (ld_volatile_u64(bs + mp) <= ms) {
-            r = (k == kReclaimKey) ? kOccupiedReclaimed : kEvict;
-          } else {
-            exch_u64(bk + mp, k);
-          }
-        }
-      }
-      if (r == 0) {
-        if (t0 == 0) t0 = global_timer_ns();
-        if (global_timer_ns() - t0 > kSpinLimitNs) r = kTimedOut;
-      }
-    }
-    r = tile.shfl(r, 0);
-    if (r == kTimedOut) {
-      if (tile.lane == 0) atomicOr(t.error, kErrSpinTimeout);
-      return kTimedOut;
-    }
-    if (r) {
-      slot = mp;
-      vkey = tile.shfl(k, 0);
-      vscore = ms;
-      return r;
-    }
-    backoff(round);
+  {  // butterfly offset 8: both virtual lanes live in this lane
+    const uint64_t a = s0, b = s1;
+    const uint32_t pa = p0, pb = p1;
+    if (b < a) { s0 = b; p0 = pb; }
+    if (a < b) { s1 = a; p1 = pa; }
   }
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) {
+    const uint64_t os0 = tile.shfl_xor(s0, o), os1 = tile.shfl_xor(s1, o);
+    const uint32_t op0 = tile.shfl_xor(p0, o), op1 = tile.shfl_xor(p1, o);
+    if (os0 < s0) { s0 = os0; p0 = op0; }
+    if (os1 < s1) { s1 = os1; p1 = op1; }
+  }
+  const uint32_t owner = static_cast<uint32_t>(owner_idx & 15);
+  ms = tile.shfl(owner >= 8 ? s1 : s0, owner & 7);
+  mp = tile.shfl(owner >= 8 ? p1 : p0, owner & 7);
 }
 
-// Writes of a locked slot after the probe; releases the lock last.
+// Holds the lock of `slot`: score/digest/size (the reference writes them
+// right after winning the slot, insert_or_assign_kernel.h:146-149, :170-174,
+// :241-252), outputs, value rows, then the release.
 template <int Mode, int S, int VW>
-__device__ __forceinline__ void upsert_commit(const TableView& t,
+__device__ __forceinline__ void upsert_locked(const TableView& t,
                                               const Tile& tile,
                                               const UpsertArgs& a, uint64_t i,
                                               const Locate& l, uint64_t key,
                                               uint64_t desired, int res,
                                               uint32_t slot, uint64_t vkey,
-                                              uint64_t vscore, uint64_t ev_idx) {
+                                              uint64_t vscore) {
   const uint32_t vb = t.value_bytes;
-  uint64_t* bk = t.keys + l.bkt * kBucket;
   const uint64_t s = l.bkt * kBucket + slot;
-  if (res == kRefused) {
-    if constexpr (Mode == kModeInsertAndEvict) {
-      if (!a.report_refused) return;
-      // reference insert_and_evict_kernel.h:553-557, :675-683
-      if (tile.lane == 0) {
-        a.ev_keys[ev_idx] = key;
-        if (a.ev_scores) a.ev_scores[ev_idx] = desired;
-      }
-      copy_row<VW>(a.ev_values + ev_idx * vb, a.values_in + i * vb, vb,
-                   tile.lane, kTile);
-    }
-    return;
-  }
-  uint8_t* row = value_ptr(t, l.bkt, slot);
+  unsigned long long ev_idx = 0;
   if (tile.lane == 0) {
     const bool ins = res != kDuplicate;
     uint64_t ns;
@@ -383,14 +264,19 @@ __device__ __forceinline__ void upsert_commit(const TableView& t,
       atomicAdd(t.sizes + l.bkt, 1);
     if constexpr (Mode == kModeInsertAndEvict) {
       if (res == kEvict) {
+        ev_idx = atomicAdd(a.ev_counter, 1ull);
+        if (!HKV_BOUND(t, ev_idx < a.n, 3)) ev_idx = 0;
         a.ev_keys[ev_idx] = vkey;
         if (a.ev_scores) a.ev_scores[ev_idx] = vscore;
       }
     }
   }
+  uint8_t* row = value_ptr(t, l.bkt, slot);
   if constexpr (Mode == kModeInsertAndEvict) {
-    if (res == kEvict)
+    if (res == kEvict) {
+      ev_idx = tile.shfl(ev_idx, 0);
       copy_row<VW>(a.ev_values + ev_idx * vb, row, vb, tile.lane, kTile);
+    }
   }
   if constexpr (Mode == kModeFindOrInsert) {
     if (res == kDuplicate)
@@ -402,7 +288,141 @@ __device__ __forceinline__ void upsert_commit(const TableView& t,
   }
   __threadfence();
   tile.sync();
-  if (tile.lane == 0) exch_u64(bk + slot, key);
+  if (tile.lane == 0) exch_u64(t.keys + s, key);
+}
+
+// One round for one key of insert_or_assign / find_or_insert /
+// insert_and_evict (reference insert_or_assign_kernel.h:77-303,
+// find_or_insert_kernel.h:72-306, insert_and_evict_kernel.h:389-691):
+//  1. digest hits: a slot holding the key -> update it (DUPLICATE); a
+//     locked hit slot may be this key being evicted -> retry;
+//  2. bucket not full: the first EMPTY_KEY slot in linear order from pos
+//     (the order the reference's group walk visits empty slots) is claimed
+//     with CAS(EMPTY -> LOCKED), trying the next candidate on failure;
+//  3. otherwise the minimum-score slot (butterfly above); refuse iff
+//     desired < min; CAS(victim -> LOCKED) and re-check its score.
+// Returns the Occupy result, or kRetry.
+template <int Mode, int S, int VW>
+__device__ __forceinline__ int upsert_round(const TableView& t, const Tile& tile,
+                                            const UpsertArgs& a, uint64_t i,
+                                            uint64_t key, uint64_t desired,
+                                            const Locate& l) {
+  uint64_t* bk = t.keys + l.bkt * kBucket;
+  const uint64_t* bs = t.scores + l.bkt * kBucket;
+  const uint32_t lo = tile.lane * kDigestsPerLane;
+  const uint4 dv =
+      __ldcg(reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) +
+             tile.lane);
+  const int32_t bsize = __ldcg(t.sizes + l.bkt);
+  // ---- 1. is the key here?
+  uint32_t hits = bytes_eq16(dv, l.d4);
+  int mine = -1;
+  bool busy = false;
+  while (hits) {
+    const uint32_t j = __ffs(hits) - 1;
+    hits &= hits - 1;
+    const uint64_t k = ld_volatile_u64(bk + lo + j);
+    if (k == key) {
+      mine = static_cast<int>(lo + j);
+      break;
+    }
+    busy |= (k == kLockedKey);
+  }
+  int res = kRetry;
+  bool got = false;
+  uint32_t slot = 0;
+  uint64_t vkey = 0, vscore = 0;
+  const uint32_t fm = tile.ballot(mine >= 0);
+  if (fm) {
+    slot = tile.shfl(static_cast<uint32_t>(mine), __ffs(fm) - 1);
+    if (tile.lane == 0) got = cas_u64(bk + slot, key, kLockedKey) == key;
+    got = tile.shfl(got, 0);
+    if (got) res = kDuplicate;
+  } else if (!tile.ballot(busy)) {
+    // ---- 2. first EMPTY slot in linear order from pos
+    if (bsize < static_cast<int32_t>(kBucket)) {
+      uint32_t empt = bytes_eq16(dv, kEmptyDigest * 0x01010101u);
+      const uint32_t sh =
+          (l.pos >= lo && l.pos < lo + kDigestsPerLane) ? l.pos - lo : 0;
+      while (true) {
+        uint32_t best = 0xFFFFFFFFu;
+        if (empt) {
+          const uint32_t hi = empt & (0xFFFFu << sh);
+          const uint32_t q = lo + __ffs(hi ? hi : empt) - 1;
+          best = (linear_rank(q, l.pos) << 8) | q;
+        }
+#pragma unroll
+        for (int o = kTile / 2; o > 0; o >>= 1)
+          best = min(best, tile.shfl_xor(best, o));
+        if (best == 0xFFFFFFFFu) break;
+        const uint32_t q = best & 0xFF;
+        const uint32_t owner = q / kDigestsPerLane;
+        bool ok = false;
+        if (tile.lane == owner) {
+          ok = cas_u64(bk + q, kEmptyKey, kLockedKey) == kEmptyKey;
+          empt &= ~(1u << (q - lo));
+        }
+        if (tile.shfl(ok, owner)) {
+          slot = q;
+          got = true;
+          res = kOccupiedEmpty;
+          break;
+        }
+      }
+    }
+    // ---- 3. evict the minimum score
+    if (!got) {
+      uint64_t ms;
+      uint32_t mp;
+      min_score_butterfly(tile, bs, l.pos, i, ms, mp);
+      if (desired < ms) {
+        res = kRefused;
+      } else {
+        uint64_t k = 0;
+        int r = 0;
+        if (tile.lane == 0) {
+          k = ld_volatile_u64(bk + mp);
+          if (k != kLockedKey && k != kEmptyKey &&
+              cas_u64(bk + mp, k, kLockedKey) == k) {
+            if (ld_volatile_u64(bs + mp) <= ms)
+              r = (k == kReclaimKey) ? kOccupiedReclaimed : kEvict;
+            else
+              exch_u64(bk + mp, k);
+          }
+        }
+        r = tile.shfl(r, 0);
+        if (r) {
+          got = true;
+          res = r;
+          slot = mp;
+          vkey = tile.shfl(k, 0);
+          vscore = ms;
+        }
+      }
+    }
+  }
+  if (got) {
+    if (!HKV_BOUND(t, slot < kBucket, 2)) slot = 0;
+    upsert_locked<Mode, S, VW>(t, tile, a, i, l, key, desired, res, slot, vkey,
+                               vscore);
+  }
+  return res;
+}
+
+// lane 0 of a tile: true once the key has been retried for kSpinLimitNs
+__device__ __forceinline__ bool retry_expired(const TableView& t, const Tile& tile,
+                                              uint64_t& t0, int site) {
+  int expired = 0;
+  if (tile.lane == 0) {
+    const uint64_t now = global_timer_ns();
+    if (t0 == 0) t0 = now;
+    expired = now - t0 > kSpinLimitNs;
+    if (expired) {
+      atomicOr(t.error, kErrSpinTimeout);
+      atomicExch(t.error + 1, site);
+    }
+  }
+  return tile.shfl(expired, 0) != 0;
 }
 
 template <int Mode, int S, int VW>
@@ -416,11 +436,12 @@ __global__ void __launch_bounds__(256) upsert_kernel(TableView t, UpsertArgs a) 
   const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x / 32);
   const uint64_t warp = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / 32;
   const uint64_t n = a.dn != nullptr ? *a.dn : a.n;
+  const uint32_t vb = t.value_bytes;
   for (uint64_t base = warp * 4; base < n; base += nwarps * 4) {
     const uint64_t i = base + (wl >> 3);
+    uint64_t key = 0, desired = 0, t0 = 0;
     int res = kIllegal;
-    uint32_t slot = 0;
-    uint64_t vkey = 0, vscore = 0, desired = 0, key = 0;
+    bool todo = false;
     Locate l;
     l.bkt = 0;
     l.pos = 0;
@@ -430,27 +451,47 @@ __global__ void __launch_bounds__(256) upsert_kernel(TableView t, UpsertArgs a) 
       if (!is_reserved(key)) {
         desired = desired_when_missed<S>(a.scores, i, a.epoch, clk);
         l = locate(t, key);
-        res = upsert_probe<S>(t, tile, l, key, desired, i, slot, vkey, vscore);
+        todo = true;
       }
+    }
+    // warp-uniform rounds; see the lock discipline above
+    for (int round = 0;; round++) {
+      bool again = false;
+      if (todo) {
+        res = upsert_round<Mode, S, VW>(t, tile, a, i, key, desired, l);
+        if (res == kRetry) {
+          if (retry_expired(t, tile, t0, 101)) {
+            res = kTimedOut;
+            todo = false;
+          } else {
+            again = true;
+          }
+        } else {
+          todo = false;
+        }
+      }
+      if (!__any_sync(0xFFFFFFFFu, again)) break;
+      backoff(round);
+    }
+    if (i < n) {
       if (a.status != nullptr && tile.lane == 0) a.status[i] = res;
+      if constexpr (Mode == kModeInsertAndEvict) {
+        if (res == kRefused && a.report_refused) {
+          // reference insert_and_evict_kernel.h:553-557, :675-683: the
+          // refused input is reported with its desired score
+          unsigned long long o = 0;
+          if (tile.lane == 0) {
+            o = atomicAdd(a.ev_counter, 1ull);
+            if (!HKV_BOUND(t, o < a.n, 4)) o = 0;
+            a.ev_keys[o] = key;
+            if (a.ev_scores) a.ev_scores[o] = desired;
+          }
+          o = tile.shfl(o, 0);
+          copy_row<VW>(a.ev_values + o * vb, a.values_in + i * vb, vb,
+                       tile.lane, kTile);
+        }
+      }
     }
-    uint64_t ev_idx = 0;
-    if constexpr (Mode == kModeInsertAndEvict) {
-      // warp-aggregated compaction: one atomic per warp (reference uses a
-      // prefix sum plus block and global atomics, insert_and_evict_kernel.h
-      // :594-642)
-      const bool need =
-          (res == kEvict || (res == kRefused && a.report_refused)) &&
-          tile.lane == 0;
-      const uint32_t vote = __ballot_sync(0xFFFFFFFFu, need);
-      unsigned long long wbase = 0;
-      if (wl == 0 && vote) wbase = atomicAdd(a.ev_counter, __popc(vote));
-      wbase = __shfl_sync(0xFFFFFFFFu, wbase, 0);
-      ev_idx = wbase + __popc(vote & ((1u << tile.shift) - 1u));
-    }
-    if (res != kIllegal && res != kTimedOut)
-      upsert_commit<Mode, S, VW>(t, tile, a, i, l, key, desired, res, slot,
-                                 vkey, vscore, ev_idx);
   }
 }
 
@@ -656,123 +697,119 @@ __global__ void __launch_bounds__(256) accum_kernel(TableView t, AccumArgs a) {
 // assign_scores (reference assign_scores_kernel_with_filter.h:38-141) and
 // erase (reference remove_kernel.h:33-113)
 // ============================================================================
-// Locks the slot holding `key` (found with the find rule when kStopRule);
-// waits on LOCKED hits. Returns slot or -1; -2 on timeout.
+// Finds the slot holding `key` with plain loads (the reference's find rule
+// when kStopRule: a digest-empty EMPTY_KEY slot earlier in the walk hides
+// it). Returns the slot, -1 if absent, -2 if a locked digest-hit slot may
+// hold the key (the caller retries).
 template <bool kStopRule>
-__device__ __forceinline__ int tile_lock_existing(const TableView& t,
-                                                  const Tile& tile,
-                                                  const Locate& l, uint64_t key,
-                                                  uint4 dv) {
-  uint64_t* bk = t.keys + l.bkt * kBucket;
+__device__ __forceinline__ int tile_locate_existing(const TableView& t,
+                                                    const Tile& tile,
+                                                    const Locate& l,
+                                                    uint64_t key) {
+  const uint64_t* bk = t.keys + l.bkt * kBucket;
+  const uint4 dv = __ldcg(
+      reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) + tile.lane);
+  const uint32_t lo = tile.lane * kDigestsPerLane;
   uint32_t hits = bytes_eq16(dv, l.d4);
-  int mine = -1, to = 0;
-  uint64_t t0 = 0;
+  int mine = -1;
+  bool busy = false;
   while (hits) {
     const uint32_t j = __ffs(hits) - 1;
-    const uint32_t q = tile.lane * kDigestsPerLane + j;
-    const uint64_t old = cas_u64(bk + q, key, kLockedKey);
-    if (old == key) {
-      mine = static_cast<int>(q);
+    hits &= hits - 1;
+    const uint64_t k = ld_volatile_u64(bk + lo + j);
+    if (k == key) {
+      mine = static_cast<int>(lo + j);
       break;
     }
-    if (old == kLockedKey) {
-      if (t0 == 0) t0 = global_timer_ns();
-      if (global_timer_ns() - t0 > kSpinLimitNs) {
-        to = 1;
-        break;
-      }
-      __nanosleep(64);
-      continue;
-    }
-    hits &= hits - 1;
+    busy |= (k == kLockedKey);
   }
   const uint32_t fm = tile.ballot(mine >= 0);
-  if (!fm) return tile.ballot(to) ? -2 : -1;
-  const int src = __ffs(fm) - 1;
-  if (mine >= 0 && static_cast<int>(tile.lane) != src) exch_u64(bk + mine, key);
-  const uint32_t p = tile.shfl(static_cast<uint32_t>(mine), src);
+  if (!fm) return tile.ballot(busy) ? -2 : -1;
+  const uint32_t p = tile.shfl(static_cast<uint32_t>(mine), __ffs(fm) - 1);
   if constexpr (kStopRule) {
-    // a digest-empty EMPTY_KEY slot before p in the walk hides the key
     uint32_t empt = bytes_eq16(dv, kEmptyDigest * 0x01010101u);
     const uint32_t pr = hit_rank(p, l.pos);
     bool stop = false;
     while (empt) {
       const uint32_t j = __ffs(empt) - 1;
       empt &= empt - 1;
-      const uint32_t q = tile.lane * kDigestsPerLane + j;
+      const uint32_t q = lo + j;
       if (empty_rank(q, l.pos) < pr && ld_volatile_u64(bk + q) == kEmptyKey)
         stop = true;
     }
-    if (tile.ballot(stop)) {
-      if (tile.lane == 0) exch_u64(bk + p, key);
-      return -1;
-    }
+    if (tile.ballot(stop)) return -1;
   }
   return static_cast<int>(p);
 }
 
-template <int S>
+// Score update of existing keys (reference assign_scores_kernel_with_filter.h
+// :38-141, score rule update_without_missed) or erase (reference
+// remove_kernel.h:33-113: RECLAIM tombstone, score 0, reclaim digest, size
+// decrement), in the warp-uniform rounds of the upsert family.
+template <int S, bool kErase>
 __global__ void __launch_bounds__(256)
-    assign_scores_kernel(TableView t, const uint64_t* __restrict__ keys,
-                         const uint64_t* __restrict__ scores, uint64_t n,
-                         uint64_t epoch) {
+    existing_key_kernel(TableView t, const uint64_t* __restrict__ keys,
+                        const uint64_t* __restrict__ scores, uint64_t n,
+                        uint64_t epoch) {
   __shared__ uint64_t s_clock;
   if (threadIdx.x == 0) s_clock = global_timer_ns();
   __syncthreads();
   const uint64_t clk = s_clock;
   const Tile tile;
-  const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / kTile);
-  for (uint64_t i = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / kTile;
-       i < n; i += ntiles) {
-    const uint64_t key = keys[i];
-    if (is_reserved(key)) continue;
-    const Locate l = locate(t, key);
-    const uint4 dv =
-        __ldcg(reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) +
-               tile.lane);
-    const int p = tile_lock_existing<true>(t, tile, l, key, dv);
-    if (p == -2) {
-      if (tile.lane == 0) atomicOr(t.error, kErrSpinTimeout);
-      continue;
+  const uint32_t wl = threadIdx.x & 31;
+  const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x / 32);
+  const uint64_t warp = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / 32;
+  for (uint64_t base = warp * 4; base < n; base += nwarps * 4) {
+    const uint64_t i = base + (wl >> 3);
+    uint64_t key = 0, t0 = 0;
+    bool todo = false;
+    Locate l;
+    l.bkt = 0;
+    l.pos = 0;
+    l.d4 = 0;
+    if (i < n) {
+      key = keys[i];
+      if (!is_reserved(key)) {
+        l = locate(t, key);
+        todo = true;
+      }
     }
-    if (p < 0) continue;
-    if (tile.lane == 0) {
-      const uint64_t s = l.bkt * kBucket + p;
-      uint64_t ns;
-      if (score_without_missed<S>(ld_volatile_u64(t.scores + s), scores, i,
-                                  epoch, clk, &ns))
-        t.scores[s] = ns;
-      __threadfence();
-      exch_u64(t.keys + s, key);
-    }
-  }
-}
-
-__global__ void __launch_bounds__(256)
-    erase_kernel(TableView t, const uint64_t* __restrict__ keys, uint64_t n) {
-  const Tile tile;
-  const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / kTile);
-  for (uint64_t i = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / kTile;
-       i < n; i += ntiles) {
-    const uint64_t key = keys[i];
-    if (is_reserved(key)) continue;
-    const Locate l = locate(t, key);
-    const uint4 dv =
-        __ldcg(reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) +
-               tile.lane);
-    const int p = tile_lock_existing<false>(t, tile, l, key, dv);
-    if (p == -2) {
-      if (tile.lane == 0) atomicOr(t.error, kErrSpinTimeout);
-      continue;
-    }
-    if (p < 0) continue;
-    if (tile.lane == 0) {
-      const uint64_t s = l.bkt * kBucket + p;
-      t.scores[s] = 0;
-      t.digests[s] = kReclaimDigest;
-      atomicSub(t.sizes + l.bkt, 1);
-      __threadfence();
-      exch_u64(t.keys + s, kReclaimKey);
+    for (int round = 0;; round++) {
+      bool again = false;
+      if (todo) {
+        const int p = tile_locate_existing<!kErase>(t, tile, l, key);
+        bool got = false;
+        const uint64_t s = l.bkt * kBucket + (p < 0 ? 0 : p);
+        if (p >= 0 && tile.lane == 0)
+          got = cas_u64(t.keys + s, key, kLockedKey) == key;
+        if (tile.shfl(got, 0)) {
+          if (tile.lane == 0) {
+            if constexpr (kErase) {
+              t.scores[s] = 0;
+              t.digests[s] = kReclaimDigest;
+              atomicSub(t.sizes + l.bkt, 1);
+              __threadfence();
+              exch_u64(t.keys + s, kReclaimKey);
+            } else {
+              uint64_t ns;
+              if (score_without_missed<S>(ld_volatile_u64(t.scores + s), scores,
+                                          i, epoch, clk, &ns))
+                t.scores[s] = ns;
+              __threadfence();
+              exch_u64(t.keys + s, key);
+            }
+          }
+          todo = false;
+        } else if (p == -1) {
+          todo = false;
+        } else if (retry_expired(t, tile, t0, 201)) {
+          todo = false;
+        } else {
+          again = true;
+        }
+      }
+      if (!__any_sync(0xFFFFFFFFu, again)) break;
+      backoff(round);
     }
   }
 }

@@ -156,8 +156,8 @@ TableImpl::TableImpl(const hkv_options& o, int key_type, int value_type,
   CUDA_TRY(cudaMalloc(&scores_, slots * 8));
   CUDA_TRY(cudaMalloc(&digests_, slots));
   CUDA_TRY(cudaMalloc(&sizes_, num_buckets_ * 4));
-  CUDA_TRY(cudaMalloc(&d_error_, sizeof(int)));
-  CUDA_TRY(cudaMemset(d_error_, 0, sizeof(int)));
+  CUDA_TRY(cudaMalloc(&d_error_, 2 * sizeof(int)));
+  CUDA_TRY(cudaMemset(d_error_, 0, 2 * sizeof(int)));
   CUDA_TRY(cudaMalloc(&d_scratch_, 4 * sizeof(unsigned long long)));
   CUDA_TRY(cudaHostAlloc(&h_scratch_, 4 * sizeof(unsigned long long),
                          cudaHostAllocDefault));
@@ -242,7 +242,7 @@ TableView TableImpl::view() const {
   v.slice_shift = slice_shift_;
   v.single_slice = slices_.size() == 1 ? 1 : 0;
   v.value_bytes = value_bytes_;
-  v.pad = 0;
+  v.num_slices = static_cast<uint32_t>(slices_.size());
   return v;
 }
 
@@ -427,7 +427,7 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
   DISPATCH_VW(vwr, gather_rows_kernel<VW><<<tile_grid(n), 256, 0, s>>>(
                        urows, rows, mode == kModeFindOrInsert ? rep_first
                                                               : rep_last,
-                       n, value_bytes_));
+                       d.dm, value_bytes_));
   CUDA_TRY(cudaGetLastError());
 
   a.keys = d.ukeys;
@@ -602,8 +602,8 @@ void TableImpl::assign_scores(size_t n, const uint64_t* keys,
   check_strategy(scores, false);
   const TableView v = view();
   DISPATCH_STRATEGY(strategy_, {
-    assign_scores_kernel<S><<<tile_grid(n), 256, 0, s>>>(v, keys, scores, n,
-                                                         epoch_);
+    existing_key_kernel<S, false><<<tile_grid(n), 256, 0, s>>>(v, keys, scores,
+                                                               n, epoch_);
   });
   CUDA_TRY(cudaGetLastError());
 }
@@ -632,7 +632,8 @@ void TableImpl::contains(size_t n, const uint64_t* keys, bool* founds,
 
 void TableImpl::erase(size_t n, const uint64_t* keys, cudaStream_t s) {
   if (n == 0 || keys == nullptr) return;
-  erase_kernel<<<tile_grid(n), 256, 0, s>>>(view(), keys, n);
+  existing_key_kernel<kLru, true><<<tile_grid(n), 256, 0, s>>>(view(), keys,
+                                                               nullptr, n, 0);
   CUDA_TRY(cudaGetLastError());
 }
 
@@ -712,13 +713,17 @@ void TableImpl::reserve(size_t new_capacity, cudaStream_t s) {
 
 void TableImpl::check_device_error(cudaStream_t s) {
   CUDA_TRY(cudaStreamSynchronize(s));
-  int e = 0;
-  CUDA_TRY(cudaMemcpy(&e, d_error_, sizeof(int), cudaMemcpyDeviceToHost));
-  if (e) {
-    CUDA_TRY(cudaMemset(d_error_, 0, sizeof(int)));
+  int e[2] = {0, 0};
+  CUDA_TRY(cudaMemcpy(e, d_error_, sizeof(e), cudaMemcpyDeviceToHost));
+  if (e[0]) {
+    CUDA_TRY(cudaMemset(d_error_, 0, sizeof(e)));
+    if (e[0] & kErrBounds)
+      throw HkvError{HKV_ERR_RUNTIME, "device index check failed at site " +
+                                          std::to_string(e[1])};
     throw HkvError{HKV_ERR_TIMEOUT,
-                   "a device lock wait exceeded its time limit; the keys "
-                   "involved were not processed"};
+                   "a device lock wait exceeded its time limit (site " +
+                       std::to_string(e[1]) +
+                       "); the keys involved were not processed"};
   }
 }
 

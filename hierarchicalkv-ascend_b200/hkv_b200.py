@@ -19,7 +19,9 @@ import os
 from dataclasses import dataclass
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libhkv_b200.so")
+# HKV_B200_LIB selects another build of the same library (e.g. the
+# self-checking libhkv_b200_checked.so); the default is the optimised one.
+LIB_PATH = os.environ.get("HKV_B200_LIB") or os.path.join(_HERE, "libhkv_b200.so")
 
 HKV_OK = 0
 HKV_ERR_INVALID = 1
