@@ -159,6 +159,25 @@ __device__ __forceinline__ uint64_t cas_u64(uint64_t* p, uint64_t expect,
 __device__ __forceinline__ uint64_t exch_u64(uint64_t* p, uint64_t v) {
   return atomicExch(reinterpret_cast<unsigned long long*>(p), v);
 }
+// Lock acquisition: CAS with acquire semantics at GPU scope, so the slot's
+// contents written before its last release are visible to the winner.
+__device__ __forceinline__ uint64_t cas_acquire_u64(uint64_t* p, uint64_t expect,
+                                                    uint64_t desired) {
+  uint64_t old;
+  asm volatile("atom.acquire.gpu.global.cas.b64 %0, [%1], %2, %3;"
+               : "=l"(old)
+               : "l"(p), "l"(expect), "l"(desired)
+               : "memory");
+  return old;
+}
+// Lock release: store of the final key word with release semantics at GPU
+// scope. Writes of the other lanes of the tile are ordered before it by the
+// tile's __syncwarp (which orders memory among its participants) and the
+// release is cumulative over them.
+__device__ __forceinline__ void store_release_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v)
+               : "memory");
+}
 
 // ---- byte compare of 16 digests: bit j set when byte j equals d ----------
 __device__ __forceinline__ uint32_t bytes_eq16(uint4 v, uint32_t d4) {

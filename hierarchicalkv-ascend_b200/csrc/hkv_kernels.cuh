@@ -255,7 +255,9 @@ __device__ __forceinline__ void upsert_locked(const TableView& t,
   if (tile.lane == 0) {
     const bool ins = res != kDuplicate;
     uint64_t ns;
-    const uint64_t old = ins ? 0 : ld_volatile_u64(t.scores + s);
+    // only the Lfu rules add to the stored score
+    const uint64_t old =
+        (ins || (S != kLfu && S != kEpochLfu)) ? 0 : ld_volatile_u64(t.scores + s);
     if (score_on_write<S>(old, a.scores, i, desired, ins, &ns)) {
       if (ins) t.digests[s] = static_cast<uint8_t>(l.d4);
       t.scores[s] = ns;
@@ -286,9 +288,8 @@ __device__ __forceinline__ void upsert_locked(const TableView& t,
   } else {
     copy_row<VW>(row, a.values_in + i * vb, vb, tile.lane, kTile);
   }
-  __threadfence();
   tile.sync();
-  if (tile.lane == 0) exch_u64(t.keys + s, key);
+  if (tile.lane == 0) store_release_u64(t.keys + s, key);
 }
 
 // One round for one key of insert_or_assign / find_or_insert /
@@ -314,14 +315,14 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const Tile& tile
       __ldcg(reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) +
              tile.lane);
   const int32_t bsize = __ldcg(t.sizes + l.bkt);
-  // ---- 1. is the key here?
+  // ---- 1. is the key here? (a digest hit that holds it is locked at once)
   uint32_t hits = bytes_eq16(dv, l.d4);
   int mine = -1;
   bool busy = false;
   while (hits) {
     const uint32_t j = __ffs(hits) - 1;
     hits &= hits - 1;
-    const uint64_t k = ld_volatile_u64(bk + lo + j);
+    const uint64_t k = cas_acquire_u64(bk + lo + j, key, kLockedKey);
     if (k == key) {
       mine = static_cast<int>(lo + j);
       break;
@@ -334,10 +335,13 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const Tile& tile
   uint64_t vkey = 0, vscore = 0;
   const uint32_t fm = tile.ballot(mine >= 0);
   if (fm) {
-    slot = tile.shfl(static_cast<uint32_t>(mine), __ffs(fm) - 1);
-    if (tile.lane == 0) got = cas_u64(bk + slot, key, kLockedKey) == key;
-    got = tile.shfl(got, 0);
-    if (got) res = kDuplicate;
+    const int src = __ffs(fm) - 1;
+    // a key lives in one slot; release any other lock defensively
+    if (mine >= 0 && static_cast<int>(tile.lane) != src)
+      store_release_u64(bk + mine, key);
+    slot = tile.shfl(static_cast<uint32_t>(mine), src);
+    got = true;
+    res = kDuplicate;
   } else if (!tile.ballot(busy)) {
     // ---- 2. first EMPTY slot in linear order from pos
     if (bsize < static_cast<int32_t>(kBucket)) {
@@ -359,7 +363,7 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const Tile& tile
         const uint32_t owner = q / kDigestsPerLane;
         bool ok = false;
         if (tile.lane == owner) {
-          ok = cas_u64(bk + q, kEmptyKey, kLockedKey) == kEmptyKey;
+          ok = cas_acquire_u64(bk + q, kEmptyKey, kLockedKey) == kEmptyKey;
           empt &= ~(1u << (q - lo));
         }
         if (tile.shfl(ok, owner)) {
@@ -383,11 +387,11 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const Tile& tile
         if (tile.lane == 0) {
           k = ld_volatile_u64(bk + mp);
           if (k != kLockedKey && k != kEmptyKey &&
-              cas_u64(bk + mp, k, kLockedKey) == k) {
+              cas_acquire_u64(bk + mp, k, kLockedKey) == k) {
             if (ld_volatile_u64(bs + mp) <= ms)
               r = (k == kReclaimKey) ? kOccupiedReclaimed : kEvict;
             else
-              exch_u64(bk + mp, k);
+              store_release_u64(bk + mp, k);
           }
         }
         r = tile.shfl(r, 0);
@@ -426,7 +430,7 @@ __device__ __forceinline__ bool retry_expired(const TableView& t, const Tile& ti
 }
 
 template <int Mode, int S, int VW>
-__global__ void __launch_bounds__(256) upsert_kernel(TableView t, UpsertArgs a) {
+__global__ void __launch_bounds__(256, 6) upsert_kernel(TableView t, UpsertArgs a) {
   __shared__ uint64_t s_clock;
   if (threadIdx.x == 0) s_clock = global_timer_ns();
   __syncthreads();
@@ -553,7 +557,8 @@ restart:
       if (hit) {
         const int src = __ffs(hit) - 1;
         uint64_t old = 0;
-        if (static_cast<int>(lane) == src) old = cas_u64(bk + q, key, kLockedKey);
+        if (static_cast<int>(lane) == src)
+          old = cas_acquire_u64(bk + q, key, kLockedKey);
         old = __shfl_sync(0xFFFFFFFFu, old, src);
         if (old == key) {
           slot = __shfl_sync(0xFFFFFFFFu, q, src);
@@ -574,7 +579,7 @@ restart:
         const int src = __ffs(em) - 1;
         uint64_t old = 0;
         if (static_cast<int>(lane) == src)
-          old = cas_u64(bk + q, kEmptyKey, kLockedKey);
+          old = cas_acquire_u64(bk + q, kEmptyKey, kLockedKey);
         old = __shfl_sync(0xFFFFFFFFu, old, src);
         if (old == kEmptyKey) {
           slot = __shfl_sync(0xFFFFFFFFu, q, src);
@@ -619,11 +624,11 @@ restart:
     const int src = __ffs(vote) - 1;
     int ok = 0;
     if (static_cast<int>(lane) == src) {
-      if (cas_u64(bk + lp, lk, kLockedKey) == lk) {
+      if (cas_acquire_u64(bk + lp, lk, kLockedKey) == lk) {
         if (ld_volatile_u64(bs + lp) <= gm)
           ok = 1;
         else
-          exch_u64(bk + lp, lk);
+          store_release_u64(bk + lp, lk);
       }
     }
     ok = __shfl_sync(0xFFFFFFFFu, ok, src);
@@ -665,7 +670,7 @@ __global__ void __launch_bounds__(256) accum_kernel(TableView t, AccumArgs a) {
         const uint64_t s = l.bkt * kBucket + slot;
         if ((is_accum && res != kDuplicate) || (!is_accum && res == kDuplicate)) {
           // reference :114-128: undo the lock and skip
-          if (lane == 0) exch_u64(bk + slot, res == kDuplicate ? key : evk);
+          if (lane == 0) store_release_u64(bk + slot, res == kDuplicate ? key : evk);
           res = kIllegal;
         } else {
           VT* dst = reinterpret_cast<VT*>(value_ptr(t, l.bkt, slot));
@@ -683,9 +688,8 @@ __global__ void __launch_bounds__(256) accum_kernel(TableView t, AccumArgs a) {
               t.scores[s] = ns;
             }
           }
-          __threadfence();
           __syncwarp();
-          if (lane == 0) exch_u64(bk + slot, key);
+          if (lane == 0) store_release_u64(bk + slot, key);
         }
       }
     }
@@ -781,22 +785,20 @@ __global__ void __launch_bounds__(256)
         bool got = false;
         const uint64_t s = l.bkt * kBucket + (p < 0 ? 0 : p);
         if (p >= 0 && tile.lane == 0)
-          got = cas_u64(t.keys + s, key, kLockedKey) == key;
+          got = cas_acquire_u64(t.keys + s, key, kLockedKey) == key;
         if (tile.shfl(got, 0)) {
           if (tile.lane == 0) {
             if constexpr (kErase) {
               t.scores[s] = 0;
               t.digests[s] = kReclaimDigest;
               atomicSub(t.sizes + l.bkt, 1);
-              __threadfence();
-              exch_u64(t.keys + s, kReclaimKey);
+              store_release_u64(t.keys + s, kReclaimKey);
             } else {
               uint64_t ns;
               if (score_without_missed<S>(ld_volatile_u64(t.scores + s), scores,
                                           i, epoch, clk, &ns))
                 t.scores[s] = ns;
-              __threadfence();
-              exch_u64(t.keys + s, key);
+              store_release_u64(t.keys + s, key);
             }
           }
           todo = false;
