@@ -10,6 +10,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "hkv_dedup.cuh"
@@ -767,6 +768,172 @@ const char* last_error() { return g_last_error.c_str(); }
 }  // namespace hkvb
 
 // ===========================================================================
+// find_or_insert without allocation (no reference counterpart).
+//
+// Some callers cannot allocate device memory while they serve lookups: an
+// embedding service that hands all of its GPU memory to a fixed arena at
+// start-up, or code running where a cudaMalloc would stall or fail. The
+// duplicate-key merge normally allocates O(n) scratch per call; this
+// variant takes it from one file-scope device array instead. The array is
+// shared by every call in the process on that device and keeps the last
+// call's contents; everything the merge needs zeroed is cleared at the start
+// of each call. Two calls that overlap on the GPU (different streams, or
+// different tables on one device) race on the array and must be ordered by
+// the caller.
+// ===========================================================================
+namespace hkvb {
+
+constexpr size_t kNoAllocMaxKeys = 16384;   // keys per call
+constexpr size_t kNoAllocMaxRowBytes = 512; // dim * sizeof(V)
+constexpr size_t kNoAllocSetSlots = 2 * kNoAllocMaxKeys;
+constexpr size_t kNoAllocScratchBytes = 10u << 20;  // 10 MiB, checked below
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+// Bump allocator over a fixed buffer (256-byte aligned pieces).
+class ScratchArena {
+ public:
+  ScratchArena(uint8_t* base, size_t bytes) : base_(base), bytes_(bytes) {}
+  template <class T>
+  T* get(size_t count) {
+    const size_t b = (count * sizeof(T) + 255) & ~size_t(255);
+    HKV_REQUIRE(used_ + b <= bytes_, HKV_ERR_RUNTIME,
+                "static scratch layout exceeds its array");
+    T* p = reinterpret_cast<T*>(base_ + used_);
+    used_ += b;
+    return p;
+  }
+
+ private:
+  uint8_t* base_;
+  size_t bytes_;
+  size_t used_ = 0;
+};
+
+}  // namespace
+
+void TableImpl::find_or_insert_in_scratch(size_t n, const uint64_t* keys,
+                                          uint8_t* values,
+                                          const uint64_t* scores,
+                                          cudaStream_t s, bool ignore,
+                                          uint8_t* scratch,
+                                          size_t scratch_bytes) {
+  if (n == 0) return;
+  HKV_REQUIRE(keys != nullptr && values != nullptr, HKV_ERR_INVALID,
+              "keys and values must not be null");
+  HKV_REQUIRE(n <= kNoAllocMaxKeys, HKV_ERR_INVALID,
+              "hkv_find_or_insert_noalloc: at most 16384 keys per call");
+  HKV_REQUIRE(value_bytes_ <= kNoAllocMaxRowBytes, HKV_ERR_INVALID,
+              "hkv_find_or_insert_noalloc: value rows of at most 512 bytes "
+              "(dim * sizeof(V))");
+  // Growing the table allocates, so this variant refuses a call that would
+  // trigger the reference's auto-grow (hkv_hashtable.h:1103-1106).
+  HKV_REQUIRE(reach_max_ || fast_load_factor(n, s) <= opt_.max_load_factor,
+              HKV_ERR_RUNTIME,
+              "hkv_find_or_insert_noalloc: this batch would grow the table, "
+              "which allocates; call hkv_reserve first");
+  check_strategy(scores, ignore);
+  const int st = ignore ? kCustomized : strategy_;
+  ScratchArena ws(scratch, scratch_bytes);
+  DedupView d;
+  d.cap = kNoAllocSetSlots;
+  d.set_keys = ws.get<uint64_t>(d.cap);
+  d.set_first = ws.get<uint32_t>(d.cap);
+  d.set_last = ws.get<uint32_t>(d.cap);
+  d.set_uid = ws.get<uint32_t>(d.cap);
+  uint32_t* slot_of = ws.get<uint32_t>(n);
+  uint32_t* rank = ws.get<uint32_t>(n);
+  uint32_t* uid_of = ws.get<uint32_t>(n);
+  const uint64_t ntiles = ceil_div(n, kScanTile);
+  uint32_t* sums = ws.get<uint32_t>(ntiles + 1);
+  uint32_t* dm = ws.get<uint32_t>(1);
+  uint64_t* ukeys = ws.get<uint64_t>(n);
+  uint32_t* rep_first = ws.get<uint32_t>(n);
+  uint32_t* rep_last = ws.get<uint32_t>(n);
+  uint64_t* uscores = scores ? ws.get<uint64_t>(n) : nullptr;
+  uint8_t* ustatus = ws.get<uint8_t>(n);
+  uint8_t* urows = ws.get<uint8_t>(n * static_cast<size_t>(value_bytes_));
+  // the array keeps the previous call's contents: reset what starts empty
+  CUDA_TRY(cudaMemsetAsync(d.set_keys, 0xFF, d.cap * 8, s));
+  CUDA_TRY(cudaMemsetAsync(d.set_first, 0xFF, d.cap * 4, s));
+  CUDA_TRY(cudaMemsetAsync(d.set_last, 0, d.cap * 4, s));
+  CUDA_TRY(cudaMemsetAsync(ustatus, kIllegal, n, s));
+  if (uscores) CUDA_TRY(cudaMemsetAsync(uscores, 0, n * 8, s));
+  const int g1 = static_cast<int>(
+      std::min<uint64_t>(ceil_div(n, 256), sm_count_ * 32ull));
+  dedup_insert_kernel<<<g1, 256, 0, s>>>(d, keys, n, slot_of, d_error_);
+  dedup_flag_kernel<<<g1, 256, 0, s>>>(d, slot_of, n, rank);
+  scan_tiles_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, s>>>(rank, n,
+                                                                       sums);
+  scan_sums_kernel<<<1, kScanThreads, 0, s>>>(sums, ntiles, dm);
+  scan_add_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, s>>>(rank, n,
+                                                                     sums);
+  dedup_emit_kernel<<<g1, 256, 0, s>>>(d, keys, slot_of, rank, n, ukeys,
+                                       rep_first, rep_last);
+  dedup_inverse_kernel<<<g1, 256, 0, s>>>(d, slot_of, n, uid_of);
+  if (scores) {
+    dedup_scores_kernel<<<g1, 256, 0, s>>>(st, scores, uid_of, rep_last, n,
+                                           uscores);
+    if (st == kEpochLfu) clamp_low32_kernel<<<g1, 256, 0, s>>>(uscores, n);
+  }
+  const int vwr = value_width({values});
+  DISPATCH_VW(vwr, gather_rows_kernel<VW><<<tile_grid(n), 256, 0, s>>>(
+                       urows, values, rep_first, dm, value_bytes_));
+  UpsertArgs a;
+  std::memset(&a, 0, sizeof a);
+  a.keys = ukeys;
+  a.values_in = urows;
+  a.values_io = urows;
+  a.scores = uscores;
+  a.n = n;
+  a.dn = dm;
+  a.epoch = epoch_;
+  a.status = ustatus;
+  const TableView v = view();
+  const int vw = value_width({urows});
+  const int grid = warp_grid(ceil_div(n, 4));
+  DISPATCH_STRATEGY(st, DISPATCH_VW(vw, {
+    upsert_kernel<kModeFindOrInsert, S, VW><<<grid, 256, 0, s>>>(v, a);
+  }));
+  DISPATCH_VW(vwr, scatter_found_rows_kernel<VW><<<tile_grid(n), 256, 0, s>>>(
+                       values, urows, uid_of, rep_first, ustatus, n,
+                       value_bytes_));
+  CUDA_TRY(cudaGetLastError());
+}
+
+namespace {
+
+// Device address of g_noalloc_scratch, looked up once per device with that
+// device current. In host code the array's name is only a host-side stand-in
+// for the symbol, so kernels must be given this address.
+std::mutex g_noalloc_mu;
+uint8_t* g_noalloc_ptr[64] = {nullptr};
+
+uint8_t* noalloc_scratch_for(int device) {
+  HKV_REQUIRE(device >= 0 && device < 64, HKV_ERR_INVALID, "device id");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[device] == nullptr) {
+    int cur = 0;
+    CUDA_TRY(cudaGetDevice(&cur));
+    if (cur != device) CUDA_TRY(cudaSetDevice(device));
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (cur != device) cudaSetDevice(cur);
+    if (e != cudaSuccess)
+      throw HkvError{HKV_ERR_CUDA,
+                     std::string("cudaGetSymbolAddress(g_noalloc_scratch): ") +
+                         cudaGetErrorString(e)};
+    g_noalloc_ptr[device] = static_cast<uint8_t*>(p);
+  }
+  return g_noalloc_ptr[device];
+}
+
+}  // namespace
+}  // namespace hkvb
+
+// ===========================================================================
 // C ABI
 // ===========================================================================
 using hkvb::HkvError;
@@ -1072,6 +1239,19 @@ int hkv_debug_get_state(hkv_table* table, uint64_t* keys, uint64_t* scores,
   HKV_API_BEGIN
   HKV_TABLE(table);
   T->get_state(keys, scores, digests, sizes, static_cast<uint8_t*>(values));
+  HKV_API_END
+}
+
+int hkv_find_or_insert_noalloc(hkv_table* table, size_t n, const void* keys,
+                               void* values, const uint64_t* scores,
+                               void* stream, bool ignore_evict_strategy) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  uint8_t* scratch = hkvb::noalloc_scratch_for(T->device());
+  T->find_or_insert_in_scratch(n, static_cast<const uint64_t*>(keys),
+                               static_cast<uint8_t*>(values), scores,
+                               as_stream(stream), ignore_evict_strategy,
+                               scratch, hkvb::kNoAllocScratchBytes);
   HKV_API_END
 }
 

@@ -127,6 +127,14 @@ class TableImpl {
   int tile_grid(size_t n) const;
   int warp_grid(size_t nwarps) const;
 
+  // find_or_insert for batches that may repeat keys, with every scratch
+  // buffer carved out of caller-provided device memory `scratch` (no
+  // allocation). Defined next to the static scratch array in hkv_table.cu.
+  void find_or_insert_in_scratch(size_t n, const uint64_t* keys,
+                                 uint8_t* values, const uint64_t* scores,
+                                 cudaStream_t s, bool ignore, uint8_t* scratch,
+                                 size_t scratch_bytes);
+
  private:
   void check_strategy(const uint64_t* scores, bool ignore) const;
   void auto_grow(size_t n, cudaStream_t s);

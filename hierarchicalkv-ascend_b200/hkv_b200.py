@@ -128,6 +128,7 @@ SIGNATURES = {
     "hkv_accum_or_assign": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _P, _B]),
     "hkv_find_or_insert": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _B, _B]),
     "hkv_assign_scores": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _B]),
+    "hkv_find_or_insert_noalloc": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _B]),
     "hkv_find": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _P]),
     "hkv_contains": (ctypes.c_int, [_P, _SZ, _P, _P, _P]),
     "hkv_erase": (ctypes.c_int, [_P, _SZ, _P, _P]),
@@ -307,6 +308,15 @@ class HashTable:
         _check(lib().hkv_find_or_insert(self._h, n, _ptr(keys), _ptr(values),
                                         _ptr(scores), _stream(stream),
                                         unique_key, ignore_evict_strategy))
+
+    def find_or_insert_noalloc(self, n, keys, values, scores=None, stream=None,
+                               ignore_evict_strategy=False):
+        """find_or_insert of a batch that may repeat keys, using the library's
+        fixed device scratch array instead of allocating (see
+        hkv_find_or_insert_noalloc in include/hkv_b200.h for its limits)."""
+        _check(lib().hkv_find_or_insert_noalloc(self._h, n, _ptr(keys), _ptr(values),
+                                                _ptr(scores), _stream(stream),
+                                                ignore_evict_strategy))
 
     def assign_scores(self, n, keys, scores=None, stream=None, unique_key=True):
         _check(lib().hkv_assign_scores(self._h, n, _ptr(keys), _ptr(scores),

@@ -181,6 +181,25 @@ int hkv_reserve(hkv_table* table, size_t new_capacity, void* stream);
 /* set_global_epoch, hkv_hashtable.h:3197. */
 int hkv_set_global_epoch(hkv_table* table, uint64_t epoch);
 
+/* No reference counterpart. find_or_insert for a batch that may repeat
+ * keys (as with unique_key = false) that allocates no device memory, for
+ * callers that cannot call cudaMalloc while serving, such as a service whose
+ * GPU memory is all handed to a fixed arena at start-up. The duplicate-key
+ * merge uses one file-scope device array of 10 MiB instead of per-call
+ * scratch, so a call takes at most 16384 keys and value rows of at most 512
+ * bytes (dim * sizeof(V)); larger calls fail with HKV_ERR_INVALID. The table
+ * never grows in this call: a batch that would trigger auto-grow fails with
+ * HKV_ERR_RUNTIME (call hkv_reserve first). The first call on a device looks
+ * up the array's device address, so make that first call before any stream
+ * capture. Every call in the process shares the array and finds the last
+ * call's contents in it (what must start empty is cleared at the start of
+ * each call); calls that overlap on the GPU race on it and must be ordered
+ * by the caller. Results are those of hkv_find_or_insert with
+ * unique_key = false. */
+int hkv_find_or_insert_noalloc(hkv_table* table, size_t n, const void* keys,
+                               void* values, const uint64_t* scores,
+                               void* stream, bool ignore_evict_strategy);
+
 /* No reference counterpart: synchronises `stream` and reports a device lock
  * wait that ran out during earlier calls (HKV_ERR_TIMEOUT), then clears it.
  * The reference's device waits have no bound (find_utils.h:169-173). */

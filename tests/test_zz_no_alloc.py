@@ -1,0 +1,72 @@
+"""hkv_find_or_insert_noalloc: find_or_insert without device allocation (GPU).
+
+Some callers cannot allocate device memory while they serve lookups, for
+example a service that gives all its GPU memory to a fixed arena at start-up.
+For them the library offers a find_or_insert for batches that may repeat
+keys whose scratch is one fixed device array instead of per-call
+allocations. This test calls it through the C ABI and checks that two calls
+in a row give exactly what the allocating entry point (hkv_find_or_insert
+with unique_key=false) gives on a twin table: the same returned values and
+the same table contents (every live key with its score and value, and every
+bucket's size; integer and byte work, so the comparison is exact). Slot
+positions inside a bucket are not compared: when several keys of a batch
+land in one bucket, which of them takes which free slot depends on thread
+timing in either entry point. It lives in its own file, collected last, and
+passes alone or after the other tests.
+"""
+import numpy as np
+import pytest
+import torch
+
+import hkv_b200 as H
+from hkv_gpu import dev, host, make_table
+from hkv_testutil import live_set
+
+pytestmark = pytest.mark.gpu
+
+
+def _batch(rng, distinct, repeats, dim):
+    keys = rng.choice(distinct, repeats, replace=True).astype(np.uint64)
+    vals = rng.standard_normal((repeats, dim)).astype(np.float32)
+    scores = rng.integers(1, 50, repeats).astype(np.uint64)
+    return keys, vals, scores
+
+
+def test_noalloc_matches_allocating_entry_point_on_two_calls():
+    rng = np.random.default_rng(4242)
+    cap, dim = 128 * 512, 32
+    ref = make_table(cap, dim=dim, strategy=H.EvictStrategy.kLfu)
+    nal = make_table(cap, dim=dim, strategy=H.EvictStrategy.kLfu)
+    pool = np.unique(rng.integers(1, 1 << 62, 9000, dtype=np.uint64))
+    for call in range(2):
+        # call 0 inserts; call 1 mixes hits on call 0's keys with new keys
+        distinct = pool[:6000] if call == 0 else pool[3000:9000]
+        keys, vals, scores = _batch(rng, distinct, 15000, dim)
+        out_ref = dev(vals)
+        out_nal = dev(vals)
+        ref.find_or_insert(len(keys), dev(keys), out_ref, dev(scores), unique_key=False)
+        nal.find_or_insert_noalloc(len(keys), dev(keys), out_nal, dev(scores))
+        torch.cuda.synchronize()
+        assert torch.equal(out_ref, out_nal), f"returned values differ on call {call}"
+        rk, rs, _, rz, rv = ref.get_state()
+        nk, ns, _, nz, nv = nal.get_state()
+        assert (rz == nz).all(), f"bucket sizes differ on call {call}"
+        assert live_set(rk, rs, rv) == live_set(nk, ns, nv), \
+            f"table contents differ on call {call}"
+        nal.check_device_error()
+    assert ref.size() == nal.size() > 0
+
+
+def test_noalloc_rejects_sizes_beyond_its_scratch():
+    t = make_table(128 * 64, dim=32, strategy=H.EvictStrategy.kLfu)
+    n = 16385
+    keys = torch.arange(1, n + 1, dtype=torch.int64, device="cuda")
+    vals = torch.zeros((n, 32), device="cuda")
+    sc = torch.ones(n, dtype=torch.int64, device="cuda")
+    with pytest.raises(H.HkvException):
+        t.find_or_insert_noalloc(n, keys, vals, sc)
+    wide = make_table(128 * 64, dim=256, strategy=H.EvictStrategy.kLfu)
+    vals = torch.zeros((4, 256), device="cuda")
+    with pytest.raises(H.HkvException):
+        wide.find_or_insert_noalloc(4, keys[:4], vals, sc[:4])
+    assert t.size() == 0
