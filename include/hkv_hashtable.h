@@ -1,0 +1,337 @@
+/*
+ * hkv_hashtable.h -- C++ drop-in for the reference's HashTable API
+ * (yangzhen92/HierarchicalKV-ascend, include/hkv_hashtable.h), implemented
+ * over the C ABI of include/hkv_b200.h (libhkv_b200.so).
+ *
+ * Same class template, method names, argument order and defaults as the
+ * reference for the hot path: init, insert_or_assign, insert_and_evict (both
+ * overloads), accum_or_assign, find_or_insert, assign_scores / assign, find,
+ * contains, erase, clear, export_batch (both overloads), size, empty,
+ * capacity, load_factor, reserve, dim, max_bucket_size, bucket_count,
+ * is_pure_hbm_mode, set_global_epoch. Streams are cudaStream_t where the
+ * reference takes aclrtStream. Errors throw HkvException (reference HKV_CHECK,
+ * debug.h:53-74), CudaException (reference NpuException, debug.h:30-51) or
+ * std::runtime_error, as the reference does.
+ *
+ * `namespace npu::hkv` is an alias of `hkv_b200`, so code written against the
+ * reference compiles unchanged apart from the stream type.
+ */
+#ifndef HKV_B200_HASHTABLE_H_
+#define HKV_B200_HASHTABLE_H_
+
+#include <cuda_runtime_api.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <type_traits>
+
+#include "hkv_b200.h"
+
+namespace hkv_b200 {
+
+/* EvictStrategy, reference hkv_hashtable.h:111-119. */
+struct EvictStrategy {
+  enum EvictStrategyEnum {
+    kLru = HKV_LRU,
+    kLfu = HKV_LFU,
+    kEpochLru = HKV_EPOCH_LRU,
+    kEpochLfu = HKV_EPOCH_LFU,
+    kCustomized = HKV_CUSTOMIZED,
+  };
+};
+
+/* HashTableOptions, reference hashtable_options.h:534-566 (the memory-pool
+ * options are not needed: scratch is stream-ordered). */
+struct HashTableOptions {
+  size_t init_capacity = 0;
+  size_t max_capacity = 0;
+  size_t max_hbm_for_vectors = 0;
+  size_t max_bucket_size = 128;
+  size_t dim = 64;
+  float max_load_factor = 0.5f;
+  int block_size = 128;
+  int io_block_size = 1024;
+  int device_id = -1;
+  bool io_by_cpu = false;
+  bool use_constant_memory = false;
+  int reserved_key_start_bit = 0;
+  size_t num_of_buckets_per_alloc = 1;
+  bool api_lock = false;
+};
+
+constexpr uint64_t IGNORED_GLOBAL_EPOCH = UINT64_C(0xFFFFFFFFFFFFFFFF);
+
+class HkvException : public std::runtime_error {
+ public:
+  explicit HkvException(const std::string& m) : std::runtime_error(m) {}
+};
+class CudaException : public std::runtime_error {
+ public:
+  explicit CudaException(const std::string& m) : std::runtime_error(m) {}
+};
+class HkvTimeout : public std::runtime_error {
+ public:
+  explicit HkvTimeout(const std::string& m) : std::runtime_error(m) {}
+};
+
+namespace detail {
+inline void check(int status) {
+  if (status == HKV_OK) return;
+  const std::string m = hkv_last_error();
+  switch (status) {
+    case HKV_ERR_INVALID:
+      throw HkvException(m);
+    case HKV_ERR_CUDA:
+      throw CudaException(m);
+    case HKV_ERR_TIMEOUT:
+      throw HkvTimeout(m);
+    default:
+      throw std::runtime_error(m);
+  }
+}
+template <class V>
+constexpr int value_code() {
+  return std::is_same<V, float>::value      ? HKV_VALUE_F32
+         : std::is_same<V, double>::value   ? HKV_VALUE_F64
+         : std::is_same<V, uint32_t>::value ? HKV_VALUE_U32
+         : std::is_same<V, uint64_t>::value ? HKV_VALUE_U64
+         : std::is_same<V, int8_t>::value   ? HKV_VALUE_I8
+         : (sizeof(V) == 2)                 ? HKV_VALUE_F16
+                                            : -1;
+}
+inline void* st(cudaStream_t s) { return reinterpret_cast<void*>(s); }
+}  // namespace detail
+
+/* HashTable<K, V, S, Strategy>, reference hkv_hashtable.h:895-3485.
+ * K: uint64_t or int64_t; S: uint64_t; V: the element type of the vectors
+ * (float, double, uint32_t, uint64_t, int8_t, or a 2-byte half type; for a
+ * 2-byte type define HKV_B200_VALUE_BF16 before including this header to
+ * select bfloat16 arithmetic in accum_or_assign). */
+template <typename K, typename V, typename S = uint64_t,
+          int Strategy = EvictStrategy::kLru>
+class HashTable {
+ public:
+  using size_type = size_t;
+  using key_type = K;
+  using value_type = V;
+  using score_type = S;
+  static constexpr int evict_strategy = Strategy;
+
+  HashTable() {
+    static_assert(std::is_same<K, int64_t>::value || std::is_same<K, uint64_t>::value,
+                  "The key_type must be int64_t or uint64_t.");
+    static_assert(std::is_same<S, uint64_t>::value, "The score_type must be uint64_t.");
+  }
+  ~HashTable() {
+    if (t_) hkv_table_destroy(t_);
+  }
+  HashTable(const HashTable&) = delete;
+  HashTable& operator=(const HashTable&) = delete;
+  HashTable(HashTable&&) = delete;
+  HashTable& operator=(HashTable&&) = delete;
+
+  /* init, reference hkv_hashtable.h:962-1042. An allocator argument is
+   * accepted for signature compatibility; memory is always cudaMalloc /
+   * cudaHostAlloc(Mapped). */
+  void init(const HashTableOptions& options, void* allocator = nullptr) {
+    (void)allocator;
+    if (t_) return;
+    hkv_options o;
+    hkv_options_init(&o);
+    o.init_capacity = options.init_capacity;
+    o.max_capacity = options.max_capacity;
+    o.max_hbm_for_vectors = options.max_hbm_for_vectors;
+    o.max_bucket_size = options.max_bucket_size;
+    o.dim = options.dim;
+    o.max_load_factor = options.max_load_factor;
+    o.block_size = options.block_size;
+    o.io_block_size = options.io_block_size;
+    o.device_id = options.device_id;
+    o.io_by_cpu = options.io_by_cpu;
+    o.use_constant_memory = options.use_constant_memory;
+    o.reserved_key_start_bit = options.reserved_key_start_bit;
+    o.num_of_buckets_per_alloc = options.num_of_buckets_per_alloc;
+    o.api_lock = options.api_lock;
+    int vc = detail::value_code<V>();
+#ifdef HKV_B200_VALUE_BF16
+    if (sizeof(V) == 2) vc = HKV_VALUE_BF16;
+#endif
+    if (vc < 0) throw HkvException("unsupported value_type");
+    detail::check(hkv_table_create(
+        &o, std::is_same<K, int64_t>::value ? HKV_KEY_I64 : HKV_KEY_U64, vc,
+        Strategy, &t_));
+    options_ = options;
+  }
+
+  void insert_or_assign(const size_type n, const key_type* keys,
+                        const value_type* values,
+                        const score_type* scores = nullptr,
+                        cudaStream_t stream = 0, bool unique_key = true,
+                        bool ignore_evict_strategy = false) {
+    detail::check(hkv_insert_or_assign(t_, n, keys, values, scores,
+                                       detail::st(stream), unique_key,
+                                       ignore_evict_strategy));
+  }
+
+  void insert_and_evict(const size_type n, const key_type* keys,
+                        const value_type* values, const score_type* scores,
+                        key_type* evicted_keys, value_type* evicted_values,
+                        score_type* evicted_scores,
+                        size_type* d_evicted_counter, cudaStream_t stream = 0,
+                        bool unique_key = true,
+                        bool ignore_evict_strategy = false) {
+    detail::check(hkv_insert_and_evict(
+        t_, n, keys, values, scores, evicted_keys, evicted_values,
+        evicted_scores, reinterpret_cast<uint64_t*>(d_evicted_counter),
+        detail::st(stream), unique_key, ignore_evict_strategy));
+  }
+
+  size_type insert_and_evict(const size_type n, const key_type* keys,
+                             const value_type* values,
+                             const score_type* scores, key_type* evicted_keys,
+                             value_type* evicted_values,
+                             score_type* evicted_scores,
+                             cudaStream_t stream = 0, bool unique_key = true,
+                             bool ignore_evict_strategy = false) {
+    size_t c = 0;
+    detail::check(hkv_insert_and_evict_count(
+        t_, n, keys, values, scores, evicted_keys, evicted_values,
+        evicted_scores, detail::st(stream), unique_key, ignore_evict_strategy,
+        &c));
+    return c;
+  }
+
+  void accum_or_assign(const size_type n, const key_type* keys,
+                       const value_type* value_or_deltas,
+                       const bool* accum_or_assigns,
+                       const score_type* scores = nullptr,
+                       cudaStream_t stream = 0,
+                       bool ignore_evict_strategy = false) {
+    detail::check(hkv_accum_or_assign(t_, n, keys, value_or_deltas,
+                                      accum_or_assigns, scores,
+                                      detail::st(stream),
+                                      ignore_evict_strategy));
+  }
+
+  void find_or_insert(const size_type n, const key_type* keys,
+                      value_type* values, score_type* scores = nullptr,
+                      cudaStream_t stream = 0, bool unique_key = true,
+                      bool ignore_evict_strategy = false) {
+    detail::check(hkv_find_or_insert(t_, n, keys, values, scores,
+                                     detail::st(stream), unique_key,
+                                     ignore_evict_strategy));
+  }
+
+  void assign_scores(const size_type n, const key_type* keys,
+                     const score_type* scores = nullptr,
+                     cudaStream_t stream = 0, bool unique_key = true) {
+    detail::check(hkv_assign_scores(t_, n, keys, scores, detail::st(stream),
+                                    unique_key));
+  }
+  void assign(const size_type n, const key_type* keys,
+              const score_type* scores = nullptr, cudaStream_t stream = 0,
+              bool unique_key = true) {
+    assign_scores(n, keys, scores, stream, unique_key);
+  }
+
+  void find(const size_type n, const key_type* keys, value_type* values,
+            bool* founds, score_type* scores = nullptr,
+            cudaStream_t stream = 0) const {
+    detail::check(
+        hkv_find(t_, n, keys, values, founds, scores, detail::st(stream)));
+  }
+
+  void contains(const size_type n, const key_type* keys, bool* founds,
+                cudaStream_t stream = 0) const {
+    detail::check(hkv_contains(t_, n, keys, founds, detail::st(stream)));
+  }
+
+  void erase(const size_type n, const key_type* keys, cudaStream_t stream = 0) {
+    detail::check(hkv_erase(t_, n, keys, detail::st(stream)));
+  }
+
+  void clear(cudaStream_t stream = 0) {
+    detail::check(hkv_clear(t_, detail::st(stream)));
+  }
+
+  void export_batch(size_type n, const size_type offset, size_type* d_counter,
+                    key_type* keys, value_type* values,
+                    score_type* scores = nullptr,
+                    cudaStream_t stream = 0) const {
+    detail::check(hkv_export_batch(t_, n, offset,
+                                   reinterpret_cast<uint64_t*>(d_counter), keys,
+                                   values, scores, detail::st(stream)));
+  }
+
+  size_type export_batch(const size_type n, const size_type offset,
+                         key_type* keys, value_type* values,
+                         score_type* scores = nullptr,
+                         cudaStream_t stream = 0) const {
+    size_t c = 0;
+    detail::check(hkv_export_batch_count(t_, n, offset, keys, values, scores,
+                                         detail::st(stream), &c));
+    return c;
+  }
+
+  bool empty(cudaStream_t stream = 0) const { return size(stream) == 0; }
+
+  size_type size(cudaStream_t stream = 0) const {
+    size_t s = 0;
+    detail::check(hkv_size(t_, detail::st(stream), &s));
+    return s;
+  }
+
+  size_type capacity() const {
+    size_t c = 0;
+    detail::check(hkv_capacity(t_, &c));
+    return c;
+  }
+
+  void reserve(const size_type new_capacity, cudaStream_t stream = 0) {
+    detail::check(hkv_reserve(t_, new_capacity, detail::st(stream)));
+  }
+
+  float load_factor(cudaStream_t stream = 0) const {
+    float f = 0;
+    detail::check(hkv_load_factor(t_, detail::st(stream), &f));
+    return f;
+  }
+
+  size_type dim() const noexcept { return options_.dim; }
+  size_type max_bucket_size() const noexcept { return options_.max_bucket_size; }
+  size_type bucket_count() const {
+    size_t c = 0;
+    detail::check(hkv_bucket_count(t_, &c));
+    return c;
+  }
+  bool is_pure_hbm_mode() const {
+    bool b = true;
+    detail::check(hkv_is_pure_hbm_mode(t_, &b));
+    return b;
+  }
+
+  void set_global_epoch(const uint64_t epoch) {
+    detail::check(hkv_set_global_epoch(t_, epoch));
+  }
+
+  /* No reference counterpart: reports a device lock wait that ran out. */
+  void check_device_error(cudaStream_t stream = 0) {
+    detail::check(hkv_check_device_error(t_, detail::st(stream)));
+  }
+
+  hkv_table* handle() const noexcept { return t_; }
+
+ private:
+  hkv_table* t_ = nullptr;
+  HashTableOptions options_;
+};
+
+}  // namespace hkv_b200
+
+namespace npu {
+namespace hkv = ::hkv_b200;
+}  // namespace npu
+
+#endif /* HKV_B200_HASHTABLE_H_ */
