@@ -43,13 +43,13 @@ __device__ __forceinline__ uint32_t owner_of(uint64_t key, uint32_t world) {
 
 // Count representatives per destination and give each its rank within it.
 __global__ void route_count_kernel(const uint64_t* __restrict__ ukeys,
-                                   const uint32_t* __restrict__ dm,
+                                   const uint32_t* __restrict__ dm, uint64_t n,
                                    uint32_t world, uint32_t* __restrict__ counts,
                                    uint32_t* __restrict__ dest,
                                    uint32_t* __restrict__ rank_in_dest) {
   __shared__ uint32_t local[kMaxWorld];
   __shared__ uint32_t base[kMaxWorld];
-  const uint64_t m = *dm;
+  const uint64_t m = dm != nullptr ? *dm : n;
   for (uint64_t b0 = blockIdx.x * (uint64_t)blockDim.x; b0 < m;
        b0 += (uint64_t)gridDim.x * blockDim.x) {
     for (uint32_t w = threadIdx.x; w < world; w += blockDim.x) local[w] = 0;
@@ -78,7 +78,7 @@ __global__ void route_pack_kernel(const uint64_t* __restrict__ ukeys,
                                   const uint64_t* __restrict__ uscores,
                                   const uint8_t* __restrict__ rows,
                                   const uint32_t* __restrict__ row_of,
-                                  const uint32_t* __restrict__ dm,
+                                  const uint32_t* __restrict__ dm, uint64_t n,
                                   const uint32_t* __restrict__ dest,
                                   const uint32_t* __restrict__ rank_in_dest,
                                   Offsets soff, uint32_t vb,
@@ -86,7 +86,7 @@ __global__ void route_pack_kernel(const uint64_t* __restrict__ ukeys,
                                   uint64_t* __restrict__ sscores,
                                   uint8_t* __restrict__ srows) {
   const Tile tile;
-  const uint64_t m = *dm;
+  const uint64_t m = dm != nullptr ? *dm : n;
   const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / kTile);
   for (uint64_t u = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / kTile;
        u < m; u += ntiles) {
@@ -96,7 +96,8 @@ __global__ void route_pack_kernel(const uint64_t* __restrict__ ukeys,
       if (sscores) sscores[p] = uscores[u];
     }
     if (srows)
-      copy_row<VW>(srows + p * vb, rows + static_cast<uint64_t>(row_of[u]) * vb,
+      copy_row<VW>(srows + p * vb,
+                   rows + static_cast<uint64_t>(row_of ? row_of[u] : u) * vb,
                    vb, tile.lane, kTile);
   }
 }
@@ -119,7 +120,7 @@ __global__ void route_unpack_kernel(int mode, const uint32_t* __restrict__ uid_o
   const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / kTile);
   for (uint64_t i = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / kTile;
        i < n; i += ntiles) {
-    const uint32_t u = uid_of[i];
+    const uint32_t u = uid_of != nullptr ? uid_of[i] : static_cast<uint32_t>(i);
     bool ok = false;
     uint64_t p = 0;
     if (u != 0xFFFFFFFFu) {
@@ -198,7 +199,13 @@ class ShardedImpl {
     // 1. merge duplicates (scores are inputs for insert-like calls only)
     const uint64_t* in_scores = kind == 0 ? nullptr : scores;
     DedupResult d;
-    if (n > 0) {
+    if (kind == 0) {
+      // lookups are read-only: every occurrence travels as it is
+      d.ukeys = const_cast<uint64_t*>(keys);
+      d.rep_first = d.rep_last = d.uid_of = nullptr;
+      d.uscores = nullptr;
+      d.dm = nullptr;
+    } else if (n > 0) {
       d = dedup_batch(n, keys, in_scores, st, ws, s, sm_count_,
                       local_->error_word());
     } else {
@@ -220,7 +227,8 @@ class ShardedImpl {
     CUDA_TRY(cudaMemsetAsync(d_counts_, 0, 2 * kMaxWorld * sizeof(uint32_t), s));
     const int g = static_cast<int>(std::min<uint64_t>(ceil_div(nn, 256),
                                                       sm_count_ * 16ull));
-    route_count_kernel<<<g, 256, 0, s>>>(d.ukeys, d.dm, world_, scnt, dest, rid);
+    route_count_kernel<<<g, 256, 0, s>>>(d.ukeys, d.dm, n, world_, scnt, dest,
+                                         rid);
     CUDA_TRY(cudaGetLastError());
     // 3a. exchange counts
     NCCL_TRY(ncclGroupStart());
@@ -253,8 +261,8 @@ class ShardedImpl {
     const int vw = local_->value_width({values, srows, rrows});
     SHARD_DISPATCH_VW(vw, route_pack_kernel<VW><<<gt, 256, 0, s>>>(
                               d.ukeys, d.uscores, send_rows ? values : nullptr,
-                              row_of, d.dm, dest, rid, so, vb, skeys, sscores,
-                              send_rows ? srows : nullptr));
+                              row_of, d.dm, n, dest, rid, so, vb, skeys,
+                              sscores, send_rows ? srows : nullptr));
     CUDA_TRY(cudaGetLastError());
     // 3b. forward exchange
     NCCL_TRY(ncclGroupStart());

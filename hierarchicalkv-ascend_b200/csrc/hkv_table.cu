@@ -131,6 +131,15 @@ TableImpl::TableImpl(const hkv_options& o, int key_type, int value_type,
   }
   CUDA_TRY(cudaDeviceGetAttribute(&sm_count_, cudaDevAttrMultiProcessorCount,
                                   device_));
+  // Per-call scratch comes from the device's stream-ordered pool; keep freed
+  // blocks cached in the pool instead of returning them to the driver at
+  // every synchronisation (the default threshold of 0 does that).
+  {
+    cudaMemPool_t pool;
+    CUDA_TRY(cudaDeviceGetDefaultMemPool(&pool, device_));
+    uint64_t keep = UINT64_MAX;
+    CUDA_TRY(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+  }
 
   // bucket count rule, reference table.h:299-309
   max_size_ = std::max(o.init_capacity, o.max_capacity);
