@@ -248,6 +248,8 @@ def run_gpu(args):
     import numpy as np
     import torch
 
+    import hkv_b200 as H
+
     rank, world, local_rank, dist = dist_setup(args.gpus)
     device = torch.device("cuda", torch.cuda.current_device())
     cap = args.capacity
@@ -288,11 +290,13 @@ def run_gpu(args):
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
+    launches0 = H.kernel_launches()
     t0.record(stream)
     for i in range(steps):
         step(warm + i, evs[i])
     t1.record(stream)
     torch.cuda.synchronize()
+    launches = H.kernel_launches() - launches0
     if dist:
         dist.barrier()
     clocks = sampler.stop()
@@ -305,6 +309,11 @@ def run_gpu(args):
         tt = torch.tensor([ms, find_ms, ins_ms], device=device)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms, find_ms, ins_ms = [float(x) for x in tt.tolist()]
+        tl = torch.tensor([launches], dtype=torch.int64, device=device)
+        dist.all_reduce(tl)  # launches of all ranks
+        launches = int(tl.item())
+    e2e_line = e2e(table, finds, inserts, vals, warm, min(steps, 20), dist, device)
+    log("e2e done")
     keys_total = 2 * BATCH * steps * world
     value = keys_total / (ms * 1e-3) / 1e9
 
@@ -348,10 +357,9 @@ def run_gpu(args):
         result["roofline"] = roof
         result["roofline_by_op"] = rf
         result["clocks"] = clocks
-        result["gpu_launches"] = 2 * steps if world == 1 else None
+        result["gpu_launches"] = launches
+        result["e2e"] = e2e_line
         if world == 1:
-            result["e2e"] = e2e(table, finds, inserts, vals, warm, min(steps, 20))
-            log("e2e done")
             if not args.no_cpu_baseline:
                 result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
                 log("cpu baseline done")
@@ -371,12 +379,15 @@ def traffic_from_profiles(kernel):
     return None if v is None else v.get("bytes_per_launch")
 
 
-def e2e(table, finds, inserts, vals, warm, steps):
+def e2e(table, finds, inserts, vals, warm, steps, dist=None, device=None):
     """Same step through the public API with host buffers: H2D of the keys
     and values from pinned memory, find + insert_or_assign, D2H of the found
-    values and flags, all inside the timed region."""
+    values and flags, all inside the timed region. On N ranks every rank
+    runs it on its own batches; the time is the maximum over ranks and the
+    value counts the keys of all ranks."""
     import torch
 
+    world = dist.get_world_size() if dist else 1
     hk = [f.cpu().pin_memory() for f in finds[warm:warm + steps]]
     hi = [f.cpu().pin_memory() for f in inserts[warm:warm + steps]]
     hv = [v.cpu().pin_memory() for v in vals[warm:warm + steps]]
@@ -403,9 +414,13 @@ def e2e(table, finds, inserts, vals, warm, steps):
     b.record(stream)
     torch.cuda.synchronize()
     ms = a.elapsed_time(b)
+    if dist:
+        tt = torch.tensor([ms], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
     h2d = BATCH * 8 * 2 + BATCH * VALUE_BYTES
     d2h = BATCH * VALUE_BYTES + BATCH
-    return {"value": round(2 * BATCH * steps / (ms * 1e-3) / 1e9, 4), "unit": UNIT,
+    return {"value": round(2 * BATCH * steps * world / (ms * 1e-3) / 1e9, 4), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps}
 
 

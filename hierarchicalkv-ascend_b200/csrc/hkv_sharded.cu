@@ -189,7 +189,7 @@ class ShardedImpl {
            bool* founds, uint64_t* scores, cudaStream_t s) {
     const uint32_t vb = local_->value_bytes();
     const int st = local_->strategy();
-    Workspace ws(s);
+    Workspace ws(s, local_->pool());
     const uint64_t nn = std::max<uint64_t>(n, 1);
     // Which buffers travel is fixed by the call kind and the strategy, so
     // every rank posts matching sends and receives.
@@ -227,7 +227,7 @@ class ShardedImpl {
     CUDA_TRY(cudaMemsetAsync(d_counts_, 0, 2 * kMaxWorld * sizeof(uint32_t), s));
     const int g = static_cast<int>(std::min<uint64_t>(ceil_div(nn, 256),
                                                       sm_count_ * 16ull));
-    route_count_kernel<<<g, 256, 0, s>>>(d.ukeys, d.dm, n, world_, scnt, dest,
+    route_count_kernel<<<g, 256, 0, counted(s)>>>(d.ukeys, d.dm, n, world_, scnt, dest,
                                          rid);
     CUDA_TRY(cudaGetLastError());
     // 3a. exchange counts
@@ -259,7 +259,7 @@ class ShardedImpl {
                                                        sm_count_ * 32ull));
     const uint32_t* row_of = kind == 1 ? d.rep_first : d.rep_last;
     const int vw = local_->value_width({values, srows, rrows});
-    SHARD_DISPATCH_VW(vw, route_pack_kernel<VW><<<gt, 256, 0, s>>>(
+    SHARD_DISPATCH_VW(vw, route_pack_kernel<VW><<<gt, 256, 0, counted(s)>>>(
                               d.ukeys, d.uscores, send_rows ? values : nullptr,
                               row_of, d.dm, n, dest, rid, so, vb, skeys,
                               sscores, send_rows ? srows : nullptr));
@@ -309,7 +309,7 @@ class ShardedImpl {
     }
     NCCL_TRY(ncclGroupEnd());
     if (n == 0) return;
-    SHARD_DISPATCH_VW(vw, route_unpack_kernel<VW><<<gt, 256, 0, s>>>(
+    SHARD_DISPATCH_VW(vw, route_unpack_kernel<VW><<<gt, 256, 0, counted(s)>>>(
                               kind == 0 ? 0 : 1, d.uid_of, n, dest, rid, so, vb,
                               brows, bflag, bscores, values,
                               kind == 0 ? founds : nullptr,
@@ -320,7 +320,7 @@ class ShardedImpl {
   size_t size(cudaStream_t s) {
     const size_t local = local_->size(s);
     unsigned long long* d = nullptr;
-    CUDA_TRY(cudaMallocAsync(&d, 8, s));
+    CUDA_TRY(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&d), 8, local_->pool(), s));
     CUDA_TRY(cudaMemcpyAsync(d, &local, 8, cudaMemcpyHostToDevice, s));
     NCCL_TRY(ncclAllReduce(d, d, 1, ncclUint64, ncclSum, comm_, s));
     unsigned long long h = 0;

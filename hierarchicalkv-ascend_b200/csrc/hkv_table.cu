@@ -19,6 +19,8 @@
 
 namespace hkvb {
 
+std::atomic<uint64_t> g_kernel_launches{0};
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -131,14 +133,18 @@ TableImpl::TableImpl(const hkv_options& o, int key_type, int value_type,
   }
   CUDA_TRY(cudaDeviceGetAttribute(&sm_count_, cudaDevAttrMultiProcessorCount,
                                   device_));
-  // Per-call scratch comes from the device's stream-ordered pool; keep freed
-  // blocks cached in the pool instead of returning them to the driver at
-  // every synchronisation (the default threshold of 0 does that).
+  // Per-call scratch comes from a pool owned by this table whose freed blocks
+  // stay reserved (a release threshold of 0 would return them to the driver
+  // at every synchronisation and map them again on the next call).
   {
-    cudaMemPool_t pool;
-    CUDA_TRY(cudaDeviceGetDefaultMemPool(&pool, device_));
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.handleTypes = cudaMemHandleTypeNone;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = device_;
+    CUDA_TRY(cudaMemPoolCreate(&pool_, &props));
     uint64_t keep = UINT64_MAX;
-    CUDA_TRY(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+    CUDA_TRY(cudaMemPoolSetAttribute(pool_, cudaMemPoolAttrReleaseThreshold, &keep));
   }
 
   // bucket count rule, reference table.h:299-309
@@ -178,7 +184,7 @@ TableImpl::TableImpl(const hkv_options& o, int key_type, int value_type,
   allocate_slices(0, num_buckets_);
   upload_slices();
   const TableView v = view();
-  init_buckets_kernel<<<std::max(1, warp_grid(num_buckets_)), 256>>>(
+  init_buckets_kernel<<<std::max(1, warp_grid(num_buckets_)), 256, 0, counted(0)>>>(
       v, 0, num_buckets_, 1);
   CUDA_TRY(cudaGetLastError());
   CUDA_TRY(cudaDeviceSynchronize());
@@ -198,6 +204,7 @@ TableImpl::~TableImpl() {
   cudaFree(sizes_);
   cudaFree(d_error_);
   cudaFree(d_scratch_);
+  if (pool_) cudaMemPoolDestroy(pool_);
   cudaFree(d_slices_);
   cudaFreeHost(h_scratch_);
 }
@@ -351,7 +358,7 @@ uint64_t TableImpl::sum_sizes(uint64_t nb, cudaStream_t s) {
   CUDA_TRY(cudaMemsetAsync(d_scratch_, 0, sizeof(unsigned long long), s));
   const int blocks = static_cast<int>(
       std::min<uint64_t>(ceil_div(nb, 256 * 4), sm_count_ * 4ull));
-  sum_sizes_kernel<<<std::max(blocks, 1), 256, 0, s>>>(sizes_, nb, d_scratch_);
+  sum_sizes_kernel<<<std::max(blocks, 1), 256, 0, counted(s)>>>(sizes_, nb, d_scratch_);
   CUDA_TRY(cudaGetLastError());
   CUDA_TRY(cudaMemcpyAsync(h_scratch_, d_scratch_, sizeof(unsigned long long),
                            cudaMemcpyDeviceToHost, s));
@@ -411,18 +418,18 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
     const int grid = warp_grid(ceil_div(n, 4));
     DISPATCH_STRATEGY(st, DISPATCH_VW(vw, {
       if (mode == kModeInsertOrAssign)
-        upsert_kernel<kModeInsertOrAssign, S, VW><<<grid, 256, 0, s>>>(v, a);
+        upsert_kernel<kModeInsertOrAssign, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
       else if (mode == kModeFindOrInsert)
-        upsert_kernel<kModeFindOrInsert, S, VW><<<grid, 256, 0, s>>>(v, a);
+        upsert_kernel<kModeFindOrInsert, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
       else
-        upsert_kernel<kModeInsertAndEvict, S, VW><<<grid, 256, 0, s>>>(v, a);
+        upsert_kernel<kModeInsertAndEvict, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
     }));
     CUDA_TRY(cudaGetLastError());
     return;
   }
 
   // ---- duplicate keys: merge to one representative per key ---------------
-  Workspace ws(s);
+  Workspace ws(s, pool_);
   const DedupResult d =
       dedup_batch(n, keys, scores, st, ws, s, sm_count_, d_error_);
   uint8_t* ustatus = ws.get<uint8_t>(n);
@@ -434,7 +441,7 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
   // insert value: last occurrence (insert_or_assign, insert_and_evict: each
   // later duplicate overwrites) or first occurrence (find_or_insert: the
   // first inserts, the rest hit and read it back)
-  DISPATCH_VW(vwr, gather_rows_kernel<VW><<<tile_grid(n), 256, 0, s>>>(
+  DISPATCH_VW(vwr, gather_rows_kernel<VW><<<tile_grid(n), 256, 0, counted(s)>>>(
                        urows, rows, mode == kModeFindOrInsert ? rep_first
                                                               : rep_last,
                        d.dm, value_bytes_));
@@ -453,21 +460,21 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
   const int grid = warp_grid(ceil_div(n, 4));
   DISPATCH_STRATEGY(st, DISPATCH_VW(vw, {
     if (mode == kModeInsertOrAssign)
-      upsert_kernel<kModeInsertOrAssign, S, VW><<<grid, 256, 0, s>>>(v, a);
+      upsert_kernel<kModeInsertOrAssign, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
     else if (mode == kModeFindOrInsert)
-      upsert_kernel<kModeFindOrInsert, S, VW><<<grid, 256, 0, s>>>(v, a);
+      upsert_kernel<kModeFindOrInsert, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
     else
-      upsert_kernel<kModeInsertAndEvict, S, VW><<<grid, 256, 0, s>>>(v, a);
+      upsert_kernel<kModeInsertAndEvict, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
   }));
   CUDA_TRY(cudaGetLastError());
   if (mode == kModeFindOrInsert) {
-    DISPATCH_VW(vwr, scatter_found_rows_kernel<VW><<<tile_grid(n), 256, 0, s>>>(
+    DISPATCH_VW(vwr, scatter_found_rows_kernel<VW><<<tile_grid(n), 256, 0, counted(s)>>>(
                          values_io, urows, uid_of, rep_first, ustatus, n,
                          value_bytes_));
   } else if (mode == kModeInsertAndEvict) {
     const int vwe = value_width({rows, ev_values});
     DISPATCH_STRATEGY(st, DISPATCH_VW(vwe, {
-      scatter_refused_kernel<S, VW><<<tile_grid(n), 256, 0, s>>>(
+      scatter_refused_kernel<S, VW><<<tile_grid(n), 256, 0, counted(s)>>>(
           keys, rows, scores, uid_of, ustatus, n, value_bytes_, epoch_,
           ev_keys, ev_values, ev_scores,
           reinterpret_cast<unsigned long long*>(d_counter));
@@ -476,8 +483,7 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
   if (status != nullptr) {
     // per-input status: each occurrence reports its representative's result
     expand_status_kernel<<<static_cast<int>(std::min<uint64_t>(
-                               ceil_div(n, 256), sm_count_ * 32ull)),
-                           256, 0, s>>>(ustatus, uid_of, n, status);
+                               ceil_div(n, 256), sm_count_ * 32ull)), 256, 0, counted(s)>>>(ustatus, uid_of, n, status);
   }
   CUDA_TRY(cudaGetLastError());
 }
@@ -509,22 +515,22 @@ DedupResult dedup_batch(size_t n, const uint64_t* keys, const uint64_t* scores,
   r.uscores = scores ? ws.get<uint64_t>(n) : nullptr;
   const int g1 = static_cast<int>(
       std::min<uint64_t>(ceil_div(n, 256), sm_count * 32ull));
-  dedup_insert_kernel<<<g1, 256, 0, s>>>(d, keys, n, slot_of, d_error);
-  dedup_flag_kernel<<<g1, 256, 0, s>>>(d, slot_of, n, rank);
-  scan_tiles_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, s>>>(rank, n,
+  dedup_insert_kernel<<<g1, 256, 0, counted(s)>>>(d, keys, n, slot_of, d_error);
+  dedup_flag_kernel<<<g1, 256, 0, counted(s)>>>(d, slot_of, n, rank);
+  scan_tiles_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, counted(s)>>>(rank, n,
                                                                        sums);
-  scan_sums_kernel<<<1, kScanThreads, 0, s>>>(sums, ntiles, r.dm);
-  scan_add_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, s>>>(rank, n,
+  scan_sums_kernel<<<1, kScanThreads, 0, counted(s)>>>(sums, ntiles, r.dm);
+  scan_add_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, counted(s)>>>(rank, n,
                                                                      sums);
-  dedup_emit_kernel<<<g1, 256, 0, s>>>(d, keys, slot_of, rank, n, r.ukeys,
+  dedup_emit_kernel<<<g1, 256, 0, counted(s)>>>(d, keys, slot_of, rank, n, r.ukeys,
                                        r.rep_first, r.rep_last);
-  dedup_inverse_kernel<<<g1, 256, 0, s>>>(d, slot_of, n, r.uid_of);
+  dedup_inverse_kernel<<<g1, 256, 0, counted(s)>>>(d, slot_of, n, r.uid_of);
   if (scores) {
     CUDA_TRY(cudaMemsetAsync(r.uscores, 0, n * 8, s));
-    dedup_scores_kernel<<<g1, 256, 0, s>>>(strategy, scores, r.uid_of,
+    dedup_scores_kernel<<<g1, 256, 0, counted(s)>>>(strategy, scores, r.uid_of,
                                            r.rep_last, n, r.uscores);
     if (strategy == kEpochLfu)
-      clamp_low32_kernel<<<g1, 256, 0, s>>>(r.uscores, n);
+      clamp_low32_kernel<<<g1, 256, 0, counted(s)>>>(r.uscores, n);
   }
   CUDA_TRY(cudaGetLastError());
   return r;
@@ -597,11 +603,11 @@ void TableImpl::accum_or_assign(size_t n, const uint64_t* keys,
   const int grid = warp_grid(n);
   DISPATCH_STRATEGY(st, {
     if (value_type_ == HKV_VALUE_F32)
-      accum_kernel<S, float><<<grid, 256, 0, s>>>(v, a);
+      accum_kernel<S, float><<<grid, 256, 0, counted(s)>>>(v, a);
     else if (value_type_ == HKV_VALUE_F16)
-      accum_kernel<S, __half><<<grid, 256, 0, s>>>(v, a);
+      accum_kernel<S, __half><<<grid, 256, 0, counted(s)>>>(v, a);
     else
-      accum_kernel<S, __nv_bfloat16><<<grid, 256, 0, s>>>(v, a);
+      accum_kernel<S, __nv_bfloat16><<<grid, 256, 0, counted(s)>>>(v, a);
   });
   CUDA_TRY(cudaGetLastError());
 }
@@ -612,7 +618,7 @@ void TableImpl::assign_scores(size_t n, const uint64_t* keys,
   check_strategy(scores, false);
   const TableView v = view();
   DISPATCH_STRATEGY(strategy_, {
-    existing_key_kernel<S, false><<<tile_grid(n), 256, 0, s>>>(v, keys, scores,
+    existing_key_kernel<S, false><<<tile_grid(n), 256, 0, counted(s)>>>(v, keys, scores,
                                                                n, epoch_);
   });
   CUDA_TRY(cudaGetLastError());
@@ -625,7 +631,7 @@ void TableImpl::find(size_t n, const uint64_t* keys, uint8_t* values,
   if (keys == nullptr || values == nullptr) return;
   const TableView v = view();
   const int vw = value_width({values});
-  DISPATCH_VW(vw, find_kernel<VW><<<tile_grid(n), 256, 0, s>>>(
+  DISPATCH_VW(vw, find_kernel<VW><<<tile_grid(n), 256, 0, counted(s)>>>(
                       v, keys, values, founds, scores, n));
   CUDA_TRY(cudaGetLastError());
 }
@@ -635,20 +641,20 @@ void TableImpl::contains(size_t n, const uint64_t* keys, bool* founds,
   if (n == 0) return;
   if (keys == nullptr || founds == nullptr) return;
   const TableView v = view();
-  find_kernel<16><<<tile_grid(n), 256, 0, s>>>(v, keys, nullptr, founds,
+  find_kernel<16><<<tile_grid(n), 256, 0, counted(s)>>>(v, keys, nullptr, founds,
                                                nullptr, n);
   CUDA_TRY(cudaGetLastError());
 }
 
 void TableImpl::erase(size_t n, const uint64_t* keys, cudaStream_t s) {
   if (n == 0 || keys == nullptr) return;
-  existing_key_kernel<kLru, true><<<tile_grid(n), 256, 0, s>>>(view(), keys,
+  existing_key_kernel<kLru, true><<<tile_grid(n), 256, 0, counted(s)>>>(view(), keys,
                                                                nullptr, n, 0);
   CUDA_TRY(cudaGetLastError());
 }
 
 void TableImpl::clear(cudaStream_t s) {
-  init_buckets_kernel<<<warp_grid(num_buckets_), 256, 0, s>>>(
+  init_buckets_kernel<<<warp_grid(num_buckets_), 256, 0, counted(s)>>>(
       view(), 0, num_buckets_, 0);
   CUDA_TRY(cudaGetLastError());
 }
@@ -662,7 +668,7 @@ void TableImpl::export_batch(size_t n, size_t offset, uint64_t* d_counter,
   n = std::min<size_t>(capacity_ - offset, n);
   if (n == 0) return;
   const int vw = value_width({values});
-  DISPATCH_VW(vw, export_kernel<VW><<<warp_grid(ceil_div(n, 32)), 256, 0, s>>>(
+  DISPATCH_VW(vw, export_kernel<VW><<<warp_grid(ceil_div(n, 32)), 256, 0, counted(s)>>>(
                       view(), offset, n,
                       reinterpret_cast<unsigned long long*>(d_counter), keys,
                       values, scores));
@@ -701,11 +707,11 @@ void TableImpl::double_capacity(cudaStream_t s) {
   capacity_ = new_slots;
   magic_for(capacity_, &div_magic_, &div_shift_);
   const TableView v = view();
-  init_buckets_kernel<<<warp_grid(old_nb), 256, 0, s>>>(v, old_nb, new_nb, 1);
+  init_buckets_kernel<<<warp_grid(old_nb), 256, 0, counted(s)>>>(v, old_nb, new_nb, 1);
   const int vw = value_width({});
   const int grid = static_cast<int>(
       std::min<uint64_t>(ceil_div(old_nb, 8), sm_count_ * 16ull));
-  DISPATCH_VW(vw, rehash_kernel<VW><<<grid, 256, 0, s>>>(v, old_nb));
+  DISPATCH_VW(vw, rehash_kernel<VW><<<grid, 256, 0, counted(s)>>>(v, old_nb));
   CUDA_TRY(cudaGetLastError());
   CUDA_TRY(cudaStreamSynchronize(s));
 }
@@ -872,23 +878,23 @@ void TableImpl::find_or_insert_in_scratch(size_t n, const uint64_t* keys,
   if (uscores) CUDA_TRY(cudaMemsetAsync(uscores, 0, n * 8, s));
   const int g1 = static_cast<int>(
       std::min<uint64_t>(ceil_div(n, 256), sm_count_ * 32ull));
-  dedup_insert_kernel<<<g1, 256, 0, s>>>(d, keys, n, slot_of, d_error_);
-  dedup_flag_kernel<<<g1, 256, 0, s>>>(d, slot_of, n, rank);
-  scan_tiles_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, s>>>(rank, n,
+  dedup_insert_kernel<<<g1, 256, 0, counted(s)>>>(d, keys, n, slot_of, d_error_);
+  dedup_flag_kernel<<<g1, 256, 0, counted(s)>>>(d, slot_of, n, rank);
+  scan_tiles_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, counted(s)>>>(rank, n,
                                                                        sums);
-  scan_sums_kernel<<<1, kScanThreads, 0, s>>>(sums, ntiles, dm);
-  scan_add_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, s>>>(rank, n,
+  scan_sums_kernel<<<1, kScanThreads, 0, counted(s)>>>(sums, ntiles, dm);
+  scan_add_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, counted(s)>>>(rank, n,
                                                                      sums);
-  dedup_emit_kernel<<<g1, 256, 0, s>>>(d, keys, slot_of, rank, n, ukeys,
+  dedup_emit_kernel<<<g1, 256, 0, counted(s)>>>(d, keys, slot_of, rank, n, ukeys,
                                        rep_first, rep_last);
-  dedup_inverse_kernel<<<g1, 256, 0, s>>>(d, slot_of, n, uid_of);
+  dedup_inverse_kernel<<<g1, 256, 0, counted(s)>>>(d, slot_of, n, uid_of);
   if (scores) {
-    dedup_scores_kernel<<<g1, 256, 0, s>>>(st, scores, uid_of, rep_last, n,
+    dedup_scores_kernel<<<g1, 256, 0, counted(s)>>>(st, scores, uid_of, rep_last, n,
                                            uscores);
-    if (st == kEpochLfu) clamp_low32_kernel<<<g1, 256, 0, s>>>(uscores, n);
+    if (st == kEpochLfu) clamp_low32_kernel<<<g1, 256, 0, counted(s)>>>(uscores, n);
   }
   const int vwr = value_width({values});
-  DISPATCH_VW(vwr, gather_rows_kernel<VW><<<tile_grid(n), 256, 0, s>>>(
+  DISPATCH_VW(vwr, gather_rows_kernel<VW><<<tile_grid(n), 256, 0, counted(s)>>>(
                        urows, values, rep_first, dm, value_bytes_));
   UpsertArgs a;
   std::memset(&a, 0, sizeof a);
@@ -904,9 +910,9 @@ void TableImpl::find_or_insert_in_scratch(size_t n, const uint64_t* keys,
   const int vw = value_width({urows});
   const int grid = warp_grid(ceil_div(n, 4));
   DISPATCH_STRATEGY(st, DISPATCH_VW(vw, {
-    upsert_kernel<kModeFindOrInsert, S, VW><<<grid, 256, 0, s>>>(v, a);
+    upsert_kernel<kModeFindOrInsert, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
   }));
-  DISPATCH_VW(vwr, scatter_found_rows_kernel<VW><<<tile_grid(n), 256, 0, s>>>(
+  DISPATCH_VW(vwr, scatter_found_rows_kernel<VW><<<tile_grid(n), 256, 0, counted(s)>>>(
                        values, urows, uid_of, rep_first, ustatus, n,
                        value_bytes_));
   CUDA_TRY(cudaGetLastError());
@@ -1053,7 +1059,7 @@ int hkv_insert_and_evict_count(hkv_table* table, size_t n, const void* keys,
   if (n == 0) return HKV_OK;
   cudaStream_t s = as_stream(stream);
   uint64_t* d = nullptr;
-  CUDA_TRY(cudaMallocAsync(&d, sizeof(uint64_t), s));
+  CUDA_TRY(cudaMallocFromPoolAsync(&d, sizeof(uint64_t), T->pool(), s));
   CUDA_TRY(cudaMemsetAsync(d, 0, sizeof(uint64_t), s));
   try {
     T->insert_and_evict(n, static_cast<const uint64_t*>(keys),
@@ -1156,7 +1162,7 @@ int hkv_export_batch_count(hkv_table* table, size_t n, size_t offset,
   HKV_REQUIRE(h_count != nullptr, HKV_ERR_INVALID, "null count");
   cudaStream_t s = as_stream(stream);
   uint64_t* d = nullptr;
-  CUDA_TRY(cudaMallocAsync(&d, sizeof(uint64_t), s));
+  CUDA_TRY(cudaMallocFromPoolAsync(&d, sizeof(uint64_t), T->pool(), s));
   try {
     T->export_batch(n, offset, d, static_cast<uint64_t*>(keys),
                     static_cast<uint8_t*>(values), scores, s);
@@ -1233,6 +1239,13 @@ int hkv_set_global_epoch(hkv_table* table, uint64_t epoch) {
   HKV_API_BEGIN
   HKV_TABLE(table);
   T->set_global_epoch(epoch);
+  HKV_API_END
+}
+
+int hkv_kernel_launches(uint64_t* out) {
+  HKV_API_BEGIN
+  HKV_REQUIRE(out != nullptr, HKV_ERR_INVALID, "null argument");
+  *out = hkvb::g_kernel_launches.load(std::memory_order_relaxed);
   HKV_API_END
 }
 

@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <string>
 #include <vector>
 
@@ -15,6 +16,14 @@ struct HkvError {
   int code;
   std::string msg;
 };
+
+// Kernels enqueued by this library in this process; every launch passes its
+// stream through counted().
+extern std::atomic<uint64_t> g_kernel_launches;
+inline cudaStream_t counted(cudaStream_t s) {
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+  return s;
+}
 
 #define HKV_REQUIRE(cond, code, msg)              \
   do {                                            \
@@ -35,23 +44,26 @@ struct Slice {
   size_t bytes;
 };
 
-// Stream-ordered scratch (cudaMallocAsync / cudaFreeAsync).
+// Stream-ordered scratch from the table's own memory pool. The pool keeps
+// freed blocks reserved, so a steady stream of same-sized calls maps device
+// memory once instead of at every call.
 class Workspace {
  public:
-  explicit Workspace(cudaStream_t s) : stream_(s) {}
+  Workspace(cudaStream_t s, cudaMemPool_t pool) : stream_(s), pool_(pool) {}
   ~Workspace() {
     for (void* p : ptrs_) cudaFreeAsync(p, stream_);
   }
   template <class T>
   T* get(size_t count) {
     void* p = nullptr;
-    CUDA_TRY(cudaMallocAsync(&p, count * sizeof(T) + 16, stream_));
+    CUDA_TRY(cudaMallocFromPoolAsync(&p, count * sizeof(T) + 16, pool_, stream_));
     ptrs_.push_back(p);
     return static_cast<T*>(p);
   }
 
  private:
   cudaStream_t stream_;
+  cudaMemPool_t pool_;
   std::vector<void*> ptrs_;
 };
 
@@ -118,6 +130,7 @@ class TableImpl {
   int strategy() const { return strategy_; }
   int value_type() const { return value_type_; }
   int device() const { return device_; }
+  cudaMemPool_t pool() const { return pool_; }
   int* error_word() const { return d_error_; }
   int value_width(std::initializer_list<const void*> ptrs) const;
   void set_global_epoch(uint64_t e) { epoch_ = e; }
@@ -154,6 +167,7 @@ class TableImpl {
   uint32_t elem_bytes_, value_bytes_;
   int device_ = 0;
   int sm_count_ = 148;
+  cudaMemPool_t pool_ = nullptr;
   uint64_t* keys_ = nullptr;
   uint64_t* scores_ = nullptr;
   uint8_t* digests_ = nullptr;

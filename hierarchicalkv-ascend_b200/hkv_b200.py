@@ -146,6 +146,7 @@ SIGNATURES = {
     "hkv_reserve": (ctypes.c_int, [_P, _SZ, _P]),
     "hkv_set_global_epoch": (ctypes.c_int, [_P, _U64]),
     "hkv_check_device_error": (ctypes.c_int, [_P, _P]),
+    "hkv_kernel_launches": (ctypes.c_int, [ctypes.POINTER(_U64)]),
     "hkv_debug_get_state": (ctypes.c_int, [_P, _P, _P, _P, _P, _P]),
     "hkv_debug_set_state": (ctypes.c_int, [_P, _P, _P, _P, _P, _P]),
     "hkv_nccl_unique_id": (ctypes.c_int, [_P]),
@@ -194,6 +195,13 @@ def _check(status: int) -> None:
     if status == HKV_ERR_UNSUPPORTED:
         raise HkvUnsupported(msg)
     raise RuntimeError(msg)
+
+
+def kernel_launches() -> int:
+    """Kernels this library has enqueued in this process (all tables)."""
+    out = _U64(0)
+    _check(lib().hkv_kernel_launches(ctypes.byref(out)))
+    return int(out.value)
 
 
 def _ptr(x):

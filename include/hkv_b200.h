@@ -205,6 +205,10 @@ int hkv_find_or_insert_noalloc(hkv_table* table, size_t n, const void* keys,
  * The reference's device waits have no bound (find_utils.h:169-173). */
 int hkv_check_device_error(hkv_table* table, void* stream);
 
+/* No reference counterpart (instrumentation): number of kernels this library
+ * has enqueued in this process so far, on every table and stream. */
+int hkv_kernel_launches(uint64_t* out);
+
 /* No reference counterpart (test support): copies the raw slot state to /
  * from HOST buffers, slot-major (capacity entries; sizes has bucket_count
  * entries; values capacity*dim elements). Any pointer may be NULL. */
@@ -216,7 +220,7 @@ int hkv_debug_set_state(hkv_table* table, const uint64_t* keys,
 
 /* ---- sharded table (no reference counterpart: the reference is one device)
  * One table shard per GPU; keys are routed to shard owner(key) =
- * Murmur3(key) % world_size and exchanged with NCCL all-to-all. ---------- */
+ * (Murmur3(key) >> 40) % world_size and exchanged with NCCL all-to-all. ---------- */
 typedef struct hkv_sharded hkv_sharded;
 
 /* NCCL unique id (128 bytes) for rank 0 to broadcast to the others. */
