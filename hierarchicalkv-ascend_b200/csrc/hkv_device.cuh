@@ -216,6 +216,32 @@ struct Tile {
   __device__ __forceinline__ void sync() const { __syncwarp(mask); }
 };
 
+// A tile of W consecutive lanes (W = 2, 4 or 8) sharing one key; each lane
+// holds kBucket / W of the bucket's digests.
+template <uint32_t W>
+struct TileW {
+  static constexpr uint32_t kWidth = W;
+  static constexpr uint32_t kDigests = kBucket / W;
+  uint32_t lane, mask, shift;
+  __device__ __forceinline__ TileW() {
+    const uint32_t wl = threadIdx.x & 31;
+    lane = wl & (W - 1);
+    shift = wl & ~(W - 1);
+    mask = ((1u << W) - 1) << shift;
+  }
+  __device__ __forceinline__ uint32_t ballot(bool p) const {
+    return (__ballot_sync(mask, p) >> shift) & ((1u << W) - 1);
+  }
+  template <class T>
+  __device__ __forceinline__ T shfl(T v, int src) const {
+    return __shfl_sync(mask, v, src, W);
+  }
+  template <class T>
+  __device__ __forceinline__ T shfl_xor(T v, int o) const {
+    return __shfl_xor_sync(mask, v, o, W);
+  }
+};
+
 // ---- probe order ------------------------------------------------------------
 // The reference walks a bucket in groups of 4 slots starting at the group of
 // the key's start position `pos` (find_utils.h:40-84). Within a group digest

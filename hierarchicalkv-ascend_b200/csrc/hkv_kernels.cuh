@@ -9,6 +9,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <type_traits>
 #include <cuda_fp16.h>
 
 #include "hkv_device.cuh"
@@ -87,74 +88,102 @@ __device__ __forceinline__ Locate locate(const TableView& t, uint64_t key) {
   return l;
 }
 
-// Exact find rule of the reference (find_utils.h:31-86) on one tile: the key
-// is found at the digest hit p holding it, unless a digest-empty slot holding
-// EMPTY_KEY comes before p in the group walk. Returns p or -1. `dv` is this
-// lane's 16 digests; keys are read with L1-bypassing loads when `coherent`.
-template <bool kCoherent>
-__device__ __forceinline__ int tile_find(const TableView& t, const Tile& tile,
-                                         const Locate& l, uint4 dv,
-                                         uint64_t key) {
-  const uint64_t* bk = t.keys + l.bkt * kBucket;
-  uint32_t hits = bytes_eq16(dv, l.d4);
-  uint32_t best = 0xFFFFFFFFu;
-  while (hits) {
-    const uint32_t j = __ffs(hits) - 1;
-    hits &= hits - 1;
-    const uint32_t q = tile.lane * kDigestsPerLane + j;
-    const uint64_t k = kCoherent ? ld_cg_u64(bk + q) : __ldg(bk + q);
-    if (k == key) best = min(best, (hit_rank(q, l.pos) << 8) | q);
-  }
-#pragma unroll
-  for (int o = kTile / 2; o > 0; o >>= 1) best = min(best, tile.shfl_xor(best, o));
-  if (best == 0xFFFFFFFFu) return -1;
-  const uint32_t prank = best >> 8;
-  uint32_t empt = bytes_eq16(dv, kEmptyDigest * 0x01010101u);
-  bool stop = false;
-  while (empt) {
-    const uint32_t j = __ffs(empt) - 1;
-    empt &= empt - 1;
-    const uint32_t q = tile.lane * kDigestsPerLane + j;
-    if (empty_rank(q, l.pos) < prank) {
-      const uint64_t k = kCoherent ? ld_cg_u64(bk + q) : __ldg(bk + q);
-      if (k == kEmptyKey) stop = true;
-    }
-  }
-  if (tile.ballot(stop)) return -1;
-  return static_cast<int>(best & 0xFF);
-}
-
 // ============================================================================
 // find / contains (reference find_with_digest_kernel.h:33-108,
 // contains_kernel.h:31-64)
+//
+// A tile of kFindTile lanes handles one key; each lane compares
+// kBucket / kFindTile digests (one to four 16-byte loads). The key of a
+// tile's next iteration is loaded one iteration ahead. Per key the tile then
+// makes three dependent trips: the digest line, the keys of the digest hits
+// (with the keys of the digest-empty slots ranked before the first hit),
+// and the value row.
 // ============================================================================
+#ifndef HKV_FIND_TILE
+#define HKV_FIND_TILE 4
+#endif
+#ifndef HKV_FIND_MIN_BLOCKS
+#define HKV_FIND_MIN_BLOCKS 8
+#endif
+#ifndef HKV_FIND_BLOCKS_PER_SM
+#define HKV_FIND_BLOCKS_PER_SM 64
+#endif
+constexpr uint32_t kFindBlocksPerSm = HKV_FIND_BLOCKS_PER_SM;
+constexpr uint32_t kFindTile = HKV_FIND_TILE;
+
+template <class M>
+__device__ __forceinline__ uint32_t low_bit(M m) {
+  if constexpr (sizeof(M) == 8)
+    return static_cast<uint32_t>(__ffsll(static_cast<long long>(m)) - 1);
+  else
+    return static_cast<uint32_t>(__ffs(static_cast<int>(m)) - 1);
+}
+
 template <int VW>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, HKV_FIND_MIN_BLOCKS)
     find_kernel(TableView t, const uint64_t* __restrict__ keys,
                 uint8_t* __restrict__ values, bool* __restrict__ founds,
                 uint64_t* __restrict__ scores, uint64_t n) {
-  const Tile tile;
-  const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / kTile);
+  using V = typename VecOf<VW>::T;
+  using Tl = TileW<kFindTile>;
+  constexpr uint32_t W = kFindTile;
+  constexpr uint32_t kD = Tl::kDigests;  // digests per lane
+  constexpr uint32_t kDV = kD / 16;      // 16-byte digest loads per lane
+  using M = typename std::conditional<(kD > 32), uint64_t, uint32_t>::type;
+  const Tl tile;
+  const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / W);
   const uint32_t vb = t.value_bytes;
-  for (uint64_t i = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / kTile;
-       i < n; i += ntiles) {
-    const uint64_t key = __ldg(keys + i);
+  const uint32_t nv = vb / VW;
+  const uint32_t lo = tile.lane * kD;
+  uint64_t i = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / W;
+  uint64_t next = i < n ? __ldg(keys + i) : 0;
+  for (; i < n; i += ntiles) {
+    const uint64_t key = next;
+    if (i + ntiles < n) next = __ldg(keys + i + ntiles);
     int p = -1;
-    Locate l;
+    uint64_t bkt = 0;
     if (!is_reserved(key)) {
-      l = locate(t, key);
-      const uint4 dv = __ldg(reinterpret_cast<const uint4*>(
-                                 t.digests + l.bkt * kBucket) +
-                             tile.lane);
-      p = tile_find<false>(t, tile, l, dv, key);
+      const Locate l = locate(t, key);
+      bkt = l.bkt;
+      const uint64_t* bk = t.keys + l.bkt * kBucket;
+      const uint4* dl =
+          reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) + tile.lane * kDV;
+      M hits = 0, empt = 0;
+#pragma unroll
+      for (uint32_t j = 0; j < kDV; j++) {
+        const uint4 dv = __ldg(dl + j);
+        hits |= static_cast<M>(bytes_eq16(dv, l.d4)) << (16 * j);
+        empt |= static_cast<M>(bytes_eq16(dv, kEmptyDigest * 0x01010101u)) << (16 * j);
+      }
+      // digest hits holding the key, best = first in the reference's walk
+      uint32_t best = 0xFFFFFFFFu;
+      for (M h = hits; h; h &= h - 1) {
+        const uint32_t q = lo + low_bit(h);
+        if (__ldg(bk + q) == key) best = min(best, (hit_rank(q, l.pos) << 8) | q);
+      }
+#pragma unroll
+      for (int o = W / 2; o > 0; o >>= 1) best = min(best, tile.shfl_xor(best, o));
+      if (best != 0xFFFFFFFFu) {
+        // an empty slot holding EMPTY_KEY ranked before the hit ends the
+        // walk (find_utils.h:58-66)
+        const uint32_t prank = best >> 8;
+        bool stop = false;
+        for (M e = empt; e; e &= e - 1) {
+          const uint32_t q = lo + low_bit(e);
+          if (empty_rank(q, l.pos) < prank && __ldg(bk + q) == kEmptyKey) stop = true;
+        }
+        if (!tile.ballot(stop)) p = static_cast<int>(best & 0xFF);
+      }
     }
     if (tile.lane == 0 && founds != nullptr) founds[i] = p >= 0;
     if (p >= 0) {
-      if (tile.lane == 0 && scores != nullptr)
-        scores[i] = __ldg(t.scores + l.bkt * kBucket + p);
-      if (values != nullptr)
-        copy_row_nc_cs<VW>(values + i * vb, value_ptr(t, l.bkt, p), vb,
-                           tile.lane, kTile);
+      if (scores != nullptr && tile.lane == 0)
+        scores[i] = __ldg(t.scores + bkt * kBucket + p);
+      if (values != nullptr) {
+        V* dst = reinterpret_cast<V*>(values + i * vb);
+        const V* src = reinterpret_cast<const V*>(value_ptr(t, bkt, p));
+        for (uint32_t v = tile.lane; v < nv; v += W) __stcs(dst + v, __ldg(src + v));
+      }
     }
   }
 }
@@ -241,6 +270,21 @@ __device__ __forceinline__ void min_score_butterfly(const Tile& tile,
 // Holds the lock of `slot`: score/digest/size (the reference writes them
 // right after winning the slot, insert_or_assign_kernel.h:146-149, :170-174,
 // :241-252), outputs, value rows, then the release.
+// Writes a value row whose first kTile vectors (vector `lane` of this lane)
+// were loaded into `head` ahead of time; the rest is copied from `src`.
+template <int VW>
+__device__ __forceinline__ void store_row_head(uint8_t* __restrict__ dst,
+                                               typename VecOf<VW>::T head,
+                                               const uint8_t* __restrict__ src,
+                                               uint32_t bytes, uint32_t lane) {
+  using V = typename VecOf<VW>::T;
+  const uint32_t nv = bytes / VW;
+  V* d = reinterpret_cast<V*>(dst);
+  const V* sv = reinterpret_cast<const V*>(src);
+  if (lane < nv) d[lane] = head;
+  for (uint32_t v = lane + kTile; v < nv; v += kTile) d[v] = sv[v];
+}
+
 template <int Mode, int S, int VW>
 __device__ __forceinline__ void upsert_locked(const TableView& t,
                                               const Tile& tile,
@@ -248,7 +292,8 @@ __device__ __forceinline__ void upsert_locked(const TableView& t,
                                               const Locate& l, uint64_t key,
                                               uint64_t desired, int res,
                                               uint32_t slot, uint64_t vkey,
-                                              uint64_t vscore) {
+                                              uint64_t vscore,
+                                              typename VecOf<VW>::T head) {
   const uint32_t vb = t.value_bytes;
   const uint64_t s = l.bkt * kBucket + slot;
   unsigned long long ev_idx = 0;
@@ -284,9 +329,9 @@ __device__ __forceinline__ void upsert_locked(const TableView& t,
     if (res == kDuplicate)
       copy_row<VW>(a.values_io + i * vb, row, vb, tile.lane, kTile);
     else
-      copy_row<VW>(row, a.values_io + i * vb, vb, tile.lane, kTile);
+      store_row_head<VW>(row, head, a.values_io + i * vb, vb, tile.lane);
   } else {
-    copy_row<VW>(row, a.values_in + i * vb, vb, tile.lane, kTile);
+    store_row_head<VW>(row, head, a.values_in + i * vb, vb, tile.lane);
   }
   tile.sync();
   if (tile.lane == 0) store_release_u64(t.keys + s, key);
@@ -307,7 +352,8 @@ template <int Mode, int S, int VW>
 __device__ __forceinline__ int upsert_round(const TableView& t, const Tile& tile,
                                             const UpsertArgs& a, uint64_t i,
                                             uint64_t key, uint64_t desired,
-                                            const Locate& l) {
+                                            const Locate& l,
+                                            typename VecOf<VW>::T head) {
   uint64_t* bk = t.keys + l.bkt * kBucket;
   const uint64_t* bs = t.scores + l.bkt * kBucket;
   const uint32_t lo = tile.lane * kDigestsPerLane;
@@ -408,7 +454,7 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const Tile& tile
   if (got) {
     if (!HKV_BOUND(t, slot < kBucket, 2)) slot = 0;
     upsert_locked<Mode, S, VW>(t, tile, a, i, l, key, desired, res, slot, vkey,
-                               vscore);
+                               vscore, head);
   }
   return res;
 }
@@ -429,8 +475,11 @@ __device__ __forceinline__ bool retry_expired(const TableView& t, const Tile& ti
   return tile.shfl(expired, 0) != 0;
 }
 
+#ifndef HKV_UPSERT_MIN_BLOCKS
+#define HKV_UPSERT_MIN_BLOCKS 6
+#endif
 template <int Mode, int S, int VW>
-__global__ void __launch_bounds__(256, 6) upsert_kernel(TableView t, UpsertArgs a) {
+__global__ void __launch_bounds__(256, HKV_UPSERT_MIN_BLOCKS) upsert_kernel(TableView t, UpsertArgs a) {
   __shared__ uint64_t s_clock;
   if (threadIdx.x == 0) s_clock = global_timer_ns();
   __syncthreads();
@@ -439,20 +488,30 @@ __global__ void __launch_bounds__(256, 6) upsert_kernel(TableView t, UpsertArgs 
   const uint32_t wl = threadIdx.x & 31;
   const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x / 32);
   const uint64_t warp = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / 32;
+  using V = typename VecOf<VW>::T;
   const uint64_t n = a.dn != nullptr ? *a.dn : a.n;
   const uint32_t vb = t.value_bytes;
+  const uint32_t nv = vb / VW;
+  const uint8_t* in_rows = Mode == kModeFindOrInsert ? a.values_io : a.values_in;
+  // keys are read one iteration ahead, the head of the input row before the
+  // probe, so neither waits behind the bucket's round trips
+  uint64_t next = warp * 4 + (wl >> 3) < n ? a.keys[warp * 4 + (wl >> 3)] : 0;
   for (uint64_t base = warp * 4; base < n; base += nwarps * 4) {
     const uint64_t i = base + (wl >> 3);
     uint64_t key = 0, desired = 0, t0 = 0;
     int res = kIllegal;
     bool todo = false;
+    V head{};
     Locate l;
     l.bkt = 0;
     l.pos = 0;
     l.d4 = 0;
     if (i < n) {
-      key = a.keys[i];
+      key = next;
+      if (i + nwarps * 4 < n) next = a.keys[i + nwarps * 4];
       if (!is_reserved(key)) {
+        if (tile.lane < nv)
+          head = reinterpret_cast<const V*>(in_rows + i * vb)[tile.lane];
         desired = desired_when_missed<S>(a.scores, i, a.epoch, clk);
         l = locate(t, key);
         todo = true;
@@ -462,7 +521,7 @@ __global__ void __launch_bounds__(256, 6) upsert_kernel(TableView t, UpsertArgs 
     for (int round = 0;; round++) {
       bool again = false;
       if (todo) {
-        res = upsert_round<Mode, S, VW>(t, tile, a, i, key, desired, l);
+        res = upsert_round<Mode, S, VW>(t, tile, a, i, key, desired, l, head);
         if (res == kRetry) {
           if (retry_expired(t, tile, t0, 101)) {
             res = kTimedOut;

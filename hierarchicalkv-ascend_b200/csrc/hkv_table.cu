@@ -268,6 +268,21 @@ int TableImpl::tile_grid(size_t n) const {
   return static_cast<int>(std::min<uint64_t>(blocks, sm_count_ * 64ull));
 }
 
+// Find blocks; each tile walks its keys with the next key loaded ahead.
+int TableImpl::find_grid(size_t n) const {
+  const uint64_t blocks = ceil_div(std::max<size_t>(n, 1), 256 / kFindTile);
+  return static_cast<int>(std::min<uint64_t>(blocks, sm_count_ * uint64_t{kFindBlocksPerSm}));
+}
+
+#ifndef HKV_UPSERT_BLOCKS_PER_SM
+#define HKV_UPSERT_BLOCKS_PER_SM 6
+#endif
+int TableImpl::upsert_grid(size_t n) const {
+  const uint64_t blocks = ceil_div(std::max<size_t>(n, 1), 256 / kTile);
+  return static_cast<int>(
+      std::min<uint64_t>(blocks, sm_count_ * uint64_t{HKV_UPSERT_BLOCKS_PER_SM}));
+}
+
 int TableImpl::warp_grid(size_t nwarps) const {
   const uint64_t blocks = ceil_div(std::max<size_t>(nwarps, 1), 8);
   return static_cast<int>(std::min<uint64_t>(blocks, sm_count_ * 64ull));
@@ -415,7 +430,7 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
     a.scores = scores;
     a.n = n;
     const int vw = value_width({rows, ev_values});
-    const int grid = warp_grid(ceil_div(n, 4));
+    const int grid = upsert_grid(n);
     DISPATCH_STRATEGY(st, DISPATCH_VW(vw, {
       if (mode == kModeInsertOrAssign)
         upsert_kernel<kModeInsertOrAssign, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
@@ -457,7 +472,7 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
   a.report_refused = 0;
   CUDA_TRY(cudaMemsetAsync(ustatus, kIllegal, n, s));
   const int vw = value_width({urows, ev_values});
-  const int grid = warp_grid(ceil_div(n, 4));
+  const int grid = upsert_grid(n);
   DISPATCH_STRATEGY(st, DISPATCH_VW(vw, {
     if (mode == kModeInsertOrAssign)
       upsert_kernel<kModeInsertOrAssign, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
@@ -631,7 +646,7 @@ void TableImpl::find(size_t n, const uint64_t* keys, uint8_t* values,
   if (keys == nullptr || values == nullptr) return;
   const TableView v = view();
   const int vw = value_width({values});
-  DISPATCH_VW(vw, find_kernel<VW><<<tile_grid(n), 256, 0, counted(s)>>>(
+  DISPATCH_VW(vw, find_kernel<VW><<<find_grid(n), 256, 0, counted(s)>>>(
                       v, keys, values, founds, scores, n));
   CUDA_TRY(cudaGetLastError());
 }
@@ -641,7 +656,7 @@ void TableImpl::contains(size_t n, const uint64_t* keys, bool* founds,
   if (n == 0) return;
   if (keys == nullptr || founds == nullptr) return;
   const TableView v = view();
-  find_kernel<16><<<tile_grid(n), 256, 0, counted(s)>>>(v, keys, nullptr, founds,
+  find_kernel<16><<<find_grid(n), 256, 0, counted(s)>>>(v, keys, nullptr, founds,
                                                nullptr, n);
   CUDA_TRY(cudaGetLastError());
 }
@@ -908,7 +923,7 @@ void TableImpl::find_or_insert_in_scratch(size_t n, const uint64_t* keys,
   a.status = ustatus;
   const TableView v = view();
   const int vw = value_width({urows});
-  const int grid = warp_grid(ceil_div(n, 4));
+  const int grid = upsert_grid(n);
   DISPATCH_STRATEGY(st, DISPATCH_VW(vw, {
     upsert_kernel<kModeFindOrInsert, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
   }));
