@@ -159,6 +159,16 @@ __device__ __forceinline__ uint64_t cas_u64(uint64_t* p, uint64_t expect,
 __device__ __forceinline__ uint64_t exch_u64(uint64_t* p, uint64_t v) {
   return atomicExch(reinterpret_cast<unsigned long long*>(p), v);
 }
+// Exchange with acquire semantics at GPU scope (victim locking: swapping
+// LOCKED_KEY in returns the key that was there in the same round trip).
+__device__ __forceinline__ uint64_t exch_acquire_u64(uint64_t* p, uint64_t v) {
+  uint64_t old;
+  asm volatile("atom.acquire.gpu.global.exch.b64 %0, [%1], %2;"
+               : "=l"(old)
+               : "l"(p), "l"(v)
+               : "memory");
+  return old;
+}
 // Lock acquisition: CAS with acquire semantics at GPU scope, so the slot's
 // contents written before its last release are visible to the winner.
 __device__ __forceinline__ uint64_t cas_acquire_u64(uint64_t* p, uint64_t expect,
@@ -240,6 +250,7 @@ struct TileW {
   __device__ __forceinline__ T shfl_xor(T v, int o) const {
     return __shfl_xor_sync(mask, v, o, W);
   }
+  __device__ __forceinline__ void sync() const { __syncwarp(mask); }
 };
 
 // ---- probe order ------------------------------------------------------------

@@ -230,71 +230,119 @@ constexpr int kRetry = 7;  // a round's result when a lock was in the way
 // Victim of a full bucket with the reference's 16-lane scan and xor
 // butterfly (insert_or_assign_kernel.h:193-238), so ties resolve exactly as
 // there: virtual lane c takes the first strictly smallest score among
-// positions c, c+16, ...; lane L of the tile holds virtual lanes L and L+8
-// (positions L+8m, even and odd m); the key's own lane is owner_idx % 16.
-__device__ __forceinline__ void min_score_butterfly(const Tile& tile,
+// positions c, c+16, ..., then the 16 virtual lanes exchange (score,
+// position) across xor offsets 8, 4, 2, 1, each keeping its own pair unless
+// the partner's score is strictly smaller; the key's own virtual lane is
+// owner_idx % 16. Here lane L of a W-lane tile reads 16-byte score pairs at
+// positions 2L + 2Wj (one coalesced 2W*8-byte run per load), so it holds
+// the complete virtual lanes c = 2L + e + 2W*h (e in {0,1}, h < 8/W),
+// stored at r = e + 2h. Exchanges between two virtual lanes of one lane
+// stay in registers; the others are tile shuffles.
+template <uint32_t W>
+__device__ __forceinline__ void min_score_butterfly(const TileW<W>& tile,
                                                     const uint64_t* bs,
                                                     uint32_t pos,
                                                     uint64_t owner_idx,
                                                     uint64_t& ms, uint32_t& mp) {
-  uint64_t s0 = kMaxScore, s1 = kMaxScore;
-  uint32_t p0 = pos, p1 = pos;
+  constexpr uint32_t R = 16 / W;  // virtual lanes per lane
+  constexpr uint32_t H = 8 / W;   // pair loads per virtual-lane pair and k
+  uint64_t sv[R];
+  uint32_t pv[R];
 #pragma unroll
-  for (int m = 0; m < 16; m++) {
-    const uint32_t q = tile.lane + 8 * m;
-    const uint64_t sc = ld_cg_u64(bs + q);
-    if (m & 1) {
-      if (sc < s1) { s1 = sc; p1 = q; }
+  for (uint32_t r = 0; r < R; r++) {
+    sv[r] = kMaxScore;
+    pv[r] = pos;
+  }
+  const uint4* b4 = reinterpret_cast<const uint4*>(bs);
+#pragma unroll
+  for (uint32_t j = 0; j < kBucket / (2 * W); j++) {
+    const uint32_t q = 2 * tile.lane + 2 * W * j;
+    const uint4 v = __ldcg(b4 + q / 2);
+    const uint64_t s0 = (static_cast<uint64_t>(v.y) << 32) | v.x;
+    const uint64_t s1 = (static_cast<uint64_t>(v.w) << 32) | v.z;
+    const uint32_t r = 2 * (j % H);
+    if (s0 < sv[r]) { sv[r] = s0; pv[r] = q; }
+    if (s1 < sv[r + 1]) { sv[r + 1] = s1; pv[r + 1] = q + 1; }
+  }
+#pragma unroll
+  for (uint32_t o = 8; o > 0; o >>= 1) {
+    if (o == 1 || o >= 2 * W) {
+      const uint32_t d = o == 1 ? 1 : o / W;
+      uint64_t ns[R];
+      uint32_t np[R];
+#pragma unroll
+      for (uint32_t r = 0; r < R; r++) {
+        const bool take = sv[r ^ d] < sv[r];
+        ns[r] = take ? sv[r ^ d] : sv[r];
+        np[r] = take ? pv[r ^ d] : pv[r];
+      }
+#pragma unroll
+      for (uint32_t r = 0; r < R; r++) {
+        sv[r] = ns[r];
+        pv[r] = np[r];
+      }
     } else {
-      if (sc < s0) { s0 = sc; p0 = q; }
+#pragma unroll
+      for (uint32_t r = 0; r < R; r++) {
+        const uint64_t os = tile.shfl_xor(sv[r], o / 2);
+        const uint32_t op = tile.shfl_xor(pv[r], o / 2);
+        if (os < sv[r]) { sv[r] = os; pv[r] = op; }
+      }
     }
   }
-  {  // butterfly offset 8: both virtual lanes live in this lane
-    const uint64_t a = s0, b = s1;
-    const uint32_t pa = p0, pb = p1;
-    if (b < a) { s0 = b; p0 = pb; }
-    if (a < b) { s1 = a; p1 = pa; }
-  }
+  const uint32_t c = static_cast<uint32_t>(owner_idx & 15);
+  const uint32_t src = (c & (2 * W - 1)) >> 1;
+  const uint32_t rc = (c & 1) | ((c / (2 * W)) << 1);
+  uint64_t s_out = sv[0];
+  uint32_t p_out = pv[0];
 #pragma unroll
-  for (int o = 4; o > 0; o >>= 1) {
-    const uint64_t os0 = tile.shfl_xor(s0, o), os1 = tile.shfl_xor(s1, o);
-    const uint32_t op0 = tile.shfl_xor(p0, o), op1 = tile.shfl_xor(p1, o);
-    if (os0 < s0) { s0 = os0; p0 = op0; }
-    if (os1 < s1) { s1 = os1; p1 = op1; }
-  }
-  const uint32_t owner = static_cast<uint32_t>(owner_idx & 15);
-  ms = tile.shfl(owner >= 8 ? s1 : s0, owner & 7);
-  mp = tile.shfl(owner >= 8 ? p1 : p0, owner & 7);
+  for (uint32_t r = 1; r < R; r++)
+    if (r == rc) { s_out = sv[r]; p_out = pv[r]; }
+  ms = tile.shfl(s_out, src);
+  mp = tile.shfl(p_out, src);
 }
+
+// The first kHead * W vectors of a value row, vector lane + k*W in v[k]:
+// an input row is loaded into registers before the probe starts.
+template <int VW, uint32_t W>
+struct RowHead {
+  using V = typename VecOf<VW>::T;
+  static constexpr uint32_t kHead = W >= 8 ? 1 : 8 / W;
+  V v[kHead];
+  __device__ __forceinline__ void load(const uint8_t* __restrict__ src,
+                                       uint32_t nv, uint32_t lane) {
+    const V* sp = reinterpret_cast<const V*>(src);
+#pragma unroll
+    for (uint32_t k = 0; k < kHead; k++)
+      v[k] = lane + k * W < nv ? sp[lane + k * W] : V{};
+  }
+  // the whole row: head from registers, the rest from src
+  __device__ __forceinline__ void store(uint8_t* __restrict__ dst,
+                                        const uint8_t* __restrict__ src,
+                                        uint32_t nv, uint32_t lane) const {
+    V* d = reinterpret_cast<V*>(dst);
+    const V* sp = reinterpret_cast<const V*>(src);
+#pragma unroll
+    for (uint32_t k = 0; k < kHead; k++)
+      if (lane + k * W < nv) d[lane + k * W] = v[k];
+    for (uint32_t x = lane + kHead * W; x < nv; x += W) d[x] = sp[x];
+  }
+};
 
 // Holds the lock of `slot`: score/digest/size (the reference writes them
 // right after winning the slot, insert_or_assign_kernel.h:146-149, :170-174,
 // :241-252), outputs, value rows, then the release.
-// Writes a value row whose first kTile vectors (vector `lane` of this lane)
-// were loaded into `head` ahead of time; the rest is copied from `src`.
-template <int VW>
-__device__ __forceinline__ void store_row_head(uint8_t* __restrict__ dst,
-                                               typename VecOf<VW>::T head,
-                                               const uint8_t* __restrict__ src,
-                                               uint32_t bytes, uint32_t lane) {
-  using V = typename VecOf<VW>::T;
-  const uint32_t nv = bytes / VW;
-  V* d = reinterpret_cast<V*>(dst);
-  const V* sv = reinterpret_cast<const V*>(src);
-  if (lane < nv) d[lane] = head;
-  for (uint32_t v = lane + kTile; v < nv; v += kTile) d[v] = sv[v];
-}
-
-template <int Mode, int S, int VW>
+template <int Mode, int S, int VW, uint32_t W>
 __device__ __forceinline__ void upsert_locked(const TableView& t,
-                                              const Tile& tile,
+                                              const TileW<W>& tile,
                                               const UpsertArgs& a, uint64_t i,
                                               const Locate& l, uint64_t key,
                                               uint64_t desired, int res,
                                               uint32_t slot, uint64_t vkey,
                                               uint64_t vscore,
-                                              typename VecOf<VW>::T head) {
+                                              const RowHead<VW, W>& head) {
   const uint32_t vb = t.value_bytes;
+  const uint32_t nv = vb / VW;
   const uint64_t s = l.bkt * kBucket + slot;
   unsigned long long ev_idx = 0;
   if (tile.lane == 0) {
@@ -322,16 +370,16 @@ __device__ __forceinline__ void upsert_locked(const TableView& t,
   if constexpr (Mode == kModeInsertAndEvict) {
     if (res == kEvict) {
       ev_idx = tile.shfl(ev_idx, 0);
-      copy_row<VW>(a.ev_values + ev_idx * vb, row, vb, tile.lane, kTile);
+      copy_row<VW>(a.ev_values + ev_idx * vb, row, vb, tile.lane, W);
     }
   }
   if constexpr (Mode == kModeFindOrInsert) {
     if (res == kDuplicate)
-      copy_row<VW>(a.values_io + i * vb, row, vb, tile.lane, kTile);
+      copy_row<VW>(a.values_io + i * vb, row, vb, tile.lane, W);
     else
-      store_row_head<VW>(row, head, a.values_io + i * vb, vb, tile.lane);
+      head.store(row, a.values_io + i * vb, nv, tile.lane);
   } else {
-    store_row_head<VW>(row, head, a.values_in + i * vb, vb, tile.lane);
+    head.store(row, a.values_in + i * vb, nv, tile.lane);
   }
   tile.sync();
   if (tile.lane == 0) store_release_u64(t.keys + s, key);
@@ -348,25 +396,32 @@ __device__ __forceinline__ void upsert_locked(const TableView& t,
 //  3. otherwise the minimum-score slot (butterfly above); refuse iff
 //     desired < min; CAS(victim -> LOCKED) and re-check its score.
 // Returns the Occupy result, or kRetry.
-template <int Mode, int S, int VW>
-__device__ __forceinline__ int upsert_round(const TableView& t, const Tile& tile,
+template <int Mode, int S, int VW, uint32_t W>
+__device__ __forceinline__ int upsert_round(const TableView& t, const TileW<W>& tile,
                                             const UpsertArgs& a, uint64_t i,
                                             uint64_t key, uint64_t desired,
                                             const Locate& l,
-                                            typename VecOf<VW>::T head) {
+                                            const RowHead<VW, W>& head) {
+  constexpr uint32_t kD = TileW<W>::kDigests;  // digests per lane
+  constexpr uint32_t kDV = kD / 16;
+  using M = typename std::conditional<(kD > 32), uint64_t, uint32_t>::type;
   uint64_t* bk = t.keys + l.bkt * kBucket;
   const uint64_t* bs = t.scores + l.bkt * kBucket;
-  const uint32_t lo = tile.lane * kDigestsPerLane;
-  const uint4 dv =
-      __ldcg(reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) +
-             tile.lane);
+  const uint32_t lo = tile.lane * kD;
+  const uint4* dl = reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) + tile.lane * kDV;
+  M hits = 0, empt = 0;
+#pragma unroll
+  for (uint32_t j = 0; j < kDV; j++) {
+    const uint4 dv = __ldcg(dl + j);
+    hits |= static_cast<M>(bytes_eq16(dv, l.d4)) << (16 * j);
+    empt |= static_cast<M>(bytes_eq16(dv, kEmptyDigest * 0x01010101u)) << (16 * j);
+  }
   const int32_t bsize = __ldcg(t.sizes + l.bkt);
   // ---- 1. is the key here? (a digest hit that holds it is locked at once)
-  uint32_t hits = bytes_eq16(dv, l.d4);
   int mine = -1;
   bool busy = false;
   while (hits) {
-    const uint32_t j = __ffs(hits) - 1;
+    const uint32_t j = low_bit(hits);
     hits &= hits - 1;
     const uint64_t k = cas_acquire_u64(bk + lo + j, key, kLockedKey);
     if (k == key) {
@@ -391,26 +446,23 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const Tile& tile
   } else if (!tile.ballot(busy)) {
     // ---- 2. first EMPTY slot in linear order from pos
     if (bsize < static_cast<int32_t>(kBucket)) {
-      uint32_t empt = bytes_eq16(dv, kEmptyDigest * 0x01010101u);
-      const uint32_t sh =
-          (l.pos >= lo && l.pos < lo + kDigestsPerLane) ? l.pos - lo : 0;
+      const uint32_t sh = (l.pos >= lo && l.pos < lo + kD) ? l.pos - lo : 0;
       while (true) {
         uint32_t best = 0xFFFFFFFFu;
         if (empt) {
-          const uint32_t hi = empt & (0xFFFFu << sh);
-          const uint32_t q = lo + __ffs(hi ? hi : empt) - 1;
+          const M hi = empt & (~static_cast<M>(0) << sh);
+          const uint32_t q = lo + low_bit(hi ? hi : empt);
           best = (linear_rank(q, l.pos) << 8) | q;
         }
 #pragma unroll
-        for (int o = kTile / 2; o > 0; o >>= 1)
-          best = min(best, tile.shfl_xor(best, o));
+        for (int o = W / 2; o > 0; o >>= 1) best = min(best, tile.shfl_xor(best, o));
         if (best == 0xFFFFFFFFu) break;
         const uint32_t q = best & 0xFF;
-        const uint32_t owner = q / kDigestsPerLane;
+        const uint32_t owner = q / kD;
         bool ok = false;
         if (tile.lane == owner) {
           ok = cas_acquire_u64(bk + q, kEmptyKey, kLockedKey) == kEmptyKey;
-          empt &= ~(1u << (q - lo));
+          empt &= ~(static_cast<M>(1) << (q - lo));
         }
         if (tile.shfl(ok, owner)) {
           slot = q;
@@ -431,9 +483,14 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const Tile& tile
         uint64_t k = 0;
         int r = 0;
         if (tile.lane == 0) {
-          k = ld_volatile_u64(bk + mp);
-          if (k != kLockedKey && k != kEmptyKey &&
-              cas_acquire_u64(bk + mp, k, kLockedKey) == k) {
+          // Swapping LOCKED_KEY in locks the victim and returns its key in
+          // one round trip. A slot another tile holds stays LOCKED_KEY (its
+          // owner's release writes the final key); an EMPTY_KEY slot is put
+          // back; a victim whose score rose since the scan is put back.
+          k = exch_acquire_u64(bk + mp, kLockedKey);
+          if (k == kEmptyKey) {
+            store_release_u64(bk + mp, kEmptyKey);
+          } else if (k != kLockedKey) {
             if (ld_volatile_u64(bs + mp) <= ms)
               r = (k == kReclaimKey) ? kOccupiedReclaimed : kEvict;
             else
@@ -453,14 +510,15 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const Tile& tile
   }
   if (got) {
     if (!HKV_BOUND(t, slot < kBucket, 2)) slot = 0;
-    upsert_locked<Mode, S, VW>(t, tile, a, i, l, key, desired, res, slot, vkey,
-                               vscore, head);
+    upsert_locked<Mode, S, VW, W>(t, tile, a, i, l, key, desired, res, slot, vkey,
+                                  vscore, head);
   }
   return res;
 }
 
 // lane 0 of a tile: true once the key has been retried for kSpinLimitNs
-__device__ __forceinline__ bool retry_expired(const TableView& t, const Tile& tile,
+template <class Tl>
+__device__ __forceinline__ bool retry_expired(const TableView& t, const Tl& tile,
                                               uint64_t& t0, int site) {
   int expired = 0;
   if (tile.lane == 0) {
@@ -475,43 +533,50 @@ __device__ __forceinline__ bool retry_expired(const TableView& t, const Tile& ti
   return tile.shfl(expired, 0) != 0;
 }
 
-#ifndef HKV_UPSERT_MIN_BLOCKS
-#define HKV_UPSERT_MIN_BLOCKS 6
+#ifndef HKV_UPSERT_TILE
+#define HKV_UPSERT_TILE 4
 #endif
+#ifndef HKV_UPSERT_MIN_BLOCKS
+#define HKV_UPSERT_MIN_BLOCKS 5
+#endif
+constexpr uint32_t kUpsertTile = HKV_UPSERT_TILE;
+
 template <int Mode, int S, int VW>
-__global__ void __launch_bounds__(256, HKV_UPSERT_MIN_BLOCKS) upsert_kernel(TableView t, UpsertArgs a) {
+__global__ void __launch_bounds__(256, HKV_UPSERT_MIN_BLOCKS)
+    upsert_kernel(TableView t, UpsertArgs a) {
+  constexpr uint32_t W = kUpsertTile;
+  constexpr uint32_t KPW = 32 / W;  // keys per warp
   __shared__ uint64_t s_clock;
   if (threadIdx.x == 0) s_clock = global_timer_ns();
   __syncthreads();
   const uint64_t clk = s_clock;
-  const Tile tile;
+  const TileW<W> tile;
   const uint32_t wl = threadIdx.x & 31;
   const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x / 32);
   const uint64_t warp = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / 32;
-  using V = typename VecOf<VW>::T;
   const uint64_t n = a.dn != nullptr ? *a.dn : a.n;
   const uint32_t vb = t.value_bytes;
   const uint32_t nv = vb / VW;
   const uint8_t* in_rows = Mode == kModeFindOrInsert ? a.values_io : a.values_in;
   // keys are read one iteration ahead, the head of the input row before the
   // probe, so neither waits behind the bucket's round trips
-  uint64_t next = warp * 4 + (wl >> 3) < n ? a.keys[warp * 4 + (wl >> 3)] : 0;
-  for (uint64_t base = warp * 4; base < n; base += nwarps * 4) {
-    const uint64_t i = base + (wl >> 3);
+  const uint64_t stride = nwarps * KPW;
+  uint64_t next = warp * KPW + wl / W < n ? a.keys[warp * KPW + wl / W] : 0;
+  for (uint64_t base = warp * KPW; base < n; base += stride) {
+    const uint64_t i = base + wl / W;
     uint64_t key = 0, desired = 0, t0 = 0;
     int res = kIllegal;
     bool todo = false;
-    V head{};
+    RowHead<VW, W> head;
     Locate l;
     l.bkt = 0;
     l.pos = 0;
     l.d4 = 0;
     if (i < n) {
       key = next;
-      if (i + nwarps * 4 < n) next = a.keys[i + nwarps * 4];
+      if (i + stride < n) next = a.keys[i + stride];
       if (!is_reserved(key)) {
-        if (tile.lane < nv)
-          head = reinterpret_cast<const V*>(in_rows + i * vb)[tile.lane];
+        head.load(in_rows + i * vb, nv, tile.lane);
         desired = desired_when_missed<S>(a.scores, i, a.epoch, clk);
         l = locate(t, key);
         todo = true;
@@ -521,7 +586,7 @@ __global__ void __launch_bounds__(256, HKV_UPSERT_MIN_BLOCKS) upsert_kernel(Tabl
     for (int round = 0;; round++) {
       bool again = false;
       if (todo) {
-        res = upsert_round<Mode, S, VW>(t, tile, a, i, key, desired, l, head);
+        res = upsert_round<Mode, S, VW, W>(t, tile, a, i, key, desired, l, head);
         if (res == kRetry) {
           if (retry_expired(t, tile, t0, 101)) {
             res = kTimedOut;
@@ -550,8 +615,7 @@ __global__ void __launch_bounds__(256, HKV_UPSERT_MIN_BLOCKS) upsert_kernel(Tabl
             if (a.ev_scores) a.ev_scores[o] = desired;
           }
           o = tile.shfl(o, 0);
-          copy_row<VW>(a.ev_values + o * vb, a.values_in + i * vb, vb,
-                       tile.lane, kTile);
+          head.store(a.ev_values + o * vb, a.values_in + i * vb, nv, tile.lane);
         }
       }
     }

@@ -275,10 +275,10 @@ int TableImpl::find_grid(size_t n) const {
 }
 
 #ifndef HKV_UPSERT_BLOCKS_PER_SM
-#define HKV_UPSERT_BLOCKS_PER_SM 6
+#define HKV_UPSERT_BLOCKS_PER_SM HKV_UPSERT_MIN_BLOCKS
 #endif
 int TableImpl::upsert_grid(size_t n) const {
-  const uint64_t blocks = ceil_div(std::max<size_t>(n, 1), 256 / kTile);
+  const uint64_t blocks = ceil_div(std::max<size_t>(n, 1), 256 / kUpsertTile);
   return static_cast<int>(
       std::min<uint64_t>(blocks, sm_count_ * uint64_t{HKV_UPSERT_BLOCKS_PER_SM}));
 }
