@@ -190,15 +190,19 @@ __device__ __forceinline__ void store_release_u64(uint64_t* p, uint64_t v) {
 }
 
 // ---- byte compare of 16 digests: bit j set when byte j equals d ----------
+// Exact zero-byte test of x = w ^ d4 ("determine if a word has a zero byte",
+// the carry-free form from Sean Anderson's Bit Twiddling Hacks): bit 7 of
+// each byte of z is set iff that byte of x is zero. The multiply by
+// 2^0 + 2^7 + 2^14 + 2^21 moves bits 7, 15, 23, 31 to bits 28..31 without
+// carries, giving the byte-order mask in four bits.
+__device__ __forceinline__ uint32_t bytes_eq4(uint32_t w, uint32_t d4) {
+  const uint32_t x = w ^ d4;
+  const uint32_t z = ~(((x & 0x7F7F7F7Fu) + 0x7F7F7F7Fu) | x | 0x7F7F7F7Fu);
+  return (z * 0x00204081u) >> 28;
+}
 __device__ __forceinline__ uint32_t bytes_eq16(uint4 v, uint32_t d4) {
-  uint32_t m0 = __vcmpeq4(v.x, d4), m1 = __vcmpeq4(v.y, d4);
-  uint32_t m2 = __vcmpeq4(v.z, d4), m3 = __vcmpeq4(v.w, d4);
-  // each 0xFF byte -> one bit (byte-sequential bit order)
-  auto pack = [](uint32_t m) -> uint32_t {
-    m &= 0x01010101u;
-    return (m | (m >> 7) | (m >> 14) | (m >> 21)) & 0xFu;
-  };
-  return pack(m0) | (pack(m1) << 4) | (pack(m2) << 8) | (pack(m3) << 12);
+  return bytes_eq4(v.x, d4) | (bytes_eq4(v.y, d4) << 4) |
+         (bytes_eq4(v.z, d4) << 8) | (bytes_eq4(v.w, d4) << 12);
 }
 
 // ---- tile helpers (8 consecutive lanes of a warp) ---------------------------
