@@ -1,8 +1,9 @@
 // hkv_kernels.cuh -- sm_100a kernels of the HierarchicalKV hot path.
 //
-// One key is handled by a tile of 8 lanes. Each lane loads 16 of the bucket's
-// 128 digests (one 16-byte load, the tile reads the whole 128-byte line),
-// compares them with __vcmpeq4, and the tile picks slots with ballots and
+// One key is handled by a tile of W lanes (4 for find and the upsert family,
+// 8 for the others). Each lane loads 128 / W of the bucket's 128 digests in
+// 16-byte loads (the tile reads the whole 128-byte line), compares them with
+// a carry-free zero-byte test, and the tile picks slots with ballots and
 // shuffles. Values move in VW-byte vectors (16 bytes for float rows whose
 // byte size is a multiple of 16). Locks are the key words themselves: a slot
 // is owned by whoever swapped its key to LOCKED_KEY (reference types.h:65).
