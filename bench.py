@@ -190,7 +190,9 @@ def build_table(world, rank, dist, capacity):
     uid = [H.ShardedHashTable.unique_id() if rank == 0 else None]
     dist.broadcast_object_list(uid, src=0)
     opts.device_id = torch.cuda.current_device()
-    s = H.ShardedHashTable(opts, rank, world, uid[0], H.EvictStrategy.kLru)
+    s = H.ShardedHashTable(opts, rank, world, uid[0], H.EvictStrategy.kLru,
+                           max_batch=0 if os.environ.get("HKV_SHARDED_NCCL") else BATCH)
+    log(f"rank {rank}: sharded transport {s.transport}")
     return s, H.HashTable.borrow(H.lib().hkv_sharded_local(s._h), H.EvictStrategy.kLru)
 
 
@@ -255,6 +257,7 @@ def run_gpu(args):
     cap = args.capacity
     log(f"rank {rank}/{world}: table of {cap} slots")
     table, local = build_table(world, rank, dist, cap)
+    transport = table.transport if world > 1 else "none"
     total = prefill(local, rank, world, device, cap)
     lf = local.load_factor()
     log(f"prefill done, load factor {lf:.4f}")
@@ -271,7 +274,7 @@ def run_gpu(args):
         table.find(BATCH, finds[i], out_vals, founds[i])
         if ev is not None:
             ev[1].record(stream)
-        table.insert_or_assign(BATCH, inserts[i], vals[i])
+        table.insert_or_assign(BATCH, inserts[i], vals[i], unique_key=True)
         if ev is not None:
             ev[2].record(stream)
 
@@ -329,7 +332,7 @@ def run_gpu(args):
                    "strategy": "kLru", "load_factor": round(lf, 4),
                    "find_hit_rate": round(hit, 4),
                    "parallelism": "single table" if world == 1 else
-                   f"sharded x{world} (NCCL all-to-all)",
+                   f"sharded x{world} ({transport} transport)",
                    "l2": "table 9.2 GB/GPU >> 126 MB L2; every step uses its own input batches"},
     }
     if rank == 0:
@@ -426,7 +429,8 @@ def e2e(table, finds, inserts, vals, warm, steps, dist=None, device=None):
         if i >= 2:
             s_run.wait_event(drained[x])  # step i-2's outputs have left B
         table.find(BATCH, B["k"], B["o"], B["f"], stream=s_run.cuda_stream)
-        table.insert_or_assign(BATCH, B["i"], B["v"], stream=s_run.cuda_stream)
+        table.insert_or_assign(BATCH, B["i"], B["v"], stream=s_run.cuda_stream,
+                               unique_key=True)
         ran[x].record(s_run)
         s_out.wait_event(ran[x])
         with torch.cuda.stream(s_out):

@@ -43,8 +43,26 @@ enum Occupy : int {
 };
 
 // Device error word bits.
+// Up to kMaxSegments key arrays looked up in one launch (the sharded table's
+// per-source inbox regions), each with its own output arrays.
+constexpr uint32_t kMaxSegments = 64;
+struct FindSegments {
+  const uint64_t* keys[kMaxSegments];
+  const uint32_t* out_index[kMaxSegments];
+  uint8_t* values[kMaxSegments];
+  bool* founds[kMaxSegments];
+  uint64_t* scores[kMaxSegments];
+};
+
+enum UpsertMode : int {
+  kModeInsertOrAssign = 0,
+  kModeFindOrInsert = 1,
+  kModeInsertAndEvict = 2
+};
+
 constexpr int kErrSpinTimeout = 1;
 constexpr int kErrBounds = 2;  // only raised by builds with HKV_CHECK_BOUNDS
+constexpr int kErrPeerOverflow = 4;  // a sharded batch overflowed a peer inbox
 
 // Murmur3 64-bit finalizer (reference utils.h:64-72).
 __host__ __device__ constexpr uint64_t murmur3(uint64_t k) {
@@ -158,6 +176,15 @@ __device__ __forceinline__ uint64_t cas_u64(uint64_t* p, uint64_t expect,
 }
 __device__ __forceinline__ uint64_t exch_u64(uint64_t* p, uint64_t v) {
   return atomicExch(reinterpret_cast<unsigned long long*>(p), v);
+}
+// Flags written and read across GPUs (peer memory over NVLink): system scope.
+__device__ __forceinline__ uint64_t ld_acquire_sys_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 // Exchange with acquire semantics at GPU scope (victim locking: swapping
 // LOCKED_KEY in returns the key that was there in the same round trip).

@@ -120,83 +120,129 @@ __device__ __forceinline__ uint32_t low_bit(M m) {
     return static_cast<uint32_t>(__ffs(static_cast<int>(m)) - 1);
 }
 
+// The find rule of the reference (find_utils.h:31-86) for one key on one
+// tile: the slot of the first digest hit holding the key in the group walk,
+// unless a digest-empty slot holding EMPTY_KEY comes before it; -1 if none.
+template <uint32_t W>
+__device__ __forceinline__ int find_probe(const TableView& t, const TileW<W>& tile,
+                                          uint64_t key, uint64_t& bkt) {
+  constexpr uint32_t kD = TileW<W>::kDigests;  // digests per lane
+  constexpr uint32_t kDV = kD / 16;            // 16-byte digest loads per lane
+  using M = typename std::conditional<(kD > 32), uint64_t, uint32_t>::type;
+  bkt = 0;
+  if (is_reserved(key)) return -1;
+  const Locate l = locate(t, key);
+  bkt = l.bkt;
+  const uint32_t lo = tile.lane * kD;
+  const uint64_t* bk = t.keys + l.bkt * kBucket;
+  const uint4* dl =
+      reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) + tile.lane * kDV;
+  M hits = 0, empt = 0;
+#pragma unroll
+  for (uint32_t j = 0; j < kDV; j++) {
+    const uint4 dv = __ldg(dl + j);
+    hits |= static_cast<M>(bytes_eq16(dv, l.d4)) << (16 * j);
+    empt |= static_cast<M>(bytes_eq16(dv, kEmptyDigest * 0x01010101u)) << (16 * j);
+  }
+  // digest hits holding the key, best = first in the reference's walk
+  uint32_t best = 0xFFFFFFFFu;
+  for (M h = hits; h; h &= h - 1) {
+    const uint32_t q = lo + low_bit(h);
+    if (__ldg(bk + q) == key) best = min(best, (hit_rank(q, l.pos) << 8) | q);
+  }
+#pragma unroll
+  for (int o = W / 2; o > 0; o >>= 1) best = min(best, tile.shfl_xor(best, o));
+  if (best == 0xFFFFFFFFu) return -1;
+  // an empty slot holding EMPTY_KEY ranked before the hit ends the walk
+  // (find_utils.h:58-66)
+  const uint32_t prank = best >> 8;
+  bool stop = false;
+  for (M e = empt; e; e &= e - 1) {
+    const uint32_t q = lo + low_bit(e);
+    if (empty_rank(q, l.pos) < prank && __ldg(bk + q) == kEmptyKey) stop = true;
+  }
+  return tile.ballot(stop) ? -1 : static_cast<int>(best & 0xFF);
+}
+
+// Writes one find result: flag, and for a hit the score and the value row.
+template <int VW, uint32_t W>
+__device__ __forceinline__ void find_output(const TableView& t, const TileW<W>& tile,
+                                            int p, uint64_t bkt, uint64_t o,
+                                            uint8_t* __restrict__ values,
+                                            bool* __restrict__ founds,
+                                            uint64_t* __restrict__ scores) {
+  using V = typename VecOf<VW>::T;
+  if (tile.lane == 0 && founds != nullptr) founds[o] = p >= 0;
+  if (p < 0) return;
+  if (scores != nullptr && tile.lane == 0) scores[o] = __ldg(t.scores + bkt * kBucket + p);
+  if (values != nullptr) {
+    const uint32_t vb = t.value_bytes;
+    V* dst = reinterpret_cast<V*>(values + o * vb);
+    const V* src = reinterpret_cast<const V*>(value_ptr(t, bkt, p));
+    for (uint32_t v = tile.lane; v < vb / VW; v += W) __stcs(dst + v, __ldg(src + v));
+  }
+}
+
 template <int VW>
 __global__ void __launch_bounds__(256, HKV_FIND_MIN_BLOCKS)
     find_kernel(TableView t, const uint64_t* __restrict__ keys,
                 uint8_t* __restrict__ values, bool* __restrict__ founds,
-                uint64_t* __restrict__ scores, uint64_t n) {
-  using V = typename VecOf<VW>::T;
-  using Tl = TileW<kFindTile>;
+                uint64_t* __restrict__ scores, uint64_t n,
+                const uint32_t* __restrict__ dn,
+                const uint32_t* __restrict__ out_index) {
+  // dn: optional device-side key count (at most n); out_index: optional
+  // output position of each key (results of key i go to out_index[i])
+  if (dn != nullptr) n = min(n, static_cast<uint64_t>(*dn));
   constexpr uint32_t W = kFindTile;
-  constexpr uint32_t kD = Tl::kDigests;  // digests per lane
-  constexpr uint32_t kDV = kD / 16;      // 16-byte digest loads per lane
-  using M = typename std::conditional<(kD > 32), uint64_t, uint32_t>::type;
-  const Tl tile;
+  const TileW<W> tile;
   const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / W);
-  const uint32_t vb = t.value_bytes;
-  const uint32_t nv = vb / VW;
-  const uint32_t lo = tile.lane * kD;
   uint64_t i = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / W;
   uint64_t next = i < n ? __ldg(keys + i) : 0;
   for (; i < n; i += ntiles) {
     const uint64_t key = next;
     if (i + ntiles < n) next = __ldg(keys + i + ntiles);
-    int p = -1;
-    uint64_t bkt = 0;
-    if (!is_reserved(key)) {
-      const Locate l = locate(t, key);
-      bkt = l.bkt;
-      const uint64_t* bk = t.keys + l.bkt * kBucket;
-      const uint4* dl =
-          reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) + tile.lane * kDV;
-      M hits = 0, empt = 0;
-#pragma unroll
-      for (uint32_t j = 0; j < kDV; j++) {
-        const uint4 dv = __ldg(dl + j);
-        hits |= static_cast<M>(bytes_eq16(dv, l.d4)) << (16 * j);
-        empt |= static_cast<M>(bytes_eq16(dv, kEmptyDigest * 0x01010101u)) << (16 * j);
-      }
-      // digest hits holding the key, best = first in the reference's walk
-      uint32_t best = 0xFFFFFFFFu;
-      for (M h = hits; h; h &= h - 1) {
-        const uint32_t q = lo + low_bit(h);
-        if (__ldg(bk + q) == key) best = min(best, (hit_rank(q, l.pos) << 8) | q);
-      }
-#pragma unroll
-      for (int o = W / 2; o > 0; o >>= 1) best = min(best, tile.shfl_xor(best, o));
-      if (best != 0xFFFFFFFFu) {
-        // an empty slot holding EMPTY_KEY ranked before the hit ends the
-        // walk (find_utils.h:58-66)
-        const uint32_t prank = best >> 8;
-        bool stop = false;
-        for (M e = empt; e; e &= e - 1) {
-          const uint32_t q = lo + low_bit(e);
-          if (empty_rank(q, l.pos) < prank && __ldg(bk + q) == kEmptyKey) stop = true;
-        }
-        if (!tile.ballot(stop)) p = static_cast<int>(best & 0xFF);
-      }
-    }
-    if (tile.lane == 0 && founds != nullptr) founds[i] = p >= 0;
-    if (p >= 0) {
-      if (scores != nullptr && tile.lane == 0)
-        scores[i] = __ldg(t.scores + bkt * kBucket + p);
-      if (values != nullptr) {
-        V* dst = reinterpret_cast<V*>(values + i * vb);
-        const V* src = reinterpret_cast<const V*>(value_ptr(t, bkt, p));
-        for (uint32_t v = tile.lane; v < nv; v += W) __stcs(dst + v, __ldg(src + v));
-      }
-    }
+    uint64_t bkt;
+    const int p = find_probe(t, tile, key, bkt);
+    const uint64_t o = out_index != nullptr ? __ldg(out_index + i) : i;
+    find_output<VW>(t, tile, p, bkt, o, values, founds, scores);
+  }
+}
+
+// find over several key arrays at once (segment s has counts[s] keys, at
+// most `bound`): the tiles walk an interleaved index v -> (segment v % nseg,
+// key v / nseg), so every segment is in flight at the same time.
+template <int VW>
+__global__ void __launch_bounds__(256, HKV_FIND_MIN_BLOCKS)
+    find_segments_kernel(TableView t, FindSegments seg, uint32_t nseg,
+                         const uint32_t* __restrict__ counts, uint64_t bound) {
+  constexpr uint32_t W = kFindTile;
+  __shared__ uint32_t cnt[kMaxSegments];
+  __shared__ uint32_t cmax;
+  if (threadIdx.x == 0) cmax = 0;
+  __syncthreads();
+  for (uint32_t k = threadIdx.x; k < nseg; k += blockDim.x) {
+    cnt[k] = static_cast<uint32_t>(min(static_cast<uint64_t>(counts[k]), bound));
+    atomicMax(&cmax, cnt[k]);
+  }
+  __syncthreads();
+  const TileW<W> tile;
+  const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / W);
+  const uint64_t total = uint64_t{cmax} * nseg;
+  for (uint64_t v = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / W; v < total;
+       v += ntiles) {
+    const uint32_t k = static_cast<uint32_t>(v % nseg);
+    const uint64_t j = v / nseg;
+    if (j >= cnt[k]) continue;
+    uint64_t bkt;
+    const int p = find_probe(t, tile, __ldg(seg.keys[k] + j), bkt);
+    const uint64_t o = seg.out_index[k] != nullptr ? __ldg(seg.out_index[k] + j) : j;
+    find_output<VW>(t, tile, p, bkt, o, seg.values[k], seg.founds[k], seg.scores[k]);
   }
 }
 
 // ============================================================================
 // Upsert family: insert_or_assign, find_or_insert, insert_and_evict
 // ============================================================================
-enum UpsertMode : int {
-  kModeInsertOrAssign = 0,
-  kModeFindOrInsert = 1,
-  kModeInsertAndEvict = 2
-};
 
 struct UpsertArgs {
   const uint64_t* keys;

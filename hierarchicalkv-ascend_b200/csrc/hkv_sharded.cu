@@ -154,12 +154,259 @@ __global__ void route_unpack_kernel(int mode, const uint32_t* __restrict__ uid_o
 
 uint64_t ceil_div(uint64_t a, uint64_t b) { return (a + b - 1) / b; }
 
+// ============================================================================
+// Peer-memory transport. Every rank exposes one "window" of device memory to
+// the others (CUDA IPC over NVLink): an inbox with one region of max_batch
+// entries per source rank, an outbox of max_batch results, and two flag rows.
+// A call is three steps per rank, with no host synchronisation:
+//   route   the requester writes each key (+ score, + value row, + its own
+//           index) straight into the owner's inbox region for this source,
+//           then the last block publishes (epoch << 32 | count) in the
+//           owner's arrive[source] flag;
+//   serve   the owner waits for all arrive flags of this epoch, runs the
+//           table kernel on each source region (find writes its results
+//           straight into the requester's outbox through out_index), and
+//           sets done[owner] = epoch in every requester's window;
+//   finish  the requester waits for all done flags, then copies its outbox
+//           into the caller's buffers.
+// A requester's next call starts only after its finish, which waited for
+// every owner to finish serving this call, so a single inbox suffices. All
+// waits are bounded (kSpinLimitNs): a rank that never arrives makes the
+// others give up, flag kErrSpinTimeout and treat its region as empty.
+// ============================================================================
+struct WinLayout {
+  uint64_t arrive, done;                        // kMaxWorld flags, 64 B apart
+  uint64_t in_keys, in_ref, in_scores, in_rows;  // world regions of M
+  uint64_t out_rows, out_flag, out_scores;      // M entries
+  uint64_t bytes;
+  uint64_t M;
+  uint32_t vb;
+};
+
+struct PeerBases {
+  uint8_t* base[kMaxWorld];
+};
+
+WinLayout make_layout(uint32_t world, uint64_t M, uint32_t vb) {
+  auto up = [](uint64_t x) { return (x + 255) & ~uint64_t{255}; };
+  WinLayout l{};
+  uint64_t o = 0;
+  l.arrive = o;
+  o = up(o + kMaxWorld * 64);
+  l.done = o;
+  o = up(o + kMaxWorld * 64);
+  const uint64_t R = uint64_t{world} * M;
+  l.in_keys = o;
+  o = up(o + R * 8);
+  l.in_ref = o;
+  o = up(o + R * 4);
+  l.in_scores = o;
+  o = up(o + R * 8);
+  l.in_rows = o;
+  o = up(o + R * vb);
+  l.out_rows = o;
+  o = up(o + M * vb);
+  l.out_flag = o;
+  o = up(o + M);
+  l.out_scores = o;
+  o = up(o + M * 8);
+  l.bytes = o;
+  l.M = M;
+  l.vb = vb;
+  return l;
+}
+
+__device__ __forceinline__ uint64_t* flag_at(uint8_t* base, uint64_t off,
+                                             uint32_t i) {
+  return reinterpret_cast<uint64_t*>(base + off + uint64_t{i} * 64);
+}
+
+// route: requester -> owners' inboxes. `keys` are the batch keys (find) or
+// the merged representatives (insert-like calls, count *dm).
+template <int VW>
+__global__ void __launch_bounds__(256)
+    p2p_route_kernel(const uint64_t* __restrict__ keys,
+                     const uint64_t* __restrict__ scores,
+                     const uint8_t* __restrict__ rows,
+                     const uint32_t* __restrict__ row_of,
+                     const uint32_t* __restrict__ dm, uint64_t n,
+                     uint32_t world, uint32_t self, PeerBases peers,
+                     WinLayout lay, uint32_t* __restrict__ counters,
+                     uint64_t epoch, int* __restrict__ err) {
+  __shared__ uint32_t cnt[kMaxWorld];
+  __shared__ uint32_t base[kMaxWorld];
+  __shared__ int last;
+  const Tile tile;
+  const uint64_t m = dm != nullptr ? min(n, static_cast<uint64_t>(*dm)) : n;
+  const uint32_t per_block = blockDim.x / kTile;
+  const uint32_t vb = lay.vb;
+  for (uint64_t b0 = uint64_t{blockIdx.x} * per_block; b0 < m;
+       b0 += uint64_t{gridDim.x} * per_block) {
+    for (uint32_t w = threadIdx.x; w < world; w += blockDim.x) cnt[w] = 0;
+    __syncthreads();
+    const uint64_t u = b0 + threadIdx.x / kTile;
+    uint32_t d = 0, r = 0;
+    uint64_t key = 0;
+    if (u < m) {
+      key = keys[u];
+      d = owner_of(key, world);
+      if (tile.lane == 0) r = atomicAdd(&cnt[d], 1u);
+    }
+    r = tile.shfl(r, 0);
+    __syncthreads();
+    for (uint32_t w = threadIdx.x; w < world; w += blockDim.x)
+      base[w] = cnt[w] ? atomicAdd(&counters[w], cnt[w]) : 0u;
+    __syncthreads();
+    if (u < m) {
+      const uint64_t pos = uint64_t{base[d]} + r;
+      if (pos < lay.M) {
+        uint8_t* pb = peers.base[d];
+        const uint64_t slot = uint64_t{self} * lay.M + pos;
+        if (tile.lane == 0) {
+          reinterpret_cast<uint64_t*>(pb + lay.in_keys)[slot] = key;
+          reinterpret_cast<uint32_t*>(pb + lay.in_ref)[slot] = static_cast<uint32_t>(u);
+          if (scores != nullptr)
+            reinterpret_cast<uint64_t*>(pb + lay.in_scores)[slot] = scores[u];
+        }
+        if (rows != nullptr)
+          copy_row<VW>(pb + lay.in_rows + slot * vb,
+                       rows + uint64_t{row_of != nullptr ? row_of[u]
+                                                         : static_cast<uint32_t>(u)} * vb,
+                       vb, tile.lane, kTile);
+      } else if (tile.lane == 0) {
+        atomicOr(err, kErrPeerOverflow);
+      }
+    }
+    __syncthreads();
+  }
+  // the last block to finish publishes the counts (every block's stores are
+  // fenced at system scope before it is counted)
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(&counters[world], 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (last) {
+    __threadfence_system();
+    for (uint32_t w = threadIdx.x; w < world; w += blockDim.x) {
+      const uint32_t c = min(atomicAdd(&counters[w], 0u), static_cast<uint32_t>(lay.M));
+      st_release_sys_u64(flag_at(peers.base[w], lay.arrive, self), (epoch << 32) | c);
+      counters[w] = 0;
+    }
+    if (threadIdx.x == 0) counters[world] = 0;
+  }
+}
+
+// Waits (bounded) until flag_i holds epoch in its high half for every i <
+// world; writes the low halves to counts (0 for a flag that never came).
+__device__ void wait_flags(uint8_t* base, uint64_t off, uint32_t world,
+                           uint64_t epoch, bool counted, uint32_t* counts,
+                           int* err, int site) {
+  for (uint32_t w = threadIdx.x; w < world; w += blockDim.x) {
+    const uint64_t* f = flag_at(base, off, w);
+    const uint64_t t0 = global_timer_ns();
+    uint64_t v = ld_acquire_sys_u64(f);
+    bool ok = true;
+    while ((counted ? (v >> 32) : v) != epoch) {
+      if (global_timer_ns() - t0 > kSpinLimitNs) {
+        ok = false;
+        atomicOr(err, kErrSpinTimeout);
+        atomicExch(err + 1, site);
+        break;
+      }
+      __nanosleep(256);
+      v = ld_acquire_sys_u64(f);
+    }
+    if (counts != nullptr) counts[w] = ok && counted ? static_cast<uint32_t>(v) : 0u;
+  }
+}
+
+__global__ void p2p_wait_arrive_kernel(uint8_t* self_base, WinLayout lay,
+                                       uint32_t world, uint64_t epoch,
+                                       uint32_t* counts, int* err) {
+  wait_flags(self_base, lay.arrive, world, epoch, true, counts, err, 301);
+}
+
+// serve, find_or_insert: result rows and Occupy codes back to the requesters
+template <int VW>
+__global__ void __launch_bounds__(256)
+    p2p_return_rows_kernel(uint8_t* self_base, PeerBases peers, WinLayout lay,
+                           uint32_t world, const uint32_t* __restrict__ counts,
+                           const uint8_t* __restrict__ status) {
+  const Tile tile;
+  const uint32_t vb = lay.vb;
+  const uint64_t ntiles = uint64_t{gridDim.x} * (blockDim.x / kTile);
+  const uint64_t t0 = (uint64_t{blockIdx.x} * blockDim.x + threadIdx.x) / kTile;
+  const uint8_t* in_rows = self_base + lay.in_rows;
+  const uint32_t* in_ref = reinterpret_cast<const uint32_t*>(self_base + lay.in_ref);
+  for (uint32_t src = 0; src < world; src++) {
+    const uint64_t c = counts[src];
+    uint8_t* pb = peers.base[src];
+    for (uint64_t j = t0; j < c; j += ntiles) {
+      const uint64_t slot = uint64_t{src} * lay.M + j;
+      const uint32_t ref = in_ref[slot];
+      if (tile.lane == 0) (pb + lay.out_flag)[ref] = status[slot];
+      copy_row<VW>(pb + lay.out_rows + uint64_t{ref} * vb, in_rows + slot * vb, vb,
+                   tile.lane, kTile);
+    }
+  }
+}
+
+// serve: every result of this epoch is out; tell each requester
+__global__ void p2p_signal_done_kernel(PeerBases peers, WinLayout lay,
+                                       uint32_t world, uint32_t self,
+                                       uint64_t epoch) {
+  __threadfence_system();
+  for (uint32_t w = threadIdx.x; w < world; w += blockDim.x)
+    st_release_sys_u64(flag_at(peers.base[w], lay.done, self), epoch);
+}
+
+// finish: wait for every owner, then copy the outbox to the caller.
+// mode 0: find (rows, flags, scores of found keys, per input);
+// mode 1: find_or_insert (rows of found or inserted representatives, to
+// every occurrence through uid_of); mode 2: insert_or_assign (wait only).
+template <int VW>
+__global__ void __launch_bounds__(256)
+    p2p_finish_kernel(int mode, uint8_t* self_base, WinLayout lay, uint32_t world,
+                      uint64_t epoch, int* err, uint64_t n,
+                      const uint32_t* __restrict__ uid_of,
+                      uint8_t* __restrict__ values, bool* __restrict__ founds,
+                      uint64_t* __restrict__ scores) {
+  wait_flags(self_base, lay.done, world, epoch, false, nullptr, err, 302);
+  __syncthreads();
+  if (mode == 2) return;
+  const Tile tile;
+  const uint32_t vb = lay.vb;
+  const uint64_t ntiles = uint64_t{gridDim.x} * (blockDim.x / kTile);
+  const uint8_t* flags = self_base + lay.out_flag;
+  const uint8_t* rows = self_base + lay.out_rows;
+  const uint64_t* osc = reinterpret_cast<const uint64_t*>(self_base + lay.out_scores);
+  for (uint64_t i = (uint64_t{blockIdx.x} * blockDim.x + threadIdx.x) / kTile; i < n;
+       i += ntiles) {
+    const uint32_t u = uid_of != nullptr ? uid_of[i] : static_cast<uint32_t>(i);
+    bool ok = false;
+    if (u != 0xFFFFFFFFu) {
+      const uint8_t f = __ldcg(flags + u);
+      ok = mode == 0 ? f != 0 : (f != kRefused && f != kIllegal && f != kTimedOut);
+    }
+    if (tile.lane == 0) {
+      if (founds != nullptr) founds[i] = ok;
+      if (ok && scores != nullptr) scores[i] = __ldcg(osc + u);
+    }
+    if (ok && values != nullptr) {
+      using V = typename VecOf<VW>::T;
+      const V* sp = reinterpret_cast<const V*>(rows + uint64_t{u} * vb);
+      V* dp = reinterpret_cast<V*>(values + i * vb);
+      for (uint32_t v = tile.lane; v < vb / VW; v += kTile) dp[v] = __ldcg(sp + v);
+    }
+  }
+}
+
 }  // namespace
 
 class ShardedImpl {
  public:
   ShardedImpl(const hkv_options& o, int key_type, int value_type, int strategy,
-              const uint8_t id[128], int rank, int world)
+              const uint8_t id[128], int rank, int world, uint64_t max_batch)
       : rank_(rank), world_(world) {
     HKV_REQUIRE(world >= 1 && world <= kMaxWorld, HKV_ERR_INVALID,
                 "world_size must be in [1, 64]");
@@ -175,18 +422,34 @@ class ShardedImpl {
     CUDA_TRY(cudaMalloc(&d_counts_, 2 * kMaxWorld * sizeof(uint32_t)));
     CUDA_TRY(cudaDeviceGetAttribute(&sm_count_, cudaDevAttrMultiProcessorCount,
                                     local_->device()));
+    if (max_batch > 0 && world > 1 && local_->at_max_capacity())
+      setup_p2p(max_batch);
   }
   ~ShardedImpl() {
+    if (p2p_) {
+      // every rank is here: no peer writes into a window after this barrier
+      cudaStream_t s = nullptr;
+      ncclAllReduce(d_counts_, d_counts_ + kMaxWorld, 1, ncclUint32, ncclSum,
+                    comm_, s);
+      cudaStreamSynchronize(s);
+      for (int p = 0; p < world_; p++)
+        if (p != rank_ && peers_.base[p]) cudaIpcCloseMemHandle(peers_.base[p]);
+      cudaFree(win_);
+      cudaFree(d_route_counters_);
+      cudaFree(d_status_);
+    }
     if (comm_) ncclCommDestroy(comm_);
     delete local_;
     cudaFree(d_counts_);
     cudaFreeHost(h_counts_);
   }
+  bool peer_transport() const { return p2p_; }
   TableImpl* local() { return local_; }
 
   // kind: 0 find, 1 find_or_insert, 2 insert_or_assign
   void run(int kind, size_t n, const uint64_t* keys, uint8_t* values,
-           bool* founds, uint64_t* scores, cudaStream_t s) {
+           bool* founds, uint64_t* scores, cudaStream_t s, bool unique) {
+    if (p2p_) return run_p2p(kind, n, keys, values, founds, scores, s, unique);
     const uint32_t vb = local_->value_bytes();
     const int st = local_->strategy();
     Workspace ws(s, local_->pool());
@@ -199,11 +462,12 @@ class ShardedImpl {
     // 1. merge duplicates (scores are inputs for insert-like calls only)
     const uint64_t* in_scores = kind == 0 ? nullptr : scores;
     DedupResult d;
-    if (kind == 0) {
-      // lookups are read-only: every occurrence travels as it is
+    if (kind == 0 || unique) {
+      // lookups are read-only, and a batch of distinct keys needs no merge:
+      // every key travels as it is
       d.ukeys = const_cast<uint64_t*>(keys);
       d.rep_first = d.rep_last = d.uid_of = nullptr;
-      d.uscores = nullptr;
+      d.uscores = const_cast<uint64_t*>(in_scores);
       d.dm = nullptr;
     } else if (n > 0) {
       d = dedup_batch(n, keys, in_scores, st, ws, s, sm_count_,
@@ -317,6 +581,195 @@ class ShardedImpl {
     CUDA_TRY(cudaGetLastError());
   }
 
+  // Collective: window allocation, IPC handle exchange over NCCL, peer
+  // mapping. Any failure on any rank leaves every rank on the NCCL path.
+  void setup_p2p(uint64_t max_batch) {
+    const uint32_t vb = local_->value_bytes();
+    lay_ = make_layout(world_, max_batch, vb);
+    cudaStream_t s = nullptr;
+    struct Rec {
+      cudaIpcMemHandle_t h;
+      int ok;
+    };
+    Rec mine{};
+    mine.ok = cudaMalloc(&win_, lay_.bytes) == cudaSuccess;
+    if (!mine.ok) {
+      cudaGetLastError();
+      win_ = nullptr;
+    }
+    if (mine.ok)
+      mine.ok = cudaMemset(win_, 0, lay_.in_keys) == cudaSuccess &&
+                cudaIpcGetMemHandle(&mine.h, win_) == cudaSuccess;
+    cudaGetLastError();
+    std::vector<Rec> all(world_);
+    exchange_bytes(&mine, all.data(), sizeof(Rec), s);
+    int ok = 1;
+    for (const Rec& r : all) ok &= r.ok;
+    std::memset(&peers_, 0, sizeof peers_);
+    if (ok) {
+      for (int p = 0; p < world_; p++) {
+        if (p == rank_) {
+          peers_.base[p] = win_;
+          continue;
+        }
+        void* ptr = nullptr;
+        if (cudaIpcOpenMemHandle(&ptr, all[p].h, cudaIpcMemLazyEnablePeerAccess) !=
+            cudaSuccess) {
+          cudaGetLastError();
+          ok = 0;
+          break;
+        }
+        peers_.base[p] = static_cast<uint8_t*>(ptr);
+      }
+    }
+    Rec again{};
+    again.ok = ok;
+    exchange_bytes(&again, all.data(), sizeof(Rec), s);
+    for (const Rec& r : all) ok &= r.ok;
+    if (ok) {
+      ok = cudaMalloc(&d_route_counters_, (kMaxWorld + 1) * sizeof(uint32_t)) ==
+               cudaSuccess &&
+           cudaMemset(d_route_counters_, 0, (kMaxWorld + 1) * sizeof(uint32_t)) ==
+               cudaSuccess &&
+           cudaMalloc(&d_status_, uint64_t{static_cast<uint32_t>(world_)} * max_batch) ==
+               cudaSuccess;
+      cudaGetLastError();
+      again.ok = ok;
+      exchange_bytes(&again, all.data(), sizeof(Rec), s);
+      for (const Rec& r : all) ok &= r.ok;
+    }
+    if (!ok) {
+      for (int p = 0; p < world_; p++)
+        if (p != rank_ && peers_.base[p]) cudaIpcCloseMemHandle(peers_.base[p]);
+      std::memset(&peers_, 0, sizeof peers_);
+      cudaFree(win_);
+      cudaFree(d_route_counters_);
+      cudaFree(d_status_);
+      win_ = nullptr;
+      d_route_counters_ = nullptr;
+      d_status_ = nullptr;
+      return;
+    }
+    max_batch_ = max_batch;
+    p2p_ = true;
+  }
+
+  // all-gather of `bytes` host bytes per rank over NCCL (setup only)
+  void exchange_bytes(const void* mine, void* all, size_t bytes, cudaStream_t s) {
+    uint8_t* d = nullptr;
+    CUDA_TRY(cudaMalloc(&d, bytes * (world_ + 1)));
+    CUDA_TRY(cudaMemcpy(d, mine, bytes, cudaMemcpyHostToDevice));
+    NCCL_TRY(ncclAllGather(d, d + bytes, bytes, ncclUint8, comm_, s));
+    CUDA_TRY(cudaStreamSynchronize(s));
+    CUDA_TRY(cudaMemcpy(all, d + bytes, bytes * world_, cudaMemcpyDeviceToHost));
+    CUDA_TRY(cudaFree(d));
+  }
+
+  // kind: 0 find, 1 find_or_insert, 2 insert_or_assign (peer transport)
+  void run_p2p(int kind, size_t n, const uint64_t* keys, uint8_t* values,
+               bool* founds, uint64_t* scores, cudaStream_t s, bool unique) {
+    HKV_REQUIRE(n <= max_batch_, HKV_ERR_INVALID,
+                "sharded batch larger than the table's max_batch");
+    const int st = local_->strategy();
+    if (kind != 0) local_->check_strategy(scores, false);
+    const bool send_scores =
+        kind != 0 && (st == kLfu || st == kEpochLfu || st == kCustomized);
+    const uint64_t M = max_batch_;
+    const uint32_t vb = lay_.vb;
+    int* err = local_->error_word();
+    epoch_++;
+    Workspace ws(s, local_->pool());
+    // 1. route (insert-like calls merge duplicates first)
+    const uint64_t* rkeys = keys;
+    const uint64_t* rscores = nullptr;
+    const uint32_t* row_of = nullptr;
+    const uint32_t* dm = nullptr;
+    const uint32_t* uid_of = nullptr;
+    uint64_t nr = n;
+    if (kind != 0 && unique) {
+      rscores = send_scores ? scores : nullptr;
+    } else if (kind != 0 && n > 0) {
+      const DedupResult d = dedup_batch(n, keys, send_scores ? scores : nullptr,
+                                        st, ws, s, sm_count_, err);
+      rkeys = d.ukeys;
+      rscores = d.uscores;
+      row_of = kind == 1 ? d.rep_first : d.rep_last;
+      dm = d.dm;
+      uid_of = d.uid_of;
+    }
+    if (kind == 0 || n == 0) nr = n;
+    const int vw = kind == 0 ? 16
+                             : local_->value_width({values, win_ + lay_.in_rows});
+    const int gr = static_cast<int>(std::max<uint64_t>(
+        1, std::min<uint64_t>(ceil_div(std::max<uint64_t>(nr, 1), 256 / kTile),
+                              sm_count_ * 8ull)));
+    SHARD_DISPATCH_VW(vw, p2p_route_kernel<VW><<<gr, 256, 0, counted(s)>>>(
+                              rkeys, rscores, kind == 0 ? nullptr : values, row_of,
+                              dm, nr, world_, rank_, peers_, lay_,
+                              d_route_counters_, epoch_, err));
+    CUDA_TRY(cudaGetLastError());
+    // 2. serve what the other ranks sent
+    uint32_t* counts = d_counts_;  // kMaxWorld entries, device
+    p2p_wait_arrive_kernel<<<1, kMaxWorld, 0, counted(s)>>>(win_, lay_, world_,
+                                                             epoch_, counts, err);
+    CUDA_TRY(cudaGetLastError());
+    const uint64_t* in_keys = reinterpret_cast<const uint64_t*>(win_ + lay_.in_keys);
+    const uint32_t* in_ref = reinterpret_cast<const uint32_t*>(win_ + lay_.in_ref);
+    uint64_t* in_scores = reinterpret_cast<uint64_t*>(win_ + lay_.in_scores);
+    if (kind == 0) {
+      // one launch over every source region: results go straight to the
+      // requesters' outboxes
+      FindSegments seg;
+      for (int src = 0; src < world_; src++) {
+        const uint64_t o = uint64_t{static_cast<uint32_t>(src)} * M;
+        uint8_t* pb = peers_.base[src];
+        seg.keys[src] = in_keys + o;
+        seg.out_index[src] = in_ref + o;
+        seg.values[src] = pb + lay_.out_rows;
+        seg.founds[src] = reinterpret_cast<bool*>(pb + lay_.out_flag);
+        seg.scores[src] = reinterpret_cast<uint64_t*>(pb + lay_.out_scores);
+      }
+      local_->find_segments(seg, static_cast<uint32_t>(world_), counts, M, s);
+    }
+    for (int src = 0; kind != 0 && src < world_; src++) {
+      const uint64_t o = uint64_t{static_cast<uint32_t>(src)} * M;
+      {
+        uint8_t* rows = win_ + lay_.in_rows + o * vb;
+        const uint64_t* sc = send_scores ? in_scores + o : nullptr;
+        if (kind == 1)
+          local_->upsert_counted(kModeFindOrInsert, M, counts + src, in_keys + o,
+                                 nullptr, rows, sc, d_status_ + o, s);
+        else
+          local_->upsert_counted(kModeInsertOrAssign, M, counts + src,
+                                 in_keys + o, rows, nullptr, sc, nullptr, s);
+      }
+    }
+    if (kind == 1) {
+      const int vwr = local_->value_width({win_ + lay_.in_rows});
+      const int g = static_cast<int>(std::min<uint64_t>(
+          ceil_div(M * kTile, 256), sm_count_ * 16ull));
+      SHARD_DISPATCH_VW(vwr, p2p_return_rows_kernel<VW><<<g, 256, 0, counted(s)>>>(
+                                 win_, peers_, lay_, world_, counts, d_status_));
+      CUDA_TRY(cudaGetLastError());
+    }
+    p2p_signal_done_kernel<<<1, kMaxWorld, 0, counted(s)>>>(peers_, lay_, world_,
+                                                             rank_, epoch_);
+    CUDA_TRY(cudaGetLastError());
+    // 3. finish: wait for every owner, then the outbox to the caller
+    const int vwf = kind == 1 ? local_->value_width({values, win_ + lay_.out_rows})
+                              : (values ? local_->value_width({values}) : 16);
+    const int gf = static_cast<int>(std::max<uint64_t>(
+        1, std::min<uint64_t>(ceil_div(std::max<uint64_t>(n, 1) * kTile, 256),
+                              sm_count_ * 16ull)));
+    SHARD_DISPATCH_VW(vwf, p2p_finish_kernel<VW><<<gf, 256, 0, counted(s)>>>(
+                               kind, win_, lay_, world_, epoch_, err, n,
+                               kind == 1 ? uid_of : nullptr,
+                               kind == 2 ? nullptr : values,
+                               kind == 0 ? founds : nullptr,
+                               kind == 0 ? scores : nullptr));
+    CUDA_TRY(cudaGetLastError());
+  }
+
   size_t size(cudaStream_t s) {
     const size_t local = local_->size(s);
     unsigned long long* d = nullptr;
@@ -337,6 +790,15 @@ class ShardedImpl {
   ncclComm_t comm_ = nullptr;
   uint32_t* d_counts_ = nullptr;
   uint32_t* h_counts_ = nullptr;
+  // peer-memory transport
+  bool p2p_ = false;
+  uint64_t max_batch_ = 0;
+  uint64_t epoch_ = 0;
+  WinLayout lay_{};
+  uint8_t* win_ = nullptr;
+  PeerBases peers_{};
+  uint32_t* d_route_counters_ = nullptr;
+  uint8_t* d_status_ = nullptr;
 };
 
 void set_last_error(const std::string& m);
@@ -381,14 +843,15 @@ int hkv_nccl_unique_id(uint8_t out[128]) {
 int hkv_sharded_create(const hkv_options* local_options, int key_type,
                        int value_type, int evict_strategy,
                        const uint8_t nccl_id[128], int rank, int world_size,
-                       hkv_sharded** out) {
+                       size_t max_batch, hkv_sharded** out) {
   HKV_API_BEGIN
   HKV_REQUIRE(local_options && nccl_id && out, HKV_ERR_INVALID, "null argument");
   *out = nullptr;
   auto* s = new hkv_sharded;
   try {
     s->impl = new hkvb::ShardedImpl(*local_options, key_type, value_type,
-                                    evict_strategy, nccl_id, rank, world_size);
+                                    evict_strategy, nccl_id, rank, world_size,
+                                    max_batch);
   } catch (...) {
     delete s;
     throw;
@@ -409,13 +872,22 @@ int hkv_sharded_destroy(hkv_sharded* s) {
 
 hkv_table* hkv_sharded_local(hkv_sharded* s) { return s ? &s->local : nullptr; }
 
+int hkv_sharded_transport(hkv_sharded* s, int* out) {
+  HKV_API_BEGIN
+  HKV_SHARDED(s);
+  HKV_REQUIRE(out != nullptr, HKV_ERR_INVALID, "null argument");
+  *out = S->peer_transport() ? HKV_TRANSPORT_PEER : HKV_TRANSPORT_NCCL;
+  HKV_API_END
+}
+
 int hkv_sharded_find_or_insert(hkv_sharded* s, size_t n, const void* keys,
                                void* values, const uint64_t* scores,
-                               void* stream) {
+                               void* stream, bool unique_key) {
   HKV_API_BEGIN
   HKV_SHARDED(s);
   S->run(1, n, static_cast<const uint64_t*>(keys), static_cast<uint8_t*>(values),
-         nullptr, const_cast<uint64_t*>(scores), static_cast<cudaStream_t>(stream));
+         nullptr, const_cast<uint64_t*>(scores), static_cast<cudaStream_t>(stream),
+         unique_key);
   HKV_API_END
 }
 
@@ -424,18 +896,19 @@ int hkv_sharded_find(hkv_sharded* s, size_t n, const void* keys, void* values,
   HKV_API_BEGIN
   HKV_SHARDED(s);
   S->run(0, n, static_cast<const uint64_t*>(keys), static_cast<uint8_t*>(values),
-         founds, scores, static_cast<cudaStream_t>(stream));
+         founds, scores, static_cast<cudaStream_t>(stream), false);
   HKV_API_END
 }
 
 int hkv_sharded_insert_or_assign(hkv_sharded* s, size_t n, const void* keys,
                                  const void* values, const uint64_t* scores,
-                                 void* stream) {
+                                 void* stream, bool unique_key) {
   HKV_API_BEGIN
   HKV_SHARDED(s);
   S->run(2, n, static_cast<const uint64_t*>(keys),
          const_cast<uint8_t*>(static_cast<const uint8_t*>(values)), nullptr,
-         const_cast<uint64_t*>(scores), static_cast<cudaStream_t>(stream));
+         const_cast<uint64_t*>(scores), static_cast<cudaStream_t>(stream),
+         unique_key);
   HKV_API_END
 }
 

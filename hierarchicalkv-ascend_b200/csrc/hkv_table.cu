@@ -409,7 +409,7 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
                        const uint64_t* scores, uint64_t* ev_keys,
                        uint8_t* ev_values, uint64_t* ev_scores,
                        uint64_t* d_counter, cudaStream_t s, bool unique,
-                       bool ignore, uint8_t* status) {
+                       bool ignore, uint8_t* status, const uint32_t* dn) {
   const int st = ignore ? kCustomized : strategy_;
   const TableView v = view();
   UpsertArgs a;
@@ -429,6 +429,7 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
     a.values_io = values_io;
     a.scores = scores;
     a.n = n;
+    a.dn = dn;
     const int vw = value_width({rows, ev_values});
     const int grid = upsert_grid(n);
     DISPATCH_STRATEGY(st, DISPATCH_VW(vw, {
@@ -647,8 +648,43 @@ void TableImpl::find(size_t n, const uint64_t* keys, uint8_t* values,
   const TableView v = view();
   const int vw = value_width({values});
   DISPATCH_VW(vw, find_kernel<VW><<<find_grid(n), 256, 0, counted(s)>>>(
-                      v, keys, values, founds, scores, n));
+                      v, keys, values, founds, scores, n, nullptr, nullptr));
   CUDA_TRY(cudaGetLastError());
+}
+
+void TableImpl::find_indexed(size_t n_bound, const uint32_t* dn,
+                             const uint64_t* keys, uint8_t* values, bool* founds,
+                             uint64_t* scores, const uint32_t* out_index,
+                             cudaStream_t s) {
+  if (n_bound == 0) return;
+  const TableView v = view();
+  const int vw = values ? value_width({values}) : 16;
+  DISPATCH_VW(vw, find_kernel<VW><<<find_grid(n_bound), 256, 0, counted(s)>>>(
+                      v, keys, values, founds, scores, n_bound, dn, out_index));
+  CUDA_TRY(cudaGetLastError());
+}
+
+void TableImpl::find_segments(const FindSegments& seg, uint32_t nseg,
+                              const uint32_t* counts, uint64_t bound,
+                              cudaStream_t s) {
+  HKV_REQUIRE(nseg >= 1 && nseg <= kMaxSegments, HKV_ERR_INVALID, "bad segment count");
+  if (bound == 0) return;
+  int vw = 16;
+  for (uint32_t k = 0; k < nseg; k++)
+    if (seg.values[k]) vw = std::min(vw, value_width({seg.values[k]}));
+  const TableView v = view();
+  DISPATCH_VW(vw, find_segments_kernel<VW><<<find_grid(bound * nseg), 256, 0, counted(s)>>>(
+                      v, seg, nseg, counts, bound));
+  CUDA_TRY(cudaGetLastError());
+}
+
+void TableImpl::upsert_counted(int mode, size_t n_bound, const uint32_t* dn,
+                               const uint64_t* keys, const uint8_t* values_in,
+                               uint8_t* values_io, const uint64_t* scores,
+                               uint8_t* status, cudaStream_t s) {
+  if (n_bound == 0) return;
+  upsert(mode, n_bound, keys, values_in, values_io, scores, nullptr, nullptr,
+         nullptr, nullptr, s, true, false, status, dn);
 }
 
 void TableImpl::contains(size_t n, const uint64_t* keys, bool* founds,
@@ -657,7 +693,7 @@ void TableImpl::contains(size_t n, const uint64_t* keys, bool* founds,
   if (keys == nullptr || founds == nullptr) return;
   const TableView v = view();
   find_kernel<16><<<find_grid(n), 256, 0, counted(s)>>>(v, keys, nullptr, founds,
-                                               nullptr, n);
+                                               nullptr, n, nullptr, nullptr);
   CUDA_TRY(cudaGetLastError());
 }
 
@@ -751,6 +787,10 @@ void TableImpl::check_device_error(cudaStream_t s) {
     if (e[0] & kErrBounds)
       throw HkvError{HKV_ERR_RUNTIME, "device index check failed at site " +
                                           std::to_string(e[1])};
+    if (e[0] & kErrPeerOverflow)
+      throw HkvError{HKV_ERR_INVALID,
+                     "a sharded call sent more keys to one shard than its "
+                     "receive area holds (every rank must keep n <= max_batch)"};
     throw HkvError{HKV_ERR_TIMEOUT,
                    "a device lock wait exceeded its time limit (site " +
                        std::to_string(e[1]) +

@@ -152,12 +152,13 @@ SIGNATURES = {
     "hkv_nccl_unique_id": (ctypes.c_int, [_P]),
     "hkv_sharded_create": (ctypes.c_int, [ctypes.POINTER(_Options), ctypes.c_int,
                                           ctypes.c_int, ctypes.c_int, _P, ctypes.c_int,
-                                          ctypes.c_int, ctypes.POINTER(_P)]),
+                                          ctypes.c_int, _SZ, ctypes.POINTER(_P)]),
+    "hkv_sharded_transport": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_int)]),
     "hkv_sharded_destroy": (ctypes.c_int, [_P]),
     "hkv_sharded_local": (_P, [_P]),
-    "hkv_sharded_find_or_insert": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P]),
+    "hkv_sharded_find_or_insert": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _B]),
     "hkv_sharded_find": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _P]),
-    "hkv_sharded_insert_or_assign": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P]),
+    "hkv_sharded_insert_or_assign": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _B]),
     "hkv_sharded_size": (ctypes.c_int, [_P, _P, ctypes.POINTER(_SZ)]),
 }
 
@@ -438,18 +439,30 @@ class ShardedHashTable:
     """One table shard per rank; collective calls route keys to their owner
     over NCCL all-to-all (no reference counterpart)."""
 
+    TRANSPORTS = {0: "nccl", 1: "peer"}
+
     def __init__(self, options: HashTableOptions, rank: int, world_size: int,
                  nccl_id: bytes, evict_strategy: int = EvictStrategy.kLru,
-                 key_dtype: str = "uint64", value_dtype: str = "float32"):
+                 key_dtype: str = "uint64", value_dtype: str = "float32",
+                 max_batch: int = 1 << 20):
+        """Collective. max_batch > 0 asks for the peer-memory transport
+        (every call's n on every rank at most max_batch); 0 selects NCCL."""
         h = ctypes.c_void_p()
         o = options._c()
         buf = ctypes.create_string_buffer(bytes(nccl_id), 128)
         _check(lib().hkv_sharded_create(ctypes.byref(o),
                                         KEY_I64 if key_dtype == "int64" else KEY_U64,
                                         VALUE_TYPES[value_dtype], evict_strategy,
-                                        buf, rank, world_size, ctypes.byref(h)))
+                                        buf, rank, world_size, max_batch,
+                                        ctypes.byref(h)))
         self._h = h.value
         self.rank, self.world_size = rank, world_size
+
+    @property
+    def transport(self) -> str:
+        out = ctypes.c_int(0)
+        _check(lib().hkv_sharded_transport(self._h, ctypes.byref(out)))
+        return self.TRANSPORTS[out.value]
 
     @staticmethod
     def unique_id() -> bytes:
@@ -468,17 +481,21 @@ class ShardedHashTable:
         except Exception:
             pass
 
-    def find_or_insert(self, n, keys, values, scores=None, stream=None):
+    def find_or_insert(self, n, keys, values, scores=None, stream=None,
+                       unique_key=False):
         _check(lib().hkv_sharded_find_or_insert(self._h, n, _ptr(keys), _ptr(values),
-                                                _ptr(scores), _stream(stream)))
+                                                _ptr(scores), _stream(stream),
+                                                unique_key))
 
     def find(self, n, keys, values, founds, scores=None, stream=None):
         _check(lib().hkv_sharded_find(self._h, n, _ptr(keys), _ptr(values),
                                       _ptr(founds), _ptr(scores), _stream(stream)))
 
-    def insert_or_assign(self, n, keys, values, scores=None, stream=None):
+    def insert_or_assign(self, n, keys, values, scores=None, stream=None,
+                         unique_key=False):
         _check(lib().hkv_sharded_insert_or_assign(self._h, n, _ptr(keys), _ptr(values),
-                                                  _ptr(scores), _stream(stream)))
+                                                  _ptr(scores), _stream(stream),
+                                                  unique_key))
 
     def size(self, stream=None) -> int:
         out = ctypes.c_size_t(0)

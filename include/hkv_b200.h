@@ -220,30 +220,50 @@ int hkv_debug_set_state(hkv_table* table, const uint64_t* keys,
 
 /* ---- sharded table (no reference counterpart: the reference is one device)
  * One table shard per GPU; keys are routed to shard owner(key) =
- * (Murmur3(key) >> 40) % world_size and exchanged with NCCL all-to-all. ---------- */
+ * (Murmur3(key) >> 40) % world_size. Two transports move the keys and rows:
+ *  - peer memory (HKV_TRANSPORT_PEER): each rank maps the others' receive
+ *    windows over NVLink (CUDA IPC); requesters write keys straight into the
+ *    owner's window, owners write results straight back, device flags order
+ *    the steps, no host synchronisation. Used when max_batch > 0, the shards
+ *    never grow (init_capacity * 2 > max_capacity) and every rank could map
+ *    every peer; each rank's window holds world_size * max_batch entries.
+ *  - NCCL grouped send/recv (HKV_TRANSPORT_NCCL) otherwise, with one host
+ *    synchronisation per call to size the receive buffers. ---------------- */
 typedef struct hkv_sharded hkv_sharded;
+
+typedef enum { HKV_TRANSPORT_NCCL = 0, HKV_TRANSPORT_PEER = 1 } hkv_transport;
 
 /* NCCL unique id (128 bytes) for rank 0 to broadcast to the others. */
 int hkv_nccl_unique_id(uint8_t out[128]);
 
+/* Collective. max_batch: the largest n any rank passes to one call of the
+ * peer transport (every rank must pass the same value; 0 selects NCCL). */
 int hkv_sharded_create(const hkv_options* local_options, int key_type,
                        int value_type, int evict_strategy,
                        const uint8_t nccl_id[128], int rank, int world_size,
-                       hkv_sharded** out);
+                       size_t max_batch, hkv_sharded** out);
 int hkv_sharded_destroy(hkv_sharded* s);
 hkv_table* hkv_sharded_local(hkv_sharded* s);
+/* The transport in use (hkv_transport). */
+int hkv_sharded_transport(hkv_sharded* s, int* out);
 
-/* Collective: every rank calls with its own batch (sizes may differ).
- * Semantics per key are those of the local op on the owner shard;
- * duplicate keys are merged as for unique_key=false. */
+/* Collective: every rank calls with its own batch (sizes may differ; with
+ * the peer transport each n must be at most max_batch). Semantics per key
+ * are those of the local op on the owner shard. unique_key = true promises
+ * that a rank's batch holds no repeated key (as the reference's unique_key);
+ * with false, repeated keys are merged as the local unique_key = false
+ * calls do. The same key sent by several ranks in one call is applied in
+ * rank order. A peer wait that runs out (a rank that never
+ * joins the call) is reported by hkv_check_device_error on the local table
+ * as HKV_ERR_TIMEOUT; the table is then in an undefined state. */
 int hkv_sharded_find_or_insert(hkv_sharded* s, size_t n, const void* keys,
                                void* values, const uint64_t* scores,
-                               void* stream);
+                               void* stream, bool unique_key);
 int hkv_sharded_find(hkv_sharded* s, size_t n, const void* keys, void* values,
                      bool* founds, uint64_t* scores, void* stream);
 int hkv_sharded_insert_or_assign(hkv_sharded* s, size_t n, const void* keys,
                                  const void* values, const uint64_t* scores,
-                                 void* stream);
+                                 void* stream, bool unique_key);
 /* Collective sum of the shard sizes. */
 int hkv_sharded_size(hkv_sharded* s, void* stream, size_t* out);
 

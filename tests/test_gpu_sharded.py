@@ -1,6 +1,7 @@
-"""The NCCL-sharded table on 2 GPUs (one process per GPU) gives what one
-table gives for the concatenation of the ranks' batches, and each shard
-holds only the keys it owns (gpu; skipped with fewer than 2 GPUs)."""
+"""The sharded table on 2 GPUs (one process per GPU), over both transports
+(peer memory and NCCL), gives what one table gives for the concatenation of
+the ranks' batches, and each shard holds only the keys it owns (gpu; skipped
+with fewer than 2 GPUs)."""
 import os
 import socket
 
@@ -23,7 +24,18 @@ def _free_port():
     return p
 
 
-def _rank(rank, world, port, outdir):
+def _unique_batch(world, rank):
+    rng = np.random.default_rng(500)
+    pool = np.unique(rng.integers(1, 1 << 62, 2500, dtype=np.uint64))
+    out = []
+    for r in range(world):
+        k = rng.choice(pool, 1500, replace=False).astype(np.uint64)
+        out.append((k, rng.standard_normal((1500, 4)).astype(np.float32),
+                    rng.integers(1, 17, 1500).astype(np.uint64)))
+    return out[rank]
+
+
+def _rank(rank, world, port, outdir, max_batch):
     import sys
     from datetime import timedelta
 
@@ -44,7 +56,9 @@ def _rank(rank, world, port, outdir):
     dist.broadcast_object_list(uid, src=0)
     opts = H.HashTableOptions(init_capacity=128 * 64, max_capacity=128 * 64,
                               max_hbm_for_vectors=1 << 30, dim=4, device_id=rank)
-    t = H.ShardedHashTable(opts, rank, world, uid[0], H.EvictStrategy.kLfu)
+    t = H.ShardedHashTable(opts, rank, world, uid[0], H.EvictStrategy.kLfu,
+                           max_batch=max_batch)
+    transport = t.transport
     results = []
     for step in range(3):
         k, v, s = _batches(world, step)[rank]
@@ -53,6 +67,12 @@ def _rank(rank, world, port, outdir):
                          torch.from_numpy(s.view(np.int64)).cuda())
         torch.cuda.synchronize()
         results.append(dv.cpu().numpy())
+    # unique-key insert_or_assign (distinct within a rank, shared across ranks)
+    uk, uv, us = _unique_batch(world, rank)
+    t.insert_or_assign(len(uk), torch.from_numpy(uk.view(np.int64)).cuda(),
+                       torch.from_numpy(uv).cuda(), torch.from_numpy(us.view(np.int64)).cuda(),
+                       unique_key=True)
+    torch.cuda.synchronize()
     # collective find of every rank's first batch
     k0, _, _ = _batches(world, 0)[rank]
     fv = torch.zeros((len(k0), 4), device="cuda")
@@ -67,25 +87,27 @@ def _rank(rank, world, port, outdir):
     np.savez(os.path.join(outdir, f"r{rank}.npz"), *results, keys=keys[live],
              scores=scores[live], fv=fv.cpu().numpy(), ff=ff.cpu().numpy(),
              fs=fs.cpu().numpy().view(np.uint64), total=np.array([total]),
-             own_ok=np.array([own_ok]))
+             own_ok=np.array([own_ok]), transport=np.array([transport]))
     dist.barrier()
     t.close()
     dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_sharded_two_gpus_match_one_table(tmp_path):
+@pytest.mark.parametrize("transport,max_batch", [("peer", 4096), ("nccl", 0)])
+def test_sharded_two_gpus_match_one_table(tmp_path, transport, max_batch):
     import sys
 
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import hkv_oracle as O
 
     world = 2
-    ctx = mp.start_processes(_rank, args=(world, _free_port(), str(tmp_path)),
+    ctx = mp.start_processes(_rank, args=(world, _free_port(), str(tmp_path), max_batch),
                              nprocs=world, join=False, start_method="spawn")
     while not ctx.join(timeout=180):
         pass
     res = [np.load(tmp_path / f"r{r}.npz") for r in range(world)]
+    assert all(str(r["transport"][0]) == transport for r in res)
     assert all(bool(r["own_ok"][0]) for r in res)
     one = O.OracleTable(128 * 128, 128 * 128, dim=4, strategy=O.LFU)
     for step in range(3):
@@ -98,6 +120,9 @@ def test_sharded_two_gpus_match_one_table(tmp_path):
             n = len(bs[r][0])
             assert (res[r][f"arr_{step}"] == out[off:off + n]).all(), (step, r)
             off += n
+    ub = [_unique_batch(world, r) for r in range(world)]
+    one.insert_or_assign(np.concatenate([b[0] for b in ub]), np.concatenate([b[1] for b in ub]),
+                         np.concatenate([b[2] for b in ub]))
     gk = np.concatenate([r["keys"] for r in res])
     gs = np.concatenate([r["scores"] for r in res])
     _, f, s = one.find(gk)
