@@ -228,13 +228,23 @@ __global__ void __launch_bounds__(256, HKV_FIND_MIN_BLOCKS)
   const TileW<W> tile;
   const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / W);
   const uint64_t total = uint64_t{cmax} * nseg;
-  for (uint64_t v = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / W; v < total;
-       v += ntiles) {
+  // keys may live in a peer's memory (and change between calls: no
+  // non-coherent cache); each tile loads its next key one iteration ahead
+  auto load_key = [&](uint64_t v) -> uint64_t {
     const uint32_t k = static_cast<uint32_t>(v % nseg);
     const uint64_t j = v / nseg;
+    return v < total && j < cnt[k] ? __ldcg(seg.keys[k] + j) : 0;
+  };
+  uint64_t v = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / W;
+  uint64_t next = load_key(v);
+  for (; v < total; v += ntiles) {
+    const uint32_t k = static_cast<uint32_t>(v % nseg);
+    const uint64_t j = v / nseg;
+    const uint64_t key = next;
+    next = load_key(v + ntiles);
     if (j >= cnt[k]) continue;
     uint64_t bkt;
-    const int p = find_probe(t, tile, __ldg(seg.keys[k] + j), bkt);
+    const int p = find_probe(t, tile, key, bkt);
     const uint64_t o = seg.out_index[k] != nullptr ? __ldg(seg.out_index[k] + j) : j;
     find_output<VW>(t, tile, p, bkt, o, seg.values[k], seg.founds[k], seg.scores[k]);
   }

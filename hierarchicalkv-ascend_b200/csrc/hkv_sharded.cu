@@ -156,28 +156,30 @@ uint64_t ceil_div(uint64_t a, uint64_t b) { return (a + b - 1) / b; }
 
 // ============================================================================
 // Peer-memory transport. Every rank exposes one "window" of device memory to
-// the others (CUDA IPC over NVLink): an inbox with one region of max_batch
-// entries per source rank, an outbox of max_batch results, and two flag rows.
-// A call is three steps per rank, with no host synchronisation:
-//   route   the requester writes each key (+ score, + value row, + its own
-//           index) straight into the owner's inbox region for this source,
-//           then the last block publishes (epoch << 32 | count) in the
-//           owner's arrive[source] flag;
-//   serve   the owner waits for all arrive flags of this epoch, runs the
-//           table kernel on each source region (find writes its results
-//           straight into the requester's outbox through out_index), and
-//           sets done[owner] = epoch in every requester's window;
-//   finish  the requester waits for all done flags, then copies its outbox
-//           into the caller's buffers.
-// A requester's next call starts only after its finish, which waited for
-// every owner to finish serving this call, so a single inbox suffices. All
+// the others (CUDA IPC over NVLink). All bulk data is written locally and
+// read by the peer that needs it: on these GPUs loads from a peer's memory
+// run at about 740 GB/s while stores into it reach about 320 GB/s.
+//   route   the requester sorts its keys (+ scores, + value rows) by owner
+//           into its own send area, one region of max_batch entries per
+//           owner, remembers where each key went, and stores
+//           (epoch << 32 | count) into the owner's arrive[requester] flag;
+//   serve   the owner waits for every arrive flag of this epoch, runs the
+//           table kernel reading each requester's region over NVLink, and
+//           writes the results into its own result area (one region per
+//           requester), then stores epoch into every requester's done[owner];
+//   finish  the requester waits for every done flag and reads its results
+//           from the owners' result areas into the caller's buffers.
+// A requester starts its next route only after its finish, which waited for
+// every owner to finish serving (and so reading) this call, and an owner
+// overwrites its result area only after every requester has arrived for the
+// next call (and so finished reading this one): single buffers suffice. All
 // waits are bounded (kSpinLimitNs): a rank that never arrives makes the
 // others give up, flag kErrSpinTimeout and treat its region as empty.
 // ============================================================================
 struct WinLayout {
-  uint64_t arrive, done;                        // kMaxWorld flags, 64 B apart
-  uint64_t in_keys, in_ref, in_scores, in_rows;  // world regions of M
-  uint64_t out_rows, out_flag, out_scores;      // M entries
+  uint64_t arrive, done;                       // kMaxWorld flags, 64 B apart
+  uint64_t snd_keys, snd_scores, snd_rows;     // world regions of M (by owner)
+  uint64_t res_rows, res_flag, res_scores;     // world regions of M (by requester)
   uint64_t bytes;
   uint64_t M;
   uint32_t vb;
@@ -196,20 +198,18 @@ WinLayout make_layout(uint32_t world, uint64_t M, uint32_t vb) {
   l.done = o;
   o = up(o + kMaxWorld * 64);
   const uint64_t R = uint64_t{world} * M;
-  l.in_keys = o;
+  l.snd_keys = o;
   o = up(o + R * 8);
-  l.in_ref = o;
-  o = up(o + R * 4);
-  l.in_scores = o;
+  l.snd_scores = o;
   o = up(o + R * 8);
-  l.in_rows = o;
+  l.snd_rows = o;
   o = up(o + R * vb);
-  l.out_rows = o;
-  o = up(o + M * vb);
-  l.out_flag = o;
-  o = up(o + M);
-  l.out_scores = o;
-  o = up(o + M * 8);
+  l.res_rows = o;
+  o = up(o + R * vb);
+  l.res_flag = o;
+  o = up(o + R);
+  l.res_scores = o;
+  o = up(o + R * 8);
   l.bytes = o;
   l.M = M;
   l.vb = vb;
@@ -221,8 +221,9 @@ __device__ __forceinline__ uint64_t* flag_at(uint8_t* base, uint64_t off,
   return reinterpret_cast<uint64_t*>(base + off + uint64_t{i} * 64);
 }
 
-// route: requester -> owners' inboxes. `keys` are the batch keys (find) or
-// the merged representatives (insert-like calls, count *dm).
+// route: sort this rank's keys by owner into its own send area. `keys` are
+// the batch keys (find, or distinct keys) or the merged representatives
+// (count *dm). where[u] = owner << 32 | position.
 template <int VW>
 __global__ void __launch_bounds__(256)
     p2p_route_kernel(const uint64_t* __restrict__ keys,
@@ -232,55 +233,66 @@ __global__ void __launch_bounds__(256)
                      const uint32_t* __restrict__ dm, uint64_t n,
                      uint32_t world, uint32_t self, PeerBases peers,
                      WinLayout lay, uint32_t* __restrict__ counters,
-                     uint64_t epoch, int* __restrict__ err) {
+                     uint64_t* __restrict__ where, uint64_t epoch,
+                     int* __restrict__ err) {
   __shared__ uint32_t cnt[kMaxWorld];
   __shared__ uint32_t base[kMaxWorld];
+  __shared__ uint64_t slot_of[256];
   __shared__ int last;
-  const Tile tile;
   const uint64_t m = dm != nullptr ? min(n, static_cast<uint64_t>(*dm)) : n;
-  const uint32_t per_block = blockDim.x / kTile;
   const uint32_t vb = lay.vb;
-  for (uint64_t b0 = uint64_t{blockIdx.x} * per_block; b0 < m;
-       b0 += uint64_t{gridDim.x} * per_block) {
+  uint8_t* win = peers.base[self];
+  uint64_t* skeys = reinterpret_cast<uint64_t*>(win + lay.snd_keys);
+  uint64_t* sscores = reinterpret_cast<uint64_t*>(win + lay.snd_scores);
+  uint8_t* srows = win + lay.snd_rows;
+  for (uint64_t b0 = uint64_t{blockIdx.x} * blockDim.x; b0 < m;
+       b0 += uint64_t{gridDim.x} * blockDim.x) {
     for (uint32_t w = threadIdx.x; w < world; w += blockDim.x) cnt[w] = 0;
     __syncthreads();
-    const uint64_t u = b0 + threadIdx.x / kTile;
+    const uint64_t u = b0 + threadIdx.x;
     uint32_t d = 0, r = 0;
     uint64_t key = 0;
     if (u < m) {
       key = keys[u];
       d = owner_of(key, world);
-      if (tile.lane == 0) r = atomicAdd(&cnt[d], 1u);
+      r = atomicAdd(&cnt[d], 1u);
     }
-    r = tile.shfl(r, 0);
     __syncthreads();
     for (uint32_t w = threadIdx.x; w < world; w += blockDim.x)
       base[w] = cnt[w] ? atomicAdd(&counters[w], cnt[w]) : 0u;
     __syncthreads();
+    uint64_t slot = ~uint64_t{0};
     if (u < m) {
       const uint64_t pos = uint64_t{base[d]} + r;
       if (pos < lay.M) {
-        uint8_t* pb = peers.base[d];
-        const uint64_t slot = uint64_t{self} * lay.M + pos;
-        if (tile.lane == 0) {
-          reinterpret_cast<uint64_t*>(pb + lay.in_keys)[slot] = key;
-          reinterpret_cast<uint32_t*>(pb + lay.in_ref)[slot] = static_cast<uint32_t>(u);
-          if (scores != nullptr)
-            reinterpret_cast<uint64_t*>(pb + lay.in_scores)[slot] = scores[u];
-        }
-        if (rows != nullptr)
-          copy_row<VW>(pb + lay.in_rows + slot * vb,
-                       rows + uint64_t{row_of != nullptr ? row_of[u]
-                                                         : static_cast<uint32_t>(u)} * vb,
-                       vb, tile.lane, kTile);
-      } else if (tile.lane == 0) {
+        slot = uint64_t{d} * lay.M + pos;
+        skeys[slot] = key;
+        if (scores != nullptr) sscores[slot] = scores[u];
+        where[u] = (uint64_t{d} << 32) | pos;
+      } else {
         atomicOr(err, kErrPeerOverflow);
+        where[u] = ~uint64_t{0};
+      }
+    }
+    if (rows != nullptr) {
+      slot_of[threadIdx.x] = slot;
+      __syncthreads();
+      // the block's rows, one 8-lane tile per row
+      const Tile tile;
+      for (uint32_t k = threadIdx.x / kTile; k < blockDim.x; k += blockDim.x / kTile) {
+        const uint64_t uk = b0 + k;
+        const uint64_t sk = slot_of[k];
+        if (uk < m && sk != ~uint64_t{0})
+          copy_row<VW>(srows + sk * vb,
+                       rows + uint64_t{row_of != nullptr ? row_of[uk]
+                                                         : static_cast<uint32_t>(uk)} * vb,
+                       vb, tile.lane, kTile);
       }
     }
     __syncthreads();
   }
-  // the last block to finish publishes the counts (every block's stores are
-  // fenced at system scope before it is counted)
+  // the last block to finish publishes the counts to the owners (every
+  // block's stores are fenced at system scope before it is counted)
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) last = atomicAdd(&counters[world], 1u) == gridDim.x - 1;
@@ -296,8 +308,9 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// Waits (bounded) until flag_i holds epoch in its high half for every i <
-// world; writes the low halves to counts (0 for a flag that never came).
+// Waits (bounded) until flag_i holds epoch (in its high half when counted)
+// for every i < world; writes the low halves to counts (0 for a flag that
+// never came).
 __device__ void wait_flags(uint8_t* base, uint64_t off, uint32_t world,
                            uint64_t epoch, bool counted, uint32_t* counts,
                            int* err, int site) {
@@ -326,32 +339,27 @@ __global__ void p2p_wait_arrive_kernel(uint8_t* self_base, WinLayout lay,
   wait_flags(self_base, lay.arrive, world, epoch, true, counts, err, 301);
 }
 
-// serve, find_or_insert: result rows and Occupy codes back to the requesters
+// serve, find_or_insert: bring each requester's input rows into the local
+// result area, where the table kernel then leaves found rows in place
 template <int VW>
 __global__ void __launch_bounds__(256)
-    p2p_return_rows_kernel(uint8_t* self_base, PeerBases peers, WinLayout lay,
-                           uint32_t world, const uint32_t* __restrict__ counts,
-                           const uint8_t* __restrict__ status) {
+    p2p_pull_rows_kernel(PeerBases peers, WinLayout lay, uint32_t world,
+                         uint32_t self, const uint32_t* __restrict__ counts) {
   const Tile tile;
   const uint32_t vb = lay.vb;
   const uint64_t ntiles = uint64_t{gridDim.x} * (blockDim.x / kTile);
   const uint64_t t0 = (uint64_t{blockIdx.x} * blockDim.x + threadIdx.x) / kTile;
-  const uint8_t* in_rows = self_base + lay.in_rows;
-  const uint32_t* in_ref = reinterpret_cast<const uint32_t*>(self_base + lay.in_ref);
+  uint8_t* res = peers.base[self] + lay.res_rows;
   for (uint32_t src = 0; src < world; src++) {
-    const uint64_t c = counts[src];
-    uint8_t* pb = peers.base[src];
-    for (uint64_t j = t0; j < c; j += ntiles) {
-      const uint64_t slot = uint64_t{src} * lay.M + j;
-      const uint32_t ref = in_ref[slot];
-      if (tile.lane == 0) (pb + lay.out_flag)[ref] = status[slot];
-      copy_row<VW>(pb + lay.out_rows + uint64_t{ref} * vb, in_rows + slot * vb, vb,
-                   tile.lane, kTile);
-    }
+    const uint64_t c = min(static_cast<uint64_t>(counts[src]), lay.M);
+    const uint8_t* in = peers.base[src] + lay.snd_rows + uint64_t{self} * lay.M * vb;
+    uint8_t* out = res + uint64_t{src} * lay.M * vb;
+    for (uint64_t j = t0; j < c; j += ntiles)
+      copy_row<VW>(out + j * vb, in + j * vb, vb, tile.lane, kTile);
   }
 }
 
-// serve: every result of this epoch is out; tell each requester
+// serve: every result of this epoch is in place; tell each requester
 __global__ void p2p_signal_done_kernel(PeerBases peers, WinLayout lay,
                                        uint32_t world, uint32_t self,
                                        uint64_t epoch) {
@@ -360,43 +368,61 @@ __global__ void p2p_signal_done_kernel(PeerBases peers, WinLayout lay,
     st_release_sys_u64(flag_at(peers.base[w], lay.done, self), epoch);
 }
 
-// finish: wait for every owner, then copy the outbox to the caller.
-// mode 0: find (rows, flags, scores of found keys, per input);
-// mode 1: find_or_insert (rows of found or inserted representatives, to
-// every occurrence through uid_of); mode 2: insert_or_assign (wait only).
+// finish: wait for every owner, then read the results from the owners'
+// result areas. mode 0: find (rows, flags, scores of found keys, per
+// input); mode 1: find_or_insert (rows of found or inserted representatives,
+// to every occurrence through uid_of); mode 2: insert_or_assign (wait only).
+// A 4-lane tile per key issues the flag, score and row loads together, so a
+// key costs one NVLink round trip; rows longer than the registers hold (16
+// vectors) finish with a second pass.
 template <int VW>
 __global__ void __launch_bounds__(256)
-    p2p_finish_kernel(int mode, uint8_t* self_base, WinLayout lay, uint32_t world,
-                      uint64_t epoch, int* err, uint64_t n,
+    p2p_finish_kernel(int mode, PeerBases peers, WinLayout lay, uint32_t world,
+                      uint32_t self, uint64_t epoch, int* err, uint64_t n,
+                      const uint64_t* __restrict__ where,
                       const uint32_t* __restrict__ uid_of,
                       uint8_t* __restrict__ values, bool* __restrict__ founds,
                       uint64_t* __restrict__ scores) {
-  wait_flags(self_base, lay.done, world, epoch, false, nullptr, err, 302);
+  wait_flags(peers.base[self], lay.done, world, epoch, false, nullptr, err, 302);
   __syncthreads();
   if (mode == 2) return;
-  const Tile tile;
+  using V = typename VecOf<VW>::T;
+  constexpr uint32_t W = 4;
+  constexpr uint32_t kHead = 4;  // row vectors per lane held in registers
+  const TileW<W> tile;
   const uint32_t vb = lay.vb;
-  const uint64_t ntiles = uint64_t{gridDim.x} * (blockDim.x / kTile);
-  const uint8_t* flags = self_base + lay.out_flag;
-  const uint8_t* rows = self_base + lay.out_rows;
-  const uint64_t* osc = reinterpret_cast<const uint64_t*>(self_base + lay.out_scores);
-  for (uint64_t i = (uint64_t{blockIdx.x} * blockDim.x + threadIdx.x) / kTile; i < n;
+  const uint32_t nv = vb / VW;
+  const uint64_t ntiles = uint64_t{gridDim.x} * (blockDim.x / W);
+  for (uint64_t i = (uint64_t{blockIdx.x} * blockDim.x + threadIdx.x) / W; i < n;
        i += ntiles) {
     const uint32_t u = uid_of != nullptr ? uid_of[i] : static_cast<uint32_t>(i);
-    bool ok = false;
-    if (u != 0xFFFFFFFFu) {
-      const uint8_t f = __ldcg(flags + u);
-      ok = mode == 0 ? f != 0 : (f != kRefused && f != kIllegal && f != kTimedOut);
+    const uint64_t w = u != 0xFFFFFFFFu ? where[u] : ~uint64_t{0};
+    if (w == ~uint64_t{0}) {
+      if (tile.lane == 0 && founds != nullptr) founds[i] = false;
+      continue;
     }
+    const uint8_t* ob = peers.base[static_cast<uint32_t>(w >> 32)];
+    const uint64_t slot = uint64_t{self} * lay.M + (w & 0xFFFFFFFFu);
+    const V* sp = reinterpret_cast<const V*>(ob + lay.res_rows + slot * vb);
+    V head[kHead];
+#pragma unroll
+    for (uint32_t h = 0; h < kHead; h++)
+      if (values != nullptr && tile.lane + h * W < nv) head[h] = __ldcg(sp + tile.lane + h * W);
+    uint64_t sc = 0;
+    if (tile.lane == 0 && scores != nullptr)
+      sc = __ldcg(reinterpret_cast<const uint64_t*>(ob + lay.res_scores) + slot);
+    const uint8_t f = __ldcg(ob + lay.res_flag + slot);
+    const bool ok = mode == 0 ? f != 0 : (f != kRefused && f != kIllegal && f != kTimedOut);
     if (tile.lane == 0) {
       if (founds != nullptr) founds[i] = ok;
-      if (ok && scores != nullptr) scores[i] = __ldcg(osc + u);
+      if (ok && scores != nullptr) scores[i] = sc;
     }
     if (ok && values != nullptr) {
-      using V = typename VecOf<VW>::T;
-      const V* sp = reinterpret_cast<const V*>(rows + uint64_t{u} * vb);
       V* dp = reinterpret_cast<V*>(values + i * vb);
-      for (uint32_t v = tile.lane; v < vb / VW; v += kTile) dp[v] = __ldcg(sp + v);
+#pragma unroll
+      for (uint32_t h = 0; h < kHead; h++)
+        if (tile.lane + h * W < nv) dp[tile.lane + h * W] = head[h];
+      for (uint32_t v = tile.lane + kHead * W; v < nv; v += W) dp[v] = __ldcg(sp + v);
     }
   }
 }
@@ -436,7 +462,7 @@ class ShardedImpl {
         if (p != rank_ && peers_.base[p]) cudaIpcCloseMemHandle(peers_.base[p]);
       cudaFree(win_);
       cudaFree(d_route_counters_);
-      cudaFree(d_status_);
+      cudaFree(d_where_);
     }
     if (comm_) ncclCommDestroy(comm_);
     delete local_;
@@ -598,7 +624,7 @@ class ShardedImpl {
       win_ = nullptr;
     }
     if (mine.ok)
-      mine.ok = cudaMemset(win_, 0, lay_.in_keys) == cudaSuccess &&
+      mine.ok = cudaMemset(win_, 0, lay_.snd_keys) == cudaSuccess &&
                 cudaIpcGetMemHandle(&mine.h, win_) == cudaSuccess;
     cudaGetLastError();
     std::vector<Rec> all(world_);
@@ -631,8 +657,7 @@ class ShardedImpl {
                cudaSuccess &&
            cudaMemset(d_route_counters_, 0, (kMaxWorld + 1) * sizeof(uint32_t)) ==
                cudaSuccess &&
-           cudaMalloc(&d_status_, uint64_t{static_cast<uint32_t>(world_)} * max_batch) ==
-               cudaSuccess;
+           cudaMalloc(&d_where_, max_batch * sizeof(uint64_t)) == cudaSuccess;
       cudaGetLastError();
       again.ok = ok;
       exchange_bytes(&again, all.data(), sizeof(Rec), s);
@@ -644,10 +669,10 @@ class ShardedImpl {
       std::memset(&peers_, 0, sizeof peers_);
       cudaFree(win_);
       cudaFree(d_route_counters_);
-      cudaFree(d_status_);
+      cudaFree(d_where_);
       win_ = nullptr;
       d_route_counters_ = nullptr;
-      d_status_ = nullptr;
+      d_where_ = nullptr;
       return;
     }
     max_batch_ = max_batch;
@@ -676,6 +701,7 @@ class ShardedImpl {
         kind != 0 && (st == kLfu || st == kEpochLfu || st == kCustomized);
     const uint64_t M = max_batch_;
     const uint32_t vb = lay_.vb;
+    const uint32_t me = static_cast<uint32_t>(rank_);
     int* err = local_->error_word();
     epoch_++;
     Workspace ws(s, local_->pool());
@@ -685,7 +711,6 @@ class ShardedImpl {
     const uint32_t* row_of = nullptr;
     const uint32_t* dm = nullptr;
     const uint32_t* uid_of = nullptr;
-    uint64_t nr = n;
     if (kind != 0 && unique) {
       rscores = send_scores ? scores : nullptr;
     } else if (kind != 0 && n > 0) {
@@ -697,72 +722,70 @@ class ShardedImpl {
       dm = d.dm;
       uid_of = d.uid_of;
     }
-    if (kind == 0 || n == 0) nr = n;
     const int vw = kind == 0 ? 16
-                             : local_->value_width({values, win_ + lay_.in_rows});
+                             : local_->value_width({values, win_ + lay_.snd_rows});
     const int gr = static_cast<int>(std::max<uint64_t>(
-        1, std::min<uint64_t>(ceil_div(std::max<uint64_t>(nr, 1), 256 / kTile),
-                              sm_count_ * 8ull)));
+        1, std::min<uint64_t>(ceil_div(std::max<uint64_t>(n, 1), 256),
+                              sm_count_ * 4ull)));
     SHARD_DISPATCH_VW(vw, p2p_route_kernel<VW><<<gr, 256, 0, counted(s)>>>(
                               rkeys, rscores, kind == 0 ? nullptr : values, row_of,
-                              dm, nr, world_, rank_, peers_, lay_,
-                              d_route_counters_, epoch_, err));
+                              dm, n, world_, me, peers_, lay_, d_route_counters_,
+                              d_where_, epoch_, err));
     CUDA_TRY(cudaGetLastError());
-    // 2. serve what the other ranks sent
+    // 2. serve what the requesters sorted for this rank
     uint32_t* counts = d_counts_;  // kMaxWorld entries, device
     p2p_wait_arrive_kernel<<<1, kMaxWorld, 0, counted(s)>>>(win_, lay_, world_,
                                                              epoch_, counts, err);
     CUDA_TRY(cudaGetLastError());
-    const uint64_t* in_keys = reinterpret_cast<const uint64_t*>(win_ + lay_.in_keys);
-    const uint32_t* in_ref = reinterpret_cast<const uint32_t*>(win_ + lay_.in_ref);
-    uint64_t* in_scores = reinterpret_cast<uint64_t*>(win_ + lay_.in_scores);
+    const uint64_t mine = uint64_t{me} * M;  // this owner's region in a send area
     if (kind == 0) {
-      // one launch over every source region: results go straight to the
-      // requesters' outboxes
       FindSegments seg;
       for (int src = 0; src < world_; src++) {
         const uint64_t o = uint64_t{static_cast<uint32_t>(src)} * M;
-        uint8_t* pb = peers_.base[src];
-        seg.keys[src] = in_keys + o;
-        seg.out_index[src] = in_ref + o;
-        seg.values[src] = pb + lay_.out_rows;
-        seg.founds[src] = reinterpret_cast<bool*>(pb + lay_.out_flag);
-        seg.scores[src] = reinterpret_cast<uint64_t*>(pb + lay_.out_scores);
+        seg.keys[src] = reinterpret_cast<const uint64_t*>(peers_.base[src] + lay_.snd_keys) + mine;
+        seg.out_index[src] = nullptr;
+        seg.values[src] = win_ + lay_.res_rows + o * vb;
+        seg.founds[src] = reinterpret_cast<bool*>(win_ + lay_.res_flag + o);
+        seg.scores[src] = reinterpret_cast<uint64_t*>(win_ + lay_.res_scores) + o;
       }
       local_->find_segments(seg, static_cast<uint32_t>(world_), counts, M, s);
-    }
-    for (int src = 0; kind != 0 && src < world_; src++) {
-      const uint64_t o = uint64_t{static_cast<uint32_t>(src)} * M;
-      {
-        uint8_t* rows = win_ + lay_.in_rows + o * vb;
-        const uint64_t* sc = send_scores ? in_scores + o : nullptr;
+    } else {
+      if (kind == 1) {
+        const int vwr = local_->value_width({win_ + lay_.snd_rows});
+        const int g = static_cast<int>(std::min<uint64_t>(
+            ceil_div(M * kTile, 256), sm_count_ * 16ull));
+        SHARD_DISPATCH_VW(vwr, p2p_pull_rows_kernel<VW><<<g, 256, 0, counted(s)>>>(
+                                   peers_, lay_, world_, me, counts));
+        CUDA_TRY(cudaGetLastError());
+      }
+      for (int src = 0; src < world_; src++) {
+        const uint64_t o = uint64_t{static_cast<uint32_t>(src)} * M;
+        uint8_t* pb = peers_.base[src];
+        const uint64_t* k = reinterpret_cast<const uint64_t*>(pb + lay_.snd_keys) + mine;
+        const uint64_t* sc =
+            send_scores ? reinterpret_cast<const uint64_t*>(pb + lay_.snd_scores) + mine
+                        : nullptr;
         if (kind == 1)
-          local_->upsert_counted(kModeFindOrInsert, M, counts + src, in_keys + o,
-                                 nullptr, rows, sc, d_status_ + o, s);
+          local_->upsert_counted(kModeFindOrInsert, M, counts + src, k, nullptr,
+                                 win_ + lay_.res_rows + o * vb, sc,
+                                 win_ + lay_.res_flag + o, s);
         else
-          local_->upsert_counted(kModeInsertOrAssign, M, counts + src,
-                                 in_keys + o, rows, nullptr, sc, nullptr, s);
+          local_->upsert_counted(kModeInsertOrAssign, M, counts + src, k,
+                                 pb + lay_.snd_rows + mine * vb, nullptr, sc, nullptr, s);
       }
     }
-    if (kind == 1) {
-      const int vwr = local_->value_width({win_ + lay_.in_rows});
-      const int g = static_cast<int>(std::min<uint64_t>(
-          ceil_div(M * kTile, 256), sm_count_ * 16ull));
-      SHARD_DISPATCH_VW(vwr, p2p_return_rows_kernel<VW><<<g, 256, 0, counted(s)>>>(
-                                 win_, peers_, lay_, world_, counts, d_status_));
-      CUDA_TRY(cudaGetLastError());
-    }
     p2p_signal_done_kernel<<<1, kMaxWorld, 0, counted(s)>>>(peers_, lay_, world_,
-                                                             rank_, epoch_);
+                                                             me, epoch_);
     CUDA_TRY(cudaGetLastError());
-    // 3. finish: wait for every owner, then the outbox to the caller
-    const int vwf = kind == 1 ? local_->value_width({values, win_ + lay_.out_rows})
-                              : (values ? local_->value_width({values}) : 16);
+    // 3. finish: wait for every owner, then read the results
+    const int vwf = (kind == 2 || values == nullptr)
+                        ? 16
+                        : local_->value_width({values, win_ + lay_.res_rows});
     const int gf = static_cast<int>(std::max<uint64_t>(
-        1, std::min<uint64_t>(ceil_div(std::max<uint64_t>(n, 1) * kTile, 256),
+        1, std::min<uint64_t>(ceil_div(std::max<uint64_t>(n, 1) * 4, 256),
                               sm_count_ * 16ull)));
     SHARD_DISPATCH_VW(vwf, p2p_finish_kernel<VW><<<gf, 256, 0, counted(s)>>>(
-                               kind, win_, lay_, world_, epoch_, err, n,
+                               kind, peers_, lay_, world_, me, epoch_, err, n, d_where_,
                                kind == 1 ? uid_of : nullptr,
                                kind == 2 ? nullptr : values,
                                kind == 0 ? founds : nullptr,
@@ -798,7 +821,7 @@ class ShardedImpl {
   uint8_t* win_ = nullptr;
   PeerBases peers_{};
   uint32_t* d_route_counters_ = nullptr;
-  uint8_t* d_status_ = nullptr;
+  uint64_t* d_where_ = nullptr;  // owner << 32 | position of each routed key
 };
 
 void set_last_error(const std::string& m);
