@@ -317,6 +317,7 @@ def run_gpu(args):
         launches = int(tl.item())
     e2e_line = e2e(table, finds, inserts, vals, warm, min(steps, 20), dist, device)
     log("e2e done")
+    local.check_device_error()  # a lock or peer wait that ran out fails the run
     keys_total = 2 * BATCH * steps * world
     value = keys_total / (ms * 1e-3) / 1e9
 
@@ -414,6 +415,9 @@ def e2e(table, finds, inserts, vals, warm, steps, dist=None, device=None):
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    if dist:
+        dist.barrier()  # the ranks start the timed region together
+        torch.cuda.synchronize()
     a.record(s_in)
     for i in range(steps):
         x = i % 2

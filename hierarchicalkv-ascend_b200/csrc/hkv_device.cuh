@@ -44,14 +44,17 @@ enum Occupy : int {
 
 // Device error word bits.
 // Up to kMaxSegments key arrays looked up in one launch (the sharded table's
-// per-source inbox regions), each with its own output arrays.
+// per-requester regions), each with its own outputs. Result j of segment k
+// goes to values[k] + j * row_stride, founds[k] + j * flag_stride (one
+// byte, 0/1) and scores[k] + j * score_stride (8 bytes), so results can be
+// packed as records.
 constexpr uint32_t kMaxSegments = 64;
 struct FindSegments {
   const uint64_t* keys[kMaxSegments];
-  const uint32_t* out_index[kMaxSegments];
   uint8_t* values[kMaxSegments];
-  bool* founds[kMaxSegments];
-  uint64_t* scores[kMaxSegments];
+  uint8_t* founds[kMaxSegments];
+  uint8_t* scores[kMaxSegments];
+  uint32_t row_stride, flag_stride, score_stride;
 };
 
 enum UpsertMode : int {

@@ -164,20 +164,25 @@ __device__ __forceinline__ int find_probe(const TableView& t, const TileW<W>& ti
   return tile.ballot(stop) ? -1 : static_cast<int>(best & 0xFF);
 }
 
-// Writes one find result: flag, and for a hit the score and the value row.
+// Writes one find result at position o: flag, and for a hit the score and
+// the value row (byte strides between consecutive results).
 template <int VW, uint32_t W>
 __device__ __forceinline__ void find_output(const TableView& t, const TileW<W>& tile,
                                             int p, uint64_t bkt, uint64_t o,
                                             uint8_t* __restrict__ values,
-                                            bool* __restrict__ founds,
-                                            uint64_t* __restrict__ scores) {
+                                            uint8_t* __restrict__ founds,
+                                            uint8_t* __restrict__ scores,
+                                            uint32_t row_stride, uint32_t flag_stride,
+                                            uint32_t score_stride) {
   using V = typename VecOf<VW>::T;
-  if (tile.lane == 0 && founds != nullptr) founds[o] = p >= 0;
+  if (tile.lane == 0 && founds != nullptr) founds[o * flag_stride] = p >= 0;
   if (p < 0) return;
-  if (scores != nullptr && tile.lane == 0) scores[o] = __ldg(t.scores + bkt * kBucket + p);
+  if (scores != nullptr && tile.lane == 0)
+    *reinterpret_cast<uint64_t*>(scores + o * score_stride) =
+        __ldg(t.scores + bkt * kBucket + p);
   if (values != nullptr) {
     const uint32_t vb = t.value_bytes;
-    V* dst = reinterpret_cast<V*>(values + o * vb);
+    V* dst = reinterpret_cast<V*>(values + o * row_stride);
     const V* src = reinterpret_cast<const V*>(value_ptr(t, bkt, p));
     for (uint32_t v = tile.lane; v < vb / VW; v += W) __stcs(dst + v, __ldg(src + v));
   }
@@ -204,7 +209,8 @@ __global__ void __launch_bounds__(256, HKV_FIND_MIN_BLOCKS)
     uint64_t bkt;
     const int p = find_probe(t, tile, key, bkt);
     const uint64_t o = out_index != nullptr ? __ldg(out_index + i) : i;
-    find_output<VW>(t, tile, p, bkt, o, values, founds, scores);
+    find_output<VW>(t, tile, p, bkt, o, values, reinterpret_cast<uint8_t*>(founds),
+                    reinterpret_cast<uint8_t*>(scores), t.value_bytes, 1, 8);
   }
 }
 
@@ -245,8 +251,8 @@ __global__ void __launch_bounds__(256, HKV_FIND_MIN_BLOCKS)
     if (j >= cnt[k]) continue;
     uint64_t bkt;
     const int p = find_probe(t, tile, key, bkt);
-    const uint64_t o = seg.out_index[k] != nullptr ? __ldg(seg.out_index[k] + j) : j;
-    find_output<VW>(t, tile, p, bkt, o, seg.values[k], seg.founds[k], seg.scores[k]);
+    find_output<VW>(t, tile, p, bkt, j, seg.values[k], seg.founds[k], seg.scores[k],
+                    seg.row_stride, seg.flag_stride, seg.score_stride);
   }
 }
 
@@ -266,6 +272,7 @@ struct UpsertArgs {
   uint64_t* ev_scores;
   unsigned long long* ev_counter;
   uint8_t* status;           // optional Occupy code per key
+  uint32_t status_stride;    // bytes between two keys' codes (0 means 1)
   const uint32_t* dn;        // optional device-side key count (overrides n)
   int report_refused;        // insert_and_evict: report refused inputs
 };
@@ -659,7 +666,8 @@ __global__ void __launch_bounds__(256, HKV_UPSERT_MIN_BLOCKS)
       backoff(round);
     }
     if (i < n) {
-      if (a.status != nullptr && tile.lane == 0) a.status[i] = res;
+      if (a.status != nullptr && tile.lane == 0)
+        a.status[i * (a.status_stride ? a.status_stride : 1)] = res;
       if constexpr (Mode == kModeInsertAndEvict) {
         if (res == kRefused && a.report_refused) {
           // reference insert_and_evict_kernel.h:553-557, :675-683: the

@@ -176,10 +176,13 @@ uint64_t ceil_div(uint64_t a, uint64_t b) { return (a + b - 1) / b; }
 // waits are bounded (kSpinLimitNs): a rank that never arrives makes the
 // others give up, flag kErrSpinTimeout and treat its region as empty.
 // ============================================================================
+// The result area holds, per requester region, value rows (vb bytes each,
+// so a row keeps the alignment of the table's rows) and 16-byte tails: the
+// score and the found flag for find, the Occupy status for find_or_insert.
 struct WinLayout {
   uint64_t arrive, done;                       // kMaxWorld flags, 64 B apart
   uint64_t snd_keys, snd_scores, snd_rows;     // world regions of M (by owner)
-  uint64_t res_rows, res_flag, res_scores;     // world regions of M (by requester)
+  uint64_t res_rows, res_tail;                 // world regions of M (by requester)
   uint64_t bytes;
   uint64_t M;
   uint32_t vb;
@@ -206,10 +209,8 @@ WinLayout make_layout(uint32_t world, uint64_t M, uint32_t vb) {
   o = up(o + R * vb);
   l.res_rows = o;
   o = up(o + R * vb);
-  l.res_flag = o;
-  o = up(o + R);
-  l.res_scores = o;
-  o = up(o + R * 8);
+  l.res_tail = o;
+  o = up(o + R * 16);
   l.bytes = o;
   l.M = M;
   l.vb = vb;
@@ -291,14 +292,16 @@ __global__ void __launch_bounds__(256)
     }
     __syncthreads();
   }
-  // the last block to finish publishes the counts to the owners (every
-  // block's stores are fenced at system scope before it is counted)
-  __threadfence_system();
+  // the last block to finish publishes the counts to the owners. Every
+  // block's stores land in this GPU's L2 (the point peers read from) before
+  // the block is counted; the flag store is a system-scope release, so an
+  // owner that acquires it sees them.
+  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) last = atomicAdd(&counters[world], 1u) == gridDim.x - 1;
   __syncthreads();
   if (last) {
-    __threadfence_system();
+    __threadfence();
     for (uint32_t w = threadIdx.x; w < world; w += blockDim.x) {
       const uint32_t c = min(atomicAdd(&counters[w], 0u), static_cast<uint32_t>(lay.M));
       st_release_sys_u64(flag_at(peers.base[w], lay.arrive, self), (epoch << 32) | c);
@@ -359,11 +362,12 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// serve: every result of this epoch is in place; tell each requester
+// serve: every result of this epoch is in place (written by the kernels
+// before this one in stream order); tell each requester with a system-scope
+// release
 __global__ void p2p_signal_done_kernel(PeerBases peers, WinLayout lay,
                                        uint32_t world, uint32_t self,
                                        uint64_t epoch) {
-  __threadfence_system();
   for (uint32_t w = threadIdx.x; w < world; w += blockDim.x)
     st_release_sys_u64(flag_at(peers.base[w], lay.done, self), epoch);
 }
@@ -408,11 +412,13 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (uint32_t h = 0; h < kHead; h++)
       if (values != nullptr && tile.lane + h * W < nv) head[h] = __ldcg(sp + tile.lane + h * W);
-    uint64_t sc = 0;
-    if (tile.lane == 0 && scores != nullptr)
-      sc = __ldcg(reinterpret_cast<const uint64_t*>(ob + lay.res_scores) + slot);
-    const uint8_t f = __ldcg(ob + lay.res_flag + slot);
+    // tail: find -> score (8 bytes) | found flag; find_or_insert -> status
+    uint4 tail = make_uint4(0, 0, 0, 0);
+    if (tile.lane == 0)
+      tail = __ldcg(reinterpret_cast<const uint4*>(ob + lay.res_tail) + slot);
+    const uint32_t f = tile.shfl(tail.z & 0xFFu, 0);
     const bool ok = mode == 0 ? f != 0 : (f != kRefused && f != kIllegal && f != kTimedOut);
+    const uint64_t sc = (uint64_t{tail.y} << 32) | tail.x;
     if (tile.lane == 0) {
       if (founds != nullptr) founds[i] = ok;
       if (ok && scores != nullptr) scores[i] = sc;
@@ -740,13 +746,15 @@ class ShardedImpl {
     const uint64_t mine = uint64_t{me} * M;  // this owner's region in a send area
     if (kind == 0) {
       FindSegments seg;
+      seg.row_stride = vb;
+      seg.flag_stride = seg.score_stride = 16;
       for (int src = 0; src < world_; src++) {
         const uint64_t o = uint64_t{static_cast<uint32_t>(src)} * M;
+        uint8_t* tail0 = win_ + lay_.res_tail + o * 16;
         seg.keys[src] = reinterpret_cast<const uint64_t*>(peers_.base[src] + lay_.snd_keys) + mine;
-        seg.out_index[src] = nullptr;
         seg.values[src] = win_ + lay_.res_rows + o * vb;
-        seg.founds[src] = reinterpret_cast<bool*>(win_ + lay_.res_flag + o);
-        seg.scores[src] = reinterpret_cast<uint64_t*>(win_ + lay_.res_scores) + o;
+        seg.scores[src] = tail0;
+        seg.founds[src] = tail0 + 8;
       }
       local_->find_segments(seg, static_cast<uint32_t>(world_), counts, M, s);
     } else {
@@ -768,10 +776,11 @@ class ShardedImpl {
         if (kind == 1)
           local_->upsert_counted(kModeFindOrInsert, M, counts + src, k, nullptr,
                                  win_ + lay_.res_rows + o * vb, sc,
-                                 win_ + lay_.res_flag + o, s);
+                                 win_ + lay_.res_tail + o * 16 + 8, 16, s);
         else
           local_->upsert_counted(kModeInsertOrAssign, M, counts + src, k,
-                                 pb + lay_.snd_rows + mine * vb, nullptr, sc, nullptr, s);
+                                 pb + lay_.snd_rows + mine * vb, nullptr, sc, nullptr,
+                                 1, s);
       }
     }
     p2p_signal_done_kernel<<<1, kMaxWorld, 0, counted(s)>>>(peers_, lay_, world_,

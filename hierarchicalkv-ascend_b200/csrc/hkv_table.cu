@@ -409,7 +409,8 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
                        const uint64_t* scores, uint64_t* ev_keys,
                        uint8_t* ev_values, uint64_t* ev_scores,
                        uint64_t* d_counter, cudaStream_t s, bool unique,
-                       bool ignore, uint8_t* status, const uint32_t* dn) {
+                       bool ignore, uint8_t* status, const uint32_t* dn,
+                       uint32_t status_stride) {
   const int st = ignore ? kCustomized : strategy_;
   const TableView v = view();
   UpsertArgs a;
@@ -421,6 +422,7 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
   a.ev_counter = reinterpret_cast<unsigned long long*>(d_counter);
   a.report_refused = 1;
   a.status = status;
+  a.status_stride = status_stride;
   const uint8_t* rows = mode == kModeFindOrInsert ? values_io : values_in;
 
   if (unique) {
@@ -652,18 +654,6 @@ void TableImpl::find(size_t n, const uint64_t* keys, uint8_t* values,
   CUDA_TRY(cudaGetLastError());
 }
 
-void TableImpl::find_indexed(size_t n_bound, const uint32_t* dn,
-                             const uint64_t* keys, uint8_t* values, bool* founds,
-                             uint64_t* scores, const uint32_t* out_index,
-                             cudaStream_t s) {
-  if (n_bound == 0) return;
-  const TableView v = view();
-  const int vw = values ? value_width({values}) : 16;
-  DISPATCH_VW(vw, find_kernel<VW><<<find_grid(n_bound), 256, 0, counted(s)>>>(
-                      v, keys, values, founds, scores, n_bound, dn, out_index));
-  CUDA_TRY(cudaGetLastError());
-}
-
 void TableImpl::find_segments(const FindSegments& seg, uint32_t nseg,
                               const uint32_t* counts, uint64_t bound,
                               cudaStream_t s) {
@@ -672,8 +662,15 @@ void TableImpl::find_segments(const FindSegments& seg, uint32_t nseg,
   int vw = 16;
   for (uint32_t k = 0; k < nseg; k++)
     if (seg.values[k]) vw = std::min(vw, value_width({seg.values[k]}));
+  while (vw > 1 && seg.row_stride % vw) vw = vw == 16 ? 4 : 1;
   const TableView v = view();
-  DISPATCH_VW(vw, find_segments_kernel<VW><<<find_grid(bound * nseg), 256, 0, counted(s)>>>(
+#ifndef HKV_SEG_BLOCKS_PER_SM
+#define HKV_SEG_BLOCKS_PER_SM 64
+#endif
+  const int grid = static_cast<int>(std::min<uint64_t>(
+      ceil_div(std::max<uint64_t>(bound * nseg, 1), 256 / kFindTile),
+      sm_count_ * uint64_t{HKV_SEG_BLOCKS_PER_SM}));
+  DISPATCH_VW(vw, find_segments_kernel<VW><<<grid, 256, 0, counted(s)>>>(
                       v, seg, nseg, counts, bound));
   CUDA_TRY(cudaGetLastError());
 }
@@ -681,10 +678,11 @@ void TableImpl::find_segments(const FindSegments& seg, uint32_t nseg,
 void TableImpl::upsert_counted(int mode, size_t n_bound, const uint32_t* dn,
                                const uint64_t* keys, const uint8_t* values_in,
                                uint8_t* values_io, const uint64_t* scores,
-                               uint8_t* status, cudaStream_t s) {
+                               uint8_t* status, uint32_t status_stride,
+                               cudaStream_t s) {
   if (n_bound == 0) return;
   upsert(mode, n_bound, keys, values_in, values_io, scores, nullptr, nullptr,
-         nullptr, nullptr, s, true, false, status, dn);
+         nullptr, nullptr, s, true, false, status, dn, status_stride);
 }
 
 void TableImpl::contains(size_t n, const uint64_t* keys, bool* founds,

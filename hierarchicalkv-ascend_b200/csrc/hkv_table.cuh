@@ -106,21 +106,17 @@ class TableImpl {
                      cudaStream_t s);
   void find(size_t n, const uint64_t* keys, uint8_t* values, bool* founds,
             uint64_t* scores, cudaStream_t s);
-  // find of up to n_bound keys (device count *dn when dn is not null) whose
-  // results go to position out_index[i] of values / founds / scores
-  void find_indexed(size_t n_bound, const uint32_t* dn, const uint64_t* keys,
-                    uint8_t* values, bool* founds, uint64_t* scores,
-                    const uint32_t* out_index, cudaStream_t s);
-  // find over nseg key arrays (segment k: counts[k] keys, at most bound),
-  // results of key j of segment k to position out_index[k][j]
+  // find over nseg key arrays (segment k: counts[k] keys, at most bound);
+  // result j of segment k goes to the strided slots described in seg
   void find_segments(const FindSegments& seg, uint32_t nseg, const uint32_t* counts,
                      uint64_t bound, cudaStream_t s);
   // unique-key insert_or_assign / find_or_insert of up to n_bound keys
-  // (device count *dn), per-key Occupy result in status; no auto-grow
+  // (device count *dn), per-key Occupy result at status[i * status_stride];
+  // no auto-grow
   void upsert_counted(int mode, size_t n_bound, const uint32_t* dn,
                       const uint64_t* keys, const uint8_t* values_in,
                       uint8_t* values_io, const uint64_t* scores,
-                      uint8_t* status, cudaStream_t s);
+                      uint8_t* status, uint32_t status_stride, cudaStream_t s);
   void contains(size_t n, const uint64_t* keys, bool* founds, cudaStream_t s);
   void erase(size_t n, const uint64_t* keys, cudaStream_t s);
   void clear(cudaStream_t s);
@@ -182,7 +178,7 @@ class TableImpl {
               const uint64_t* scores, uint64_t* ev_keys, uint8_t* ev_values,
               uint64_t* ev_scores, uint64_t* d_counter, cudaStream_t s,
               bool unique, bool ignore, uint8_t* status,
-              const uint32_t* dn = nullptr);
+              const uint32_t* dn = nullptr, uint32_t status_stride = 1);
 
   hkv_options opt_;
   int key_type_, value_type_, strategy_;
