@@ -1,17 +1,19 @@
 // hkv_sharded.cu -- table sharded over the GPUs of one node (no reference
 // counterpart: the reference drives a single device).
 //
-// Each rank owns one TableImpl. A collective call takes every rank's batch:
-//   1. merge duplicate keys of the local batch (hkv_dedup.cuh),
-//   2. route each distinct key to owner = (Murmur3(key) >> 40) % world,
-//   3. exchange per-peer counts, then keys / scores / value rows with NCCL
-//      grouped send/recv (an all-to-all over NVLink/NVSwitch),
-//   4. run the local operation on the owner (duplicates across sources are
-//      merged again there),
-//   5. return value rows (and found flags / scores) the same way and scatter
-//      them to every occurrence in the caller's batch.
-// The owner uses hash bits 40.. so that a shard's keys do not share the low
-// hash bits that choose their bucket and start slot.
+// Each rank owns one TableImpl; a key belongs to owner = (Murmur3(key) >> 40)
+// % world (hash bits 40.. so that a shard's keys do not share the low hash
+// bits that choose their bucket and start slot). A collective call takes
+// every rank's batch, merges duplicate keys of insert-like batches
+// (hkv_dedup.cuh; skipped for unique_key batches), moves each key to its
+// owner, runs the local operation there (the same key from several ranks is
+// applied in rank order) and brings results back. Two transports:
+//   * peer memory (default when the shards never grow): CUDA IPC windows
+//     over NVLink, data written locally and read remotely, device flags
+//     between the steps, no host synchronisation (see the transport
+//     section below);
+//   * NCCL grouped send/recv: counts, then keys / scores / value rows, with
+//     one host synchronisation per call to size the receive buffers.
 #include <nccl.h>
 
 #include <algorithm>
