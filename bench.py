@@ -262,7 +262,9 @@ def run_gpu(args):
     lf = local.load_factor()
     log(f"prefill done, load factor {lf:.4f}")
     steps, warm = args.steps, args.warmup
-    finds, inserts, vals = prepare_batches(steps + warm, rank, world, total, device, 1234, cap)
+    n_e2e = min(steps, 20)  # the e2e steps get batches of their own, after the timed ones
+    finds, inserts, vals = prepare_batches(steps + warm + n_e2e, rank, world, total, device,
+                                           1234, cap)
     log("batches ready")
     out_vals = torch.empty((BATCH, DIM), device=device)
     founds = [torch.zeros(BATCH, dtype=torch.bool, device=device) for _ in range(steps + warm)]
@@ -315,7 +317,7 @@ def run_gpu(args):
         tl = torch.tensor([launches], dtype=torch.int64, device=device)
         dist.all_reduce(tl)  # launches of all ranks
         launches = int(tl.item())
-    e2e_line = e2e(table, finds, inserts, vals, warm, min(steps, 20), dist, device)
+    e2e_line = e2e(table, finds, inserts, vals, warm + steps, n_e2e, dist, device)
     log("e2e done")
     local.check_device_error()  # a lock or peer wait that ran out fails the run
     keys_total = 2 * BATCH * steps * world
@@ -383,7 +385,7 @@ def traffic_from_profiles(kernel):
     return None if v is None else v.get("bytes_per_launch")
 
 
-def e2e(table, finds, inserts, vals, warm, steps, dist=None, device=None):
+def e2e(table, finds, inserts, vals, first, steps, dist=None, device=None):
     """Same step through the public API with host buffers: every step copies
     its find keys, insert keys and insert values from pinned host memory,
     runs find + insert_or_assign, and copies the found values and flags back,
@@ -397,9 +399,9 @@ def e2e(table, finds, inserts, vals, warm, steps, dist=None, device=None):
     import torch
 
     world = dist.get_world_size() if dist else 1
-    hk = [f.cpu().pin_memory() for f in finds[warm:warm + steps]]
-    hi = [f.cpu().pin_memory() for f in inserts[warm:warm + steps]]
-    hv = [v.cpu().pin_memory() for v in vals[warm:warm + steps]]
+    hk = [f.cpu().pin_memory() for f in finds[first:first + steps]]
+    hi = [f.cpu().pin_memory() for f in inserts[first:first + steps]]
+    hv = [v.cpu().pin_memory() for v in vals[first:first + steps]]
     out_h = [torch.empty((BATCH, DIM)).pin_memory() for _ in range(2)]
     fnd_h = [torch.empty(BATCH, dtype=torch.bool).pin_memory() for _ in range(2)]
     bufs = [dict(k=torch.empty(BATCH, dtype=torch.int64, device="cuda"),
