@@ -1,7 +1,7 @@
-"""The sharded table on 2 GPUs (one process per GPU), over both transports
-(peer memory and NCCL), gives what one table gives for the concatenation of
-the ranks' batches, and each shard holds only the keys it owns (gpu; skipped
-with fewer than 2 GPUs)."""
+"""The sharded table on every visible GPU (one process per GPU), over both
+transports (peer memory and NCCL), gives what one table gives for the
+concatenation of the ranks' batches, and each shard holds only the keys it
+owns (gpu; skipped with fewer than 2 GPUs)."""
 import os
 import socket
 
@@ -95,13 +95,14 @@ def _rank(rank, world, port, outdir, max_batch):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("transport,max_batch", [("peer", 4096), ("nccl", 0)])
-def test_sharded_two_gpus_match_one_table(tmp_path, transport, max_batch):
+def test_sharded_gpus_match_one_table(tmp_path, transport, max_batch):
+    """One rank per visible GPU (2, 4 or 8)."""
     import sys
 
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import hkv_oracle as O
 
-    world = 2
+    world = min(torch.cuda.device_count(), 8)
     ctx = mp.start_processes(_rank, args=(world, _free_port(), str(tmp_path), max_batch),
                              nprocs=world, join=False, start_method="spawn")
     while not ctx.join(timeout=180):
