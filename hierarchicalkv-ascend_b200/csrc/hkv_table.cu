@@ -15,6 +15,8 @@
 
 #include "hkv_dedup.cuh"
 #include "hkv_kernels.cuh"
+#include <cstdio>
+
 #include "hkv_table.cuh"
 
 namespace hkvb {
@@ -725,6 +727,88 @@ void TableImpl::export_batch(size_t n, size_t offset, uint64_t* d_counter,
 }
 
 // ---------------------------------------------------------------------------
+// save / load, reference hkv_hashtable.h:3021-3195
+// ---------------------------------------------------------------------------
+namespace {
+// pinned host staging for one chunk of tuples: keys | scores | values
+struct HostChunk {
+  uint8_t* p = nullptr;
+  explicit HostChunk(size_t bytes) {
+    CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&p), std::max<size_t>(bytes, 1),
+                           cudaHostAllocDefault));
+  }
+  ~HostChunk() { cudaFreeHost(p); }
+};
+}  // namespace
+
+size_t TableImpl::save(hkv_kv_write_fn write, void* user, size_t max_ws,
+                       cudaStream_t s) {
+  const size_t tuple = 8 + 8 + value_bytes_;
+  HKV_REQUIRE(max_ws >= tuple, HKV_ERR_INVALID,
+              "[HierarchicalKV] max_workspace_size is smaller than a single "
+              "`key + score + value` tuple! Please set a larger value!");
+  const size_t total = capacity_;
+  const size_t n = std::min(max_ws / tuple, total);
+  HostChunk h(n * tuple);
+  uint64_t* hk = reinterpret_cast<uint64_t*>(h.p);
+  uint64_t* hs = hk + n;
+  uint8_t* hv = reinterpret_cast<uint8_t*>(hs + n);
+  Workspace ws(s, pool_);
+  uint64_t* dcount = ws.get<uint64_t>(1);
+  uint64_t* dk = ws.get<uint64_t>(n);
+  uint64_t* dsc = ws.get<uint64_t>(n);
+  uint8_t* dv = ws.get<uint8_t>(n * value_bytes_);
+  size_t saved = 0;
+  for (size_t i = 0; i < total; i += n) {
+    export_batch(std::min(total - i, n), i, dcount, dk, dv, dsc, s);
+    uint64_t c = 0;
+    CUDA_TRY(cudaMemcpyAsync(&c, dcount, 8, cudaMemcpyDeviceToHost, s));
+    CUDA_TRY(cudaStreamSynchronize(s));
+    if (c == 0) continue;
+    CUDA_TRY(cudaMemcpyAsync(hk, dk, c * 8, cudaMemcpyDeviceToHost, s));
+    CUDA_TRY(cudaMemcpyAsync(hs, dsc, c * 8, cudaMemcpyDeviceToHost, s));
+    CUDA_TRY(cudaMemcpyAsync(hv, dv, c * value_bytes_, cudaMemcpyDeviceToHost, s));
+    CUDA_TRY(cudaStreamSynchronize(s));
+    write(user, c, opt_.dim, hk, hv, hs);
+    saved += c;
+  }
+  return saved;
+}
+
+size_t TableImpl::load(hkv_kv_read_fn read, void* user, size_t max_ws,
+                       cudaStream_t s) {
+  const size_t tuple = 8 + 8 + value_bytes_;
+  HKV_REQUIRE(max_ws >= tuple, HKV_ERR_INVALID,
+              "[HierarchicalKV] max_workspace_size is smaller than a single "
+              "`key + score + value` tuple! Please set a larger value!");
+  const size_t n = max_ws / tuple;
+  HostChunk h(n * tuple);
+  uint64_t* hk = reinterpret_cast<uint64_t*>(h.p);
+  uint64_t* hs = hk + n;
+  uint8_t* hv = reinterpret_cast<uint8_t*>(hs + n);
+  size_t c = read(user, n, opt_.dim, hk, hv, hs);
+  if (c == 0) return 0;
+  Workspace ws(s, pool_);
+  uint64_t* dk = ws.get<uint64_t>(n);
+  uint64_t* dsc = ws.get<uint64_t>(n);
+  uint8_t* dv = ws.get<uint8_t>(n * value_bytes_);
+  size_t loaded = 0;
+  do {
+    c = std::min(c, n);
+    CUDA_TRY(cudaMemcpyAsync(dk, hk, c * 8, cudaMemcpyHostToDevice, s));
+    CUDA_TRY(cudaMemcpyAsync(dsc, hs, c * 8, cudaMemcpyHostToDevice, s));
+    CUDA_TRY(cudaMemcpyAsync(dv, hv, c * value_bytes_, cudaMemcpyHostToDevice, s));
+    // the reference sets the epoch to IGNORED_GLOBAL_EPOCH and leaves it there
+    epoch_ = kIgnoredEpoch;
+    insert_or_assign(c, dk, dv, dsc, s, true, true);
+    loaded += c;
+    CUDA_TRY(cudaStreamSynchronize(s));
+    c = read(user, n, opt_.dim, hk, hv, hs);
+  } while (c > 0);
+  return loaded;
+}
+
+// ---------------------------------------------------------------------------
 // reserve, reference hkv_hashtable.h:2873-2935 and table.h:360-377
 // ---------------------------------------------------------------------------
 void TableImpl::double_capacity(cudaStream_t s) {
@@ -1228,6 +1312,92 @@ int hkv_export_batch_count(hkv_table* table, size_t n, size_t offset,
   CUDA_TRY(cudaFreeAsync(d, s));
   CUDA_TRY(cudaStreamSynchronize(s));
   *h_count = h;
+  HKV_API_END
+}
+
+int hkv_save(hkv_table* table, hkv_kv_write_fn write, void* user,
+             size_t max_workspace_size, void* stream, size_t* out_count) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  HKV_REQUIRE(write != nullptr && out_count != nullptr, HKV_ERR_INVALID,
+              "null argument");
+  *out_count = T->save(write, user, max_workspace_size, as_stream(stream));
+  HKV_API_END
+}
+
+int hkv_load(hkv_table* table, hkv_kv_read_fn read, void* user,
+             size_t max_workspace_size, void* stream, size_t* out_count) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  HKV_REQUIRE(read != nullptr && out_count != nullptr, HKV_ERR_INVALID,
+              "null argument");
+  *out_count = T->load(read, user, max_workspace_size, as_stream(stream));
+  HKV_API_END
+}
+
+namespace {
+// LocalKVFile (reference types.h:349-464): three stdio streams.
+struct KVFiles {
+  FILE* f[3] = {nullptr, nullptr, nullptr};
+  size_t kb, vb;  // key bytes, value bytes per element
+  ~KVFiles() {
+    for (FILE* x : f)
+      if (x) std::fclose(x);
+  }
+  bool open(const char* k, const char* v, const char* sc, const char* mode) {
+    f[0] = std::fopen(k, mode);
+    f[1] = f[0] ? std::fopen(v, mode) : nullptr;
+    f[2] = f[1] ? std::fopen(sc, mode) : nullptr;
+    return f[2] != nullptr;
+  }
+  static size_t write(void* u, size_t n, size_t dim, const void* keys,
+                      const void* values, const uint64_t* scores) {
+    auto* F = static_cast<KVFiles*>(u);
+    const size_t a = std::fwrite(keys, F->kb, n, F->f[0]);
+    const size_t b = std::fwrite(values, F->vb * dim, n, F->f[1]);
+    const size_t c = std::fwrite(scores, sizeof(uint64_t), n, F->f[2]);
+    return (a == b && a == c) ? a : 0;
+  }
+  static size_t read(void* u, size_t n, size_t dim, void* keys, void* values,
+                     uint64_t* scores) {
+    auto* F = static_cast<KVFiles*>(u);
+    const size_t a = std::fread(keys, F->kb, n, F->f[0]);
+    const size_t b = std::fread(values, F->vb * dim, n, F->f[1]);
+    const size_t c = std::fread(scores, sizeof(uint64_t), n, F->f[2]);
+    return (a == b && a == c) ? a : 0;
+  }
+};
+}  // namespace
+
+int hkv_save_files(hkv_table* table, const char* keys_path,
+                   const char* values_path, const char* scores_path,
+                   size_t max_workspace_size, void* stream, size_t* out_count) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  HKV_REQUIRE(keys_path && values_path && scores_path && out_count,
+              HKV_ERR_INVALID, "null argument");
+  KVFiles F;
+  F.kb = 8;
+  F.vb = T->value_bytes() / T->dim();
+  HKV_REQUIRE(F.open(keys_path, values_path, scores_path, "wb"), HKV_ERR_RUNTIME,
+              "cannot open the key, value or score file for writing");
+  *out_count = T->save(&KVFiles::write, &F, max_workspace_size, as_stream(stream));
+  HKV_API_END
+}
+
+int hkv_load_files(hkv_table* table, const char* keys_path,
+                   const char* values_path, const char* scores_path,
+                   size_t max_workspace_size, void* stream, size_t* out_count) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  HKV_REQUIRE(keys_path && values_path && scores_path && out_count,
+              HKV_ERR_INVALID, "null argument");
+  KVFiles F;
+  F.kb = 8;
+  F.vb = T->value_bytes() / T->dim();
+  HKV_REQUIRE(F.open(keys_path, values_path, scores_path, "rb"), HKV_ERR_RUNTIME,
+              "cannot open the key, value or score file for reading");
+  *out_count = T->load(&KVFiles::read, &F, max_workspace_size, as_stream(stream));
   HKV_API_END
 }
 

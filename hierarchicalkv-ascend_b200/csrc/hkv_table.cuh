@@ -127,6 +127,9 @@ class TableImpl {
   float load_factor(cudaStream_t s);
   void reserve(size_t new_capacity, cudaStream_t s);
   void check_device_error(cudaStream_t s);
+  // save / load through BaseKVFile-style callbacks (synchronous)
+  size_t save(hkv_kv_write_fn write, void* user, size_t max_ws, cudaStream_t s);
+  size_t load(hkv_kv_read_fn read, void* user, size_t max_ws, cudaStream_t s);
   void get_state(uint64_t* keys, uint64_t* scores, uint8_t* digests,
                  int32_t* sizes, uint8_t* values);
   void set_state(const uint64_t* keys, const uint64_t* scores,

@@ -147,6 +147,12 @@ SIGNATURES = {
     "hkv_set_global_epoch": (ctypes.c_int, [_P, _U64]),
     "hkv_check_device_error": (ctypes.c_int, [_P, _P]),
     "hkv_kernel_launches": (ctypes.c_int, [ctypes.POINTER(_U64)]),
+    "hkv_save_files": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_char_p,
+                                      ctypes.c_char_p, _SZ, _P, ctypes.POINTER(_SZ)]),
+    "hkv_load_files": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_char_p,
+                                      ctypes.c_char_p, _SZ, _P, ctypes.POINTER(_SZ)]),
+    "hkv_save": (ctypes.c_int, [_P, _P, _P, _SZ, _P, ctypes.POINTER(_SZ)]),
+    "hkv_load": (ctypes.c_int, [_P, _P, _P, _SZ, _P, ctypes.POINTER(_SZ)]),
     "hkv_debug_get_state": (ctypes.c_int, [_P, _P, _P, _P, _P, _P]),
     "hkv_debug_set_state": (ctypes.c_int, [_P, _P, _P, _P, _P, _P]),
     "hkv_nccl_unique_id": (ctypes.c_int, [_P]),
@@ -337,6 +343,25 @@ class HashTable:
     def find(self, n, keys, values, founds, scores=None, stream=None):
         _check(lib().hkv_find(self._h, n, _ptr(keys), _ptr(values),
                               _ptr(founds), _ptr(scores), _stream(stream)))
+
+    def save(self, keys_path, values_path, scores_path,
+             max_workspace_size=1 << 20, stream=None) -> int:
+        """save() into the reference's LocalKVFile format (three raw binary
+        files: keys, value rows, scores). Returns the number of tuples."""
+        out = _SZ(0)
+        _check(lib().hkv_save_files(self._h, str(keys_path).encode(),
+                                    str(values_path).encode(), str(scores_path).encode(),
+                                    max_workspace_size, _stream(stream), ctypes.byref(out)))
+        return out.value
+
+    def load(self, keys_path, values_path, scores_path,
+             max_workspace_size=1 << 20, stream=None) -> int:
+        """load() from the LocalKVFile format. Returns the number of tuples."""
+        out = _SZ(0)
+        _check(lib().hkv_load_files(self._h, str(keys_path).encode(),
+                                    str(values_path).encode(), str(scores_path).encode(),
+                                    max_workspace_size, _stream(stream), ctypes.byref(out)))
+        return out.value
 
     def contains(self, n, keys, founds, stream=None):
         _check(lib().hkv_contains(self._h, n, _ptr(keys), _ptr(founds),

@@ -181,6 +181,40 @@ int hkv_reserve(hkv_table* table, size_t new_capacity, void* stream);
 /* set_global_epoch, hkv_hashtable.h:3197. */
 int hkv_set_global_epoch(hkv_table* table, uint64_t epoch);
 
+/* ---- save / load, hkv_hashtable.h:3021-3195 --------------------------------
+ * The reference takes a BaseKVFile (types.h:291-334) whose read/write move
+ * n (key, vector, score) tuples between host buffers and a file. Here that
+ * object is a pair of callbacks on HOST buffers, returning the number of
+ * tuples moved. Both functions synchronise `stream`. */
+typedef size_t (*hkv_kv_write_fn)(void* user, size_t n, size_t dim,
+                                  const void* keys, const void* values,
+                                  const uint64_t* scores);
+typedef size_t (*hkv_kv_read_fn)(void* user, size_t n, size_t dim, void* keys,
+                                 void* values, uint64_t* scores);
+
+/* save, hkv_hashtable.h:3021-3112: walks the slots in chunks of
+ * max_workspace_size / (sizeof key + sizeof score + dim * sizeof value)
+ * tuples (the export of each chunk), hands each chunk to `write`. */
+int hkv_save(hkv_table* table, hkv_kv_write_fn write, void* user,
+             size_t max_workspace_size, void* stream, size_t* out_count);
+
+/* load, hkv_hashtable.h:3125-3195: reads chunks of the same size with `read`
+ * until it returns 0 and inserts each with insert_or_assign(unique_key =
+ * true, ignore_evict_strategy = true) after setting the global epoch to
+ * IGNORED_GLOBAL_EPOCH (which it stays at, as in the reference). */
+int hkv_load(hkv_table* table, hkv_kv_read_fn read, void* user,
+             size_t max_workspace_size, void* stream, size_t* out_count);
+
+/* save / load through the reference's LocalKVFile format (types.h:349-464):
+ * three files of raw keys, raw value rows and raw uint64 scores, written
+ * ("wb") or read ("rb") in the same order. */
+int hkv_save_files(hkv_table* table, const char* keys_path,
+                   const char* values_path, const char* scores_path,
+                   size_t max_workspace_size, void* stream, size_t* out_count);
+int hkv_load_files(hkv_table* table, const char* keys_path,
+                   const char* values_path, const char* scores_path,
+                   size_t max_workspace_size, void* stream, size_t* out_count);
+
 /* No reference counterpart. find_or_insert for a batch that may repeat
  * keys (as with unique_key = false) that allocates no device memory, for
  * callers that cannot call cudaMalloc while serving, such as a service whose

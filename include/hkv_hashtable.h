@@ -23,6 +23,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <cstdio>
 #include <stdexcept>
 #include <string>
 #include <type_traits>
@@ -103,6 +104,60 @@ constexpr int value_code() {
 }
 inline void* st(cudaStream_t s) { return reinterpret_cast<void*>(s); }
 }  // namespace detail
+
+/* BaseKVFile / LocalKVFile, reference types.h:291-464: save() and load()
+ * move (key, vector, score) tuples between the table and a file through
+ * these. LocalKVFile keeps the reference's on-disk format: three files of
+ * raw keys, raw vectors and raw scores in the same order. */
+template <class K, class V, class S>
+class BaseKVFile {
+ public:
+  virtual ~BaseKVFile() {}
+  virtual size_t read(const size_t n, const size_t dim, K* keys, V* vectors,
+                      S* scores) = 0;
+  virtual size_t write(const size_t n, const size_t dim, const K* keys,
+                       const V* vectors, const S* scores) = 0;
+};
+
+template <class K, class V, class S>
+class LocalKVFile : public BaseKVFile<K, V, S> {
+ public:
+  LocalKVFile() = default;
+  ~LocalKVFile() { close(); }
+  bool open(const std::string& keys_path, const std::string& values_path,
+            const std::string& scores_path, const char* mode) {
+    close();
+    fp_[0] = std::fopen(keys_path.c_str(), mode);
+    fp_[1] = fp_[0] ? std::fopen(values_path.c_str(), mode) : nullptr;
+    fp_[2] = fp_[1] ? std::fopen(scores_path.c_str(), mode) : nullptr;
+    if (!fp_[2]) close();
+    return fp_[2] != nullptr;
+  }
+  void close() noexcept {
+    for (auto& f : fp_)
+      if (f) {
+        std::fclose(f);
+        f = nullptr;
+      }
+  }
+  size_t read(const size_t n, const size_t dim, K* keys, V* vectors,
+              S* scores) override {
+    const size_t a = std::fread(keys, sizeof(K), n, fp_[0]);
+    const size_t b = std::fread(vectors, sizeof(V) * dim, n, fp_[1]);
+    const size_t c = std::fread(scores, sizeof(S), n, fp_[2]);
+    return (a == b && a == c) ? a : 0;
+  }
+  size_t write(const size_t n, const size_t dim, const K* keys,
+               const V* vectors, const S* scores) override {
+    const size_t a = std::fwrite(keys, sizeof(K), n, fp_[0]);
+    const size_t b = std::fwrite(vectors, sizeof(V) * dim, n, fp_[1]);
+    const size_t c = std::fwrite(scores, sizeof(S), n, fp_[2]);
+    return (a == b && a == c) ? a : 0;
+  }
+
+ private:
+  std::FILE* fp_[3] = {nullptr, nullptr, nullptr};
+};
 
 /* HashTable<K, V, S, Strategy>, reference hkv_hashtable.h:895-3485.
  * K: uint64_t or int64_t; S: uint64_t; V: the element type of the vectors
@@ -312,6 +367,24 @@ class HashTable {
     return b;
   }
 
+  /* save / load, reference hkv_hashtable.h:3021-3195 (synchronous). */
+  size_type save(BaseKVFile<K, V, S>* file,
+                 const size_t max_workspace_size = 1L * 1024 * 1024,
+                 cudaStream_t stream = 0) const {
+    size_t n = 0;
+    detail::check(hkv_save(t_, &write_trampoline, file, max_workspace_size,
+                           detail::st(stream), &n));
+    return n;
+  }
+  size_type load(BaseKVFile<K, V, S>* file,
+                 const size_t max_workspace_size = 1L * 1024 * 1024,
+                 cudaStream_t stream = 0) {
+    size_t n = 0;
+    detail::check(hkv_load(t_, &read_trampoline, file, max_workspace_size,
+                           detail::st(stream), &n));
+    return n;
+  }
+
   void set_global_epoch(const uint64_t epoch) {
     detail::check(hkv_set_global_epoch(t_, epoch));
   }
@@ -324,6 +397,16 @@ class HashTable {
   hkv_table* handle() const noexcept { return t_; }
 
  private:
+  static size_t write_trampoline(void* u, size_t n, size_t dim, const void* k,
+                                 const void* v, const uint64_t* sc) {
+    return static_cast<BaseKVFile<K, V, S>*>(u)->write(
+        n, dim, static_cast<const K*>(k), static_cast<const V*>(v), sc);
+  }
+  static size_t read_trampoline(void* u, size_t n, size_t dim, void* k, void* v,
+                                uint64_t* sc) {
+    return static_cast<BaseKVFile<K, V, S>*>(u)->read(
+        n, dim, static_cast<K*>(k), static_cast<V*>(v), sc);
+  }
   hkv_table* t_ = nullptr;
   HashTableOptions options_;
 };

@@ -244,6 +244,20 @@ class OracleTable:
         c = L.hkvo_export_batch(self.h, n, offset, _p(keys), _p(values), _p(scores))
         return keys[:c], values[:c], scores[:c]
 
+    def load_chunks(self, keys, values, scores, max_workspace_size=1 << 20):
+        """The reference's load (hkv_hashtable.h:3125-3195) on tuples already
+        read from a file: chunks of max_workspace_size // (16 + value row
+        bytes) tuples, each inserted with insert_or_assign(unique_key=true,
+        ignore_evict_strategy=true) after setting the global epoch to
+        IGNORED_GLOBAL_EPOCH."""
+        tuple_bytes = 16 + self.dim * self.vdt.itemsize
+        n = max_workspace_size // tuple_bytes
+        for s in range(0, len(keys), n):
+            self.set_global_epoch(0xFFFFFFFFFFFFFFFF)
+            self.insert_or_assign(keys[s:s + n], values[s:s + n], scores[s:s + n],
+                                  ignore=True)
+        return len(keys)
+
     def reserve(self, new_capacity):
         L.hkvo_reserve(self.h, new_capacity)
 

@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <string>
 #include <vector>
 
 #include "hkv_hashtable.h"
@@ -32,7 +33,7 @@ using S = uint64_t;
     }                                                              \
   } while (0)
 
-int main() {
+int main(int argc, char** argv) {
   constexpr size_t dim = 16, n = 4096;
   HashTableOptions options;
   options.init_capacity = 128 * 256;
@@ -94,6 +95,28 @@ int main() {
     threw = true;
   }
   EXPECT(threw);
+  // save to the LocalKVFile format, load into a second table (reference
+  // hkv_hashtable.h:3021-3195; small workspace: several chunks)
+  const std::string base = std::string(argc > 1 ? argv[1] : "/tmp") + "/dropin";
+  {
+    LocalKVFile<K, V, S> f;
+    EXPECT(f.open(base + "_keys", base + "_values", base + "_scores", "wb"));
+    EXPECT(table.save(&f, 64 * 1024) == n);
+  }
+  HashTable<K, V, S, EvictStrategy::kLfu> copy;
+  copy.init(options);
+  {
+    LocalKVFile<K, V, S> f;
+    EXPECT(f.open(base + "_keys", base + "_values", base + "_scores", "rb"));
+    EXPECT(copy.load(&f, 64 * 1024) == n);
+  }
+  EXPECT(copy.size() == n);
+  copy.find(n, dk, dv, df, out_s);
+  CK(cudaDeviceSynchronize());
+  CK(cudaMemcpy(got.data(), out_s, n * sizeof(S), cudaMemcpyDeviceToHost));
+  CK(cudaMemcpy(found.data(), df, n * sizeof(bool), cudaMemcpyDeviceToHost));
+  for (size_t i = 0; i < n; i++) EXPECT(found[i] && got[i] == 2 * hs[i]);
+
   table.erase(n / 2, dk);
   EXPECT(table.size() == n - n / 2);
   table.clear();

@@ -28,6 +28,6 @@ def test_cpp_mirror_compiles_and_links(tmp_path):
 def test_cpp_mirror_runs(tmp_path):
     exe = str(tmp_path / "dropin")
     build(exe)
-    r = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    r = subprocess.run([exe, str(tmp_path)], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "cpp drop-in ok" in r.stdout
