@@ -365,6 +365,9 @@ def run_gpu(args):
         result["clocks"] = clocks
         result["gpu_launches"] = launches
         result["e2e"] = e2e_line
+        if world == 1 and args.save_load:
+            result["save_load"] = save_load_times(device)
+            log("save/load done")
         if world == 1:
             if not args.no_cpu_baseline:
                 result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
@@ -457,6 +460,48 @@ def e2e(table, finds, inserts, vals, first, steps, dist=None, device=None):
     return {"value": round(2 * BATCH * steps * world / (ms * 1e-3) / 1e9, 4), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
             "pipelined": "H2D / table calls / D2H on three streams, two buffer sets"}
+
+
+def save_load_times(device, capacity=8 << 20):
+    """save() and load() of a full table through the LocalKVFile format (three
+    raw files in a temporary directory), host wall time around each call
+    (both synchronise)."""
+    import shutil
+    import tempfile
+
+    import torch
+
+    import hkv_b200 as H
+
+    opts = H.HashTableOptions(init_capacity=capacity, max_capacity=capacity,
+                              max_hbm_for_vectors=capacity * VALUE_BYTES * 2, dim=DIM,
+                              max_load_factor=1.0)
+    src = H.HashTable(H.EvictStrategy.kLru)
+    src.init(opts)
+    vals = torch.rand((4 << 20, DIM), device=device)
+    for start in range(0, capacity, 4 << 20):
+        src.insert_or_assign(4 << 20, keys_from_counters(start, 4 << 20, device), vals)
+    torch.cuda.synchronize()
+    n_live = src.size()
+    d = tempfile.mkdtemp(prefix="hkv_save_")
+    try:
+        paths = [os.path.join(d, x) for x in ("keys", "values", "scores")]
+        t0 = time.perf_counter()
+        n_saved = src.save(*paths, max_workspace_size=64 << 20)
+        t_save = time.perf_counter() - t0
+        dst = H.HashTable(H.EvictStrategy.kLru)
+        dst.init(opts)
+        t0 = time.perf_counter()
+        n_loaded = dst.load(*paths, max_workspace_size=64 << 20)
+        t_load = time.perf_counter() - t0
+        ok = n_saved == n_loaded == n_live == dst.size()
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+    tb = 16 + VALUE_BYTES
+    return {"tuples": n_saved, "tuple_bytes": tb, "workspace_bytes": 64 << 20,
+            "save_s": round(t_save, 3), "load_s": round(t_load, 3),
+            "save_gbs": round(n_saved * tb / t_save / 1e9, 3),
+            "load_gbs": round(n_loaded * tb / t_load / 1e9, 3), "counts_match": ok}
 
 
 # --------------------------------------------------------------------------
@@ -576,6 +621,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--save-load", action="store_true",
+                    help="also time save/load (LocalKVFile files in a temporary "
+                         "directory) of an 8 Mi-slot table; adds a save_load key")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--capacity", type=int, default=CAPACITY,
                     help="slots per GPU (diagnostics; the metric uses the default)")
