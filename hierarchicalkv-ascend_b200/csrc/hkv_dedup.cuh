@@ -284,4 +284,24 @@ __global__ void expand_status_kernel(const uint8_t* __restrict__ ustatus,
   }
 }
 
+// find_or_insert* with repeated keys: every occurrence gets its
+// representative's row address; the first occurrence reports whether the
+// key was there before, later ones find it if the first got a slot.
+__global__ void scatter_ptrs_kernel(uint8_t** __restrict__ value_ptrs,
+                                    bool* __restrict__ founds,
+                                    uint8_t* const* __restrict__ uptrs,
+                                    const bool* __restrict__ ufound,
+                                    const uint32_t* __restrict__ uid_of,
+                                    const uint32_t* __restrict__ rep_first,
+                                    uint64_t n) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t u = uid_of[i];
+    uint8_t* p = u != 0xFFFFFFFFu ? uptrs[u] : nullptr;
+    value_ptrs[i] = p;
+    if (founds != nullptr)
+      founds[i] = u != 0xFFFFFFFFu && (rep_first[u] == i ? ufound[u] : p != nullptr);
+  }
+}
+
 }  // namespace hkvb

@@ -60,7 +60,8 @@ struct FindSegments {
 enum UpsertMode : int {
   kModeInsertOrAssign = 0,
   kModeFindOrInsert = 1,
-  kModeInsertAndEvict = 2
+  kModeInsertAndEvict = 2,
+  kModeFindOrInsertPtr = 3  // find_or_insert* : row addresses, no value copy
 };
 
 constexpr int kErrSpinTimeout = 1;

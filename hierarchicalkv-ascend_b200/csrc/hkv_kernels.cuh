@@ -214,6 +214,27 @@ __global__ void __launch_bounds__(256, HKV_FIND_MIN_BLOCKS)
   }
 }
 
+// find* (reference find_ptr_with_digest_kernel.h:33-160): the address of
+// each found key's value row (and its score), nullptr for a missed key.
+__global__ void __launch_bounds__(256, HKV_FIND_MIN_BLOCKS)
+    find_ptr_kernel(TableView t, const uint64_t* __restrict__ keys,
+                    uint8_t** __restrict__ value_ptrs, bool* __restrict__ founds,
+                    uint64_t* __restrict__ scores, uint64_t n) {
+  constexpr uint32_t W = kFindTile;
+  const TileW<W> tile;
+  const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / W);
+  for (uint64_t i = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / W; i < n;
+       i += ntiles) {
+    uint64_t bkt;
+    const int p = find_probe(t, tile, __ldg(keys + i), bkt);
+    if (tile.lane == 0) {
+      value_ptrs[i] = p >= 0 ? value_ptr(t, bkt, p) : nullptr;
+      if (founds != nullptr) founds[i] = p >= 0;
+      if (p >= 0 && scores != nullptr) scores[i] = __ldg(t.scores + bkt * kBucket + p);
+    }
+  }
+}
+
 // find over several key arrays at once (segment s has counts[s] keys, at
 // most `bound`): the tiles walk an interleaved index v -> (segment v % nseg,
 // key v / nseg), so every segment is in flight at the same time.
@@ -275,6 +296,8 @@ struct UpsertArgs {
   uint32_t status_stride;    // bytes between two keys' codes (0 means 1)
   const uint32_t* dn;        // optional device-side key count (overrides n)
   int report_refused;        // insert_and_evict: report refused inputs
+  uint8_t** value_ptrs;      // find_or_insert*: address of each key's row
+  bool* founds;              // find_or_insert*: the key was already there
 };
 
 // ---------------------------------------------------------------------------
@@ -431,6 +454,14 @@ __device__ __forceinline__ void upsert_locked(const TableView& t,
     }
   }
   uint8_t* row = value_ptr(t, l.bkt, slot);
+  if constexpr (Mode == kModeFindOrInsertPtr) {
+    // the caller reads or writes the row through its address
+    // (find_or_insert_ptr_kernel_v2.h:275-286)
+    if (tile.lane == 0) {
+      a.value_ptrs[i] = row;
+      if (a.founds != nullptr) a.founds[i] = res == kDuplicate;
+    }
+  }
   if constexpr (Mode == kModeInsertAndEvict) {
     if (res == kEvict) {
       ev_idx = tile.shfl(ev_idx, 0);
@@ -442,7 +473,7 @@ __device__ __forceinline__ void upsert_locked(const TableView& t,
       copy_row<VW>(a.values_io + i * vb, row, vb, tile.lane, W);
     else
       head.store(row, a.values_io + i * vb, nv, tile.lane);
-  } else {
+  } else if constexpr (Mode != kModeFindOrInsertPtr) {
     head.store(row, a.values_in + i * vb, nv, tile.lane);
   }
   tile.sync();
@@ -640,7 +671,7 @@ __global__ void __launch_bounds__(256, HKV_UPSERT_MIN_BLOCKS)
       key = next;
       if (i + stride < n) next = a.keys[i + stride];
       if (!is_reserved(key)) {
-        head.load(in_rows + i * vb, nv, tile.lane);
+        if constexpr (Mode != kModeFindOrInsertPtr) head.load(in_rows + i * vb, nv, tile.lane);
         desired = desired_when_missed<S>(a.scores, i, a.epoch, clk);
         l = locate(t, key);
         todo = true;
@@ -668,6 +699,14 @@ __global__ void __launch_bounds__(256, HKV_UPSERT_MIN_BLOCKS)
     if (i < n) {
       if (a.status != nullptr && tile.lane == 0)
         a.status[i * (a.status_stride ? a.status_stride : 1)] = res;
+      if constexpr (Mode == kModeFindOrInsertPtr) {
+        // refused, reserved or timed-out keys get no address
+        if (tile.lane == 0 && res != kDuplicate && res != kOccupiedEmpty &&
+            res != kOccupiedReclaimed && res != kEvict) {
+          a.value_ptrs[i] = nullptr;
+          if (a.founds != nullptr) a.founds[i] = false;
+        }
+      }
       if constexpr (Mode == kModeInsertAndEvict) {
         if (res == kRefused && a.report_refused) {
           // reference insert_and_evict_kernel.h:553-557, :675-683: the

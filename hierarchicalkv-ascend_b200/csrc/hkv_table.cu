@@ -412,7 +412,8 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
                        uint8_t* ev_values, uint64_t* ev_scores,
                        uint64_t* d_counter, cudaStream_t s, bool unique,
                        bool ignore, uint8_t* status, const uint32_t* dn,
-                       uint32_t status_stride) {
+                       uint32_t status_stride, uint8_t** value_ptrs,
+                       bool* founds) {
   const int st = ignore ? kCustomized : strategy_;
   const TableView v = view();
   UpsertArgs a;
@@ -425,6 +426,8 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
   a.report_refused = 1;
   a.status = status;
   a.status_stride = status_stride;
+  a.value_ptrs = value_ptrs;
+  a.founds = founds;
   const uint8_t* rows = mode == kModeFindOrInsert ? values_io : values_in;
 
   if (unique) {
@@ -441,9 +444,37 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
         upsert_kernel<kModeInsertOrAssign, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
       else if (mode == kModeFindOrInsert)
         upsert_kernel<kModeFindOrInsert, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
+      else if (mode == kModeFindOrInsertPtr)
+        upsert_kernel<kModeFindOrInsertPtr, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
       else
         upsert_kernel<kModeInsertAndEvict, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
     }));
+    CUDA_TRY(cudaGetLastError());
+    return;
+  }
+
+  if (mode == kModeFindOrInsertPtr) {
+    // repeated keys: the representatives get addresses, every occurrence
+    // then takes its representative's
+    Workspace ws(s, pool_);
+    const DedupResult d = dedup_batch(n, keys, scores, st, ws, s, sm_count_, d_error_);
+    uint8_t** uptrs = ws.get<uint8_t*>(n);
+    bool* ufound = ws.get<bool>(n);
+    a.keys = d.ukeys;
+    a.scores = d.uscores;
+    a.n = n;
+    a.dn = d.dm;
+    a.value_ptrs = uptrs;
+    a.founds = ufound;
+    const int grid = upsert_grid(n);
+    DISPATCH_STRATEGY(st, {
+      upsert_kernel<kModeFindOrInsertPtr, S, 16><<<grid, 256, 0, counted(s)>>>(v, a);
+    });
+    CUDA_TRY(cudaGetLastError());
+    scatter_ptrs_kernel<<<static_cast<int>(std::min<uint64_t>(ceil_div(n, 256),
+                                                             sm_count_ * 32ull)),
+                          256, 0, counted(s)>>>(value_ptrs, founds, uptrs, ufound,
+                                                d.uid_of, d.rep_first, n);
     CUDA_TRY(cudaGetLastError());
     return;
   }
@@ -654,6 +685,31 @@ void TableImpl::find(size_t n, const uint64_t* keys, uint8_t* values,
   DISPATCH_VW(vw, find_kernel<VW><<<find_grid(n), 256, 0, counted(s)>>>(
                       v, keys, values, founds, scores, n, nullptr, nullptr));
   CUDA_TRY(cudaGetLastError());
+}
+
+void TableImpl::find_ptr(size_t n, const uint64_t* keys, uint8_t** value_ptrs,
+                         bool* founds, uint64_t* scores, cudaStream_t s) {
+  if (n == 0) return;
+  // reference find_ptr_with_digest_kernel.h:21-23: null keys or outputs ->
+  // nothing written
+  if (keys == nullptr || value_ptrs == nullptr) return;
+  find_ptr_kernel<<<find_grid(n), 256, 0, counted(s)>>>(view(), keys, value_ptrs,
+                                                        founds, scores, n);
+  CUDA_TRY(cudaGetLastError());
+}
+
+void TableImpl::find_or_insert_ptr(size_t n, const uint64_t* keys,
+                                   uint8_t** value_ptrs, bool* founds,
+                                   const uint64_t* scores, cudaStream_t s,
+                                   bool unique, bool ignore) {
+  if (n == 0) return;
+  auto_grow(n, s);
+  if (!ignore) check_strategy(scores, false);
+  HKV_REQUIRE(keys != nullptr && value_ptrs != nullptr && founds != nullptr,
+              HKV_ERR_INVALID, "keys, values and founds must not be null");
+  upsert(kModeFindOrInsertPtr, n, keys, nullptr, nullptr, scores, nullptr,
+         nullptr, nullptr, nullptr, s, unique, ignore, nullptr, nullptr, 1,
+         value_ptrs, founds);
 }
 
 void TableImpl::find_segments(const FindSegments& seg, uint32_t nseg,
@@ -1312,6 +1368,29 @@ int hkv_export_batch_count(hkv_table* table, size_t n, size_t offset,
   CUDA_TRY(cudaFreeAsync(d, s));
   CUDA_TRY(cudaStreamSynchronize(s));
   *h_count = h;
+  HKV_API_END
+}
+
+int hkv_find_ptr(hkv_table* table, size_t n, const void* keys, void** values,
+                 bool* founds, uint64_t* scores, void* stream) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  T->find_ptr(n, static_cast<const uint64_t*>(keys),
+              reinterpret_cast<uint8_t**>(values), founds, scores, as_stream(stream));
+  HKV_API_END
+}
+
+int hkv_find_or_insert_ptr(hkv_table* table, size_t n, const void* keys,
+                           void** values, bool* founds, const uint64_t* scores,
+                           void* stream, bool unique_key,
+                           bool ignore_evict_strategy, void** locked_key_ptrs) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  HKV_REQUIRE(locked_key_ptrs == nullptr, HKV_ERR_UNSUPPORTED,
+              "locked_key_ptrs (keys left locked after the call) is not supported");
+  T->find_or_insert_ptr(n, static_cast<const uint64_t*>(keys),
+                        reinterpret_cast<uint8_t**>(values), founds, scores,
+                        as_stream(stream), unique_key, ignore_evict_strategy);
   HKV_API_END
 }
 

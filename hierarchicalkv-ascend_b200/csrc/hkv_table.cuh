@@ -117,6 +117,12 @@ class TableImpl {
                       const uint64_t* keys, const uint8_t* values_in,
                       uint8_t* values_io, const uint64_t* scores,
                       uint8_t* status, uint32_t status_stride, cudaStream_t s);
+  // find* / find_or_insert*: addresses of the value rows instead of copies
+  void find_ptr(size_t n, const uint64_t* keys, uint8_t** value_ptrs, bool* founds,
+                uint64_t* scores, cudaStream_t s);
+  void find_or_insert_ptr(size_t n, const uint64_t* keys, uint8_t** value_ptrs,
+                          bool* founds, const uint64_t* scores, cudaStream_t s,
+                          bool unique, bool ignore);
   void contains(size_t n, const uint64_t* keys, bool* founds, cudaStream_t s);
   void erase(size_t n, const uint64_t* keys, cudaStream_t s);
   void clear(cudaStream_t s);
@@ -181,7 +187,8 @@ class TableImpl {
               const uint64_t* scores, uint64_t* ev_keys, uint8_t* ev_values,
               uint64_t* ev_scores, uint64_t* d_counter, cudaStream_t s,
               bool unique, bool ignore, uint8_t* status,
-              const uint32_t* dn = nullptr, uint32_t status_stride = 1);
+              const uint32_t* dn = nullptr, uint32_t status_stride = 1,
+              uint8_t** value_ptrs = nullptr, bool* founds = nullptr);
 
   hkv_options opt_;
   int key_type_, value_type_, strategy_;

@@ -147,6 +147,8 @@ SIGNATURES = {
     "hkv_set_global_epoch": (ctypes.c_int, [_P, _U64]),
     "hkv_check_device_error": (ctypes.c_int, [_P, _P]),
     "hkv_kernel_launches": (ctypes.c_int, [ctypes.POINTER(_U64)]),
+    "hkv_find_ptr": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _P]),
+    "hkv_find_or_insert_ptr": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _P, _B, _B, _P]),
     "hkv_save_files": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_char_p,
                                       ctypes.c_char_p, _SZ, _P, ctypes.POINTER(_SZ)]),
     "hkv_load_files": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_char_p,
@@ -343,6 +345,21 @@ class HashTable:
     def find(self, n, keys, values, founds, scores=None, stream=None):
         _check(lib().hkv_find(self._h, n, _ptr(keys), _ptr(values),
                               _ptr(founds), _ptr(scores), _stream(stream)))
+
+    def find_ptr(self, n, keys, value_ptrs, founds=None, scores=None, stream=None):
+        """find* : value_ptrs (int64 device tensor of n) receives the device
+        address of each found key's value row, 0 for a missed key."""
+        _check(lib().hkv_find_ptr(self._h, n, _ptr(keys), _ptr(value_ptrs),
+                                  _ptr(founds), _ptr(scores), _stream(stream)))
+
+    def find_or_insert_ptr(self, n, keys, value_ptrs, founds, scores=None,
+                           stream=None, unique_key=True, ignore_evict_strategy=False):
+        """find_or_insert* : finds or inserts each key (find_or_insert rules)
+        without copying values; value_ptrs receives each key's row address
+        (0 when refused), founds whether the key was there before."""
+        _check(lib().hkv_find_or_insert_ptr(self._h, n, _ptr(keys), _ptr(value_ptrs),
+                                            _ptr(founds), _ptr(scores), _stream(stream),
+                                            unique_key, ignore_evict_strategy, None))
 
     def save(self, keys_path, values_path, scores_path,
              max_workspace_size=1 << 20, stream=None) -> int:

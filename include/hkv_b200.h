@@ -142,6 +142,31 @@ int hkv_assign_scores(hkv_table* table, size_t n, const void* keys,
 int hkv_find(hkv_table* table, size_t n, const void* keys, void* values,
              bool* founds, uint64_t* scores, void* stream);
 
+/* find* (pointer-returning find), hkv_hashtable.h:2244-2264: values[i] is
+ * the device address of key i's value row in the table (a mapped host
+ * address for rows in host memory), NULL for a missed or reserved key;
+ * founds and scores (nullable) as in find. The addresses stay valid until
+ * the next call that can move or evict rows (insert-like calls, erase,
+ * clear, reserve). */
+int hkv_find_ptr(hkv_table* table, size_t n, const void* keys, void** values,
+                 bool* founds, uint64_t* scores, void* stream);
+
+/* find_or_insert* (pointer-returning), hkv_hashtable.h:1658-1727: finds or
+ * inserts each key as find_or_insert does (same placement, eviction and
+ * score rules) but copies no value: values[i] is the address of the key's
+ * row (for an inserted key the row still holds the previous occupant's
+ * bytes; the caller writes it), NULL for a refused or reserved key;
+ * founds[i] tells whether the key was there before. As in the reference, a
+ * later key of the same batch may evict a key placed earlier in it and then
+ * owns that row. With repeated keys
+ * (unique_key = false) every occurrence gets the same address and only the
+ * first can report a new key. locked_key_ptrs (keys left locked for a later
+ * unlock_keys) must be NULL: HKV_ERR_UNSUPPORTED otherwise. */
+int hkv_find_or_insert_ptr(hkv_table* table, size_t n, const void* keys,
+                           void** values, bool* founds, const uint64_t* scores,
+                           void* stream, bool unique_key,
+                           bool ignore_evict_strategy, void** locked_key_ptrs);
+
 /* contains, hkv_hashtable.h:2330-2348. */
 int hkv_contains(hkv_table* table, size_t n, const void* keys, bool* founds,
                  void* stream);

@@ -298,6 +298,28 @@ class HashTable {
         hkv_find(t_, n, keys, values, founds, scores, detail::st(stream)));
   }
 
+  /* find* (addresses of the value rows), reference hkv_hashtable.h:2244-2264. */
+  void find(const size_type n, const key_type* keys, value_type** values,
+            bool* founds, score_type* scores = nullptr, cudaStream_t stream = 0,
+            bool unique_key = true) const {
+    (void)unique_key;
+    detail::check(hkv_find_ptr(t_, n, keys, reinterpret_cast<void**>(values),
+                               founds, scores, detail::st(stream)));
+  }
+
+  /* find_or_insert* (addresses of the value rows), reference
+   * hkv_hashtable.h:1658-1727; locked_key_ptrs must be nullptr. */
+  void find_or_insert(const size_type n, const key_type* keys, value_type** values,
+                      bool* founds, score_type* scores = nullptr,
+                      cudaStream_t stream = 0, bool unique_key = true,
+                      bool ignore_evict_strategy = false,
+                      key_type** locked_key_ptrs = nullptr) {
+    detail::check(hkv_find_or_insert_ptr(
+        t_, n, keys, reinterpret_cast<void**>(values), founds, scores,
+        detail::st(stream), unique_key, ignore_evict_strategy,
+        reinterpret_cast<void**>(locked_key_ptrs)));
+  }
+
   void contains(const size_type n, const key_type* keys, bool* founds,
                 cudaStream_t stream = 0) const {
     detail::check(hkv_contains(t_, n, keys, founds, detail::st(stream)));
