@@ -17,6 +17,7 @@
 #include "hkv_kernels.cuh"
 #include <cstdio>
 
+#include "../../include/hkv_scan.cuh"
 #include "hkv_table.cuh"
 
 namespace hkvb {
@@ -242,6 +243,23 @@ void TableImpl::upload_slices() {
   for (size_t i = 0; i < slices_.size(); i++) p[i] = slices_[i].dev;
   CUDA_TRY(cudaMemcpy(d_slices_, p.data(), p.size() * sizeof(uint8_t*),
                       cudaMemcpyHostToDevice));
+}
+
+hkv_table_view TableImpl::public_view() const {
+  hkv_table_view v;
+  v.keys = keys_;
+  v.scores = scores_;
+  v.digests = digests_;
+  v.sizes = sizes_;
+  v.slices = d_slices_;
+  v.capacity = capacity_;
+  v.num_buckets = num_buckets_;
+  v.bucket_size = kBucket;
+  v.slice_shift = slice_shift_;
+  v.value_bytes = value_bytes_;
+  v.dim = static_cast<uint32_t>(opt_.dim);
+  v.reclaim_digest = kReclaimDigest;
+  return v;
 }
 
 TableView TableImpl::view() const {
@@ -1368,6 +1386,101 @@ int hkv_export_batch_count(hkv_table* table, size_t n, size_t offset,
   CUDA_TRY(cudaFreeAsync(d, s));
   CUDA_TRY(cudaStreamSynchronize(s));
   *h_count = h;
+  HKV_API_END
+}
+
+namespace {
+// the C ABI's built-in predicate (hkv_predicate)
+struct BuiltinPred {
+  uint64_t key_mask, key_value, threshold;
+  int cmp;
+  __device__ __forceinline__ bool operator()(const uint64_t& key, const uint8_t*,
+                                             const uint64_t& score, int) const {
+    if ((key & key_mask) != key_value) return false;
+    switch (cmp) {
+      case HKV_CMP_LT: return score < threshold;
+      case HKV_CMP_LE: return score <= threshold;
+      case HKV_CMP_GT: return score > threshold;
+      case HKV_CMP_GE: return score >= threshold;
+      case HKV_CMP_EQ: return score == threshold;
+      default: return true;
+    }
+  }
+};
+BuiltinPred builtin(const hkv_predicate* p) {
+  HKV_REQUIRE(p != nullptr, HKV_ERR_INVALID, "null predicate");
+  HKV_REQUIRE(p->score_cmp >= HKV_CMP_ANY && p->score_cmp <= HKV_CMP_EQ, HKV_ERR_INVALID,
+              "bad score comparison");
+  return BuiltinPred{p->key_mask, p->key_value, p->threshold, p->score_cmp};
+}
+}  // namespace
+
+int hkv_table_get_view(hkv_table* table, hkv_table_view* out) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  HKV_REQUIRE(out != nullptr, HKV_ERR_INVALID, "null argument");
+  *out = T->public_view();
+  HKV_API_END
+}
+
+int hkv_erase_if(hkv_table* table, const hkv_predicate* pred, void* stream,
+                 size_t* out_count) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  HKV_REQUIRE(out_count != nullptr, HKV_ERR_INVALID, "null count");
+  const BuiltinPred p = builtin(pred);
+  cudaStream_t s = as_stream(stream);
+  const hkv_table_view v = T->public_view();
+  unsigned long long* d = nullptr;
+  CUDA_TRY(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&d), 8, T->pool(), s));
+  CUDA_TRY(cudaMemsetAsync(d, 0, 8, s));
+  hkv_b200::scan::erase_if_kernel<uint64_t, uint8_t, uint64_t>
+      <<<hkv_b200::scan::grid_for(v.capacity), 256, 0, hkvb::counted(s)>>>(
+          v, p, v.reclaim_digest, d);
+  CUDA_TRY(cudaGetLastError());
+  unsigned long long h = 0;
+  CUDA_TRY(cudaMemcpyAsync(&h, d, 8, cudaMemcpyDeviceToHost, s));
+  CUDA_TRY(cudaFreeAsync(d, s));
+  CUDA_TRY(cudaStreamSynchronize(s));
+  *out_count = h;
+  HKV_API_END
+}
+
+int hkv_export_batch_if(hkv_table* table, const hkv_predicate* pred, size_t n,
+                        size_t offset, uint64_t* d_counter, void* keys,
+                        void* values, uint64_t* scores, void* stream) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  HKV_REQUIRE(d_counter != nullptr, HKV_ERR_INVALID, "d_counter is null");
+  const BuiltinPred p = builtin(pred);
+  cudaStream_t s = as_stream(stream);
+  CUDA_TRY(cudaMemsetAsync(d_counter, 0, 8, s));
+  const hkv_table_view v = T->public_view();
+  if (offset >= v.capacity) return HKV_OK;
+  n = std::min<size_t>(n, v.capacity - offset);
+  if (n == 0) return HKV_OK;
+  HKV_REQUIRE(keys != nullptr, HKV_ERR_INVALID, "keys must not be null");
+  hkv_b200::scan::export_if_kernel<uint64_t, uint8_t, uint64_t>
+      <<<hkv_b200::scan::grid_for(n), 256, 0, hkvb::counted(s)>>>(
+          v, p, offset, n, reinterpret_cast<unsigned long long*>(d_counter),
+          static_cast<uint64_t*>(keys), static_cast<uint8_t*>(values), scores);
+  CUDA_TRY(cudaGetLastError());
+  HKV_API_END
+}
+
+int hkv_size_if(hkv_table* table, const hkv_predicate* pred, uint64_t* d_counter,
+                void* stream) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  HKV_REQUIRE(d_counter != nullptr, HKV_ERR_INVALID, "d_counter is null");
+  const BuiltinPred p = builtin(pred);
+  cudaStream_t s = as_stream(stream);
+  CUDA_TRY(cudaMemsetAsync(d_counter, 0, 8, s));
+  const hkv_table_view v = T->public_view();
+  hkv_b200::scan::size_if_kernel<uint64_t, uint8_t, uint64_t>
+      <<<hkv_b200::scan::grid_for(v.capacity), 256, 0, hkvb::counted(s)>>>(
+          v, p, reinterpret_cast<unsigned long long*>(d_counter));
+  CUDA_TRY(cudaGetLastError());
   HKV_API_END
 }
 

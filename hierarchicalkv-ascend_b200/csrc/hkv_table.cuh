@@ -87,6 +87,7 @@ class TableImpl {
   ~TableImpl();
 
   TableView view() const;
+  hkv_table_view public_view() const;
 
   void insert_or_assign(size_t n, const uint64_t* keys, const uint8_t* values,
                         const uint64_t* scores, cudaStream_t s, bool unique,

@@ -83,6 +83,21 @@ class _Options(ctypes.Structure):
     ]
 
 
+class _Predicate(ctypes.Structure):
+    _fields_ = [("key_mask", ctypes.c_uint64), ("key_value", ctypes.c_uint64),
+                ("score_cmp", ctypes.c_int), ("threshold", ctypes.c_uint64)]
+
+
+SCORE_CMP = {None: 0, "<": 1, "<=": 2, ">": 3, ">=": 4, "==": 5}
+
+
+def predicate(key_mask=0, key_value=0, score_cmp=None, threshold=0):
+    """Built-in scan predicate: (key & key_mask) == key_value and
+    score <score_cmp> threshold (score_cmp one of None, '<', '<=', '>', '>=',
+    '==')."""
+    return _Predicate(key_mask, key_value, SCORE_CMP[score_cmp], threshold)
+
+
 @dataclass
 class HashTableOptions:
     """HashTableOptions, reference hashtable_options.h:534-566."""
@@ -148,6 +163,10 @@ SIGNATURES = {
     "hkv_check_device_error": (ctypes.c_int, [_P, _P]),
     "hkv_kernel_launches": (ctypes.c_int, [ctypes.POINTER(_U64)]),
     "hkv_find_ptr": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _P]),
+    "hkv_erase_if": (ctypes.c_int, [_P, _P, _P, ctypes.POINTER(_SZ)]),
+    "hkv_export_batch_if": (ctypes.c_int, [_P, _P, _SZ, _SZ, _P, _P, _P, _P, _P]),
+    "hkv_size_if": (ctypes.c_int, [_P, _P, _P, _P]),
+    "hkv_table_get_view": (ctypes.c_int, [_P, _P]),
     "hkv_find_or_insert_ptr": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _P, _B, _B, _P]),
     "hkv_save_files": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_char_p,
                                       ctypes.c_char_p, _SZ, _P, ctypes.POINTER(_SZ)]),
@@ -345,6 +364,24 @@ class HashTable:
     def find(self, n, keys, values, founds, scores=None, stream=None):
         _check(lib().hkv_find(self._h, n, _ptr(keys), _ptr(values),
                               _ptr(founds), _ptr(scores), _stream(stream)))
+
+    def erase_if(self, pred, stream=None) -> int:
+        """erase_if with a built-in predicate (see predicate()); returns the
+        number erased."""
+        out = _SZ(0)
+        _check(lib().hkv_erase_if(self._h, ctypes.byref(pred), _stream(stream),
+                                  ctypes.byref(out)))
+        return out.value
+
+    def export_batch_if(self, pred, n, offset, d_counter, keys, values, scores=None,
+                        stream=None):
+        _check(lib().hkv_export_batch_if(self._h, ctypes.byref(pred), n, offset,
+                                         _ptr(d_counter), _ptr(keys), _ptr(values),
+                                         _ptr(scores), _stream(stream)))
+
+    def size_if(self, pred, d_counter, stream=None):
+        _check(lib().hkv_size_if(self._h, ctypes.byref(pred), _ptr(d_counter),
+                                 _stream(stream)))
 
     def find_ptr(self, n, keys, value_ptrs, founds=None, scores=None, stream=None):
         """find* : value_ptrs (int64 device tensor of n) receives the device

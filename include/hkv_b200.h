@@ -206,6 +206,65 @@ int hkv_reserve(hkv_table* table, size_t new_capacity, void* stream);
 /* set_global_epoch, hkv_hashtable.h:3197. */
 int hkv_set_global_epoch(hkv_table* table, uint64_t epoch);
 
+/* ---- slot scans with predicates ---------------------------------------------
+ * The reference's erase_if / export_batch_if / size_if take a device
+ * functor as a template argument (hkv_hashtable.h:2409-2476, :2623-2731,
+ * :2829-2846) and for_each an execution functor (:2754-2775). C++ callers
+ * compiled with nvcc get those member templates from include/hkv_scan.cuh
+ * through include/hkv_hashtable.h. Other callers pass this built-in
+ * predicate: a live slot matches when (key & key_mask) == key_value and
+ * score <cmp> threshold. It covers the predicates of the reference's tests
+ * (score thresholds, key bit patterns, both). */
+typedef enum {
+  HKV_CMP_ANY = 0,
+  HKV_CMP_LT = 1,
+  HKV_CMP_LE = 2,
+  HKV_CMP_GT = 3,
+  HKV_CMP_GE = 4,
+  HKV_CMP_EQ = 5
+} hkv_score_cmp;
+
+typedef struct {
+  uint64_t key_mask;
+  uint64_t key_value;
+  int score_cmp; /* hkv_score_cmp */
+  uint64_t threshold;
+} hkv_predicate;
+
+/* erase_if: matching slots become tombstones; the count erased returns on
+ * the host (synchronises `stream`). */
+int hkv_erase_if(hkv_table* table, const hkv_predicate* pred, void* stream,
+                 size_t* out_count);
+/* export_batch_if: matching slots of [offset, offset + n) compacted to the
+ * outputs (order not specified), *d_counter set to their number. */
+int hkv_export_batch_if(hkv_table* table, const hkv_predicate* pred, size_t n,
+                        size_t offset, uint64_t* d_counter, void* keys,
+                        void* values, uint64_t* scores, void* stream);
+/* size_if: number of matching slots into *d_counter (device). */
+int hkv_size_if(hkv_table* table, const hkv_predicate* pred,
+                uint64_t* d_counter, void* stream);
+
+/* No reference counterpart: the table's raw device arrays, for the scan
+ * kernels of include/hkv_scan.cuh. Slot g lives in bucket g / bucket_size;
+ * its value row is slices[b >> slice_shift] + ((b & (2^slice_shift - 1)) *
+ * bucket_size + g % bucket_size) * value_bytes. Valid until the next call
+ * that can reallocate the table (reserve, auto-grow). */
+typedef struct {
+  uint64_t* keys;
+  uint64_t* scores;
+  uint8_t* digests;
+  int32_t* sizes;
+  uint8_t** slices; /* device array of slice base addresses */
+  uint64_t capacity;
+  uint64_t num_buckets;
+  uint32_t bucket_size;
+  uint32_t slice_shift;
+  uint32_t value_bytes;
+  uint32_t dim;
+  uint8_t reclaim_digest;
+} hkv_table_view;
+int hkv_table_get_view(hkv_table* table, hkv_table_view* out);
+
 /* ---- save / load, hkv_hashtable.h:3021-3195 --------------------------------
  * The reference takes a BaseKVFile (types.h:291-334) whose read/write move
  * n (key, vector, score) tuples between host buffers and a file. Here that

@@ -29,6 +29,9 @@
 #include <type_traits>
 
 #include "hkv_b200.h"
+#ifdef __CUDACC__
+#include "hkv_scan.cuh"
+#endif
 
 namespace hkv_b200 {
 
@@ -91,6 +94,9 @@ inline void check(int status) {
     default:
       throw std::runtime_error(m);
   }
+}
+inline void cuda(cudaError_t e) {
+  if (e != cudaSuccess) throw CudaException(cudaGetErrorString(e));
 }
 template <class V>
 constexpr int value_code() {
@@ -389,6 +395,56 @@ class HashTable {
     return b;
   }
 
+#ifdef __CUDACC__
+  /* Slot scans with caller functors (nvcc translation units only; the
+   * kernels are in hkv_scan.cuh): erase_if / erase_if_v2, reference
+   * hkv_hashtable.h:2409-2476; export_batch_if / export_batch_if_v2,
+   * :2623-2731; size_if, :2829-2846; for_each, :2754-2775. */
+  template <template <typename, typename> class PredFunctor>
+  size_type erase_if(const key_type& pattern, const score_type& threshold,
+                     cudaStream_t stream = 0) {
+    scan::PredV1<K, V, S, PredFunctor> p{pattern, threshold};
+    return erase_if_impl(p, stream);
+  }
+  template <typename PredFunctor>
+  size_type erase_if_v2(PredFunctor& pred, cudaStream_t stream = 0) {
+    return erase_if_impl(pred, stream);
+  }
+  template <template <typename, typename> class PredFunctor>
+  void export_batch_if(const key_type& pattern, const score_type& threshold,
+                       size_type n, const size_type offset, size_type* d_counter,
+                       key_type* keys, value_type* values,
+                       score_type* scores = nullptr, cudaStream_t stream = 0) const {
+    scan::PredV1<K, V, S, PredFunctor> p{pattern, threshold};
+    export_if_impl(p, n, offset, d_counter, keys, values, scores, stream);
+  }
+  template <typename PredFunctor>
+  void export_batch_if_v2(PredFunctor& pred, size_type n, const size_type offset,
+                          size_type* d_counter, key_type* keys, value_type* values,
+                          score_type* scores = nullptr, cudaStream_t stream = 0) const {
+    export_if_impl(pred, n, offset, d_counter, keys, values, scores, stream);
+  }
+  template <template <typename, typename> class PredFunctor>
+  void size_if(const key_type& pattern, const score_type& threshold,
+               size_type* d_counter, cudaStream_t stream = 0) const {
+    scan::PredV1<K, V, S, PredFunctor> p{pattern, threshold};
+    const hkv_table_view v = view();
+    detail::cuda(cudaMemsetAsync(d_counter, 0, sizeof(size_type), stream));
+    scan::size_if_kernel<K, V, S><<<scan::grid_for(v.capacity), 256, 0, stream>>>(
+        v, p, reinterpret_cast<unsigned long long*>(d_counter));
+    detail::cuda(cudaGetLastError());
+  }
+  template <typename ExecutionFunc>
+  void for_each(const size_type first, const size_type last, ExecutionFunc& f,
+                cudaStream_t stream = 0) {
+    const hkv_table_view v = view();
+    if (first >= v.capacity || last > v.capacity || first >= last) return;
+    scan::for_each_kernel<K, V, S><<<scan::grid_for(last - first), 256, 0, stream>>>(
+        v, first, last - first, f);
+    detail::cuda(cudaGetLastError());
+  }
+#endif
+
   /* save / load, reference hkv_hashtable.h:3021-3195 (synchronous). */
   size_type save(BaseKVFile<K, V, S>* file,
                  const size_t max_workspace_size = 1L * 1024 * 1024,
@@ -419,6 +475,42 @@ class HashTable {
   hkv_table* handle() const noexcept { return t_; }
 
  private:
+#ifdef __CUDACC__
+  hkv_table_view view() const {
+    hkv_table_view v;
+    detail::check(hkv_table_get_view(t_, &v));
+    return v;
+  }
+  template <class P>
+  size_type erase_if_impl(P& p, cudaStream_t stream) {
+    const hkv_table_view v = view();
+    unsigned long long* d = nullptr;
+    detail::cuda(cudaMallocAsync(reinterpret_cast<void**>(&d), 8, stream));
+    detail::cuda(cudaMemsetAsync(d, 0, 8, stream));
+    scan::erase_if_kernel<K, V, S><<<scan::grid_for(v.capacity), 256, 0, stream>>>(
+        v, p, v.reclaim_digest, d);
+    detail::cuda(cudaGetLastError());
+    unsigned long long h = 0;
+    detail::cuda(cudaMemcpyAsync(&h, d, 8, cudaMemcpyDeviceToHost, stream));
+    detail::cuda(cudaFreeAsync(d, stream));
+    detail::cuda(cudaStreamSynchronize(stream));
+    return static_cast<size_type>(h);
+  }
+  template <class P>
+  void export_if_impl(P& p, size_type n, size_type offset, size_type* d_counter,
+                      key_type* keys, value_type* values, score_type* scores,
+                      cudaStream_t stream) const {
+    const hkv_table_view v = view();
+    detail::cuda(cudaMemsetAsync(d_counter, 0, sizeof(size_type), stream));
+    if (offset >= v.capacity) return;
+    n = n < v.capacity - offset ? n : v.capacity - offset;
+    if (n == 0) return;
+    scan::export_if_kernel<K, V, S><<<scan::grid_for(n), 256, 0, stream>>>(
+        v, p, offset, n, reinterpret_cast<unsigned long long*>(d_counter), keys,
+        values, scores);
+    detail::cuda(cudaGetLastError());
+  }
+#endif
   static size_t write_trampoline(void* u, size_t n, size_t dim, const void* k,
                                  const void* v, const uint64_t* sc) {
     return static_cast<BaseKVFile<K, V, S>*>(u)->write(
