@@ -124,7 +124,7 @@ TableImpl::TableImpl(const hkv_options& o, int key_type, int value_type,
               "`max_hbm_for_vectors` is not 0!");
   HKV_REQUIRE(!o.io_by_cpu, HKV_ERR_UNSUPPORTED,
               "io_by_cpu is not supported: values are read zero-copy");
-  HKV_REQUIRE(!o.api_lock, HKV_ERR_UNSUPPORTED, "api_lock is not supported");
+  if (o.api_lock) api_mutex_.reset(new GroupMutex);
   value_bytes_ = static_cast<uint32_t>(o.dim * elem_bytes_);
 
   if (o.device_id >= 0) {
@@ -1187,6 +1187,30 @@ static inline cudaStream_t as_stream(void* s) {
   return reinterpret_cast<cudaStream_t>(s);
 }
 
+// Takes the table's api_lock (when it has one) for the rest of a C ABI call
+// and gives it back after the call's stream has drained.
+class ApiLock {
+ public:
+  ApiLock(TableImpl* t, hkvb::GroupMutex::Mode m, void* stream)
+      : mu_(t->api_mutex()), mode_(m), stream_(as_stream(stream)) {
+    if (mu_) mu_->lock(mode_);
+  }
+  ~ApiLock() {
+    if (!mu_) return;
+    cudaStreamSynchronize(stream_);
+    mu_->unlock(mode_);
+  }
+  ApiLock(const ApiLock&) = delete;
+  ApiLock& operator=(const ApiLock&) = delete;
+
+ private:
+  hkvb::GroupMutex* mu_;
+  hkvb::GroupMutex::Mode mode_;
+  cudaStream_t stream_;
+};
+
+#define HKV_LOCK(mode, stream) ApiLock api_lock_guard_(T, hkvb::GroupMutex::mode, stream)
+
 extern "C" {
 
 void hkv_options_init(hkv_options* o) {
@@ -1234,6 +1258,7 @@ int hkv_insert_or_assign(hkv_table* table, size_t n, const void* keys,
                          bool ignore_evict_strategy) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kUnique, stream);
   T->insert_or_assign(n, static_cast<const uint64_t*>(keys),
                       static_cast<const uint8_t*>(values), scores,
                       as_stream(stream), unique_key, ignore_evict_strategy);
@@ -1248,6 +1273,7 @@ int hkv_insert_and_evict(hkv_table* table, size_t n, const void* keys,
                          bool ignore_evict_strategy) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kUnique, stream);
   T->insert_and_evict(n, static_cast<const uint64_t*>(keys),
                       static_cast<const uint8_t*>(values), scores,
                       static_cast<uint64_t*>(evicted_keys),
@@ -1265,6 +1291,7 @@ int hkv_insert_and_evict_count(hkv_table* table, size_t n, const void* keys,
                                size_t* h_evicted_count) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kUnique, stream);
   HKV_REQUIRE(h_evicted_count != nullptr, HKV_ERR_INVALID, "null count");
   *h_evicted_count = 0;
   if (n == 0) return HKV_OK;
@@ -1296,6 +1323,7 @@ int hkv_accum_or_assign(hkv_table* table, size_t n, const void* keys,
                         void* stream, bool ignore_evict_strategy) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kUnique, stream);
   T->accum_or_assign(n, static_cast<const uint64_t*>(keys),
                      static_cast<const uint8_t*>(value_or_deltas),
                      accum_or_assigns, scores, as_stream(stream),
@@ -1308,6 +1336,7 @@ int hkv_find_or_insert(hkv_table* table, size_t n, const void* keys,
                        bool unique_key, bool ignore_evict_strategy) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kUnique, stream);
   T->find_or_insert(n, static_cast<const uint64_t*>(keys),
                     static_cast<uint8_t*>(values), scores, as_stream(stream),
                     unique_key, ignore_evict_strategy);
@@ -1318,6 +1347,7 @@ int hkv_assign_scores(hkv_table* table, size_t n, const void* keys,
                       const uint64_t* scores, void* stream, bool unique_key) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kUpdate, stream);
   (void)unique_key;  // duplicates serialise on the key lock either way
   T->assign_scores(n, static_cast<const uint64_t*>(keys), scores,
                    as_stream(stream));
@@ -1328,6 +1358,7 @@ int hkv_find(hkv_table* table, size_t n, const void* keys, void* values,
              bool* founds, uint64_t* scores, void* stream) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kRead, stream);
   T->find(n, static_cast<const uint64_t*>(keys), static_cast<uint8_t*>(values),
           founds, scores, as_stream(stream));
   HKV_API_END
@@ -1337,6 +1368,7 @@ int hkv_contains(hkv_table* table, size_t n, const void* keys, bool* founds,
                  void* stream) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kRead, stream);
   T->contains(n, static_cast<const uint64_t*>(keys), founds, as_stream(stream));
   HKV_API_END
 }
@@ -1344,6 +1376,7 @@ int hkv_contains(hkv_table* table, size_t n, const void* keys, bool* founds,
 int hkv_erase(hkv_table* table, size_t n, const void* keys, void* stream) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kUnique, stream);
   T->erase(n, static_cast<const uint64_t*>(keys), as_stream(stream));
   HKV_API_END
 }
@@ -1351,6 +1384,7 @@ int hkv_erase(hkv_table* table, size_t n, const void* keys, void* stream) {
 int hkv_clear(hkv_table* table, void* stream) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kUnique, stream);
   T->clear(as_stream(stream));
   HKV_API_END
 }
@@ -1360,6 +1394,7 @@ int hkv_export_batch(hkv_table* table, size_t n, size_t offset,
                      uint64_t* scores, void* stream) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kRead, stream);
   T->export_batch(n, offset, d_counter, static_cast<uint64_t*>(keys),
                   static_cast<uint8_t*>(values), scores, as_stream(stream));
   HKV_API_END
@@ -1370,6 +1405,7 @@ int hkv_export_batch_count(hkv_table* table, size_t n, size_t offset,
                            void* stream, size_t* h_count) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kRead, stream);
   HKV_REQUIRE(h_count != nullptr, HKV_ERR_INVALID, "null count");
   cudaStream_t s = as_stream(stream);
   uint64_t* d = nullptr;
@@ -1427,6 +1463,7 @@ int hkv_erase_if(hkv_table* table, const hkv_predicate* pred, void* stream,
                  size_t* out_count) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kUnique, stream);
   HKV_REQUIRE(out_count != nullptr, HKV_ERR_INVALID, "null count");
   const BuiltinPred p = builtin(pred);
   cudaStream_t s = as_stream(stream);
@@ -1451,6 +1488,7 @@ int hkv_export_batch_if(hkv_table* table, const hkv_predicate* pred, size_t n,
                         void* values, uint64_t* scores, void* stream) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kRead, stream);
   HKV_REQUIRE(d_counter != nullptr, HKV_ERR_INVALID, "d_counter is null");
   const BuiltinPred p = builtin(pred);
   cudaStream_t s = as_stream(stream);
@@ -1472,6 +1510,7 @@ int hkv_size_if(hkv_table* table, const hkv_predicate* pred, uint64_t* d_counter
                 void* stream) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kRead, stream);
   HKV_REQUIRE(d_counter != nullptr, HKV_ERR_INVALID, "d_counter is null");
   const BuiltinPred p = builtin(pred);
   cudaStream_t s = as_stream(stream);
@@ -1488,6 +1527,7 @@ int hkv_find_ptr(hkv_table* table, size_t n, const void* keys, void** values,
                  bool* founds, uint64_t* scores, void* stream) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kRead, stream);
   T->find_ptr(n, static_cast<const uint64_t*>(keys),
               reinterpret_cast<uint8_t**>(values), founds, scores, as_stream(stream));
   HKV_API_END
@@ -1499,6 +1539,7 @@ int hkv_find_or_insert_ptr(hkv_table* table, size_t n, const void* keys,
                            bool ignore_evict_strategy, void** locked_key_ptrs) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kUnique, stream);
   HKV_REQUIRE(locked_key_ptrs == nullptr, HKV_ERR_UNSUPPORTED,
               "locked_key_ptrs (keys left locked after the call) is not supported");
   T->find_or_insert_ptr(n, static_cast<const uint64_t*>(keys),
@@ -1511,6 +1552,7 @@ int hkv_save(hkv_table* table, hkv_kv_write_fn write, void* user,
              size_t max_workspace_size, void* stream, size_t* out_count) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kUnique, stream);
   HKV_REQUIRE(write != nullptr && out_count != nullptr, HKV_ERR_INVALID,
               "null argument");
   *out_count = T->save(write, user, max_workspace_size, as_stream(stream));
@@ -1521,6 +1563,7 @@ int hkv_load(hkv_table* table, hkv_kv_read_fn read, void* user,
              size_t max_workspace_size, void* stream, size_t* out_count) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kUnique, stream);
   HKV_REQUIRE(read != nullptr && out_count != nullptr, HKV_ERR_INVALID,
               "null argument");
   *out_count = T->load(read, user, max_workspace_size, as_stream(stream));
@@ -1566,6 +1609,7 @@ int hkv_save_files(hkv_table* table, const char* keys_path,
                    size_t max_workspace_size, void* stream, size_t* out_count) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kUnique, stream);
   HKV_REQUIRE(keys_path && values_path && scores_path && out_count,
               HKV_ERR_INVALID, "null argument");
   KVFiles F;
@@ -1582,6 +1626,7 @@ int hkv_load_files(hkv_table* table, const char* keys_path,
                    size_t max_workspace_size, void* stream, size_t* out_count) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kUnique, stream);
   HKV_REQUIRE(keys_path && values_path && scores_path && out_count,
               HKV_ERR_INVALID, "null argument");
   KVFiles F;
@@ -1596,6 +1641,7 @@ int hkv_load_files(hkv_table* table, const char* keys_path,
 int hkv_size(hkv_table* table, void* stream, size_t* out) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kRead, stream);
   *out = T->size(as_stream(stream));
   HKV_API_END
 }
@@ -1610,6 +1656,7 @@ int hkv_capacity(hkv_table* table, size_t* out) {
 int hkv_load_factor(hkv_table* table, void* stream, float* out) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kRead, stream);
   *out = T->load_factor(as_stream(stream));
   HKV_API_END
 }
@@ -1646,6 +1693,7 @@ int hkv_is_pure_hbm_mode(hkv_table* table, bool* out) {
 int hkv_reserve(hkv_table* table, size_t new_capacity, void* stream) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kUnique, stream);
   T->reserve(new_capacity, as_stream(stream));
   HKV_API_END
 }
@@ -1684,6 +1732,7 @@ int hkv_find_or_insert_noalloc(hkv_table* table, size_t n, const void* keys,
                                void* stream, bool ignore_evict_strategy) {
   HKV_API_BEGIN
   HKV_TABLE(table);
+  HKV_LOCK(kUnique, stream);
   uint8_t* scratch = hkvb::noalloc_scratch_for(T->device());
   T->find_or_insert_in_scratch(n, static_cast<const uint64_t*>(keys),
                                static_cast<uint8_t*>(values), scores,

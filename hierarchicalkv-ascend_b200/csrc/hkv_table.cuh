@@ -4,6 +4,9 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <condition_variable>
+#include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -80,6 +83,49 @@ struct DedupResult {
 DedupResult dedup_batch(size_t n, const uint64_t* keys, const uint64_t* scores,
                         int strategy, Workspace& ws, cudaStream_t s,
                         int sm_count, int* d_error);
+
+// The reference's api_lock (group_lock.h:45-406): readers share it
+// (find, contains, export, size), updaters share it (assign_scores), and
+// inserts / erases / clear / reserve / scans that modify / save take it
+// alone. A holder keeps it until its stream has drained, so the lock covers
+// the kernels it launched. Host-side only: the reference's device counters
+// serve waits on the device, which this build does not do across streams.
+class GroupMutex {
+ public:
+  enum Mode { kRead = 0, kUpdate = 1, kUnique = 2 };
+  void lock(Mode m) {
+    std::unique_lock<std::mutex> lk(mu_);
+    if (m == kRead) {
+      cv_.wait(lk, [&] { return updaters_ == 0 && !unique_; });
+      readers_++;
+    } else if (m == kUpdate) {
+      cv_.wait(lk, [&] { return readers_ == 0 && !unique_; });
+      updaters_++;
+    } else {
+      cv_.wait(lk, [&] { return !unique_; });
+      unique_ = true;  // no new reader or updater from here on
+      cv_.wait(lk, [&] { return readers_ == 0 && updaters_ == 0; });
+    }
+  }
+  void unlock(Mode m) {
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      if (m == kRead)
+        readers_--;
+      else if (m == kUpdate)
+        updaters_--;
+      else
+        unique_ = false;
+    }
+    cv_.notify_all();
+  }
+
+ private:
+  std::mutex mu_;
+  std::condition_variable cv_;
+  int readers_ = 0, updaters_ = 0;
+  bool unique_ = false;
+};
 
 class TableImpl {
  public:
@@ -175,6 +221,8 @@ class TableImpl {
   void check_strategy(const uint64_t* scores, bool ignore) const;
   // init_capacity * 2 > max_capacity: the table never grows
   bool at_max_capacity() const { return reach_max_; }
+  // the api_lock group mutex, nullptr when options.api_lock is false
+  GroupMutex* api_mutex() { return api_mutex_.get(); }
 
  private:
   void auto_grow(size_t n, cudaStream_t s);
@@ -197,6 +245,7 @@ class TableImpl {
   int device_ = 0;
   int sm_count_ = 148;
   cudaMemPool_t pool_ = nullptr;
+  std::unique_ptr<GroupMutex> api_mutex_;
   uint64_t* keys_ = nullptr;
   uint64_t* scores_ = nullptr;
   uint8_t* digests_ = nullptr;

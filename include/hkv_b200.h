@@ -81,7 +81,11 @@ typedef struct {
   int use_constant_memory;      /* reserved */
   int reserved_key_start_bit;   /* 0 only */
   uint64_t num_of_buckets_per_alloc;
-  int api_lock;                 /* must be 0 */
+  int api_lock;                 /* 1: calls from several host threads
+                                   serialise as in the reference (readers
+                                   share, updaters share, inserts and
+                                   erases alone); each call then also
+                                   synchronises its stream */
 } hkv_options;
 
 typedef struct hkv_table hkv_table;

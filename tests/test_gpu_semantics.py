@@ -290,3 +290,50 @@ def test_int64_keys():
     f = torch.zeros(3, dtype=torch.bool, device="cuda")
     t.contains(3, keys, f)
     assert f.all().item()
+
+
+def test_api_lock_serialises_host_threads():
+    """options.api_lock (reference group_lock.h): inserts from several host
+    threads on their own streams, with finds running beside them, give the
+    table that one thread would build."""
+    import threading
+
+    dim, cap = 8, 128 * 256
+    t = H.HashTable(H.EvictStrategy.kLru)
+    t.init(H.HashTableOptions(init_capacity=cap, max_capacity=cap,
+                              max_hbm_for_vectors=1 << 30, dim=dim, api_lock=True))
+    rng = np.random.default_rng(77)
+    keys = np.unique(rng.integers(1, 1 << 62, 40000, dtype=np.uint64))[:16000]
+    vals = rng.standard_normal((len(keys), dim)).astype(np.float32)
+    parts = np.array_split(np.arange(len(keys)), 4)
+    errors = []
+
+    def writer(idx):
+        try:
+            s = torch.cuda.Stream()
+            for chunk in np.array_split(idx, 8):
+                t.insert_or_assign(len(chunk), dev(keys[chunk]), dev(vals[chunk]), stream=s)
+        except Exception as e:  # noqa: BLE001
+            errors.append(e)
+
+    def reader():
+        try:
+            s = torch.cuda.Stream()
+            out = torch.zeros((4000, dim), device="cuda")
+            f = torch.zeros(4000, dtype=torch.bool, device="cuda")
+            for _ in range(8):
+                t.find(4000, dev(keys[:4000]), out, f, stream=s)
+        except Exception as e:  # noqa: BLE001
+            errors.append(e)
+
+    th = [threading.Thread(target=writer, args=(p,)) for p in parts]
+    th += [threading.Thread(target=reader) for _ in range(2)]
+    for x in th:
+        x.start()
+    for x in th:
+        x.join(timeout=120)
+    assert not errors and not any(x.is_alive() for x in th)
+    torch.cuda.synchronize()
+    assert t.size() == len(keys)
+    v, f, _ = GpuOps(t, dim).find(keys)
+    assert f.all() and (v == vals).all()
