@@ -505,6 +505,125 @@ def save_load_times(device, capacity=8 << 20):
 
 
 # --------------------------------------------------------------------------
+# --workload zipf: find_or_insert of power-law (Zipf-like) keys with repeats
+# (unique_key = false), dim 64: 128 Mi slots, kEpochLfu, 2 Mi keys per step on
+# one GPU; 256 Mi slots per GPU, kLfu, 8 Mi keys per GPU per step when
+# sharded. Not the headline metric; run on request.
+# --------------------------------------------------------------------------
+def zipf_ids(n, s, universe, gen, device):
+    """Power-law ids on [0, universe): the inverse CDF of the continuous
+    density x^-s on [1, universe] (a stand-in for Zipf(s))."""
+    import torch
+
+    u = torch.rand(n, generator=gen, device=device, dtype=torch.float64)
+    a = 1.0 - s
+    x = ((universe ** a - 1.0) * u + 1.0) ** (1.0 / a)
+    return (x.floor().to(torch.int64) - 1).clamp_(0, universe - 1)
+
+
+def run_zipf(args):
+    import torch
+
+    import hkv_b200 as H
+
+    rank, world, local_rank, dist = dist_setup(args.gpus)
+    device = torch.device("cuda", torch.cuda.current_device())
+    if world == 1:
+        cap, dim, batch, s_exp, strat = 128 << 20, 64, 2 << 20, 1.05, H.EvictStrategy.kEpochLfu
+    else:  # one shard per GPU
+        cap, dim, batch, s_exp, strat = 256 << 20, 64, 8 << 20, 1.1, H.EvictStrategy.kLfu
+    cap = min(cap, args.capacity) if args.capacity != CAPACITY else cap
+    opts = H.HashTableOptions(init_capacity=cap, max_capacity=cap,
+                              max_hbm_for_vectors=cap * dim * 8, dim=dim, max_load_factor=1.0)
+    if world == 1:
+        table = H.HashTable(strat)
+        table.init(opts)
+        local = table
+    else:
+        uid = [H.ShardedHashTable.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        opts.device_id = torch.cuda.current_device()
+        table = H.ShardedHashTable(opts, rank, world, uid[0], strat, max_batch=batch)
+        local = H.HashTable.borrow(H.lib().hkv_sharded_local(table._h), strat)
+    epoch = 1
+    if strat == H.EvictStrategy.kEpochLfu:
+        local.set_global_epoch(epoch)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(99 + rank)
+    # prefill: capacity distinct keys (each rank its own part of the stream)
+    chunk = 4 << 20
+    pv = torch.randn((chunk, dim), device=device)
+    for st in range(0, cap * world, chunk):
+        k = keys_from_counters(st, chunk, device)
+        if world > 1:
+            k = k[owner_t(k, world) == rank]
+        sc = torch.randint(1, 17, (k.numel(),), generator=gen, device=device)
+        local.insert_or_assign(k.numel(), k, pv[:k.numel()], sc)
+    torch.cuda.synchronize()
+    log(f"zipf prefill done, load factor {local.load_factor():.3f}")
+    steps, warm = args.steps, args.warmup
+    nb = min(steps + warm, 8)
+    batches = []
+    for b in range(nb):
+        ids = zipf_ids(batch, s_exp, 1 << 30, gen, device)
+        k = key_of(ids)
+        batches.append((k, torch.randn((batch, dim), generator=gen, device=device),
+                        torch.randint(1, 17, (batch,), generator=gen, device=device)))
+    uniq = sum(int(torch.unique(b[0]).numel()) for b in batches) / (nb * batch)
+
+    def step(i):
+        # values are in/out: a found key's row overwrites its input row, a
+        # missing key is inserted with whatever its row holds
+        nonlocal epoch
+        k, v, sc = batches[i % nb]
+        table.find_or_insert(batch, k, v, sc, unique_key=False)
+        if strat == H.EvictStrategy.kEpochLfu and (i + 1) % 10 == 0:
+            epoch += 1
+            local.set_global_epoch(epoch)
+
+    for i in range(warm):
+        step(i)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    stream = torch.cuda.current_stream()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record(stream)
+    for i in range(steps):
+        step(warm + i)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    if dist:
+        tt = torch.tensor([ms], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    local.check_device_error()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "B-KV/s for find_or_insert of Zipf keys with repeats (unique_key=false)",
+            "value": round(batch * steps * world / (ms * 1e-3) / 1e9, 4), "unit": UNIT,
+            "n_gpus": world, "steps": steps, "warmup": warm,
+            "ms_per_step": round(ms / steps, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u64 keys / f32 values",
+            "data": "synthetic (power-law ids, seeded)",
+            "config": {"workload": ("BASELINE config 3: 128 Mi slots, dim 64, kEpochLfu, "
+                                    "2 Mi keys per step, Zipf(1.05) stand-in")
+                       if world == 1 else
+                       ("BASELINE config 5: 256 Mi slots per GPU, dim 64, kLfu, 8 Mi keys "
+                        "per GPU per step, Zipf(1.1) stand-in, sharded peer transport"),
+                       "capacity_per_gpu": cap, "dim": dim, "batch_per_gpu": batch,
+                       "distinct_fraction": round(uniq, 4),
+                       "batches_cycled": nb}}), flush=True)
+    if world > 1:
+        table.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# --------------------------------------------------------------------------
 # CPU arm: the reference's algorithm (oracle/ restatement) on host threads.
 # --------------------------------------------------------------------------
 def cpu_run(capacity, steps, warm, threads, min_seconds=0.0, max_steps=None):
@@ -627,9 +746,15 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--capacity", type=int, default=CAPACITY,
                     help="slots per GPU (diagnostics; the metric uses the default)")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "zipf"],
+                    help="cfg2: the headline metric; zipf: find_or_insert of "
+                         "power-law keys with repeats (dim 64)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.workload == "zipf":
+        run_zipf(args)
         return
     run_gpu(args)
 
