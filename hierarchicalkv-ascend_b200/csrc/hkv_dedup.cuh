@@ -18,35 +18,115 @@ struct DedupView {
   uint32_t* set_first;  // [cap] smallest input index holding that key
   uint32_t* set_last;   // [cap] largest input index holding that key
   uint32_t* set_uid;    // [cap] representative number of that key
+  unsigned long long* set_sum;  // [cap] summed scores (score_mode kScoreSum*)
   uint64_t cap;         // power of two
 };
 
-// Stage 1: insert every non-reserved key; slot_of[i] = its set slot
-// (kNoIndex for reserved keys, which the table ignores anyway).
-__global__ void dedup_insert_kernel(DedupView d, const uint64_t* __restrict__ keys,
-                                    uint64_t n, uint32_t* __restrict__ slot_of,
-                                    int* error) {
-  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
-       i += (uint64_t)gridDim.x * blockDim.x) {
-    const uint64_t key = keys[i];
-    if (is_reserved(key)) {
-      slot_of[i] = kNoIndex;
-      continue;
+// How the scores of one key's occurrences merge: Lfu sums them (a hit adds
+// every occurrence's score, score_functor.h:157-160); EpochLfu sums their
+// low 32 bits and saturates (:297-309); the other rules keep the last
+// occurrence's score (each later occurrence overwrites, :431-455).
+enum DedupScoreMode : int { kScoreNone = 0, kScoreLast = 1, kScoreSum = 2, kScoreSumLow32 = 3 };
+
+__host__ __device__ inline int dedup_score_mode(int strategy, bool has_scores) {
+  if (!has_scores) return kScoreNone;
+  if (strategy == kLfu) return kScoreSum;
+  if (strategy == kEpochLfu) return kScoreSumLow32;
+  return kScoreLast;
+}
+
+// Stage 1 merges each block's chunk of the batch in shared memory first, so
+// a key repeated across the batch (a hot key of a power-law stream) costs one
+// global set update per block instead of one per occurrence; then every
+// distinct key of the chunk is entered in the global set with the chunk's
+// smallest and largest index (and its summed score). slot_of[i] = the key's
+// global set slot (kNoIndex for reserved keys, which the table ignores).
+constexpr int kDedupThreads = 256;
+constexpr int kDedupPerThread = 4;
+constexpr int kDedupChunk = kDedupThreads * kDedupPerThread;
+constexpr int kDedupLocal = 2 * kDedupChunk;  // local set at load factor <= 0.5
+
+__device__ __forceinline__ uint64_t dedup_hash(uint64_t key) {
+  return murmur3(key ^ 0x9E3779B97F4A7C15ull);
+}
+
+__global__ void __launch_bounds__(kDedupThreads)
+dedup_insert_kernel(DedupView d, const uint64_t* __restrict__ keys, uint64_t n,
+                    const uint64_t* __restrict__ scores, int score_mode,
+                    uint32_t* __restrict__ slot_of, int* error) {
+  __shared__ uint64_t lkey[kDedupLocal];
+  __shared__ uint32_t lfirst[kDedupLocal];  // after the global phase: global slot
+  __shared__ uint32_t llast[kDedupLocal];
+  __shared__ unsigned long long lsum[kDedupLocal];
+  const bool sum = score_mode >= kScoreSum;
+  for (uint64_t c0 = uint64_t{blockIdx.x} * kDedupChunk; c0 < n;
+       c0 += uint64_t{gridDim.x} * kDedupChunk) {
+    for (int l = threadIdx.x; l < kDedupLocal; l += kDedupThreads) {
+      lkey[l] = kEmptyKey;
+      lfirst[l] = kNoIndex;
+      llast[l] = 0;
+      lsum[l] = 0;
     }
-    uint64_t s = murmur3(key ^ 0x9E3779B97F4A7C15ull) & (d.cap - 1);
-    uint32_t res = kNoIndex;
-    for (uint64_t probe = 0; probe < d.cap; probe++) {
-      const uint64_t old = cas_u64(d.set_keys + s, kEmptyKey, key);
-      if (old == kEmptyKey || old == key) {
-        atomicMin(d.set_first + s, static_cast<uint32_t>(i));
-        atomicMax(d.set_last + s, static_cast<uint32_t>(i));
-        res = static_cast<uint32_t>(s);
-        break;
+    __syncthreads();
+    uint32_t mine[kDedupPerThread];
+#pragma unroll
+    for (int j = 0; j < kDedupPerThread; j++) {
+      const uint64_t i = c0 + static_cast<uint64_t>(j) * kDedupThreads + threadIdx.x;
+      mine[j] = kNoIndex;
+      if (i >= n) continue;
+      const uint64_t key = keys[i];
+      if (is_reserved(key)) continue;
+      uint32_t l = static_cast<uint32_t>(dedup_hash(key)) & (kDedupLocal - 1);
+      // at most kDedupChunk distinct keys in 2x slots: a free or matching
+      // slot is always found within kDedupLocal probes
+      for (int probe = 0; probe < kDedupLocal; probe++) {
+        const unsigned long long old = atomicCAS(
+            reinterpret_cast<unsigned long long*>(lkey + l), kEmptyKey, key);
+        if (old == kEmptyKey || old == key) break;
+        l = (l + 1) & (kDedupLocal - 1);
       }
-      s = (s + 1) & (d.cap - 1);
+      mine[j] = l;
+      atomicMin(lfirst + l, static_cast<uint32_t>(i));
+      atomicMax(llast + l, static_cast<uint32_t>(i));
+      if (sum) {
+        const uint64_t sc = score_mode == kScoreSumLow32 ? (scores[i] & 0xFFFFFFFFull)
+                                                         : scores[i];
+        atomicAdd(lsum + l, static_cast<unsigned long long>(sc));
+      }
     }
-    if (res == kNoIndex) atomicOr(error, kErrSpinTimeout);  // set full: cannot happen at 2x
-    slot_of[i] = res;
+    __syncthreads();
+    for (int l = threadIdx.x; l < kDedupLocal; l += kDedupThreads) {
+      const uint64_t key = lkey[l];
+      if (key == kEmptyKey) continue;
+      uint64_t g = dedup_hash(key) & (d.cap - 1);
+      uint32_t res = kNoIndex;
+      for (uint64_t probe = 0; probe < d.cap; probe++) {
+        // a plain L2 read first: a key already entered by another block
+        // needs no CAS (a stale EMPTY only costs the CAS below)
+        uint64_t cur = __ldcg(d.set_keys + g);
+        if (cur == kEmptyKey) cur = cas_u64(d.set_keys + g, kEmptyKey, key);
+        if (cur == kEmptyKey || cur == key) {
+          res = static_cast<uint32_t>(g);
+          break;
+        }
+        g = (g + 1) & (d.cap - 1);
+      }
+      if (res == kNoIndex) {
+        atomicOr(error, kErrSpinTimeout);  // set full: cannot happen at 2x
+      } else {
+        atomicMin(d.set_first + res, lfirst[l]);
+        atomicMax(d.set_last + res, llast[l]);
+        if (sum) atomicAdd(d.set_sum + res, lsum[l]);
+      }
+      lfirst[l] = res;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kDedupPerThread; j++) {
+      const uint64_t i = c0 + static_cast<uint64_t>(j) * kDedupThreads + threadIdx.x;
+      if (i < n) slot_of[i] = mine[j] == kNoIndex ? kNoIndex : lfirst[mine[j]];
+    }
+    __syncthreads();  // the next chunk re-initialises the local set
   }
 }
 
@@ -141,22 +221,34 @@ __global__ void __launch_bounds__(kScanThreads)
 }
 
 // Stage 3: representatives. For first occurrence i with rank u:
-// ukeys[u] = key, set_uid[slot] = u, rep_first[u] = i.
+// ukeys[u] = key, set_uid[slot] = u, rep_first[u] = i, rep_last[u] = the
+// key's last index, uscores[u] = its merged score (score_mode).
 __global__ void dedup_emit_kernel(DedupView d, const uint64_t* __restrict__ keys,
                                   const uint32_t* __restrict__ slot_of,
                                   const uint32_t* __restrict__ rank, uint64_t n,
                                   uint64_t* __restrict__ ukeys,
                                   uint32_t* __restrict__ rep_first,
-                                  uint32_t* __restrict__ rep_last) {
+                                  uint32_t* __restrict__ rep_last,
+                                  const uint64_t* __restrict__ scores, int score_mode,
+                                  uint64_t* __restrict__ uscores) {
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
        i += (uint64_t)gridDim.x * blockDim.x) {
     const uint32_t s = slot_of[i];
     if (s == kNoIndex || d.set_first[s] != static_cast<uint32_t>(i)) continue;
     const uint32_t u = rank[i];
+    const uint32_t last = d.set_last[s];
     ukeys[u] = keys[i];
     d.set_uid[s] = u;
     rep_first[u] = static_cast<uint32_t>(i);
-    if (rep_last) rep_last[u] = d.set_last[s];
+    if (rep_last) rep_last[u] = last;
+    if (score_mode == kScoreLast) {
+      uscores[u] = scores[last];
+    } else if (score_mode == kScoreSum) {
+      uscores[u] = d.set_sum[s];
+    } else if (score_mode == kScoreSumLow32) {
+      const uint64_t t = d.set_sum[s];
+      uscores[u] = t > 0xFFFFFFFFull ? 0xFFFFFFFFull : t;
+    }
   }
 }
 
@@ -169,35 +261,6 @@ __global__ void dedup_inverse_kernel(DedupView d,
     const uint32_t s = slot_of[i];
     uid_of[i] = s == kNoIndex ? kNoIndex : d.set_uid[s];
   }
-}
-
-// Merged input score of each representative. Lfu: sum of all occurrences
-// (a hit adds every occurrence's score, score_functor.h:157-160); EpochLfu:
-// saturating sum of the low 32 bits (:297-309); others: the last
-// occurrence's score (each later occurrence overwrites, :431-455).
-__global__ void dedup_scores_kernel(int strategy, const uint64_t* __restrict__ scores,
-                                    const uint32_t* __restrict__ uid_of,
-                                    const uint32_t* __restrict__ rep_last,
-                                    uint64_t n, uint64_t* __restrict__ uscores) {
-  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
-       i += (uint64_t)gridDim.x * blockDim.x) {
-    const uint32_t u = uid_of[i];
-    if (u == kNoIndex) continue;
-    if (strategy == kLfu) {
-      atomicAdd(reinterpret_cast<unsigned long long*>(uscores + u), scores[i]);
-    } else if (strategy == kEpochLfu) {
-      atomicAdd(reinterpret_cast<unsigned long long*>(uscores + u),
-                scores[i] & 0xFFFFFFFFull);
-    } else if (rep_last[u] == static_cast<uint32_t>(i)) {
-      uscores[u] = scores[i];
-    }
-  }
-}
-
-__global__ void clamp_low32_kernel(uint64_t* __restrict__ s, uint64_t m) {
-  for (uint64_t u = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; u < m;
-       u += (uint64_t)gridDim.x * blockDim.x)
-    if (s[u] > 0xFFFFFFFFull) s[u] = 0xFFFFFFFFull;
 }
 
 // Gather rows: dst[u] = src[idx[u]] for u < *dm (representatives only).

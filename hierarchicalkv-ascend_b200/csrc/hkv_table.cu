@@ -557,51 +557,61 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
   CUDA_TRY(cudaGetLastError());
 }
 
+// The merge stages on a set d whose arrays this resets; every other array
+// is written before it is read.
+void dedup_stages(const DedupView& d, size_t n, const uint64_t* keys,
+                  const uint64_t* scores, int score_mode, uint32_t* slot_of,
+                  uint32_t* rank, uint32_t* sums, uint32_t* dm, uint64_t* ukeys,
+                  uint32_t* rep_first, uint32_t* rep_last, uint32_t* uid_of,
+                  uint64_t* uscores, cudaStream_t s, int sm_count, int* d_error) {
+  CUDA_TRY(cudaMemsetAsync(d.set_keys, 0xFF, d.cap * 8, s));
+  CUDA_TRY(cudaMemsetAsync(d.set_first, 0xFF, d.cap * 4, s));
+  CUDA_TRY(cudaMemsetAsync(d.set_last, 0, d.cap * 4, s));
+  if (score_mode >= kScoreSum) CUDA_TRY(cudaMemsetAsync(d.set_sum, 0, d.cap * 8, s));
+  const uint64_t ntiles = ceil_div(n, kScanTile);
+  const int g1 = static_cast<int>(
+      std::min<uint64_t>(ceil_div(n, 256), sm_count * 32ull));
+  const int gi = static_cast<int>(
+      std::min<uint64_t>(ceil_div(n, kDedupChunk), sm_count * 4ull));
+  dedup_insert_kernel<<<gi, kDedupThreads, 0, counted(s)>>>(d, keys, n, scores, score_mode,
+                                                            slot_of, d_error);
+  dedup_flag_kernel<<<g1, 256, 0, counted(s)>>>(d, slot_of, n, rank);
+  scan_tiles_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, counted(s)>>>(rank, n,
+                                                                               sums);
+  scan_sums_kernel<<<1, kScanThreads, 0, counted(s)>>>(sums, ntiles, dm);
+  scan_add_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, counted(s)>>>(rank, n,
+                                                                             sums);
+  dedup_emit_kernel<<<g1, 256, 0, counted(s)>>>(d, keys, slot_of, rank, n, ukeys, rep_first,
+                                                rep_last, scores, score_mode, uscores);
+  dedup_inverse_kernel<<<g1, 256, 0, counted(s)>>>(d, slot_of, n, uid_of);
+  CUDA_TRY(cudaGetLastError());
+}
+
 DedupResult dedup_batch(size_t n, const uint64_t* keys, const uint64_t* scores,
                         int strategy, Workspace& ws, cudaStream_t s,
                         int sm_count, int* d_error) {
   uint64_t cap = 1024;
   while (cap < 2 * static_cast<uint64_t>(n)) cap <<= 1;
+  const int score_mode = dedup_score_mode(strategy, scores != nullptr);
   DedupView d;
   d.cap = cap;
   d.set_keys = ws.get<uint64_t>(cap);
   d.set_first = ws.get<uint32_t>(cap);
   d.set_last = ws.get<uint32_t>(cap);
   d.set_uid = ws.get<uint32_t>(cap);
-  CUDA_TRY(cudaMemsetAsync(d.set_keys, 0xFF, cap * 8, s));
-  CUDA_TRY(cudaMemsetAsync(d.set_first, 0xFF, cap * 4, s));
-  CUDA_TRY(cudaMemsetAsync(d.set_last, 0, cap * 4, s));
+  d.set_sum = score_mode >= kScoreSum ? ws.get<unsigned long long>(cap) : nullptr;
   DedupResult r;
   uint32_t* slot_of = ws.get<uint32_t>(n);
   uint32_t* rank = ws.get<uint32_t>(n);
   r.uid_of = ws.get<uint32_t>(n);
-  const uint64_t ntiles = ceil_div(n, kScanTile);
-  uint32_t* sums = ws.get<uint32_t>(ntiles + 1);
+  uint32_t* sums = ws.get<uint32_t>(ceil_div(n, kScanTile) + 1);
   r.dm = ws.get<uint32_t>(1);
   r.ukeys = ws.get<uint64_t>(n);
   r.rep_first = ws.get<uint32_t>(n);
   r.rep_last = ws.get<uint32_t>(n);
   r.uscores = scores ? ws.get<uint64_t>(n) : nullptr;
-  const int g1 = static_cast<int>(
-      std::min<uint64_t>(ceil_div(n, 256), sm_count * 32ull));
-  dedup_insert_kernel<<<g1, 256, 0, counted(s)>>>(d, keys, n, slot_of, d_error);
-  dedup_flag_kernel<<<g1, 256, 0, counted(s)>>>(d, slot_of, n, rank);
-  scan_tiles_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, counted(s)>>>(rank, n,
-                                                                       sums);
-  scan_sums_kernel<<<1, kScanThreads, 0, counted(s)>>>(sums, ntiles, r.dm);
-  scan_add_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, counted(s)>>>(rank, n,
-                                                                     sums);
-  dedup_emit_kernel<<<g1, 256, 0, counted(s)>>>(d, keys, slot_of, rank, n, r.ukeys,
-                                       r.rep_first, r.rep_last);
-  dedup_inverse_kernel<<<g1, 256, 0, counted(s)>>>(d, slot_of, n, r.uid_of);
-  if (scores) {
-    CUDA_TRY(cudaMemsetAsync(r.uscores, 0, n * 8, s));
-    dedup_scores_kernel<<<g1, 256, 0, counted(s)>>>(strategy, scores, r.uid_of,
-                                           r.rep_last, n, r.uscores);
-    if (strategy == kEpochLfu)
-      clamp_low32_kernel<<<g1, 256, 0, counted(s)>>>(r.uscores, n);
-  }
-  CUDA_TRY(cudaGetLastError());
+  dedup_stages(d, n, keys, scores, score_mode, slot_of, rank, sums, r.dm, r.ukeys,
+               r.rep_first, r.rep_last, r.uid_of, r.uscores, s, sm_count, d_error);
   return r;
 }
 
@@ -1063,17 +1073,18 @@ void TableImpl::find_or_insert_in_scratch(size_t n, const uint64_t* keys,
   check_strategy(scores, ignore);
   const int st = ignore ? kCustomized : strategy_;
   ScratchArena ws(scratch, scratch_bytes);
+  const int score_mode = dedup_score_mode(st, scores != nullptr);
   DedupView d;
   d.cap = kNoAllocSetSlots;
   d.set_keys = ws.get<uint64_t>(d.cap);
   d.set_first = ws.get<uint32_t>(d.cap);
   d.set_last = ws.get<uint32_t>(d.cap);
   d.set_uid = ws.get<uint32_t>(d.cap);
+  d.set_sum = ws.get<unsigned long long>(d.cap);
   uint32_t* slot_of = ws.get<uint32_t>(n);
   uint32_t* rank = ws.get<uint32_t>(n);
   uint32_t* uid_of = ws.get<uint32_t>(n);
-  const uint64_t ntiles = ceil_div(n, kScanTile);
-  uint32_t* sums = ws.get<uint32_t>(ntiles + 1);
+  uint32_t* sums = ws.get<uint32_t>(ceil_div(n, kScanTile) + 1);
   uint32_t* dm = ws.get<uint32_t>(1);
   uint64_t* ukeys = ws.get<uint64_t>(n);
   uint32_t* rep_first = ws.get<uint32_t>(n);
@@ -1082,28 +1093,9 @@ void TableImpl::find_or_insert_in_scratch(size_t n, const uint64_t* keys,
   uint8_t* ustatus = ws.get<uint8_t>(n);
   uint8_t* urows = ws.get<uint8_t>(n * static_cast<size_t>(value_bytes_));
   // the array keeps the previous call's contents: reset what starts empty
-  CUDA_TRY(cudaMemsetAsync(d.set_keys, 0xFF, d.cap * 8, s));
-  CUDA_TRY(cudaMemsetAsync(d.set_first, 0xFF, d.cap * 4, s));
-  CUDA_TRY(cudaMemsetAsync(d.set_last, 0, d.cap * 4, s));
   CUDA_TRY(cudaMemsetAsync(ustatus, kIllegal, n, s));
-  if (uscores) CUDA_TRY(cudaMemsetAsync(uscores, 0, n * 8, s));
-  const int g1 = static_cast<int>(
-      std::min<uint64_t>(ceil_div(n, 256), sm_count_ * 32ull));
-  dedup_insert_kernel<<<g1, 256, 0, counted(s)>>>(d, keys, n, slot_of, d_error_);
-  dedup_flag_kernel<<<g1, 256, 0, counted(s)>>>(d, slot_of, n, rank);
-  scan_tiles_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, counted(s)>>>(rank, n,
-                                                                       sums);
-  scan_sums_kernel<<<1, kScanThreads, 0, counted(s)>>>(sums, ntiles, dm);
-  scan_add_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, counted(s)>>>(rank, n,
-                                                                     sums);
-  dedup_emit_kernel<<<g1, 256, 0, counted(s)>>>(d, keys, slot_of, rank, n, ukeys,
-                                       rep_first, rep_last);
-  dedup_inverse_kernel<<<g1, 256, 0, counted(s)>>>(d, slot_of, n, uid_of);
-  if (scores) {
-    dedup_scores_kernel<<<g1, 256, 0, counted(s)>>>(st, scores, uid_of, rep_last, n,
-                                           uscores);
-    if (st == kEpochLfu) clamp_low32_kernel<<<g1, 256, 0, counted(s)>>>(uscores, n);
-  }
+  dedup_stages(d, n, keys, scores, score_mode, slot_of, rank, sums, dm, ukeys, rep_first,
+               rep_last, uid_of, uscores, s, sm_count_, d_error_);
   const int vwr = value_width({values});
   DISPATCH_VW(vwr, gather_rows_kernel<VW><<<tile_grid(n), 256, 0, counted(s)>>>(
                        urows, values, rep_first, dm, value_bytes_));
