@@ -263,27 +263,11 @@ __global__ void dedup_inverse_kernel(DedupView d,
   }
 }
 
-// Gather rows: dst[u] = src[idx[u]] for u < *dm (representatives only).
+// find_or_insert scatter: the representatives found or inserted their keys
+// in place (at their first occurrence's row); every later occurrence reads
+// its representative's row. values is both source and destination.
 template <int VW>
-__global__ void gather_rows_kernel(uint8_t* __restrict__ dst,
-                                   const uint8_t* __restrict__ src,
-                                   const uint32_t* __restrict__ idx,
-                                   const uint32_t* __restrict__ dm,
-                                   uint32_t vb) {
-  const Tile tile;
-  const uint64_t m = *dm;
-  const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / kTile);
-  for (uint64_t u = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / kTile;
-       u < m; u += ntiles)
-    copy_row<VW>(dst + u * vb, src + static_cast<uint64_t>(idx[u]) * vb, vb,
-                 tile.lane, kTile);
-}
-
-// find_or_insert scatter: every non-representative occurrence whose
-// representative was found or inserted reads the representative's row.
-template <int VW>
-__global__ void scatter_found_rows_kernel(uint8_t* __restrict__ values,
-                                          const uint8_t* __restrict__ urows,
+__global__ void scatter_found_rows_kernel(uint8_t* values,
                                           const uint32_t* __restrict__ uid_of,
                                           const uint32_t* __restrict__ rep_first,
                                           const uint8_t* __restrict__ ustatus,
@@ -294,10 +278,12 @@ __global__ void scatter_found_rows_kernel(uint8_t* __restrict__ values,
        i < n; i += ntiles) {
     const uint32_t u = uid_of[i];
     if (u == kNoIndex) continue;
+    const uint32_t f = rep_first[u];
+    if (f == static_cast<uint32_t>(i)) continue;
     const uint8_t st = ustatus[u];
     if (st == kRefused || st == kIllegal || st == kTimedOut) continue;
-    copy_row<VW>(values + i * vb, urows + static_cast<uint64_t>(u) * vb, vb,
-                 tile.lane, kTile);
+    copy_row<VW>(values + i * vb, values + static_cast<uint64_t>(f) * vb, vb, tile.lane,
+                 kTile);
   }
 }
 

@@ -298,7 +298,14 @@ struct UpsertArgs {
   int report_refused;        // insert_and_evict: report refused inputs
   uint8_t** value_ptrs;      // find_or_insert*: address of each key's row
   bool* founds;              // find_or_insert*: the key was already there
+  const uint32_t* row_index; // optional: key i's input/output row is row_index[i]
 };
+
+// Row of key i in the caller's value array: a merged batch of repeated keys
+// keeps each representative's row where its chosen occurrence has it.
+__device__ __forceinline__ uint64_t key_row(const UpsertArgs& a, uint64_t i) {
+  return a.row_index != nullptr ? a.row_index[i] : i;
+}
 
 // ---------------------------------------------------------------------------
 // Lock discipline. A slot is owned by whoever swapped its key word to
@@ -470,11 +477,11 @@ __device__ __forceinline__ void upsert_locked(const TableView& t,
   }
   if constexpr (Mode == kModeFindOrInsert) {
     if (res == kDuplicate)
-      copy_row<VW>(a.values_io + i * vb, row, vb, tile.lane, W);
+      copy_row<VW>(a.values_io + key_row(a, i) * vb, row, vb, tile.lane, W);
     else
-      head.store(row, a.values_io + i * vb, nv, tile.lane);
+      head.store(row, a.values_io + key_row(a, i) * vb, nv, tile.lane);
   } else if constexpr (Mode != kModeFindOrInsertPtr) {
-    head.store(row, a.values_in + i * vb, nv, tile.lane);
+    head.store(row, a.values_in + key_row(a, i) * vb, nv, tile.lane);
   }
   tile.sync();
   if (tile.lane == 0) store_release_u64(t.keys + s, key);
@@ -671,7 +678,8 @@ __global__ void __launch_bounds__(256, HKV_UPSERT_MIN_BLOCKS)
       key = next;
       if (i + stride < n) next = a.keys[i + stride];
       if (!is_reserved(key)) {
-        if constexpr (Mode != kModeFindOrInsertPtr) head.load(in_rows + i * vb, nv, tile.lane);
+        if constexpr (Mode != kModeFindOrInsertPtr)
+          head.load(in_rows + key_row(a, i) * vb, nv, tile.lane);
         desired = desired_when_missed<S>(a.scores, i, a.epoch, clk);
         l = locate(t, key);
         todo = true;
@@ -719,7 +727,7 @@ __global__ void __launch_bounds__(256, HKV_UPSERT_MIN_BLOCKS)
             if (a.ev_scores) a.ev_scores[o] = desired;
           }
           o = tile.shfl(o, 0);
-          head.store(a.ev_values + o * vb, a.values_in + i * vb, nv, tile.lane);
+          head.store(a.ev_values + o * vb, a.values_in + key_row(a, i) * vb, nv, tile.lane);
         }
       }
     }

@@ -502,30 +502,23 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
   const DedupResult d =
       dedup_batch(n, keys, scores, st, ws, s, sm_count_, d_error_);
   uint8_t* ustatus = ws.get<uint8_t>(n);
-  uint8_t* urows = ws.get<uint8_t>(n * static_cast<size_t>(value_bytes_));
-  const uint32_t* rep_first = d.rep_first;
-  const uint32_t* rep_last = d.rep_last;
   const uint32_t* uid_of = d.uid_of;
-  const int vwr = value_width({rows});
-  // insert value: last occurrence (insert_or_assign, insert_and_evict: each
-  // later duplicate overwrites) or first occurrence (find_or_insert: the
-  // first inserts, the rest hit and read it back)
-  DISPATCH_VW(vwr, gather_rows_kernel<VW><<<tile_grid(n), 256, 0, counted(s)>>>(
-                       urows, rows, mode == kModeFindOrInsert ? rep_first
-                                                              : rep_last,
-                       d.dm, value_bytes_));
-  CUDA_TRY(cudaGetLastError());
-
+  // Each representative works on the caller's row of one of its
+  // occurrences, in place: the last (insert_or_assign, insert_and_evict:
+  // each later duplicate overwrites) or the first (find_or_insert: the first
+  // inserts, the rest hit and read it back).
   a.keys = d.ukeys;
-  a.values_in = urows;
-  a.values_io = urows;
+  a.values_in = values_in;
+  a.values_io = values_io;
+  a.row_index = mode == kModeFindOrInsert ? d.rep_first : d.rep_last;
   a.scores = d.uscores;
   a.n = n;
   a.dn = d.dm;
   a.status = ustatus;
   a.report_refused = 0;
   CUDA_TRY(cudaMemsetAsync(ustatus, kIllegal, n, s));
-  const int vw = value_width({urows, ev_values});
+  const int vwr = value_width({rows});
+  const int vw = value_width({rows, ev_values});
   const int grid = upsert_grid(n);
   DISPATCH_STRATEGY(st, DISPATCH_VW(vw, {
     if (mode == kModeInsertOrAssign)
@@ -538,8 +531,7 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
   CUDA_TRY(cudaGetLastError());
   if (mode == kModeFindOrInsert) {
     DISPATCH_VW(vwr, scatter_found_rows_kernel<VW><<<tile_grid(n), 256, 0, counted(s)>>>(
-                         values_io, urows, uid_of, rep_first, ustatus, n,
-                         value_bytes_));
+                         values_io, uid_of, d.rep_first, ustatus, n, value_bytes_));
   } else if (mode == kModeInsertAndEvict) {
     const int vwe = value_width({rows, ev_values});
     DISPATCH_STRATEGY(st, DISPATCH_VW(vwe, {
@@ -1020,9 +1012,8 @@ const char* last_error() { return g_last_error.c_str(); }
 namespace hkvb {
 
 constexpr size_t kNoAllocMaxKeys = 16384;   // keys per call
-constexpr size_t kNoAllocMaxRowBytes = 512; // dim * sizeof(V)
 constexpr size_t kNoAllocSetSlots = 2 * kNoAllocMaxKeys;
-constexpr size_t kNoAllocScratchBytes = 10u << 20;  // 10 MiB, checked below
+constexpr size_t kNoAllocScratchBytes = 2u << 20;  // 2 MiB, checked by ScratchArena
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -1061,9 +1052,6 @@ void TableImpl::find_or_insert_in_scratch(size_t n, const uint64_t* keys,
               "keys and values must not be null");
   HKV_REQUIRE(n <= kNoAllocMaxKeys, HKV_ERR_INVALID,
               "hkv_find_or_insert_noalloc: at most 16384 keys per call");
-  HKV_REQUIRE(value_bytes_ <= kNoAllocMaxRowBytes, HKV_ERR_INVALID,
-              "hkv_find_or_insert_noalloc: value rows of at most 512 bytes "
-              "(dim * sizeof(V))");
   // Growing the table allocates, so this variant refuses a call that would
   // trigger the reference's auto-grow (hkv_hashtable.h:1103-1106).
   HKV_REQUIRE(reach_max_ || fast_load_factor(n, s) <= opt_.max_load_factor,
@@ -1091,33 +1079,30 @@ void TableImpl::find_or_insert_in_scratch(size_t n, const uint64_t* keys,
   uint32_t* rep_last = ws.get<uint32_t>(n);
   uint64_t* uscores = scores ? ws.get<uint64_t>(n) : nullptr;
   uint8_t* ustatus = ws.get<uint8_t>(n);
-  uint8_t* urows = ws.get<uint8_t>(n * static_cast<size_t>(value_bytes_));
   // the array keeps the previous call's contents: reset what starts empty
   CUDA_TRY(cudaMemsetAsync(ustatus, kIllegal, n, s));
   dedup_stages(d, n, keys, scores, score_mode, slot_of, rank, sums, dm, ukeys, rep_first,
                rep_last, uid_of, uscores, s, sm_count_, d_error_);
-  const int vwr = value_width({values});
-  DISPATCH_VW(vwr, gather_rows_kernel<VW><<<tile_grid(n), 256, 0, counted(s)>>>(
-                       urows, values, rep_first, dm, value_bytes_));
+  // representatives find or insert in place at their first occurrence's row
   UpsertArgs a;
   std::memset(&a, 0, sizeof a);
   a.keys = ukeys;
-  a.values_in = urows;
-  a.values_io = urows;
+  a.values_in = values;
+  a.values_io = values;
+  a.row_index = rep_first;
   a.scores = uscores;
   a.n = n;
   a.dn = dm;
   a.epoch = epoch_;
   a.status = ustatus;
   const TableView v = view();
-  const int vw = value_width({urows});
+  const int vw = value_width({values});
   const int grid = upsert_grid(n);
   DISPATCH_STRATEGY(st, DISPATCH_VW(vw, {
     upsert_kernel<kModeFindOrInsert, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
   }));
-  DISPATCH_VW(vwr, scatter_found_rows_kernel<VW><<<tile_grid(n), 256, 0, counted(s)>>>(
-                       values, urows, uid_of, rep_first, ustatus, n,
-                       value_bytes_));
+  DISPATCH_VW(vw, scatter_found_rows_kernel<VW><<<tile_grid(n), 256, 0, counted(s)>>>(
+                      values, uid_of, rep_first, ustatus, n, value_bytes_));
   CUDA_TRY(cudaGetLastError());
 }
 

@@ -307,9 +307,9 @@ int hkv_load_files(hkv_table* table, const char* keys_path,
  * keys (as with unique_key = false) that allocates no device memory, for
  * callers that cannot call cudaMalloc while serving, such as a service whose
  * GPU memory is all handed to a fixed arena at start-up. The duplicate-key
- * merge uses one file-scope device array of 10 MiB instead of per-call
- * scratch, so a call takes at most 16384 keys and value rows of at most 512
- * bytes (dim * sizeof(V)); larger calls fail with HKV_ERR_INVALID. The table
+ * merge uses one file-scope device array of 2 MiB instead of per-call
+ * scratch, so a call takes at most 16384 keys; larger calls fail with
+ * HKV_ERR_INVALID. The table
  * never grows in this call: a batch that would trigger auto-grow fails with
  * HKV_ERR_RUNTIME (call hkv_reserve first). The first call on a device looks
  * up the array's device address, so make that first call before any stream

@@ -57,7 +57,7 @@ def test_noalloc_matches_allocating_entry_point_on_two_calls():
     assert ref.size() == nal.size() > 0
 
 
-def test_noalloc_rejects_sizes_beyond_its_scratch():
+def test_noalloc_rejects_batches_beyond_its_scratch():
     t = make_table(128 * 64, dim=32, strategy=H.EvictStrategy.kLfu)
     n = 16385
     keys = torch.arange(1, n + 1, dtype=torch.int64, device="cuda")
@@ -65,8 +65,14 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     sc = torch.ones(n, dtype=torch.int64, device="cuda")
     with pytest.raises(H.HkvException):
         t.find_or_insert_noalloc(n, keys, vals, sc)
-    wide = make_table(128 * 64, dim=256, strategy=H.EvictStrategy.kLfu)
-    vals = torch.zeros((4, 256), device="cuda")
-    with pytest.raises(H.HkvException):
-        wide.find_or_insert_noalloc(4, keys[:4], vals, sc[:4])
     assert t.size() == 0
+    # rows are found or inserted in place, so any row width works
+    wide = make_table(128 * 64, dim=256, strategy=H.EvictStrategy.kLfu)
+    k4 = torch.tensor([5, 6, 5, 7], dtype=torch.int64, device="cuda")
+    vals = torch.arange(4 * 256, dtype=torch.float32, device="cuda").reshape(4, 256)
+    first = vals.clone()
+    wide.find_or_insert_noalloc(4, k4, vals, sc[:4])
+    torch.cuda.synchronize()
+    assert wide.size() == 3
+    # the repeated key reads back its first occurrence's row
+    assert torch.equal(vals[2], first[0]) and torch.equal(vals[[0, 1, 3]], first[[0, 1, 3]])
