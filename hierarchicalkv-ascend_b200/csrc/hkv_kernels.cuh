@@ -236,44 +236,35 @@ __global__ void __launch_bounds__(256, HKV_FIND_MIN_BLOCKS)
 }
 
 // find over several key arrays at once (segment s has counts[s] keys, at
-// most `bound`): the tiles walk an interleaved index v -> (segment v % nseg,
-// key v / nseg), so every segment is in flight at the same time.
+// most `bound`). The host launches a multiple of nseg blocks: block b works on
+// segment b % nseg, so neighbouring blocks keep every segment in flight,
+// while the tiles of one block take consecutive keys of their segment, so a
+// warp's key loads (which may cross NVLink) are one contiguous read.
 template <int VW>
 __global__ void __launch_bounds__(256, HKV_FIND_MIN_BLOCKS)
     find_segments_kernel(TableView t, FindSegments seg, uint32_t nseg,
                          const uint32_t* __restrict__ counts, uint64_t bound) {
   constexpr uint32_t W = kFindTile;
-  __shared__ uint32_t cnt[kMaxSegments];
-  __shared__ uint32_t cmax;
-  if (threadIdx.x == 0) cmax = 0;
-  __syncthreads();
-  for (uint32_t k = threadIdx.x; k < nseg; k += blockDim.x) {
-    cnt[k] = static_cast<uint32_t>(min(static_cast<uint64_t>(counts[k]), bound));
-    atomicMax(&cmax, cnt[k]);
-  }
-  __syncthreads();
+  constexpr uint32_t kTilesPerBlock = 256 / W;
   const TileW<W> tile;
-  const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / W);
-  const uint64_t total = uint64_t{cmax} * nseg;
+  const uint32_t k = blockIdx.x % nseg;
+  const uint64_t step = uint64_t{gridDim.x / nseg} * kTilesPerBlock;
+  const uint64_t cnt = min(static_cast<uint64_t>(counts[k]), bound);
   // keys may live in a peer's memory (and change between calls: no
   // non-coherent cache); each tile loads its next key one iteration ahead
-  auto load_key = [&](uint64_t v) -> uint64_t {
-    const uint32_t k = static_cast<uint32_t>(v % nseg);
-    const uint64_t j = v / nseg;
-    return v < total && j < cnt[k] ? __ldcg(seg.keys[k] + j) : 0;
-  };
-  uint64_t v = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / W;
-  uint64_t next = load_key(v);
-  for (; v < total; v += ntiles) {
-    const uint32_t k = static_cast<uint32_t>(v % nseg);
-    const uint64_t j = v / nseg;
+  const uint64_t* keys = seg.keys[k];
+  uint8_t* values = seg.values[k];
+  uint8_t* founds = seg.founds[k];
+  uint8_t* scores = seg.scores[k];
+  uint64_t j = uint64_t{blockIdx.x / nseg} * kTilesPerBlock + threadIdx.x / W;
+  uint64_t next = j < cnt ? __ldcg(keys + j) : 0;
+  for (; j < cnt; j += step) {
     const uint64_t key = next;
-    next = load_key(v + ntiles);
-    if (j >= cnt[k]) continue;
+    if (j + step < cnt) next = __ldcg(keys + j + step);
     uint64_t bkt;
     const int p = find_probe(t, tile, key, bkt);
-    find_output<VW>(t, tile, p, bkt, j, seg.values[k], seg.founds[k], seg.scores[k],
-                    seg.row_stride, seg.flag_stride, seg.score_stride);
+    find_output<VW>(t, tile, p, bkt, j, values, founds, scores, seg.row_stride,
+                    seg.flag_stride, seg.score_stride);
   }
 }
 
@@ -643,19 +634,16 @@ __device__ __forceinline__ bool retry_expired(const TableView& t, const Tl& tile
 #endif
 constexpr uint32_t kUpsertTile = HKV_UPSERT_TILE;
 
+// The upsert loop: keys [0, n) of `a`, warp `warp` of `nwarps` taking
+// keys warp * KPW, then every nwarps * KPW.
 template <int Mode, int S, int VW>
-__global__ void __launch_bounds__(256, HKV_UPSERT_MIN_BLOCKS)
-    upsert_kernel(TableView t, UpsertArgs a) {
+__device__ __forceinline__ void upsert_body(const TableView& t, const UpsertArgs& a,
+                                            uint64_t clk, uint64_t warp,
+                                            uint64_t nwarps) {
   constexpr uint32_t W = kUpsertTile;
   constexpr uint32_t KPW = 32 / W;  // keys per warp
-  __shared__ uint64_t s_clock;
-  if (threadIdx.x == 0) s_clock = global_timer_ns();
-  __syncthreads();
-  const uint64_t clk = s_clock;
   const TileW<W> tile;
   const uint32_t wl = threadIdx.x & 31;
-  const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x / 32);
-  const uint64_t warp = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / 32;
   const uint64_t n = a.dn != nullptr ? *a.dn : a.n;
   const uint32_t vb = t.value_bytes;
   const uint32_t nv = vb / VW;
@@ -732,6 +720,17 @@ __global__ void __launch_bounds__(256, HKV_UPSERT_MIN_BLOCKS)
       }
     }
   }
+}
+
+template <int Mode, int S, int VW>
+__global__ void __launch_bounds__(256, HKV_UPSERT_MIN_BLOCKS)
+    upsert_kernel(TableView t, UpsertArgs a) {
+  __shared__ uint64_t s_clock;
+  if (threadIdx.x == 0) s_clock = global_timer_ns();
+  __syncthreads();
+  upsert_body<Mode, S, VW>(t, a, s_clock,
+                           (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / 32,
+                           (uint64_t)gridDim.x * (blockDim.x / 32));
 }
 
 // ============================================================================

@@ -236,7 +236,8 @@ __global__ void __launch_bounds__(256)
                      const uint32_t* __restrict__ dm, uint64_t n,
                      uint32_t world, uint32_t self, PeerBases peers,
                      WinLayout lay, uint32_t* __restrict__ counters,
-                     uint64_t* __restrict__ where, uint64_t epoch,
+                     uint64_t* __restrict__ where, uint32_t* __restrict__ inv,
+                     uint32_t* __restrict__ sent, uint64_t epoch,
                      int* __restrict__ err) {
   __shared__ uint32_t cnt[kMaxWorld];
   __shared__ uint32_t base[kMaxWorld];
@@ -272,6 +273,7 @@ __global__ void __launch_bounds__(256)
         skeys[slot] = key;
         if (scores != nullptr) sscores[slot] = scores[u];
         where[u] = (uint64_t{d} << 32) | pos;
+        inv[slot] = static_cast<uint32_t>(u);
       } else {
         atomicOr(err, kErrPeerOverflow);
         where[u] = ~uint64_t{0};
@@ -306,6 +308,7 @@ __global__ void __launch_bounds__(256)
     __threadfence();
     for (uint32_t w = threadIdx.x; w < world; w += blockDim.x) {
       const uint32_t c = min(atomicAdd(&counters[w], 0u), static_cast<uint32_t>(lay.M));
+      sent[w] = c;
       st_release_sys_u64(flag_at(peers.base[w], lay.arrive, self), (epoch << 32) | c);
       counters[w] = 0;
     }
@@ -435,6 +438,64 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// finish in owner order (find, and find_or_insert of a batch without merged
+// duplicates): block b reads owner b % world's result region for this rank
+// front to back, so the tiles of a warp read consecutive rows and tails over
+// NVLink; inv (written by route) maps each position back to its input.
+// sent[o] is the number of keys this rank routed to owner o.
+template <int VW>
+__global__ void __launch_bounds__(256)
+    p2p_finish_ordered_kernel(int mode, PeerBases peers, WinLayout lay, uint32_t world,
+                              uint32_t self, uint64_t epoch, int* err,
+                              const uint32_t* __restrict__ sent,
+                              const uint32_t* __restrict__ inv,
+                              uint8_t* __restrict__ values, bool* __restrict__ founds,
+                              uint64_t* __restrict__ scores) {
+  wait_flags(peers.base[self], lay.done, world, epoch, false, nullptr, err, 302);
+  __syncthreads();
+  using V = typename VecOf<VW>::T;
+  constexpr uint32_t W = 4;
+  constexpr uint32_t kTilesPerBlock = 256 / W;
+  constexpr uint32_t kHead = 4;  // row vectors per lane held in registers
+  const TileW<W> tile;
+  const uint32_t vb = lay.vb;
+  const uint32_t nv = vb / VW;
+  const uint32_t o = blockIdx.x % world;
+  const uint64_t step = uint64_t{gridDim.x / world} * kTilesPerBlock;
+  const uint64_t c = min(static_cast<uint64_t>(sent[o]), lay.M);
+  const uint8_t* ob = peers.base[o];
+  const uint64_t region = uint64_t{self} * lay.M;
+  const uint32_t* invo = inv + uint64_t{o} * lay.M;
+  for (uint64_t pos = uint64_t{blockIdx.x / world} * kTilesPerBlock + threadIdx.x / W;
+       pos < c; pos += step) {
+    const uint64_t slot = region + pos;
+    const V* sp = reinterpret_cast<const V*>(ob + lay.res_rows + slot * vb);
+    V head[kHead];
+#pragma unroll
+    for (uint32_t h = 0; h < kHead; h++)
+      if (values != nullptr && tile.lane + h * W < nv) head[h] = __ldcg(sp + tile.lane + h * W);
+    // tail: find -> score (8 bytes) | found flag; find_or_insert -> status
+    uint4 tail = make_uint4(0, 0, 0, 0);
+    if (tile.lane == 0)
+      tail = __ldcg(reinterpret_cast<const uint4*>(ob + lay.res_tail) + slot);
+    const uint64_t i = invo[pos];
+    const uint32_t f = tile.shfl(tail.z & 0xFFu, 0);
+    const bool ok = mode == 0 ? f != 0 : (f != kRefused && f != kIllegal && f != kTimedOut);
+    const uint64_t sc = (uint64_t{tail.y} << 32) | tail.x;
+    if (tile.lane == 0) {
+      if (founds != nullptr) founds[i] = ok;
+      if (ok && scores != nullptr) scores[i] = sc;
+    }
+    if (ok && values != nullptr) {
+      V* dp = reinterpret_cast<V*>(values + i * vb);
+#pragma unroll
+      for (uint32_t h = 0; h < kHead; h++)
+        if (tile.lane + h * W < nv) dp[tile.lane + h * W] = head[h];
+      for (uint32_t v = tile.lane + kHead * W; v < nv; v += W) dp[v] = __ldcg(sp + v);
+    }
+  }
+}
+
 }  // namespace
 
 class ShardedImpl {
@@ -471,6 +532,8 @@ class ShardedImpl {
       cudaFree(win_);
       cudaFree(d_route_counters_);
       cudaFree(d_where_);
+      cudaFree(d_inv_);
+      cudaFree(d_sent_);
     }
     if (comm_) ncclCommDestroy(comm_);
     delete local_;
@@ -665,7 +728,9 @@ class ShardedImpl {
                cudaSuccess &&
            cudaMemset(d_route_counters_, 0, (kMaxWorld + 1) * sizeof(uint32_t)) ==
                cudaSuccess &&
-           cudaMalloc(&d_where_, max_batch * sizeof(uint64_t)) == cudaSuccess;
+           cudaMalloc(&d_where_, max_batch * sizeof(uint64_t)) == cudaSuccess &&
+           cudaMalloc(&d_inv_, world_ * max_batch * sizeof(uint32_t)) == cudaSuccess &&
+           cudaMalloc(&d_sent_, kMaxWorld * sizeof(uint32_t)) == cudaSuccess;
       cudaGetLastError();
       again.ok = ok;
       exchange_bytes(&again, all.data(), sizeof(Rec), s);
@@ -678,9 +743,13 @@ class ShardedImpl {
       cudaFree(win_);
       cudaFree(d_route_counters_);
       cudaFree(d_where_);
+      cudaFree(d_inv_);
+      cudaFree(d_sent_);
       win_ = nullptr;
       d_route_counters_ = nullptr;
       d_where_ = nullptr;
+      d_inv_ = nullptr;
+      d_sent_ = nullptr;
       return;
     }
     max_batch_ = max_batch;
@@ -738,7 +807,7 @@ class ShardedImpl {
     SHARD_DISPATCH_VW(vw, p2p_route_kernel<VW><<<gr, 256, 0, counted(s)>>>(
                               rkeys, rscores, kind == 0 ? nullptr : values, row_of,
                               dm, n, world_, me, peers_, lay_, d_route_counters_,
-                              d_where_, epoch_, err));
+                              d_where_, d_inv_, d_sent_, epoch_, err));
     CUDA_TRY(cudaGetLastError());
     // 2. serve what the requesters sorted for this rank
     uint32_t* counts = d_counts_;  // kMaxWorld entries, device
@@ -768,6 +837,9 @@ class ShardedImpl {
                                    peers_, lay_, world_, me, counts));
         CUDA_TRY(cudaGetLastError());
       }
+      // one launch per requester, in rank order: a key sent by several
+      // requesters is applied once per requester, in rank order (concurrent
+      // inserts of one new key could both claim an empty slot)
       for (int src = 0; src < world_; src++) {
         const uint64_t o = uint64_t{static_cast<uint32_t>(src)} * M;
         uint8_t* pb = peers_.base[src];
@@ -792,15 +864,25 @@ class ShardedImpl {
     const int vwf = (kind == 2 || values == nullptr)
                         ? 16
                         : local_->value_width({values, win_ + lay_.res_rows});
-    const int gf = static_cast<int>(std::max<uint64_t>(
-        1, std::min<uint64_t>(ceil_div(std::max<uint64_t>(n, 1) * 4, 256),
-                              sm_count_ * 16ull)));
-    SHARD_DISPATCH_VW(vwf, p2p_finish_kernel<VW><<<gf, 256, 0, counted(s)>>>(
-                               kind, peers_, lay_, world_, me, epoch_, err, n, d_where_,
-                               kind == 1 ? uid_of : nullptr,
-                               kind == 2 ? nullptr : values,
-                               kind == 0 ? founds : nullptr,
-                               kind == 0 ? scores : nullptr));
+    if (kind == 0 || (kind == 1 && uid_of == nullptr)) {
+      // a multiple of world blocks: block b reads owner b % world's results
+      const uint64_t per_owner = std::max<uint64_t>(
+          1, std::min<uint64_t>(ceil_div(std::max<uint64_t>(n, 1) * 4, 256),
+                                sm_count_ * 16ull / world_));
+      const int gf = static_cast<int>(per_owner * world_);
+      SHARD_DISPATCH_VW(vwf, p2p_finish_ordered_kernel<VW><<<gf, 256, 0, counted(s)>>>(
+                                 kind, peers_, lay_, world_, me, epoch_, err, d_sent_,
+                                 d_inv_, values, kind == 0 ? founds : nullptr,
+                                 kind == 0 ? scores : nullptr));
+    } else {
+      const int gf = static_cast<int>(std::max<uint64_t>(
+          1, std::min<uint64_t>(ceil_div(std::max<uint64_t>(n, 1) * 4, 256),
+                                sm_count_ * 16ull)));
+      SHARD_DISPATCH_VW(vwf, p2p_finish_kernel<VW><<<gf, 256, 0, counted(s)>>>(
+                                 kind, peers_, lay_, world_, me, epoch_, err, n, d_where_,
+                                 kind == 1 ? uid_of : nullptr,
+                                 kind == 2 ? nullptr : values, nullptr, nullptr));
+    }
     CUDA_TRY(cudaGetLastError());
   }
 
@@ -833,6 +915,8 @@ class ShardedImpl {
   PeerBases peers_{};
   uint32_t* d_route_counters_ = nullptr;
   uint64_t* d_where_ = nullptr;  // owner << 32 | position of each routed key
+  uint32_t* d_inv_ = nullptr;    // [world][max_batch] input of each routed position
+  uint32_t* d_sent_ = nullptr;   // [kMaxWorld] keys routed to each owner
 };
 
 void set_last_error(const std::string& m);

@@ -745,9 +745,11 @@ void TableImpl::find_segments(const FindSegments& seg, uint32_t nseg,
 #ifndef HKV_SEG_BLOCKS_PER_SM
 #define HKV_SEG_BLOCKS_PER_SM 64
 #endif
-  const int grid = static_cast<int>(std::min<uint64_t>(
-      ceil_div(std::max<uint64_t>(bound * nseg, 1), 256 / kFindTile),
-      sm_count_ * uint64_t{HKV_SEG_BLOCKS_PER_SM}));
+  // a multiple of nseg blocks: block b serves segment b % nseg
+  const uint64_t per_seg = std::max<uint64_t>(
+      1, std::min<uint64_t>(ceil_div(bound, 256 / kFindTile),
+                            sm_count_ * uint64_t{HKV_SEG_BLOCKS_PER_SM} / nseg));
+  const int grid = static_cast<int>(per_seg * nseg);
   DISPATCH_VW(vw, find_segments_kernel<VW><<<grid, 256, 0, counted(s)>>>(
                       v, seg, nseg, counts, bound));
   CUDA_TRY(cudaGetLastError());
