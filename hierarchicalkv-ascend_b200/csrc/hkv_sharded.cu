@@ -801,9 +801,10 @@ class ShardedImpl {
     }
     const int vw = kind == 0 ? 16
                              : local_->value_width({values, win_ + lay_.snd_rows});
+    // a full wave (8 blocks of 256 per SM): the row copies are latency-bound
     const int gr = static_cast<int>(std::max<uint64_t>(
         1, std::min<uint64_t>(ceil_div(std::max<uint64_t>(n, 1), 256),
-                              sm_count_ * 4ull)));
+                              sm_count_ * 8ull)));
     SHARD_DISPATCH_VW(vw, p2p_route_kernel<VW><<<gr, 256, 0, counted(s)>>>(
                               rkeys, rscores, kind == 0 ? nullptr : values, row_of,
                               dm, n, world_, me, peers_, lay_, d_route_counters_,
