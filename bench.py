@@ -505,6 +505,145 @@ def save_load_times(device, capacity=8 << 20):
 
 
 # --------------------------------------------------------------------------
+# --suite: every table operation on the config-2 table (one GPU, load factor
+# 1.0), each timed with CUDA events over its own inputs and set against its
+# algorithmic bytes per key (per slot for export_batch and reserve; dim 32,
+# 128-byte rows). Not the headline metric; run on request.
+# --------------------------------------------------------------------------
+SUITE_BYTES = {
+    "find_hit": 401,            # key 8, digest line 128, key 8, row 128 in + out, found 1
+    "find_miss": 141,           # key 8, digest line 128, found 1, ~0.5 false digest hits
+    "contains_hit": 145,        # key 8, digest line 128, key 8, found 1
+    "insert_or_assign": 928.5,  # 50 % hits (416), 50 % evicting misses (1441)
+    "find_or_insert": 928.5,    # same mix; hits copy the row out, misses in
+    "insert_and_evict": 1064.5,  # evicting misses also write the victim out (+272)
+    "accum_or_assign": 537,     # hits: key, flag, digest line, key, delta + row in, row out, score
+    "assign_scores": 152,       # hits: key, digest line, key, score out
+    "erase": 165,               # hits: key, digest line, key, key + score + digest + size out
+    "export_batch": 288,        # per live slot: key, row, score in; key, row, score out
+    "reserve": 290,             # per old slot: key, score, digest, row read once and written once
+}
+
+
+def run_suite(args):
+    import torch
+
+    import hkv_b200 as H
+
+    dev = torch.device("cuda", 0)
+    cap = args.capacity
+    steps, warm = args.steps, args.warmup
+    table, local = build_table(1, 0, None, cap)
+    total = prefill(local, 0, 1, dev, cap)
+    nb = steps + warm
+    finds, inserts, vals = prepare_batches(4 * nb, 0, 1, total, dev, 11, cap)
+    n = BATCH
+    misses = [keys_from_counters((1 << 40) + i * BATCH, BATCH, dev) for i in range(nb)]
+    out = torch.empty((n, DIM), device=dev)
+    founds = torch.zeros(n, dtype=torch.bool, device=dev)
+    ev_keys = torch.empty(n, dtype=torch.int64, device=dev)
+    ev_vals = torch.empty((n, DIM), device=dev)
+    ev_scores = torch.empty(n, dtype=torch.int64, device=dev)
+    counter = torch.zeros(1, dtype=torch.int64, device=dev)
+    flags = torch.ones(n, dtype=torch.bool, device=dev)
+    ins_i = [0]
+
+    def next_insert():
+        i = ins_i[0]
+        ins_i[0] += 1
+        return inserts[i], vals[i]
+
+    ops = {
+        "find_hit": lambda i: table.find(n, finds[i], out, founds),
+        "find_miss": lambda i: table.find(n, misses[i], out, founds),
+        "contains_hit": lambda i: table.contains(n, finds[i], founds),
+        "insert_or_assign": lambda i: table.insert_or_assign(n, *next_insert(), unique_key=True),
+        "find_or_insert": lambda i: table.find_or_insert(n, *next_insert(), unique_key=True),
+        "insert_and_evict": lambda i: (counter.zero_(), table.insert_and_evict(
+            n, *next_insert(), None, ev_keys, ev_vals, ev_scores, counter, unique_key=True)),
+        "accum_or_assign": lambda i: table.accum_or_assign(n, finds[i], vals[i], flags),
+        "assign_scores": lambda i: table.assign_scores(n, finds[i]),
+    }
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    peak, peak_kind = peaks()
+    rows = []
+
+    def record(name, ms, units, launches):
+        b = SUITE_BYTES[name]
+        gbs = units * b / (ms * 1e-3) / 1e9
+        rows.append({"op": name, "ms_per_call": round(ms, 4),
+                     "bkvs": round(units / (ms * 1e-3) / 1e9, 4), "bytes_per_unit": b,
+                     "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+                     "gpu_launches_per_call": launches})
+        log(f"{name:18s} {ms * 1000:9.1f} us  {rows[-1]['bkvs']:7.3f} B/s  {gbs:7.0f} GB/s")
+
+    for name, fn in ops.items():
+        for i in range(warm):
+            fn(i)
+        torch.cuda.synchronize()
+        l0 = H.kernel_launches()
+        ev0.record()
+        for i in range(warm, nb):
+            fn(i)
+        ev1.record()
+        torch.cuda.synchronize()
+        record(name, ev0.elapsed_time(ev1) / steps, n, (H.kernel_launches() - l0) / steps)
+    # erase resident keys, then put them back (untimed) so the table stays full
+    times = []
+    for i in range(nb):
+        k = finds[i]
+        torch.cuda.synchronize()
+        ev0.record()
+        table.erase(n, k)
+        ev1.record()
+        torch.cuda.synchronize()
+        if i >= warm:
+            times.append(ev0.elapsed_time(ev1))
+        table.insert_or_assign(n, k, vals[i], unique_key=True)
+    record("erase", statistics.median(times), n, 1)
+    # export the whole table in 8 Mi-slot pieces
+    piece = min(8 << 20, cap)
+    ek = torch.empty(piece, dtype=torch.int64, device=dev)
+    evv = torch.empty((piece, DIM), device=dev)
+    es = torch.empty(piece, dtype=torch.int64, device=dev)
+    live = table.size()
+    torch.cuda.synchronize()
+    ev0.record()
+    for off in range(0, cap, piece):
+        table.export_batch(piece, off, ek, evv, es, d_counter=counter)
+    ev1.record()
+    torch.cuda.synchronize()
+    record("export_batch", ev0.elapsed_time(ev1), live, cap // piece)
+    table.check_device_error()
+    # reserve: a growable table (max = 2 x capacity) at load factor 0.75
+    # doubles once (rehash of every slot)
+    del table, local
+    grow = H.HashTable(H.EvictStrategy.kLru)
+    grow.init(H.HashTableOptions(init_capacity=cap, max_capacity=2 * cap,
+                                 max_hbm_for_vectors=2 * cap * VALUE_BYTES, dim=DIM,
+                                 max_load_factor=1.0))
+    fill = cap * 3 // 4
+    for st in range(0, fill, n):  # n-row value batches
+        m = min(n, fill - st)
+        grow.insert_or_assign(m, keys_from_counters((1 << 41) + st, m, dev), vals[0][:m])
+    torch.cuda.synchronize()
+    l0 = H.kernel_launches()
+    ev0.record()
+    grow.reserve(2 * cap)
+    ev1.record()
+    torch.cuda.synchronize()
+    assert grow.capacity() == 2 * cap
+    record("reserve", ev0.elapsed_time(ev1), cap, H.kernel_launches() - l0)
+    grow.check_device_error()
+    print(json.dumps({"suite": rows, "capacity": cap, "dim": DIM, "batch": n,
+                      "strategy": "kLru", "load_factor_before": 1.0,
+                      "steps": steps, "warmup": warm,
+                      "peak_gbs": peak, "peak_kind": peak_kind}),
+          flush=True)
+
+
+# --------------------------------------------------------------------------
 # --workload zipf: find_or_insert of power-law (Zipf-like) keys with repeats
 # (unique_key = false), dim 64: 128 Mi slots, kEpochLfu, 2 Mi keys per step on
 # one GPU; 256 Mi slots per GPU, kLfu, 8 Mi keys per GPU per step when
@@ -746,6 +885,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--capacity", type=int, default=CAPACITY,
                     help="slots per GPU (diagnostics; the metric uses the default)")
+    ap.add_argument("--suite", action="store_true",
+                    help="time every table operation on one GPU (not the headline)")
     ap.add_argument("--workload", default="cfg2", choices=["cfg2", "zipf"],
                     help="cfg2: the headline metric; zipf: find_or_insert of "
                          "power-law keys with repeats (dim 64)")
@@ -755,6 +896,9 @@ def main():
         return
     if args.workload == "zipf":
         run_zipf(args)
+        return
+    if args.suite:
+        run_suite(args)
         return
     run_gpu(args)
 

@@ -171,8 +171,13 @@ __device__ __forceinline__ void backoff(int round) {
 __device__ __forceinline__ uint64_t ld_cg_u64(const uint64_t* p) {
   return __ldcg(reinterpret_cast<const unsigned long long*>(p));
 }
-__device__ __forceinline__ uint64_t ld_volatile_u64(const uint64_t* p) {
-  return *reinterpret_cast<const volatile unsigned long long*>(p);
+// A strong load at GPU scope (table words are only written by kernels on
+// the table's own GPU). A C++ volatile load would be relaxed at system scope,
+// which after an acquire on the same slot measured ~10x slower per key.
+__device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 __device__ __forceinline__ uint64_t cas_u64(uint64_t* p, uint64_t expect,
                                             uint64_t desired) {

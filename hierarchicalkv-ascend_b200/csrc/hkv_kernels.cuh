@@ -435,7 +435,7 @@ __device__ __forceinline__ void upsert_locked(const TableView& t,
     uint64_t ns;
     // only the Lfu rules add to the stored score
     const uint64_t old =
-        (ins || (S != kLfu && S != kEpochLfu)) ? 0 : ld_volatile_u64(t.scores + s);
+        (ins || (S != kLfu && S != kEpochLfu)) ? 0 : ld_relaxed_u64(t.scores + s);
     if (score_on_write<S>(old, a.scores, i, desired, ins, &ns)) {
       if (ins) t.digests[s] = static_cast<uint8_t>(l.d4);
       t.scores[s] = ns;
@@ -584,7 +584,7 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const TileW<W>& 
           if (k == kEmptyKey) {
             store_release_u64(bk + mp, kEmptyKey);
           } else if (k != kLockedKey) {
-            if (ld_volatile_u64(bs + mp) <= ms)
+            if (ld_relaxed_u64(bs + mp) <= ms)
               r = (k == kReclaimKey) ? kOccupiedReclaimed : kEvict;
             else
               store_release_u64(bk + mp, k);
@@ -786,7 +786,7 @@ restart:
   for (uint32_t w = 0; w < kBucket; w += 32) {
     const uint32_t q = (l.pos + w + lane) & (kBucket - 1);
     while (true) {
-      const uint64_t k = ld_volatile_u64(bk + q);
+      const uint64_t k = ld_relaxed_u64(bk + q);
       const uint32_t hit = __ballot_sync(0xFFFFFFFFu, k == key);
       if (hit) {
         const int src = __ffs(hit) - 1;
@@ -831,11 +831,11 @@ restart:
   uint32_t lp = 0;
   for (uint32_t w = 0; w < kBucket; w += 32) {
     const uint32_t q = (l.pos + w + lane) & (kBucket - 1);
-    const uint64_t sc = ld_volatile_u64(bs + q);
+    const uint64_t sc = ld_relaxed_u64(bs + q);
     if (sc < lm) {
       uint64_t k;
       bool gave_up = false;
-      while ((k = ld_volatile_u64(bk + q)) == kLockedKey) {
+      while ((k = ld_relaxed_u64(bk + q)) == kLockedKey) {
         if (expired()) {
           gave_up = true;
           break;
@@ -859,7 +859,7 @@ restart:
     int ok = 0;
     if (static_cast<int>(lane) == src) {
       if (cas_acquire_u64(bk + lp, lk, kLockedKey) == lk) {
-        if (ld_volatile_u64(bs + lp) <= gm)
+        if (ld_relaxed_u64(bs + lp) <= gm)
           ok = 1;
         else
           store_release_u64(bk + lp, lk);
@@ -916,8 +916,10 @@ __global__ void __launch_bounds__(256) accum_kernel(TableView t, AccumArgs a) {
               atomicAdd(t.sizes + l.bkt, 1);
             const bool ins = res != kDuplicate;
             uint64_t ns;
-            if (score_on_write<S>(ld_volatile_u64(t.scores + s), a.scores, i,
-                                  desired, ins, &ns)) {
+            const uint64_t old = (ins || (S != kLfu && S != kEpochLfu))
+                                     ? 0
+                                     : ld_relaxed_u64(t.scores + s);
+            if (score_on_write<S>(old, a.scores, i, desired, ins, &ns)) {
               t.digests[s] = static_cast<uint8_t>(l.d4);
               t.scores[s] = ns;
             }
@@ -954,7 +956,7 @@ __device__ __forceinline__ int tile_locate_existing(const TableView& t,
   while (hits) {
     const uint32_t j = __ffs(hits) - 1;
     hits &= hits - 1;
-    const uint64_t k = ld_volatile_u64(bk + lo + j);
+    const uint64_t k = ld_relaxed_u64(bk + lo + j);
     if (k == key) {
       mine = static_cast<int>(lo + j);
       break;
@@ -972,7 +974,7 @@ __device__ __forceinline__ int tile_locate_existing(const TableView& t,
       const uint32_t j = __ffs(empt) - 1;
       empt &= empt - 1;
       const uint32_t q = lo + j;
-      if (empty_rank(q, l.pos) < pr && ld_volatile_u64(bk + q) == kEmptyKey)
+      if (empty_rank(q, l.pos) < pr && ld_relaxed_u64(bk + q) == kEmptyKey)
         stop = true;
     }
     if (tile.ballot(stop)) return -1;
@@ -1029,8 +1031,10 @@ __global__ void __launch_bounds__(256)
               store_release_u64(t.keys + s, kReclaimKey);
             } else {
               uint64_t ns;
-              if (score_without_missed<S>(ld_volatile_u64(t.scores + s), scores,
-                                          i, epoch, clk, &ns))
+              // only the Lfu rules read the stored score
+              const uint64_t old =
+                  (S == kLfu || S == kEpochLfu) ? ld_relaxed_u64(t.scores + s) : 0;
+              if (score_without_missed<S>(old, scores, i, epoch, clk, &ns))
                 t.scores[s] = ns;
               store_release_u64(t.keys + s, key);
             }
