@@ -171,6 +171,19 @@ __device__ __forceinline__ void backoff(int round) {
 __device__ __forceinline__ uint64_t ld_cg_u64(const uint64_t* p) {
   return __ldcg(reinterpret_cast<const unsigned long long*>(p));
 }
+// Output position for a counter shared by the whole grid: the lanes of a
+// warp that call this together take consecutive positions with one atomic
+// (one per warp instead of one per lane on a single hot word).
+__device__ __forceinline__ unsigned long long warp_claim(unsigned long long* counter) {
+  const uint32_t act = __activemask();
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t leader = __ffs(act) - 1;
+  unsigned long long base = 0;
+  if (lane == leader) base = atomicAdd(counter, static_cast<unsigned long long>(__popc(act)));
+  base = __shfl_sync(act, base, leader);
+  return base + __popc(act & ((1u << lane) - 1));
+}
+
 // A strong load at GPU scope (table words are only written by kernels on
 // the table's own GPU). A C++ volatile load would be relaxed at system scope,
 // which after an acquire on the same slot measured ~10x slower per key.

@@ -444,7 +444,7 @@ __device__ __forceinline__ void upsert_locked(const TableView& t,
       atomicAdd(t.sizes + l.bkt, 1);
     if constexpr (Mode == kModeInsertAndEvict) {
       if (res == kEvict) {
-        ev_idx = atomicAdd(a.ev_counter, 1ull);
+        ev_idx = warp_claim(a.ev_counter);
         if (!HKV_BOUND(t, ev_idx < a.n, 3)) ev_idx = 0;
         a.ev_keys[ev_idx] = vkey;
         if (a.ev_scores) a.ev_scores[ev_idx] = vscore;
@@ -709,7 +709,7 @@ __device__ __forceinline__ void upsert_body(const TableView& t, const UpsertArgs
           // refused input is reported with its desired score
           unsigned long long o = 0;
           if (tile.lane == 0) {
-            o = atomicAdd(a.ev_counter, 1ull);
+            o = warp_claim(a.ev_counter);
             if (!HKV_BOUND(t, o < a.n, 4)) o = 0;
             a.ev_keys[o] = key;
             if (a.ev_scores) a.ev_scores[o] = desired;
@@ -733,11 +733,57 @@ __global__ void __launch_bounds__(256, HKV_UPSERT_MIN_BLOCKS)
                            (uint64_t)gridDim.x * (blockDim.x / 32));
 }
 
+// Finds the slot holding `key` with plain loads (the reference's find rule
+// when kStopRule: a digest-empty EMPTY_KEY slot earlier in the walk hides
+// it). Returns the slot, -1 if absent, -2 if a locked digest-hit slot may
+// hold the key (the caller retries).
+template <bool kStopRule>
+__device__ __forceinline__ int tile_locate_existing(const TableView& t,
+                                                    const Tile& tile,
+                                                    const Locate& l,
+                                                    uint64_t key) {
+  const uint64_t* bk = t.keys + l.bkt * kBucket;
+  const uint4 dv = __ldcg(
+      reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) + tile.lane);
+  const uint32_t lo = tile.lane * kDigestsPerLane;
+  uint32_t hits = bytes_eq16(dv, l.d4);
+  int mine = -1;
+  bool busy = false;
+  while (hits) {
+    const uint32_t j = __ffs(hits) - 1;
+    hits &= hits - 1;
+    const uint64_t k = ld_relaxed_u64(bk + lo + j);
+    if (k == key) {
+      mine = static_cast<int>(lo + j);
+      break;
+    }
+    busy |= (k == kLockedKey);
+  }
+  const uint32_t fm = tile.ballot(mine >= 0);
+  if (!fm) return tile.ballot(busy) ? -2 : -1;
+  const uint32_t p = tile.shfl(static_cast<uint32_t>(mine), __ffs(fm) - 1);
+  if constexpr (kStopRule) {
+    uint32_t empt = bytes_eq16(dv, kEmptyDigest * 0x01010101u);
+    const uint32_t pr = hit_rank(p, l.pos);
+    bool stop = false;
+    while (empt) {
+      const uint32_t j = __ffs(empt) - 1;
+      empt &= empt - 1;
+      const uint32_t q = lo + j;
+      if (empty_rank(q, l.pos) < pr && ld_relaxed_u64(bk + q) == kEmptyKey)
+        stop = true;
+    }
+    if (tile.ballot(stop)) return -1;
+  }
+  return static_cast<int>(p);
+}
+
 // ============================================================================
 // accum_or_assign (reference accum_or_assign_kernel.h:55-155 with
-// find_and_lock, find_utils.h:94-228): one warp per key, 32-slot windows
-// from pos. Waits on LOCKED slots (bounded), so duplicate keys in one batch
-// serialise on the key word.
+// find_and_lock, find_utils.h:94-228). A present key is found through its
+// digest line by an 8-lane tile and locked with one CAS; any other key takes
+// the whole warp: 32-slot windows from pos, waiting on LOCKED slots
+// (bounded), so duplicate keys in one batch serialise on the key word.
 // ============================================================================
 struct AccumArgs {
   const uint64_t* keys;
@@ -876,60 +922,111 @@ restart:
   goto restart;
 }
 
+// With `slot` locked (res as warp_find_and_lock returns it): undo when the
+// operation does not apply (reference :114-128), else accumulate or assign
+// the row, set size, digest and score, and release. `width` lanes of the
+// calling group take part; sync() orders their row writes before the release.
+template <int S, class VT, class Sync>
+__device__ __forceinline__ int accum_apply(const TableView& t, const AccumArgs& a,
+                                           uint64_t i, uint64_t key, bool is_accum,
+                                           uint64_t desired, const Locate& l,
+                                           uint32_t slot, uint64_t evk, int res,
+                                           uint32_t lane, uint32_t width, Sync sync) {
+  uint64_t* bk = t.keys + l.bkt * kBucket;
+  const uint64_t s = l.bkt * kBucket + slot;
+  if ((is_accum && res != kDuplicate) || (!is_accum && res == kDuplicate)) {
+    if (lane == 0) store_release_u64(bk + slot, res == kDuplicate ? key : evk);
+    return kIllegal;
+  }
+  const uint32_t vb = t.value_bytes;
+  const uint32_t ne = vb / sizeof(VT);
+  VT* dst = reinterpret_cast<VT*>(value_ptr(t, l.bkt, slot));
+  const VT* src = reinterpret_cast<const VT*>(a.values + i * vb);
+  for (uint32_t e = lane; e < ne; e += width)
+    dst[e] = is_accum ? AccumOps<VT>::add(src[e], dst[e]) : src[e];
+  if (lane == 0) {
+    if (res == kOccupiedEmpty || res == kOccupiedReclaimed) atomicAdd(t.sizes + l.bkt, 1);
+    const bool ins = res != kDuplicate;
+    uint64_t ns;
+    const uint64_t old =
+        (ins || (S != kLfu && S != kEpochLfu)) ? 0 : ld_relaxed_u64(t.scores + s);
+    if (score_on_write<S>(old, a.scores, i, desired, ins, &ns)) {
+      t.digests[s] = static_cast<uint8_t>(l.d4);
+      t.scores[s] = ns;
+    }
+  }
+  sync();
+  if (lane == 0) store_release_u64(bk + slot, key);
+  return res;
+}
+
+// Four keys per warp, one 8-lane tile each: a present, unlocked key is found
+// through its digest line and locked with one CAS (the common case). The
+// others (absent keys, keys whose slot another lane holds, keys being
+// inserted) then go one at a time through the whole warp's window scan,
+// which waits on locked slots, so repeats of a key serialise on its word.
 template <int S, class VT>
 __global__ void __launch_bounds__(256) accum_kernel(TableView t, AccumArgs a) {
   __shared__ uint64_t s_clock;
   if (threadIdx.x == 0) s_clock = global_timer_ns();
   __syncthreads();
   const uint64_t clk = s_clock;
-  const uint32_t lane = threadIdx.x & 31;
+  const Tile tile;
+  const uint32_t wl = threadIdx.x & 31;
   const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x / 32);
-  const uint32_t vb = t.value_bytes;
-  const uint32_t ne = vb / sizeof(VT);
-  for (uint64_t i = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / 32;
-       i < a.n; i += nwarps) {
-    const uint64_t key = a.keys[i];
+  const uint64_t warp = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / 32;
+  for (uint64_t base = warp * 4; base < a.n; base += nwarps * 4) {
+    const uint64_t i = base + (wl >> 3);
+    const bool in = i < a.n;
+    const uint64_t key = in ? a.keys[i] : 0;
+    const bool valid = in && !is_reserved(key);
     int res = kIllegal;
-    if (!is_reserved(key)) {
-      const uint64_t desired = desired_when_missed<S>(a.scores, i, a.epoch, clk);
-      const bool is_accum = a.accum_or_assigns[i];
-      const Locate l = locate(t, key);
+    bool pending = false;
+    uint64_t desired = 0;
+    bool is_accum = false;
+    Locate l;
+    l.bkt = 0;
+    l.pos = 0;
+    l.d4 = 0;
+    if (valid) {
+      desired = desired_when_missed<S>(a.scores, i, a.epoch, clk);
+      is_accum = a.accum_or_assigns[i];
+      l = locate(t, key);
+      const int p = tile_locate_existing<false>(t, tile, l, key);
+      bool got = false;
+      if (p >= 0 && tile.lane == 0)
+        got = cas_acquire_u64(t.keys + l.bkt * kBucket + p, key, kLockedKey) == key;
+      if (tile.shfl(got, 0))
+        res = accum_apply<S, VT>(t, a, i, key, is_accum, desired, l,
+                                 static_cast<uint32_t>(p), key, kDuplicate, tile.lane, kTile,
+                                 [&]() { tile.sync(); });
+      else
+        pending = true;
+    }
+    uint32_t todo = __ballot_sync(0xFFFFFFFFu, pending && tile.lane == 0);
+    while (todo) {
+      const int src = __ffs(todo) - 1;
+      todo &= todo - 1;
+      const uint64_t wi = __shfl_sync(0xFFFFFFFFu, i, src);
+      const uint64_t wk = __shfl_sync(0xFFFFFFFFu, key, src);
+      const uint64_t wd = __shfl_sync(0xFFFFFFFFu, desired, src);
+      const bool wa = __shfl_sync(0xFFFFFFFFu, is_accum, src);
+      Locate wlc;
+      wlc.bkt = __shfl_sync(0xFFFFFFFFu, l.bkt, src);
+      wlc.pos = __shfl_sync(0xFFFFFFFFu, l.pos, src);
+      wlc.d4 = __shfl_sync(0xFFFFFFFFu, l.d4, src);
       uint32_t slot = 0;
       uint64_t evk = 0;
-      res = warp_find_and_lock(t, l, key, desired, slot, evk);
-      if (res == kTimedOut) {
-        if (lane == 0) atomicOr(t.error, kErrSpinTimeout);
-      } else if (res != kRefused) {
-        uint64_t* bk = t.keys + l.bkt * kBucket;
-        const uint64_t s = l.bkt * kBucket + slot;
-        if ((is_accum && res != kDuplicate) || (!is_accum && res == kDuplicate)) {
-          // reference :114-128: undo the lock and skip
-          if (lane == 0) store_release_u64(bk + slot, res == kDuplicate ? key : evk);
-          res = kIllegal;
-        } else {
-          VT* dst = reinterpret_cast<VT*>(value_ptr(t, l.bkt, slot));
-          const VT* src = reinterpret_cast<const VT*>(a.values + i * vb);
-          for (uint32_t e = lane; e < ne; e += 32)
-            dst[e] = is_accum ? AccumOps<VT>::add(src[e], dst[e]) : src[e];
-          if (lane == 0) {
-            if (res == kOccupiedEmpty || res == kOccupiedReclaimed)
-              atomicAdd(t.sizes + l.bkt, 1);
-            const bool ins = res != kDuplicate;
-            uint64_t ns;
-            const uint64_t old = (ins || (S != kLfu && S != kEpochLfu))
-                                     ? 0
-                                     : ld_relaxed_u64(t.scores + s);
-            if (score_on_write<S>(old, a.scores, i, desired, ins, &ns)) {
-              t.digests[s] = static_cast<uint8_t>(l.d4);
-              t.scores[s] = ns;
-            }
-          }
-          __syncwarp();
-          if (lane == 0) store_release_u64(bk + slot, key);
-        }
+      int r = warp_find_and_lock(t, wlc, wk, wd, slot, evk);
+      if (r == kTimedOut) {
+        if (wl == 0) atomicOr(t.error, kErrSpinTimeout);
+      } else if (r != kRefused) {
+        r = accum_apply<S, VT>(t, a, wi, wk, wa, wd, wlc, slot, evk, r, wl, 32,
+                               []() { __syncwarp(); });
       }
+      if ((wl >> 3) == (static_cast<uint32_t>(src) >> 3)) res = r;
     }
-    if (a.status != nullptr && lane == 0) a.status[i] = res;
+    if (in && a.status != nullptr && tile.lane == 0) a.status[i] = res;
   }
 }
 
@@ -937,51 +1034,6 @@ __global__ void __launch_bounds__(256) accum_kernel(TableView t, AccumArgs a) {
 // assign_scores (reference assign_scores_kernel_with_filter.h:38-141) and
 // erase (reference remove_kernel.h:33-113)
 // ============================================================================
-// Finds the slot holding `key` with plain loads (the reference's find rule
-// when kStopRule: a digest-empty EMPTY_KEY slot earlier in the walk hides
-// it). Returns the slot, -1 if absent, -2 if a locked digest-hit slot may
-// hold the key (the caller retries).
-template <bool kStopRule>
-__device__ __forceinline__ int tile_locate_existing(const TableView& t,
-                                                    const Tile& tile,
-                                                    const Locate& l,
-                                                    uint64_t key) {
-  const uint64_t* bk = t.keys + l.bkt * kBucket;
-  const uint4 dv = __ldcg(
-      reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) + tile.lane);
-  const uint32_t lo = tile.lane * kDigestsPerLane;
-  uint32_t hits = bytes_eq16(dv, l.d4);
-  int mine = -1;
-  bool busy = false;
-  while (hits) {
-    const uint32_t j = __ffs(hits) - 1;
-    hits &= hits - 1;
-    const uint64_t k = ld_relaxed_u64(bk + lo + j);
-    if (k == key) {
-      mine = static_cast<int>(lo + j);
-      break;
-    }
-    busy |= (k == kLockedKey);
-  }
-  const uint32_t fm = tile.ballot(mine >= 0);
-  if (!fm) return tile.ballot(busy) ? -2 : -1;
-  const uint32_t p = tile.shfl(static_cast<uint32_t>(mine), __ffs(fm) - 1);
-  if constexpr (kStopRule) {
-    uint32_t empt = bytes_eq16(dv, kEmptyDigest * 0x01010101u);
-    const uint32_t pr = hit_rank(p, l.pos);
-    bool stop = false;
-    while (empt) {
-      const uint32_t j = __ffs(empt) - 1;
-      empt &= empt - 1;
-      const uint32_t q = lo + j;
-      if (empty_rank(q, l.pos) < pr && ld_relaxed_u64(bk + q) == kEmptyKey)
-        stop = true;
-    }
-    if (tile.ballot(stop)) return -1;
-  }
-  return static_cast<int>(p);
-}
-
 // Score update of existing keys (reference assign_scores_kernel_with_filter.h
 // :38-141, score rule update_without_missed) or erase (reference
 // remove_kernel.h:33-113: RECLAIM tombstone, score 0, reclaim digest, size
@@ -1109,11 +1161,19 @@ __global__ void __launch_bounds__(256)
 
 // ============================================================================
 // Rehash after the bucket count doubles (reference rehash_kernel.h:30-207).
-// One warp per old bucket. The bucket and its new sibling are staged in
-// shared memory; every lane runs the reference's sequential algorithm on the
-// staged copy (identical decisions, warp-uniform control flow), lane 0
-// writes the staged state, and the whole warp moves each value row as the
-// algorithm moves its key. The final layout is the reference's, slot for
+// One warp per old bucket. The bucket's keys and scores and its new
+// sibling's are staged in shared memory, where lane 0 runs the reference's
+// sequential algorithm (copy_key_to_new_bucket :30-67, then
+// defragmentation_for_rehash :77-135, then the scan starts again) on
+// metadata only, recording for every final slot which original slot its
+// entry came from. The reference restarts the scan at slot 0 after each
+// moved key. Entries the scan has passed stay in the bucket wherever the
+// back-shifts put them, so the scan resumes instead at the lowest slot that
+// received an entry not yet passed (a flag per slot travels with its entry)
+// -- the same decisions, without the quadratic rescan. The
+// value rows then move in parallel: rows bound for the new bucket straight
+// from their old slots, rows that change slot inside the old bucket through
+// the warp's scratch rows. The final layout is the reference's, slot for
 // slot.
 // ============================================================================
 struct RehashStage {
@@ -1122,28 +1182,47 @@ struct RehashStage {
   uint64_t nkeys[kBucket];
   uint64_t nscores[kBucket];
   uint8_t ohome[kBucket];
+  uint8_t osrc[kBucket];  // original slot of the entry now at q (old bucket)
+  uint8_t nsrc[kBucket];  // original slot of the entry now at q (new bucket)
+  uint8_t seen[kBucket];  // the entry now at q was passed by the scan
 };
 
-template <int VW>
-__device__ __forceinline__ void warp_move_value(const TableView& t,
-                                                uint64_t sb, uint32_t sp,
-                                                uint64_t db, uint32_t dp,
-                                                uint32_t lane) {
-  copy_row<VW>(value_ptr(t, db, dp), value_ptr(t, sb, sp), t.value_bytes,
-               lane, 32);
+// Copies, for every q < kBucket with pick(q), the row of slot src(q) of
+// bucket sb to slot q of bucket db (or scratch rows when dst_scratch / from
+// scratch rows when src_scratch); the warp's lanes split the row vectors.
+template <int VW, class Pick, class Src>
+__device__ __forceinline__ void warp_copy_rows(const TableView& t, uint64_t sb, uint64_t db,
+                                               uint8_t* scratch, bool src_scratch,
+                                               bool dst_scratch, Pick pick, Src src,
+                                               uint32_t lane) {
+  using V = typename VecOf<VW>::T;
+  const uint32_t vb = t.value_bytes;
+  const uint32_t nv = vb / VW;
+  for (uint32_t x = lane; x < kBucket * nv; x += 32) {
+    const uint32_t q = x / nv;
+    const uint32_t v = x - q * nv;
+    if (!pick(q)) continue;
+    const uint32_t sq = src(q);
+    const V* sp = reinterpret_cast<const V*>(
+        src_scratch ? scratch + uint64_t{sq} * vb : value_ptr(t, sb, sq));
+    V* dp = reinterpret_cast<V*>(dst_scratch ? scratch + uint64_t{q} * vb
+                                             : value_ptr(t, db, q));
+    dp[v] = sp[v];
+  }
 }
 
 template <int VW>
 __global__ void __launch_bounds__(256)
-    rehash_kernel(TableView t, uint64_t old_nb) {
+    rehash_kernel(TableView t, uint64_t old_nb, uint8_t* __restrict__ scratch) {
   __shared__ RehashStage stage[8];
   const uint32_t lane = threadIdx.x & 31;
   const uint32_t wi = threadIdx.x >> 5;
   RehashStage& st = stage[wi];
   const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x / 32);
+  const uint64_t gw = blockIdx.x * (uint64_t)(blockDim.x / 32) + wi;
+  uint8_t* rows = scratch + gw * kBucket * t.value_bytes;  // this warp's scratch rows
   const uint64_t new_cap = t.capacity;  // power of two after doubling
-  for (uint64_t b = blockIdx.x * (uint64_t)(blockDim.x / 32) + wi; b < old_nb;
-       b += nwarps) {
+  for (uint64_t b = gw; b < old_nb; b += nwarps) {
     const uint64_t nbk = b + old_nb;
     for (uint32_t q = lane; q < kBucket; q += 32) {
       const uint64_t k = t.keys[b * kBucket + q];
@@ -1152,70 +1231,81 @@ __global__ void __launch_bounds__(256)
       st.nkeys[q] = kEmptyKey;
       st.nscores[q] = 0;
       st.ohome[q] = static_cast<uint8_t>(murmur3(k) & (kBucket - 1));
+      st.osrc[q] = static_cast<uint8_t>(q);
+      st.nsrc[q] = static_cast<uint8_t>(q);
+      st.seen[q] = 0;
     }
     __syncwarp();
     int32_t moved = 0, removed = 0;
-    uint32_t kp = 0;
-    while (kp < kBucket) {
-      const uint64_t k = st.okeys[kp];
-      if (k == kEmptyKey || k == kReclaimKey) {
-        kp++;
-        continue;
-      }
-      const uint64_t g = murmur3(k) & (new_cap - 1);
-      if ((g >> kBucketShift) == b) {
-        kp++;
-        continue;
-      }
-      // copy_key_to_new_bucket, rehash_kernel.h:30-67
-      const uint32_t npos = static_cast<uint32_t>(g & (kBucket - 1));
-      uint32_t dst = kBucket;
-      for (uint32_t off = 0; off < kBucket; off++) {
-        const uint32_t p = (npos + off) & (kBucket - 1);
-        if (st.nkeys[p] == kEmptyKey) {
-          dst = p;
-          break;
+    if (lane == 0) {
+      uint32_t kp = 0;
+      while (kp < kBucket) {
+        const uint64_t k = st.okeys[kp];
+        if (k == kEmptyKey || k == kReclaimKey) {
+          st.seen[kp] = 1;
+          kp++;
+          continue;
         }
-      }
-      if (dst < kBucket) {
-        warp_move_value<VW>(t, b, kp, nbk, dst, lane);
-        __syncwarp();
-        if (lane == 0) {
-          st.nkeys[dst] = k;
-          st.nscores[dst] = st.oscores[kp];
+        const uint64_t g = murmur3(k) & (new_cap - 1);
+        if ((g >> kBucketShift) == b) {
+          st.seen[kp] = 1;
+          kp++;
+          continue;
         }
-        moved++;
-      }
-      removed++;
-      if (lane == 0) st.okeys[kp] = kEmptyKey;
-      __syncwarp();
-      // defragmentation_for_rehash, rehash_kernel.h:77-135
-      uint32_t rm = kp, off = 1;
-      while (off < kBucket) {
-        const uint32_t cur = (rm + off) & (kBucket - 1);
-        const uint64_t ck = st.okeys[cur];
-        if (ck == kEmptyKey) break;
-        const uint32_t start = st.ohome[cur];
-        if ((start <= rm && rm < cur) || (cur < start && start <= rm) ||
-            (rm < cur && cur < start)) {
-          warp_move_value<VW>(t, b, cur, b, rm, lane);
-          __syncwarp();
-          if (lane == 0) {
+        // copy_key_to_new_bucket: first EMPTY slot from the new position
+        const uint32_t npos = static_cast<uint32_t>(g & (kBucket - 1));
+        for (uint32_t off = 0; off < kBucket; off++) {
+          const uint32_t p = (npos + off) & (kBucket - 1);
+          if (st.nkeys[p] == kEmptyKey) {
+            st.nkeys[p] = k;
+            st.nscores[p] = st.oscores[kp];
+            st.nsrc[p] = st.osrc[kp];
+            moved++;
+            break;
+          }
+        }
+        removed++;
+        st.okeys[kp] = kEmptyKey;
+        // defragmentation_for_rehash: shift later entries back into the hole
+        uint32_t resume = kp;
+        uint32_t rm = kp, off = 1;
+        while (off < kBucket) {
+          const uint32_t cur = (rm + off) & (kBucket - 1);
+          const uint64_t ck = st.okeys[cur];
+          if (ck == kEmptyKey) break;
+          const uint32_t start = st.ohome[cur];
+          if ((start <= rm && rm < cur) || (cur < start && start <= rm) ||
+              (rm < cur && cur < start)) {
             st.okeys[rm] = ck;
             st.oscores[rm] = st.oscores[cur];
             st.ohome[rm] = st.ohome[cur];
+            st.osrc[rm] = st.osrc[cur];
+            st.seen[rm] = st.seen[cur];
             st.okeys[cur] = kEmptyKey;
+            if (!st.seen[rm]) resume = min(resume, rm);  // not yet scanned: rescan from rm
+            rm = cur;
+            off = 1;
+          } else {
+            off++;
           }
-          __syncwarp();
-          rm = cur;
-          off = 1;
-        } else {
-          off++;
         }
+        kp = resume;
       }
-      kp = 0;
     }
     __syncwarp();
+    // rows: new bucket from the old slots, and the old bucket's moving rows
+    // into scratch, before any old row is overwritten
+    warp_copy_rows<VW>(
+        t, b, nbk, rows, false, false, [&](uint32_t q) { return st.nkeys[q] != kEmptyKey; },
+        [&](uint32_t q) { return static_cast<uint32_t>(st.nsrc[q]); }, lane);
+    auto stays_moved = [&](uint32_t q) {
+      return st.okeys[q] != kEmptyKey && st.okeys[q] != kReclaimKey && st.osrc[q] != q;
+    };
+    warp_copy_rows<VW>(t, b, b, rows, false, true, stays_moved,
+                       [&](uint32_t q) { return static_cast<uint32_t>(st.osrc[q]); }, lane);
+    __syncwarp();
+    warp_copy_rows<VW>(t, b, b, rows, true, false, stays_moved,
+                       [&](uint32_t q) { return q; }, lane);
     for (uint32_t q = lane; q < kBucket; q += 32) {
       const uint64_t ok = st.okeys[q], nk = st.nkeys[q];
       t.keys[b * kBucket + q] = ok;

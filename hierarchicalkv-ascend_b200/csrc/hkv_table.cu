@@ -920,11 +920,20 @@ void TableImpl::double_capacity(cudaStream_t s) {
   const TableView v = view();
   init_buckets_kernel<<<warp_grid(old_nb), 256, 0, counted(s)>>>(v, old_nb, new_nb, 1);
   const int vw = value_width({});
+  // one warp per old bucket, each with kBucket scratch rows for the rows that
+  // change slot inside their bucket (at most 512 MB of scratch)
+  const uint64_t row_block = uint64_t{kBucket} * value_bytes_;
+  const uint64_t max_warps = std::max<uint64_t>(
+      8, std::min<uint64_t>(sm_count_ * 64ull, (512ull << 20) / row_block));
   const int grid = static_cast<int>(
-      std::min<uint64_t>(ceil_div(old_nb, 8), sm_count_ * 16ull));
-  DISPATCH_VW(vw, rehash_kernel<VW><<<grid, 256, 0, counted(s)>>>(v, old_nb));
-  CUDA_TRY(cudaGetLastError());
-  CUDA_TRY(cudaStreamSynchronize(s));
+      std::max<uint64_t>(1, std::min<uint64_t>(ceil_div(old_nb, 8), max_warps / 8)));
+  {
+    Workspace ws(s, pool_);
+    uint8_t* scratch = ws.get<uint8_t>(uint64_t{static_cast<uint32_t>(grid)} * 8 * row_block);
+    DISPATCH_VW(vw, rehash_kernel<VW><<<grid, 256, 0, counted(s)>>>(v, old_nb, scratch));
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaStreamSynchronize(s));
+  }
 }
 
 void TableImpl::reserve(size_t new_capacity, cudaStream_t s) {
