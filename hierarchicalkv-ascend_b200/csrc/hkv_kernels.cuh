@@ -1110,10 +1110,12 @@ __global__ void __launch_bounds__(256)
 // score reset.
 
 // ============================================================================
-// export_batch (reference dump_kernel.h:37-123): slots [offset, offset+len);
-// each warp takes 32 consecutive slots, ballot-compacts the live ones and
-// reserves its output range with one atomic. Output order is not
-// deterministic (same as the reference).
+// export_batch (reference dump_kernel.h:37-123): slots [offset, offset+len).
+// A block takes 256 consecutive slots: each warp ballot-compacts its 32, the
+// block reserves its whole output range with one atomic (one per 256 slots
+// on a single counter word), and the warp's lanes then copy the 16-byte
+// vectors of its live rows. Output order is not deterministic (same as the
+// reference).
 // ============================================================================
 template <int VW>
 __global__ void __launch_bounds__(256)
@@ -1121,41 +1123,48 @@ __global__ void __launch_bounds__(256)
                   unsigned long long* __restrict__ counter,
                   uint64_t* __restrict__ out_keys, uint8_t* __restrict__ out_values,
                   uint64_t* __restrict__ out_scores) {
+  using V = typename VecOf<VW>::T;
+  __shared__ uint32_t warp_cnt[8];
+  __shared__ unsigned long long block_base;
   const uint32_t lane = threadIdx.x & 31;
-  const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x / 32);
+  const uint32_t wi = threadIdx.x >> 5;
   const uint32_t vb = t.value_bytes;
-  const Tile tile;
-  for (uint64_t w = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / 32;
-       w * 32 < len; w += nwarps) {
-    const uint64_t r = w * 32 + lane;
+  const uint32_t nv = vb / VW;
+  for (uint64_t c0 = uint64_t{blockIdx.x} * 256; c0 < len; c0 += uint64_t{gridDim.x} * 256) {
+    const uint64_t r = c0 + threadIdx.x;
     const uint64_t s = offset + r;
     uint64_t k = kEmptyKey;
     if (r < len) k = t.keys[s];
     const bool live = !is_reserved(k);
     const uint32_t vote = __ballot_sync(0xFFFFFFFFu, live);
-    if (!vote) continue;
-    unsigned long long base = 0;
-    if (lane == 0) base = atomicAdd(counter, __popc(vote));
-    base = __shfl_sync(0xFFFFFFFFu, base, 0);
+    if (lane == 0) warp_cnt[wi] = __popc(vote);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t total = 0;
+      for (uint32_t j = 0; j < 8; j++) total += warp_cnt[j];
+      block_base = total ? atomicAdd(counter, static_cast<unsigned long long>(total)) : 0;
+    }
+    __syncthreads();
+    unsigned long long base = block_base;
+    for (uint32_t j = 0; j < wi; j++) base += warp_cnt[j];
     if (live) {
       const uint64_t o = base + __popc(vote & ((1u << lane) - 1u));
       out_keys[o] = k;
       if (out_scores != nullptr) out_scores[o] = t.scores[s];
     }
-    if (out_values == nullptr) continue;
-    // tile j copies the live slots with rank j, j+4, ...
-    const uint32_t cnt = __popc(vote);
-    uint32_t rest = vote;
-    for (uint32_t rank = 0; rank < cnt; rank++) {
-      const uint32_t src = __ffs(rest) - 1;
-      rest &= rest - 1;
-      if ((rank & 3) != (lane >> 3)) continue;
-      const uint64_t ss = offset + w * 32 + src;
-      copy_row<VW>(out_values + (base + rank) * vb,
-                   value_ptr(t, ss >> kBucketShift,
-                             static_cast<uint32_t>(ss & (kBucket - 1))),
-                   vb, tile.lane, kTile);
+    if (out_values != nullptr) {
+      const uint32_t nvec = __popc(vote) * nv;
+      const uint64_t w0 = offset + c0 + wi * 32;  // slot of this warp's lane 0
+      for (uint32_t x = lane; x < nvec; x += 32) {
+        const uint32_t rank = x / nv;
+        const uint32_t v = x - rank * nv;
+        const uint64_t ss = w0 + __fns(vote, 0, static_cast<int>(rank) + 1);
+        const V* sp = reinterpret_cast<const V*>(
+            value_ptr(t, ss >> kBucketShift, static_cast<uint32_t>(ss & (kBucket - 1))));
+        reinterpret_cast<V*>(out_values + (base + rank) * vb)[v] = sp[v];
+      }
     }
+    __syncthreads();  // warp_cnt and block_base are rewritten next chunk
   }
 }
 
