@@ -109,19 +109,40 @@ __global__ void erase_if_kernel(hkv_table_view v, Pred pred, uint8_t reclaim_dig
 }
 
 // export_batch_if (reference dump_kernel_if.h, dump_kernel_if_v2.h): the
-// matching live slots of [offset, offset + n) compacted to the outputs, one
-// atomic per warp; *counter (zeroed by the caller) receives the total.
+// matching live slots of [offset, offset + n) compacted to the outputs; a
+// block takes blockDim.x consecutive slots, reserves its output range with
+// one atomic and each warp's lanes then copy the matching rows' 16-byte (or
+// 4-byte, or 1-byte, by alignment) pieces. *counter (zeroed by the caller)
+// receives the total.
+template <class U>
+__device__ __forceinline__ void copy_rows_of_vote(const hkv_table_view& v, uint32_t vote,
+                                                  uint64_t first_slot, uint8_t* out,
+                                                  uint32_t lane) {
+  const uint32_t n = v.value_bytes / sizeof(U);
+  const uint32_t total = __popc(vote) * n;
+  for (uint32_t x = lane; x < total; x += 32) {
+    const uint32_t rank = x / n;
+    const uint32_t e = x - rank * n;
+    const uint64_t slot = first_slot + __fns(vote, 0, static_cast<int>(rank) + 1);
+    reinterpret_cast<U*>(out + rank * uint64_t{v.value_bytes})[e] =
+        reinterpret_cast<const U*>(row_of(v, slot))[e];
+  }
+}
+
 template <class K, class V, class S, class Pred>
 __global__ void export_if_kernel(hkv_table_view v, Pred pred, uint64_t offset, uint64_t n,
                                  unsigned long long* counter, K* keys, V* values,
                                  S* scores) {
-  const uint64_t nthreads = uint64_t{gridDim.x} * blockDim.x;
+  __shared__ uint32_t warp_cnt[32];
+  __shared__ unsigned long long block_base;
   const uint32_t lane = threadIdx.x & 31;
+  const uint32_t wi = threadIdx.x >> 5;
   const uint64_t end = n;  // n is already clamped to the capacity
-  // the loop runs warp-uniformly so that the ballots see every lane
-  for (uint64_t base = (uint64_t{blockIdx.x} * blockDim.x + threadIdx.x) & ~uint64_t{31};
-       base < end; base += nthreads) {
-    const uint64_t i = base + lane;
+  // the loop runs block-uniformly so that the ballots and barriers see every
+  // thread
+  for (uint64_t c0 = uint64_t{blockIdx.x} * blockDim.x; c0 < end;
+       c0 += uint64_t{gridDim.x} * blockDim.x) {
+    const uint64_t i = c0 + threadIdx.x;
     bool hit = false;
     uint64_t slot = 0, key = 0;
     if (i < end) {
@@ -132,19 +153,34 @@ __global__ void export_if_kernel(hkv_table_view v, Pred pred, uint64_t offset, u
                       static_cast<S>(v.scores[slot]));
     }
     const uint32_t mask = __ballot_sync(0xFFFFFFFFu, hit);
-    unsigned long long at = 0;
-    if (lane == 0 && mask) at = atomicAdd(counter, static_cast<unsigned long long>(__popc(mask)));
-    at = __shfl_sync(0xFFFFFFFFu, at, 0);
+    if (lane == 0) warp_cnt[wi] = __popc(mask);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t total = 0;
+      for (uint32_t j = 0; j < blockDim.x / 32; j++) total += warp_cnt[j];
+      block_base = total ? atomicAdd(counter, static_cast<unsigned long long>(total)) : 0;
+    }
+    __syncthreads();
+    unsigned long long at = block_base;
+    for (uint32_t j = 0; j < wi; j++) at += warp_cnt[j];
     if (hit) {
       const uint64_t o = at + __popc(mask & ((1u << lane) - 1));
       keys[o] = static_cast<K>(key);
       if (scores != nullptr) scores[o] = static_cast<S>(v.scores[slot]);
-      if (values != nullptr) {
-        const uint8_t* src = row_of(v, slot);
-        uint8_t* dst = reinterpret_cast<uint8_t*>(values) + o * v.value_bytes;
-        for (uint32_t b = 0; b < v.value_bytes; b++) dst[b] = src[b];
-      }
     }
+    if (values != nullptr && mask) {
+      uint8_t* out = reinterpret_cast<uint8_t*>(values) + at * v.value_bytes;
+      const uint64_t first = offset + c0 + wi * 32;
+      // rows sit at value_bytes strides from allocation-aligned slice bases
+      const uintptr_t al = reinterpret_cast<uintptr_t>(values) | v.value_bytes;
+      if ((al & 15) == 0)
+        copy_rows_of_vote<uint4>(v, mask, first, out, lane);
+      else if ((al & 3) == 0)
+        copy_rows_of_vote<uint32_t>(v, mask, first, out, lane);
+      else
+        copy_rows_of_vote<uint8_t>(v, mask, first, out, lane);
+    }
+    __syncthreads();  // warp_cnt and block_base are rewritten next chunk
   }
 }
 
