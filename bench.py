@@ -644,6 +644,110 @@ def run_suite(args):
 
 
 # --------------------------------------------------------------------------
+# --workload hybrid: value rows split between HBM and pinned host memory
+# (BASELINE config 4 at reduced size: 64 Mi slots, dim 128, 1/16 of the value
+# bytes in HBM as in 16 GB of 256 GB, load factor 0.75). find of resident
+# keys, 80 % of them in HBM-resident buckets; insert_or_assign of uniform keys
+# (half resident, half new). Host-resident rows cross the host link zero-copy.
+# --------------------------------------------------------------------------
+def run_hybrid(args):
+    import ctypes
+
+    import torch
+
+    import hkv_b200 as H
+
+    class View(ctypes.Structure):
+        _fields_ = [("keys", ctypes.c_void_p), ("scores", ctypes.c_void_p),
+                    ("digests", ctypes.c_void_p), ("sizes", ctypes.c_void_p),
+                    ("slices", ctypes.c_void_p), ("capacity", ctypes.c_uint64),
+                    ("num_buckets", ctypes.c_uint64), ("bucket_size", ctypes.c_uint32),
+                    ("slice_shift", ctypes.c_uint32), ("value_bytes", ctypes.c_uint32),
+                    ("dim", ctypes.c_uint32), ("reclaim_digest", ctypes.c_uint8)]
+
+    dev = torch.device("cuda", 0)
+    cap = args.capacity if args.capacity != CAPACITY else 64 << 20
+    dim = 128
+    vb = dim * 4
+    hbm = cap * vb // 16
+    n = BATCH
+    steps, warm = args.steps, args.warmup
+    t = H.HashTable(H.EvictStrategy.kLru)
+    t0 = time.time()
+    t.init(H.HashTableOptions(init_capacity=cap, max_capacity=cap, max_hbm_for_vectors=hbm,
+                              dim=dim, max_load_factor=1.0))
+    view = View()
+    H._check(H.lib().hkv_table_get_view(ctypes.c_void_p(t._h), ctypes.byref(view)))
+    per_slice = 1 << view.slice_shift
+    hbm_buckets = min(view.num_buckets, (hbm // (per_slice * 128 * vb)) * per_slice)
+    if hbm_buckets == 0 or hbm_buckets == view.num_buckets:
+        raise SystemExit("hybrid: no value slice (or every slice) fits the HBM budget "
+                         "at this capacity; choose another --capacity")
+    log(f"hybrid table: {cap} slots, dim {dim}, {hbm_buckets}/{view.num_buckets} buckets' "
+        f"rows in HBM, created in {time.time() - t0:.1f}s")
+    fill = cap * 3 // 4
+    rows = torch.randn((n, dim), device=dev)
+    for st in range(0, fill, n):
+        m = min(n, fill - st)
+        t.insert_or_assign(m, keys_from_counters(st, m, dev), rows[:m])
+    torch.cuda.synchronize()
+    resident = keys_from_counters(0, fill, dev)
+    bucket = (fmix_t(resident) & (cap - 1)) >> 7
+    in_hbm = resident[bucket < hbm_buckets]
+    in_host = resident[bucket >= hbm_buckets]
+    del resident, bucket
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    nh = n * 4 // 5
+    finds, inserts = [], []
+    for i in range(steps + warm):
+        k = torch.cat([in_hbm[torch.randint(0, in_hbm.numel(), (nh,), generator=g, device=dev)],
+                       in_host[torch.randint(0, in_host.numel(), (n - nh,), generator=g,
+                                             device=dev)]])
+        finds.append(k[torch.randperm(n, generator=g, device=dev)])
+        old = keys_from_counters(0, fill, dev)[torch.randperm(fill, generator=g, device=dev)[:n // 2]]
+        new = keys_from_counters(fill + i * n, n // 2, dev)
+        inserts.append(torch.cat([old, new])[torch.randperm(n, generator=g, device=dev)])
+    out = torch.empty((n, dim), device=dev)
+    founds = torch.zeros(n, dtype=torch.bool, device=dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    res = {}
+    for name in ("find", "insert_or_assign"):
+        def call(i):
+            if name == "find":
+                t.find(n, finds[i], out, founds)
+            else:
+                t.insert_or_assign(n, inserts[i], rows)
+        for i in range(warm):
+            call(i)
+        torch.cuda.synchronize()
+        e0.record()
+        for i in range(warm, warm + steps):
+            call(i)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        # rows that cross the host link per call: found rows of host buckets
+        # (find), inserted rows of host buckets (insert, 1 - 1/16 of uniform keys)
+        host_frac = (n - nh) / n if name == "find" else 1 - hbm_buckets / view.num_buckets
+        link = n * host_frac * vb
+        res[name] = {"ms_per_call": round(ms, 4), "bkvs": round(n / (ms * 1e-3) / 1e9, 4),
+                     "host_rows_fraction": round(host_frac, 4),
+                     "host_link_bytes_per_call": int(link),
+                     "host_link_gbs": round(link / (ms * 1e-3) / 1e9, 1)}
+        log(f"hybrid {name}: {ms * 1000:.1f} us per call, {res[name]['host_link_gbs']} GB/s "
+            f"over the host link")
+    hit = float(founds.float().mean().item())
+    t.check_device_error()
+    print(json.dumps({"workload": "hybrid (BASELINE config 4 at 64 Mi slots)", "dim": dim,
+                      "capacity": cap, "max_hbm_for_vectors": hbm,
+                      "hbm_bucket_fraction": round(hbm_buckets / view.num_buckets, 4),
+                      "load_factor": 0.75, "batch": n, "steps": steps, "warmup": warm,
+                      "find_hit_rate_last_call": round(hit, 4), "ops": res}), flush=True)
+
+
+# --------------------------------------------------------------------------
 # --workload zipf: find_or_insert of power-law (Zipf-like) keys with repeats
 # (unique_key = false), dim 64: 128 Mi slots, kEpochLfu, 2 Mi keys per step on
 # one GPU; 256 Mi slots per GPU, kLfu, 8 Mi keys per GPU per step when
@@ -887,15 +991,19 @@ def main():
                     help="slots per GPU (diagnostics; the metric uses the default)")
     ap.add_argument("--suite", action="store_true",
                     help="time every table operation on one GPU (not the headline)")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "zipf"],
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "zipf", "hybrid"],
                     help="cfg2: the headline metric; zipf: find_or_insert of "
-                         "power-law keys with repeats (dim 64)")
+                         "power-law keys with repeats (dim 64); hybrid: values split "
+                         "between HBM and pinned host memory (dim 128)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
         return
     if args.workload == "zipf":
         run_zipf(args)
+        return
+    if args.workload == "hybrid":
+        run_hybrid(args)
         return
     if args.suite:
         run_suite(args)
