@@ -25,6 +25,10 @@ constexpr uint32_t kBucketShift = 7;
 constexpr uint64_t kEmptyKey = 0xFFFFFFFFFFFFFFFFull;
 constexpr uint64_t kReclaimKey = 0xFFFFFFFFFFFFFFFEull;
 constexpr uint64_t kLockedKey = 0xFFFFFFFFFFFFFFFDull;
+// A key word a caller holds locked across calls (lock_keys, find_or_insert*
+// with locked_key_ptrs): the fourth reserved value, so that the kernels can
+// tell a caller's lock from the short lock of an operation in flight.
+constexpr uint64_t kUserLockedKey = 0xFFFFFFFFFFFFFFFCull;
 constexpr uint64_t kReservedMask = 0xFFFFFFFFFFFFFFFCull;
 constexpr uint64_t kMaxScore = 0xFFFFFFFFFFFFFFFFull;
 constexpr uint64_t kIgnoredEpoch = 0xFFFFFFFFFFFFFFFFull;
@@ -96,6 +100,7 @@ struct TableView {
   uint64_t* scores;
   uint8_t* digests;
   int32_t* sizes;
+  int32_t* user_locks;     // per bucket: slots a caller holds locked
   uint8_t* const* slices;  // device array of slice base pointers
   uint8_t* values0;        // slice 0 (used directly when single_slice)
   int* error;              // device error word

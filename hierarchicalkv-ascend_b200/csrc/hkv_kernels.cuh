@@ -42,7 +42,10 @@ __global__ void init_buckets_kernel(TableView t, uint64_t b0, uint64_t b1,
 #pragma unroll
       for (int j = 0; j < 8; j++) s4[j] = make_uint4(0, 0, 0, 0);
     }
-    if ((s & (kBucket - 1)) == 0) t.sizes[s >> kBucketShift] = 0;
+    if ((s & (kBucket - 1)) == 0) {
+      t.sizes[s >> kBucketShift] = 0;
+      t.user_locks[s >> kBucketShift] = 0;
+    }
   }
 }
 
@@ -290,6 +293,7 @@ struct UpsertArgs {
   uint8_t** value_ptrs;      // find_or_insert*: address of each key's row
   bool* founds;              // find_or_insert*: the key was already there
   const uint32_t* row_index; // optional: key i's input/output row is row_index[i]
+  uint64_t** locked_key_ptrs;  // find_or_insert*: keep each slot locked for the caller
 };
 
 // Row of key i in the caller's value array: a merged batch of repeated keys
@@ -328,7 +332,8 @@ __device__ __forceinline__ void min_score_butterfly(const TileW<W>& tile,
                                                     const uint64_t* bs,
                                                     uint32_t pos,
                                                     uint64_t owner_idx,
-                                                    uint64_t& ms, uint32_t& mp) {
+                                                    uint64_t& ms, uint32_t& mp,
+                                                    const uint64_t* skip_user = nullptr) {
   constexpr uint32_t R = 16 / W;  // virtual lanes per lane
   constexpr uint32_t H = 8 / W;   // pair loads per virtual-lane pair and k
   uint64_t sv[R];
@@ -343,8 +348,14 @@ __device__ __forceinline__ void min_score_butterfly(const TileW<W>& tile,
   for (uint32_t j = 0; j < kBucket / (2 * W); j++) {
     const uint32_t q = 2 * tile.lane + 2 * W * j;
     const uint4 v = __ldcg(b4 + q / 2);
-    const uint64_t s0 = (static_cast<uint64_t>(v.y) << 32) | v.x;
-    const uint64_t s1 = (static_cast<uint64_t>(v.w) << 32) | v.z;
+    uint64_t s0 = (static_cast<uint64_t>(v.y) << 32) | v.x;
+    uint64_t s1 = (static_cast<uint64_t>(v.w) << 32) | v.z;
+    if (skip_user != nullptr) {
+      // a bucket holding caller locks: their slots are never victims (the
+      // reference's scan skips locked key words, insert_or_assign_kernel.h:214)
+      if (ld_relaxed_u64(skip_user + q) == kUserLockedKey) s0 = kMaxScore;
+      if (ld_relaxed_u64(skip_user + q + 1) == kUserLockedKey) s1 = kMaxScore;
+    }
     const uint32_t r = 2 * (j % H);
     if (s0 < sv[r]) { sv[r] = s0; pv[r] = q; }
     if (s1 < sv[r + 1]) { sv[r + 1] = s1; pv[r + 1] = q + 1; }
@@ -475,7 +486,17 @@ __device__ __forceinline__ void upsert_locked(const TableView& t,
     head.store(row, a.values_in + key_row(a, i) * vb, nv, tile.lane);
   }
   tile.sync();
-  if (tile.lane == 0) store_release_u64(t.keys + s, key);
+  if (tile.lane == 0) {
+    if (Mode == kModeFindOrInsertPtr && a.locked_key_ptrs != nullptr) {
+      // the slot stays locked for the caller (find_or_insert_ptr_kernel_v2.h:
+      // locked_key_ptrs), counted per bucket so that evictions pass it by
+      atomicAdd(t.user_locks + l.bkt, 1);
+      store_release_u64(t.keys + s, kUserLockedKey);
+      a.locked_key_ptrs[i] = t.keys + s;
+    } else {
+      store_release_u64(t.keys + s, key);
+    }
+  }
 }
 
 // One round for one key of insert_or_assign / find_or_insert /
@@ -521,7 +542,9 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const TileW<W>& 
       mine = static_cast<int>(lo + j);
       break;
     }
-    busy |= (k == kLockedKey);
+    // an operation in flight, or a caller holding this key locked: wait
+    // (bounded) rather than insert a second copy of the key
+    busy |= (k == kLockedKey || k == kUserLockedKey);
   }
   int res = kRetry;
   bool got = false;
@@ -569,7 +592,8 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const TileW<W>& 
     if (!got) {
       uint64_t ms;
       uint32_t mp;
-      min_score_butterfly(tile, bs, l.pos, i, ms, mp);
+      const int32_t held = __ldcg(t.user_locks + l.bkt);
+      min_score_butterfly(tile, bs, l.pos, i, ms, mp, held > 0 ? bk : nullptr);
       if (desired < ms) {
         res = kRefused;
       } else {
@@ -581,8 +605,9 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const TileW<W>& 
           // owner's release writes the final key); an EMPTY_KEY slot is put
           // back; a victim whose score rose since the scan is put back.
           k = exch_acquire_u64(bk + mp, kLockedKey);
-          if (k == kEmptyKey) {
-            store_release_u64(bk + mp, kEmptyKey);
+          if (k == kEmptyKey || k == kUserLockedKey) {
+            // put back an empty slot, or a caller's lock taken after the scan
+            store_release_u64(bk + mp, k);
           } else if (k != kLockedKey) {
             if (ld_relaxed_u64(bs + mp) <= ms)
               r = (k == kReclaimKey) ? kOccupiedReclaimed : kEvict;
@@ -701,6 +726,7 @@ __device__ __forceinline__ void upsert_body(const TableView& t, const UpsertArgs
             res != kOccupiedReclaimed && res != kEvict) {
           a.value_ptrs[i] = nullptr;
           if (a.founds != nullptr) a.founds[i] = false;
+          if (a.locked_key_ptrs != nullptr) a.locked_key_ptrs[i] = nullptr;
         }
       }
       if constexpr (Mode == kModeInsertAndEvict) {
@@ -888,7 +914,7 @@ restart:
         }
         __nanosleep(64);
       }
-      if (!gave_up && k != kEmptyKey) {
+      if (!gave_up && k != kEmptyKey && k != kUserLockedKey) {
         lm = sc;
         lp = q;
         lk = k;
@@ -1103,6 +1129,102 @@ __global__ void __launch_bounds__(256)
       if (!__any_sync(0xFFFFFFFFu, again)) break;
       backoff(round);
     }
+  }
+}
+
+// lock_keys (reference lock_keys_kernel.h:17-140): each present key is
+// found through its digests, locked, given its score by the hit rule
+// (update_with_digest with new_insert = false) and left locked with the
+// caller-lock word; its key-word address goes to locked_key_ptrs[i]. Absent
+// keys get nullptr and false.
+template <int S>
+__global__ void __launch_bounds__(256)
+    lock_keys_kernel(TableView t, const uint64_t* __restrict__ keys,
+                     uint64_t** __restrict__ locked_key_ptrs, bool* __restrict__ succeeded,
+                     const uint64_t* __restrict__ scores, uint64_t n, uint64_t epoch) {
+  __shared__ uint64_t s_clock;
+  if (threadIdx.x == 0) s_clock = global_timer_ns();
+  __syncthreads();
+  const uint64_t clk = s_clock;
+  const Tile tile;
+  const uint32_t wl = threadIdx.x & 31;
+  const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x / 32);
+  const uint64_t warp = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / 32;
+  for (uint64_t base = warp * 4; base < n; base += nwarps * 4) {
+    const uint64_t i = base + (wl >> 3);
+    uint64_t key = 0, t0 = 0;
+    bool todo = false, ok = false;
+    uint64_t* addr = nullptr;
+    Locate l;
+    l.bkt = 0;
+    l.pos = 0;
+    l.d4 = 0;
+    if (i < n) {
+      key = keys[i];
+      if (!is_reserved(key)) {
+        l = locate(t, key);
+        todo = true;
+      }
+    }
+    for (int round = 0;; round++) {
+      bool again = false;
+      if (todo) {
+        const int p = tile_locate_existing<false>(t, tile, l, key);
+        bool got = false;
+        const uint64_t s = l.bkt * kBucket + (p < 0 ? 0 : p);
+        if (p >= 0 && tile.lane == 0)
+          got = cas_acquire_u64(t.keys + s, key, kLockedKey) == key;
+        if (tile.shfl(got, 0)) {
+          if (tile.lane == 0) {
+            uint64_t ns;
+            const uint64_t old =
+                (S == kLfu || S == kEpochLfu) ? ld_relaxed_u64(t.scores + s) : 0;
+            const uint64_t desired = desired_when_missed<S>(scores, i, epoch, clk);
+            if (score_on_write<S>(old, scores, i, desired, false, &ns)) t.scores[s] = ns;
+            atomicAdd(t.user_locks + l.bkt, 1);
+            store_release_u64(t.keys + s, kUserLockedKey);
+          }
+          addr = t.keys + s;
+          ok = true;
+          todo = false;
+        } else if (p == -1) {
+          todo = false;
+        } else if (retry_expired(t, tile, t0, 203)) {
+          todo = false;
+        } else {
+          again = true;
+        }
+      }
+      if (!__any_sync(0xFFFFFFFFu, again)) break;
+      backoff(round);
+    }
+    if (i < n && tile.lane == 0) {
+      locked_key_ptrs[i] = ok ? addr : nullptr;
+      if (succeeded != nullptr) succeeded[i] = ok;
+    }
+  }
+}
+
+// unlock_keys (reference unlock_keys_kernel.h:17-60): a key word that still
+// holds the caller-lock word gets its key back; any other pointer (null,
+// outside this table's key array, or a word that is not locked) fails.
+__global__ void __launch_bounds__(256)
+    unlock_keys_kernel(TableView t, uint64_t n, uint64_t* const* __restrict__ locked_key_ptrs,
+                       const uint64_t* __restrict__ keys, bool* __restrict__ succeeded) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    uint64_t* p = locked_key_ptrs[i];
+    const uint64_t key = keys[i];
+    bool ok = false;
+    if (p != nullptr && p >= t.keys && p < t.keys + t.capacity && !is_reserved(key)) {
+      const uint64_t slot = static_cast<uint64_t>(p - t.keys);
+      ok = cas_u64(p, kUserLockedKey, kLockedKey) == kUserLockedKey;
+      if (ok) {
+        atomicSub(t.user_locks + (slot >> kBucketShift), 1);
+        store_release_u64(p, key);
+      }
+    }
+    if (succeeded != nullptr) succeeded[i] = ok;
   }
 }
 

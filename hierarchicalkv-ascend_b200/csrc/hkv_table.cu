@@ -175,6 +175,7 @@ TableImpl::TableImpl(const hkv_options& o, int key_type, int value_type,
   CUDA_TRY(cudaMalloc(&scores_, slots * 8));
   CUDA_TRY(cudaMalloc(&digests_, slots));
   CUDA_TRY(cudaMalloc(&sizes_, num_buckets_ * 4));
+  CUDA_TRY(cudaMalloc(&user_locks_, num_buckets_ * 4));
   CUDA_TRY(cudaMalloc(&d_error_, 2 * sizeof(int)));
   CUDA_TRY(cudaMemset(d_error_, 0, 2 * sizeof(int)));
   CUDA_TRY(cudaMalloc(&d_scratch_, 4 * sizeof(unsigned long long)));
@@ -205,6 +206,7 @@ TableImpl::~TableImpl() {
   cudaFree(scores_);
   cudaFree(digests_);
   cudaFree(sizes_);
+  cudaFree(user_locks_);
   cudaFree(d_error_);
   cudaFree(d_scratch_);
   if (pool_) cudaMemPoolDestroy(pool_);
@@ -268,6 +270,7 @@ TableView TableImpl::view() const {
   v.scores = scores_;
   v.digests = digests_;
   v.sizes = sizes_;
+  v.user_locks = user_locks_;
   v.slices = d_slices_;
   v.values0 = slices_.empty() ? nullptr : slices_[0].dev;
   v.error = d_error_;
@@ -390,10 +393,14 @@ void TableImpl::check_strategy(const uint64_t* scores, bool ignore) const {
 }
 
 uint64_t TableImpl::sum_sizes(uint64_t nb, cudaStream_t s) {
+  return sum_counts(sizes_, nb, s);
+}
+
+uint64_t TableImpl::sum_counts(const int32_t* counts, uint64_t nb, cudaStream_t s) {
   CUDA_TRY(cudaMemsetAsync(d_scratch_, 0, sizeof(unsigned long long), s));
   const int blocks = static_cast<int>(
       std::min<uint64_t>(ceil_div(nb, 256 * 4), sm_count_ * 4ull));
-  sum_sizes_kernel<<<std::max(blocks, 1), 256, 0, counted(s)>>>(sizes_, nb, d_scratch_);
+  sum_sizes_kernel<<<std::max(blocks, 1), 256, 0, counted(s)>>>(counts, nb, d_scratch_);
   CUDA_TRY(cudaGetLastError());
   CUDA_TRY(cudaMemcpyAsync(h_scratch_, d_scratch_, sizeof(unsigned long long),
                            cudaMemcpyDeviceToHost, s));
@@ -431,7 +438,7 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
                        uint64_t* d_counter, cudaStream_t s, bool unique,
                        bool ignore, uint8_t* status, const uint32_t* dn,
                        uint32_t status_stride, uint8_t** value_ptrs,
-                       bool* founds) {
+                       bool* founds, uint64_t** locked_key_ptrs) {
   const int st = ignore ? kCustomized : strategy_;
   const TableView v = view();
   UpsertArgs a;
@@ -446,6 +453,7 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
   a.status_stride = status_stride;
   a.value_ptrs = value_ptrs;
   a.founds = founds;
+  a.locked_key_ptrs = locked_key_ptrs;
   const uint8_t* rows = mode == kModeFindOrInsert ? values_io : values_in;
 
   if (unique) {
@@ -721,15 +729,43 @@ void TableImpl::find_ptr(size_t n, const uint64_t* keys, uint8_t** value_ptrs,
 void TableImpl::find_or_insert_ptr(size_t n, const uint64_t* keys,
                                    uint8_t** value_ptrs, bool* founds,
                                    const uint64_t* scores, cudaStream_t s,
-                                   bool unique, bool ignore) {
+                                   bool unique, bool ignore,
+                                   uint64_t** locked_key_ptrs) {
   if (n == 0) return;
+  // a repeated key cannot be held locked by two of its occurrences
+  HKV_REQUIRE(locked_key_ptrs == nullptr || unique, HKV_ERR_UNSUPPORTED,
+              "locked_key_ptrs needs unique_key = true");
   auto_grow(n, s);
   if (!ignore) check_strategy(scores, false);
   HKV_REQUIRE(keys != nullptr && value_ptrs != nullptr && founds != nullptr,
               HKV_ERR_INVALID, "keys, values and founds must not be null");
   upsert(kModeFindOrInsertPtr, n, keys, nullptr, nullptr, scores, nullptr,
          nullptr, nullptr, nullptr, s, unique, ignore, nullptr, nullptr, 1,
-         value_ptrs, founds);
+         value_ptrs, founds, locked_key_ptrs);
+}
+
+void TableImpl::lock_keys(size_t n, const uint64_t* keys, uint64_t** locked_key_ptrs,
+                          bool* succeeded, const uint64_t* scores, cudaStream_t s) {
+  if (n == 0) return;
+  // reference lock_keys_kernel.h:23-25: null keys or outputs -> nothing done
+  if (keys == nullptr || locked_key_ptrs == nullptr) return;
+  check_strategy(scores, false);
+  const TableView v = view();
+  DISPATCH_STRATEGY(strategy_, {
+    lock_keys_kernel<S><<<tile_grid(n), 256, 0, counted(s)>>>(v, keys, locked_key_ptrs,
+                                                              succeeded, scores, n, epoch_);
+  });
+  CUDA_TRY(cudaGetLastError());
+}
+
+void TableImpl::unlock_keys(size_t n, uint64_t* const* locked_key_ptrs,
+                            const uint64_t* keys, bool* succeeded, cudaStream_t s) {
+  if (n == 0) return;
+  // reference unlock_keys_kernel.h:21-23: null inputs -> nothing done
+  if (keys == nullptr || locked_key_ptrs == nullptr) return;
+  unlock_keys_kernel<<<static_cast<int>(std::min<uint64_t>(ceil_div(n, 256), sm_count_ * 16ull)),
+                       256, 0, counted(s)>>>(view(), n, locked_key_ptrs, keys, succeeded);
+  CUDA_TRY(cudaGetLastError());
 }
 
 void TableImpl::find_segments(const FindSegments& seg, uint32_t nseg,
@@ -890,6 +926,11 @@ size_t TableImpl::load(hkv_kv_read_fn read, void* user, size_t max_ws,
 // reserve, reference hkv_hashtable.h:2873-2935 and table.h:360-377
 // ---------------------------------------------------------------------------
 void TableImpl::double_capacity(cudaStream_t s) {
+  // a rehash would move a key a caller holds locked away from the address
+  // the caller was given
+  HKV_REQUIRE(sum_counts(user_locks_, num_buckets_, s) == 0, HKV_ERR_RUNTIME,
+              "the table cannot grow while keys are locked (lock_keys or "
+              "find_or_insert with locked_key_ptrs): unlock them first");
   const uint64_t old_nb = num_buckets_, new_nb = old_nb * 2;
   const size_t old_slots = old_nb * kBucket, new_slots = new_nb * kBucket;
   uint64_t *nk = nullptr, *ns = nullptr;
@@ -908,10 +949,13 @@ void TableImpl::double_capacity(cudaStream_t s) {
   cudaFree(scores_);
   cudaFree(digests_);
   cudaFree(sizes_);
+  cudaFree(user_locks_);
   keys_ = nk;
   scores_ = ns;
   digests_ = nd;
   sizes_ = nz;
+  CUDA_TRY(cudaMalloc(&user_locks_, new_nb * 4));
+  CUDA_TRY(cudaMemset(user_locks_, 0, new_nb * 4));
   allocate_slices(old_nb, new_nb);
   upload_slices();
   num_buckets_ = new_nb;
@@ -1528,11 +1572,31 @@ int hkv_find_or_insert_ptr(hkv_table* table, size_t n, const void* keys,
   HKV_API_BEGIN
   HKV_TABLE(table);
   HKV_LOCK(kUnique, stream);
-  HKV_REQUIRE(locked_key_ptrs == nullptr, HKV_ERR_UNSUPPORTED,
-              "locked_key_ptrs (keys left locked after the call) is not supported");
   T->find_or_insert_ptr(n, static_cast<const uint64_t*>(keys),
                         reinterpret_cast<uint8_t**>(values), founds, scores,
-                        as_stream(stream), unique_key, ignore_evict_strategy);
+                        as_stream(stream), unique_key, ignore_evict_strategy,
+                        reinterpret_cast<uint64_t**>(locked_key_ptrs));
+  HKV_API_END
+}
+
+int hkv_lock_keys(hkv_table* table, size_t n, const void* keys, void** locked_key_ptrs,
+                  bool* succeededs, void* stream, const uint64_t* scores) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  HKV_LOCK(kUnique, stream);
+  T->lock_keys(n, static_cast<const uint64_t*>(keys),
+               reinterpret_cast<uint64_t**>(locked_key_ptrs), succeededs, scores,
+               as_stream(stream));
+  HKV_API_END
+}
+
+int hkv_unlock_keys(hkv_table* table, size_t n, void** locked_key_ptrs, const void* keys,
+                    bool* succeededs, void* stream) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  HKV_LOCK(kUnique, stream);
+  T->unlock_keys(n, reinterpret_cast<uint64_t* const*>(locked_key_ptrs),
+                 static_cast<const uint64_t*>(keys), succeededs, as_stream(stream));
   HKV_API_END
 }
 

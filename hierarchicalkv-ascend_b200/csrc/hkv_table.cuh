@@ -169,7 +169,13 @@ class TableImpl {
                 uint64_t* scores, cudaStream_t s);
   void find_or_insert_ptr(size_t n, const uint64_t* keys, uint8_t** value_ptrs,
                           bool* founds, const uint64_t* scores, cudaStream_t s,
-                          bool unique, bool ignore);
+                          bool unique, bool ignore,
+                          uint64_t** locked_key_ptrs = nullptr);
+  // keys held locked by the caller across calls (lock_keys / unlock_keys)
+  void lock_keys(size_t n, const uint64_t* keys, uint64_t** locked_key_ptrs,
+                 bool* succeeded, const uint64_t* scores, cudaStream_t s);
+  void unlock_keys(size_t n, uint64_t* const* locked_key_ptrs, const uint64_t* keys,
+                   bool* succeeded, cudaStream_t s);
   void contains(size_t n, const uint64_t* keys, bool* founds, cudaStream_t s);
   void erase(size_t n, const uint64_t* keys, cudaStream_t s);
   void clear(cudaStream_t s);
@@ -228,6 +234,7 @@ class TableImpl {
   void auto_grow(size_t n, cudaStream_t s);
   float fast_load_factor(size_t delta, cudaStream_t s);
   uint64_t sum_sizes(uint64_t nb, cudaStream_t s);
+  uint64_t sum_counts(const int32_t* counts, uint64_t nb, cudaStream_t s);
   void allocate_slices(uint64_t b0, uint64_t b1);
   void upload_slices();
   void double_capacity(cudaStream_t s);
@@ -237,7 +244,8 @@ class TableImpl {
               uint64_t* ev_scores, uint64_t* d_counter, cudaStream_t s,
               bool unique, bool ignore, uint8_t* status,
               const uint32_t* dn = nullptr, uint32_t status_stride = 1,
-              uint8_t** value_ptrs = nullptr, bool* founds = nullptr);
+              uint8_t** value_ptrs = nullptr, bool* founds = nullptr,
+              uint64_t** locked_key_ptrs = nullptr);
 
   hkv_options opt_;
   int key_type_, value_type_, strategy_;
@@ -250,6 +258,7 @@ class TableImpl {
   uint64_t* scores_ = nullptr;
   uint8_t* digests_ = nullptr;
   int32_t* sizes_ = nullptr;
+  int32_t* user_locks_ = nullptr;  // per bucket: slots a caller holds locked
   int* d_error_ = nullptr;
   unsigned long long* d_scratch_ = nullptr;  // small device counters
   unsigned long long* h_scratch_ = nullptr;  // pinned host mirror

@@ -168,6 +168,8 @@ SIGNATURES = {
     "hkv_size_if": (ctypes.c_int, [_P, _P, _P, _P]),
     "hkv_table_get_view": (ctypes.c_int, [_P, _P]),
     "hkv_find_or_insert_ptr": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _P, _B, _B, _P]),
+    "hkv_lock_keys": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _P]),
+    "hkv_unlock_keys": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P]),
     "hkv_save_files": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_char_p,
                                       ctypes.c_char_p, _SZ, _P, ctypes.POINTER(_SZ)]),
     "hkv_load_files": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_char_p,
@@ -390,13 +392,29 @@ class HashTable:
                                   _ptr(founds), _ptr(scores), _stream(stream)))
 
     def find_or_insert_ptr(self, n, keys, value_ptrs, founds, scores=None,
-                           stream=None, unique_key=True, ignore_evict_strategy=False):
+                           stream=None, unique_key=True, ignore_evict_strategy=False,
+                           locked_key_ptrs=None):
         """find_or_insert* : finds or inserts each key (find_or_insert rules)
         without copying values; value_ptrs receives each key's row address
-        (0 when refused), founds whether the key was there before."""
+        (0 when refused), founds whether the key was there before. With
+        locked_key_ptrs the keys stay locked (their key-word addresses go
+        there) until unlock_keys."""
         _check(lib().hkv_find_or_insert_ptr(self._h, n, _ptr(keys), _ptr(value_ptrs),
                                             _ptr(founds), _ptr(scores), _stream(stream),
-                                            unique_key, ignore_evict_strategy, None))
+                                            unique_key, ignore_evict_strategy,
+                                            _ptr(locked_key_ptrs)))
+
+    def lock_keys(self, n, keys, locked_key_ptrs, succeededs=None, stream=None,
+                  scores=None):
+        """lock_keys: locks each present key (hit score rule) and writes its
+        key-word address to locked_key_ptrs (0 and False when absent)."""
+        _check(lib().hkv_lock_keys(self._h, n, _ptr(keys), _ptr(locked_key_ptrs),
+                                   _ptr(succeededs), _stream(stream), _ptr(scores)))
+
+    def unlock_keys(self, n, locked_key_ptrs, keys, succeededs=None, stream=None):
+        """unlock_keys: puts each key back at its locked key word."""
+        _check(lib().hkv_unlock_keys(self._h, n, _ptr(locked_key_ptrs), _ptr(keys),
+                                     _ptr(succeededs), _stream(stream)))
 
     def save(self, keys_path, values_path, scores_path,
              max_workspace_size=1 << 20, stream=None) -> int:

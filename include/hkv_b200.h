@@ -164,12 +164,36 @@ int hkv_find_ptr(hkv_table* table, size_t n, const void* keys, void** values,
  * later key of the same batch may evict a key placed earlier in it and then
  * owns that row. With repeated keys
  * (unique_key = false) every occurrence gets the same address and only the
- * first can report a new key. locked_key_ptrs (keys left locked for a later
- * unlock_keys) must be NULL: HKV_ERR_UNSUPPORTED otherwise. */
+ * first can report a new key. With locked_key_ptrs (unique_key = true only,
+ * HKV_ERR_UNSUPPORTED otherwise) every placed or found key stays locked for
+ * the caller and locked_key_ptrs[i] is the address of its key word (NULL
+ * where values[i] is NULL); release them with hkv_unlock_keys. */
 int hkv_find_or_insert_ptr(hkv_table* table, size_t n, const void* keys,
                            void** values, bool* founds, const uint64_t* scores,
                            void* stream, bool unique_key,
                            bool ignore_evict_strategy, void** locked_key_ptrs);
+
+/* lock_keys, hkv_hashtable.h:1744-1768: each present key is locked, its
+ * score set by the hit rule (scores as in find_or_insert; NULL for Lru),
+ * and the address of its key word written to locked_key_ptrs[i]; absent or
+ * reserved keys get NULL and succeededs[i] = false. A locked key is not
+ * found by find / contains / assign_scores / erase / accum_or_assign (its
+ * key word holds a lock marker, as in the reference) and its slot is never
+ * chosen as an eviction victim. Deviations from the reference: the marker is
+ * 0xFFFFFFFFFFFFFFFC (the fourth reserved key; the reference writes
+ * LOCKED_KEY, 0xFFFFFFFFFFFFFFFD), and an insert-like call of a locked key
+ * waits for its unlock (bounded: HKV_ERR_TIMEOUT after 1 s) where the
+ * reference would insert a second copy of the key. The table cannot grow
+ * (reserve, auto-grow) while keys are locked: HKV_ERR_RUNTIME. */
+int hkv_lock_keys(hkv_table* table, size_t n, const void* keys, void** locked_key_ptrs,
+                  bool* succeededs, void* stream, const uint64_t* scores);
+
+/* unlock_keys, hkv_hashtable.h:1788-1806: puts keys[i] back into the key
+ * word at locked_key_ptrs[i] if that word is still locked by the caller;
+ * succeededs[i] tells whether it was (false for NULL, for an address outside
+ * this table's keys, or for a word that is not locked). */
+int hkv_unlock_keys(hkv_table* table, size_t n, void** locked_key_ptrs, const void* keys,
+                    bool* succeededs, void* stream);
 
 /* contains, hkv_hashtable.h:2330-2348. */
 int hkv_contains(hkv_table* table, size_t n, const void* keys, bool* founds,

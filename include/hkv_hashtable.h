@@ -314,7 +314,8 @@ class HashTable {
   }
 
   /* find_or_insert* (addresses of the value rows), reference
-   * hkv_hashtable.h:1658-1727; locked_key_ptrs must be nullptr. */
+   * hkv_hashtable.h:1658-1727; with locked_key_ptrs (unique_key only) the
+   * keys stay locked until unlock_keys. */
   void find_or_insert(const size_type n, const key_type* keys, value_type** values,
                       bool* founds, score_type* scores = nullptr,
                       cudaStream_t stream = 0, bool unique_key = true,
@@ -324,6 +325,20 @@ class HashTable {
         t_, n, keys, reinterpret_cast<void**>(values), founds, scores,
         detail::st(stream), unique_key, ignore_evict_strategy,
         reinterpret_cast<void**>(locked_key_ptrs)));
+  }
+
+  /* lock_keys / unlock_keys, reference hkv_hashtable.h:1744-1806 (see
+   * hkv_lock_keys in hkv_b200.h for the lock marker and the bounded wait). */
+  void lock_keys(const size_type n, key_type const* keys, key_type** locked_key_ptrs,
+                 bool* succeededs = nullptr, cudaStream_t stream = 0,
+                 score_type const* scores = nullptr) {
+    detail::check(hkv_lock_keys(t_, n, keys, reinterpret_cast<void**>(locked_key_ptrs),
+                                succeededs, detail::st(stream), scores));
+  }
+  void unlock_keys(const size_type n, key_type** locked_key_ptrs, const key_type* keys,
+                   bool* succeededs = nullptr, cudaStream_t stream = 0) {
+    detail::check(hkv_unlock_keys(t_, n, reinterpret_cast<void**>(locked_key_ptrs), keys,
+                                  succeededs, detail::st(stream)));
   }
 
   void contains(const size_type n, const key_type* keys, bool* founds,
