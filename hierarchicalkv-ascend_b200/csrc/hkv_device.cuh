@@ -29,6 +29,10 @@ constexpr uint64_t kLockedKey = 0xFFFFFFFFFFFFFFFDull;
 // with locked_key_ptrs): the fourth reserved value, so that the kernels can
 // tell a caller's lock from the short lock of an operation in flight.
 constexpr uint64_t kUserLockedKey = 0xFFFFFFFFFFFFFFFCull;
+// A bucket's size word: live slots in the low 16 bits, the slots a caller
+// holds locked above them (read together, so the probe pays nothing for it).
+constexpr int32_t kSizeMask = 0xFFFF;
+constexpr int kLockShift = 16;
 constexpr uint64_t kReservedMask = 0xFFFFFFFFFFFFFFFCull;
 constexpr uint64_t kMaxScore = 0xFFFFFFFFFFFFFFFFull;
 constexpr uint64_t kIgnoredEpoch = 0xFFFFFFFFFFFFFFFFull;
@@ -99,8 +103,8 @@ struct TableView {
   uint64_t* keys;
   uint64_t* scores;
   uint8_t* digests;
-  int32_t* sizes;
-  int32_t* user_locks;     // per bucket: slots a caller holds locked
+  int32_t* sizes;          // per bucket: live slots (low 16 bits) and slots a
+                           // caller holds locked (bits 16 and up)
   uint8_t* const* slices;  // device array of slice base pointers
   uint8_t* values0;        // slice 0 (used directly when single_slice)
   int* error;              // device error word

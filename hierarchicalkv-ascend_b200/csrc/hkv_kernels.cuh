@@ -42,10 +42,7 @@ __global__ void init_buckets_kernel(TableView t, uint64_t b0, uint64_t b1,
 #pragma unroll
       for (int j = 0; j < 8; j++) s4[j] = make_uint4(0, 0, 0, 0);
     }
-    if ((s & (kBucket - 1)) == 0) {
-      t.sizes[s >> kBucketShift] = 0;
-      t.user_locks[s >> kBucketShift] = 0;
-    }
+    if ((s & (kBucket - 1)) == 0) t.sizes[s >> kBucketShift] = 0;
   }
 }
 
@@ -53,12 +50,13 @@ __global__ void init_buckets_kernel(TableView t, uint64_t b0, uint64_t b1,
 // Reductions for size() and fast_load_factor()
 // ============================================================================
 // Sum of sizes[0, nb) into *out (out zeroed by the caller).
+// shift 0 sums the live slots, kLockShift the slots callers hold locked.
 __global__ void sum_sizes_kernel(const int32_t* __restrict__ sizes, uint64_t nb,
-                                 unsigned long long* out) {
+                                 unsigned long long* out, int shift) {
   int64_t s = 0;
   for (uint64_t b = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; b < nb;
        b += (uint64_t)gridDim.x * blockDim.x)
-    s += sizes[b];
+    s += (sizes[b] >> shift) & kSizeMask;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
   __shared__ int64_t part[32];
@@ -327,13 +325,13 @@ constexpr int kRetry = 7;  // a round's result when a lock was in the way
 // the complete virtual lanes c = 2L + e + 2W*h (e in {0,1}, h < 8/W),
 // stored at r = e + 2h. Exchanges between two virtual lanes of one lane
 // stay in registers; the others are tile shuffles.
-template <uint32_t W>
+template <uint32_t W, bool kSkipUser = false>
 __device__ __forceinline__ void min_score_butterfly(const TileW<W>& tile,
                                                     const uint64_t* bs,
                                                     uint32_t pos,
                                                     uint64_t owner_idx,
                                                     uint64_t& ms, uint32_t& mp,
-                                                    const uint64_t* skip_user = nullptr) {
+                                                    const uint64_t* bk = nullptr) {
   constexpr uint32_t R = 16 / W;  // virtual lanes per lane
   constexpr uint32_t H = 8 / W;   // pair loads per virtual-lane pair and k
   uint64_t sv[R];
@@ -350,11 +348,11 @@ __device__ __forceinline__ void min_score_butterfly(const TileW<W>& tile,
     const uint4 v = __ldcg(b4 + q / 2);
     uint64_t s0 = (static_cast<uint64_t>(v.y) << 32) | v.x;
     uint64_t s1 = (static_cast<uint64_t>(v.w) << 32) | v.z;
-    if (skip_user != nullptr) {
+    if constexpr (kSkipUser) {
       // a bucket holding caller locks: their slots are never victims (the
       // reference's scan skips locked key words, insert_or_assign_kernel.h:214)
-      if (ld_relaxed_u64(skip_user + q) == kUserLockedKey) s0 = kMaxScore;
-      if (ld_relaxed_u64(skip_user + q + 1) == kUserLockedKey) s1 = kMaxScore;
+      if (ld_relaxed_u64(bk + q) == kUserLockedKey) s0 = kMaxScore;
+      if (ld_relaxed_u64(bk + q + 1) == kUserLockedKey) s1 = kMaxScore;
     }
     const uint32_t r = 2 * (j % H);
     if (s0 < sv[r]) { sv[r] = s0; pv[r] = q; }
@@ -490,7 +488,7 @@ __device__ __forceinline__ void upsert_locked(const TableView& t,
     if (Mode == kModeFindOrInsertPtr && a.locked_key_ptrs != nullptr) {
       // the slot stays locked for the caller (find_or_insert_ptr_kernel_v2.h:
       // locked_key_ptrs), counted per bucket so that evictions pass it by
-      atomicAdd(t.user_locks + l.bkt, 1);
+      atomicAdd(t.sizes + l.bkt, 1 << kLockShift);
       store_release_u64(t.keys + s, kUserLockedKey);
       a.locked_key_ptrs[i] = t.keys + s;
     } else {
@@ -530,7 +528,7 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const TileW<W>& 
     hits |= static_cast<M>(bytes_eq16(dv, l.d4)) << (16 * j);
     empt |= static_cast<M>(bytes_eq16(dv, kEmptyDigest * 0x01010101u)) << (16 * j);
   }
-  const int32_t bsize = __ldcg(t.sizes + l.bkt);
+  const int32_t bword = __ldcg(t.sizes + l.bkt);  // size, caller locks above it
   // ---- 1. is the key here? (a digest hit that holds it is locked at once)
   int mine = -1;
   bool busy = false;
@@ -542,9 +540,11 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const TileW<W>& 
       mine = static_cast<int>(lo + j);
       break;
     }
-    // an operation in flight, or a caller holding this key locked: wait
-    // (bounded) rather than insert a second copy of the key
-    busy |= (k == kLockedKey || k == kUserLockedKey);
+    // an operation in flight may hold the key: retry. A caller's lock says
+    // nothing about which key it hides (a digest hit may belong to another
+    // key): like the reference, which compares the word with the key itself
+    // (insert_or_assign_kernel.h:128-140), such a slot is not the key.
+    busy |= (k == kLockedKey);
   }
   int res = kRetry;
   bool got = false;
@@ -561,7 +561,7 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const TileW<W>& 
     res = kDuplicate;
   } else if (!tile.ballot(busy)) {
     // ---- 2. first EMPTY slot in linear order from pos
-    if (bsize < static_cast<int32_t>(kBucket)) {
+    if ((bword & kSizeMask) < static_cast<int32_t>(kBucket)) {
       const uint32_t sh = (l.pos >= lo && l.pos < lo + kD) ? l.pos - lo : 0;
       while (true) {
         uint32_t best = 0xFFFFFFFFu;
@@ -592,8 +592,10 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const TileW<W>& 
     if (!got) {
       uint64_t ms;
       uint32_t mp;
-      const int32_t held = __ldcg(t.user_locks + l.bkt);
-      min_score_butterfly(tile, bs, l.pos, i, ms, mp, held > 0 ? bk : nullptr);
+      if ((bword >> kLockShift) > 0)
+        min_score_butterfly<W, true>(tile, bs, l.pos, i, ms, mp, bk);
+      else
+        min_score_butterfly<W, false>(tile, bs, l.pos, i, ms, mp);
       if (desired < ms) {
         res = kRefused;
       } else {
@@ -1181,7 +1183,7 @@ __global__ void __launch_bounds__(256)
                 (S == kLfu || S == kEpochLfu) ? ld_relaxed_u64(t.scores + s) : 0;
             const uint64_t desired = desired_when_missed<S>(scores, i, epoch, clk);
             if (score_on_write<S>(old, scores, i, desired, false, &ns)) t.scores[s] = ns;
-            atomicAdd(t.user_locks + l.bkt, 1);
+            atomicAdd(t.sizes + l.bkt, 1 << kLockShift);
             store_release_u64(t.keys + s, kUserLockedKey);
           }
           addr = t.keys + s;
@@ -1220,7 +1222,7 @@ __global__ void __launch_bounds__(256)
       const uint64_t slot = static_cast<uint64_t>(p - t.keys);
       ok = cas_u64(p, kUserLockedKey, kLockedKey) == kUserLockedKey;
       if (ok) {
-        atomicSub(t.user_locks + (slot >> kBucketShift), 1);
+        atomicSub(t.sizes + (slot >> kBucketShift), 1 << kLockShift);
         store_release_u64(p, key);
       }
     }

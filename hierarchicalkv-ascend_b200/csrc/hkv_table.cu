@@ -175,7 +175,6 @@ TableImpl::TableImpl(const hkv_options& o, int key_type, int value_type,
   CUDA_TRY(cudaMalloc(&scores_, slots * 8));
   CUDA_TRY(cudaMalloc(&digests_, slots));
   CUDA_TRY(cudaMalloc(&sizes_, num_buckets_ * 4));
-  CUDA_TRY(cudaMalloc(&user_locks_, num_buckets_ * 4));
   CUDA_TRY(cudaMalloc(&d_error_, 2 * sizeof(int)));
   CUDA_TRY(cudaMemset(d_error_, 0, 2 * sizeof(int)));
   CUDA_TRY(cudaMalloc(&d_scratch_, 4 * sizeof(unsigned long long)));
@@ -206,7 +205,6 @@ TableImpl::~TableImpl() {
   cudaFree(scores_);
   cudaFree(digests_);
   cudaFree(sizes_);
-  cudaFree(user_locks_);
   cudaFree(d_error_);
   cudaFree(d_scratch_);
   if (pool_) cudaMemPoolDestroy(pool_);
@@ -270,7 +268,6 @@ TableView TableImpl::view() const {
   v.scores = scores_;
   v.digests = digests_;
   v.sizes = sizes_;
-  v.user_locks = user_locks_;
   v.slices = d_slices_;
   v.values0 = slices_.empty() ? nullptr : slices_[0].dev;
   v.error = d_error_;
@@ -393,14 +390,15 @@ void TableImpl::check_strategy(const uint64_t* scores, bool ignore) const {
 }
 
 uint64_t TableImpl::sum_sizes(uint64_t nb, cudaStream_t s) {
-  return sum_counts(sizes_, nb, s);
+  return sum_counts(nb, 0, s);
 }
 
-uint64_t TableImpl::sum_counts(const int32_t* counts, uint64_t nb, cudaStream_t s) {
+uint64_t TableImpl::sum_counts(uint64_t nb, int shift, cudaStream_t s) {
   CUDA_TRY(cudaMemsetAsync(d_scratch_, 0, sizeof(unsigned long long), s));
   const int blocks = static_cast<int>(
       std::min<uint64_t>(ceil_div(nb, 256 * 4), sm_count_ * 4ull));
-  sum_sizes_kernel<<<std::max(blocks, 1), 256, 0, counted(s)>>>(counts, nb, d_scratch_);
+  sum_sizes_kernel<<<std::max(blocks, 1), 256, 0, counted(s)>>>(sizes_, nb, d_scratch_,
+                                                                 shift);
   CUDA_TRY(cudaGetLastError());
   CUDA_TRY(cudaMemcpyAsync(h_scratch_, d_scratch_, sizeof(unsigned long long),
                            cudaMemcpyDeviceToHost, s));
@@ -928,7 +926,7 @@ size_t TableImpl::load(hkv_kv_read_fn read, void* user, size_t max_ws,
 void TableImpl::double_capacity(cudaStream_t s) {
   // a rehash would move a key a caller holds locked away from the address
   // the caller was given
-  HKV_REQUIRE(sum_counts(user_locks_, num_buckets_, s) == 0, HKV_ERR_RUNTIME,
+  HKV_REQUIRE(sum_counts(num_buckets_, kLockShift, s) == 0, HKV_ERR_RUNTIME,
               "the table cannot grow while keys are locked (lock_keys or "
               "find_or_insert with locked_key_ptrs): unlock them first");
   const uint64_t old_nb = num_buckets_, new_nb = old_nb * 2;
@@ -949,13 +947,10 @@ void TableImpl::double_capacity(cudaStream_t s) {
   cudaFree(scores_);
   cudaFree(digests_);
   cudaFree(sizes_);
-  cudaFree(user_locks_);
   keys_ = nk;
   scores_ = ns;
   digests_ = nd;
   sizes_ = nz;
-  CUDA_TRY(cudaMalloc(&user_locks_, new_nb * 4));
-  CUDA_TRY(cudaMemset(user_locks_, 0, new_nb * 4));
   allocate_slices(old_nb, new_nb);
   upload_slices();
   num_buckets_ = new_nb;
@@ -1017,7 +1012,10 @@ void TableImpl::get_state(uint64_t* keys, uint64_t* scores, uint8_t* digests,
   if (keys) CUDA_TRY(cudaMemcpy(keys, keys_, capacity_ * 8, cudaMemcpyDeviceToHost));
   if (scores) CUDA_TRY(cudaMemcpy(scores, scores_, capacity_ * 8, cudaMemcpyDeviceToHost));
   if (digests) CUDA_TRY(cudaMemcpy(digests, digests_, capacity_, cudaMemcpyDeviceToHost));
-  if (sizes) CUDA_TRY(cudaMemcpy(sizes, sizes_, num_buckets_ * 4, cudaMemcpyDeviceToHost));
+  if (sizes) {
+    CUDA_TRY(cudaMemcpy(sizes, sizes_, num_buckets_ * 4, cudaMemcpyDeviceToHost));
+    for (uint64_t b = 0; b < num_buckets_; b++) sizes[b] &= kSizeMask;  // live slots only
+  }
   if (values) {
     size_t off = 0;
     for (auto& sl : slices_) {

@@ -234,7 +234,8 @@ class TableImpl {
   void auto_grow(size_t n, cudaStream_t s);
   float fast_load_factor(size_t delta, cudaStream_t s);
   uint64_t sum_sizes(uint64_t nb, cudaStream_t s);
-  uint64_t sum_counts(const int32_t* counts, uint64_t nb, cudaStream_t s);
+  // sum over buckets of (size word >> shift) & kSizeMask
+  uint64_t sum_counts(uint64_t nb, int shift, cudaStream_t s);
   void allocate_slices(uint64_t b0, uint64_t b1);
   void upload_slices();
   void double_capacity(cudaStream_t s);
@@ -257,8 +258,7 @@ class TableImpl {
   uint64_t* keys_ = nullptr;
   uint64_t* scores_ = nullptr;
   uint8_t* digests_ = nullptr;
-  int32_t* sizes_ = nullptr;
-  int32_t* user_locks_ = nullptr;  // per bucket: slots a caller holds locked
+  int32_t* sizes_ = nullptr;  // live slots, caller locks from bit kLockShift
   int* d_error_ = nullptr;
   unsigned long long* d_scratch_ = nullptr;  // small device counters
   unsigned long long* h_scratch_ = nullptr;  // pinned host mirror

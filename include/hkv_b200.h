@@ -181,10 +181,10 @@ int hkv_find_or_insert_ptr(hkv_table* table, size_t n, const void* keys,
  * key word holds a lock marker, as in the reference) and its slot is never
  * chosen as an eviction victim. Deviations from the reference: the marker is
  * 0xFFFFFFFFFFFFFFFC (the fourth reserved key; the reference writes
- * LOCKED_KEY, 0xFFFFFFFFFFFFFFFD), and an insert-like call of a locked key
- * waits for its unlock (bounded: HKV_ERR_TIMEOUT after 1 s) where the
- * reference would insert a second copy of the key. The table cannot grow
- * (reserve, auto-grow) while keys are locked: HKV_ERR_RUNTIME. */
+ * LOCKED_KEY, 0xFFFFFFFFFFFFFFFD), and the table cannot grow (reserve,
+ * auto-grow) while keys are locked: HKV_ERR_RUNTIME. As in the reference, an
+ * insert-like call of a key that is locked does not see it and places a
+ * second copy. */
 int hkv_lock_keys(hkv_table* table, size_t n, const void* keys, void** locked_key_ptrs,
                   bool* succeededs, void* stream, const uint64_t* scores);
 
@@ -281,7 +281,8 @@ typedef struct {
   uint64_t* keys;
   uint64_t* scores;
   uint8_t* digests;
-  int32_t* sizes;
+  int32_t* sizes;   /* per bucket: live slots in the low 16 bits (keys held
+                      * by hkv_lock_keys are counted from bit 16) */
   uint8_t** slices; /* device array of slice base addresses */
   uint64_t capacity;
   uint64_t num_buckets;

@@ -4,10 +4,9 @@ Reference: HashTable::lock_keys / unlock_keys (hkv_hashtable.h:1744-1806,
 lock_keys_kernel.h, unlock_keys_kernel.h) and the expectations of
 tests/test_lock_unlock_keys.cpp: present keys lock with a non-null key-word
 address and succeed, absent keys get null and fail, unlock succeeds once.
-Also the properties this build adds (documented at hkv_lock_keys): a locked
-key is not found by lookups, its slot is never an eviction victim, the table
-cannot grow while keys are locked, and an insert of a locked key waits
-(bounded) for the unlock.
+Also the properties documented at hkv_lock_keys: a locked key is not found
+by lookups or inserts, its slot is never an eviction victim, and the table
+cannot grow while keys are locked.
 """
 import numpy as np
 import pytest
@@ -179,7 +178,9 @@ def test_reserve_refused_while_locked_and_bad_unlocks():
     assert t.capacity() == 128 * 64 and g.contains(keys).all()
 
 
-def test_insert_of_a_locked_key_waits_with_a_bounded_error():
+def test_insert_of_a_locked_key_places_a_second_copy():
+    """As in the reference (insert_or_assign_kernel.h:128-140 compares the key
+    word with the key itself), an insert does not see a locked key."""
     rng = np.random.default_rng(76)
     t = make_table(128 * 16, dim=4, strategy=H.EvictStrategy.kLru)
     g = GpuOps(t, 4)
@@ -187,9 +188,10 @@ def test_insert_of_a_locked_key_waits_with_a_bounded_error():
     g.insert_or_assign(keys, np.zeros((10, 4), np.float32))
     dptrs, _, ok = lock(t, keys[:1])
     assert ok.all()
-    t.insert_or_assign(1, dev(keys[:1]), dev(np.ones((1, 4), np.float32)))
-    with pytest.raises(H.HkvTimeout):
-        t.check_device_error()
-    assert t.size() == 10  # no second copy of the key
+    g.insert_or_assign(keys[:1], np.ones((1, 4), np.float32))
+    t.check_device_error()
+    assert t.size() == 11
+    v, f, _ = g.find(keys[:1])
+    assert f.all() and (v == 1).all()
     assert unlock(t, dptrs, keys[:1]).all()
     assert g.contains(keys).all()

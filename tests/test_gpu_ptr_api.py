@@ -162,7 +162,10 @@ def test_find_or_insert_ptr_repeated_keys_and_refusal():
     assert int(host(p3)[0]) == 0 and not bool(host(f3)[0])
 
 
-def test_locked_key_ptrs_not_supported():
+def test_locked_key_ptrs_need_unique_keys():
+    """locked_key_ptrs keeps each placed key locked for the caller, which a
+    key repeated in the batch cannot be twice: unique_key=false is refused
+    (the locking itself is covered by test_gpu_lock_keys.py)."""
     t = make_table(128 * 8, dim=4, strategy=H.EvictStrategy.kLru)
     k = dev(np.array([5, 6], np.uint64))
     p = ptrs(2)
@@ -170,5 +173,6 @@ def test_locked_key_ptrs_not_supported():
     lk = ptrs(2)
     with pytest.raises(H.HkvUnsupported):
         H._check(H.lib().hkv_find_or_insert_ptr(t._h, 2, H._ptr(k), H._ptr(p), H._ptr(f),
-                                                None, H._stream(None), True, False,
+                                                None, H._stream(None), False, False,
                                                 H._ptr(lk)))
+    assert t.size() == 0
