@@ -508,7 +508,7 @@ __device__ __forceinline__ void upsert_locked(const TableView& t,
 //  3. otherwise the minimum-score slot (butterfly above); refuse iff
 //     desired < min; CAS(victim -> LOCKED) and re-check its score.
 // Returns the Occupy result, or kRetry.
-template <int Mode, int S, int VW, uint32_t W>
+template <int Mode, int S, int VW, uint32_t W, bool kLocks>
 __device__ __forceinline__ int upsert_round(const TableView& t, const TileW<W>& tile,
                                             const UpsertArgs& a, uint64_t i,
                                             uint64_t key, uint64_t desired,
@@ -592,8 +592,10 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const TileW<W>& 
     if (!got) {
       uint64_t ms;
       uint32_t mp;
-      if ((bword >> kLockShift) > 0)
-        min_score_butterfly<W, true>(tile, bs, l.pos, i, ms, mp, bk);
+      // kernels launched while the caller may hold locks pass them by; the
+      // others carry no trace of that scan
+      if (kLocks && (bword >> kLockShift) > 0)
+        min_score_butterfly<W, kLocks>(tile, bs, l.pos, i, ms, mp, bk);
       else
         min_score_butterfly<W, false>(tile, bs, l.pos, i, ms, mp);
       if (desired < ms) {
@@ -663,7 +665,7 @@ constexpr uint32_t kUpsertTile = HKV_UPSERT_TILE;
 
 // The upsert loop: keys [0, n) of `a`, warp `warp` of `nwarps` taking
 // keys warp * KPW, then every nwarps * KPW.
-template <int Mode, int S, int VW>
+template <int Mode, int S, int VW, bool kLocks>
 __device__ __forceinline__ void upsert_body(const TableView& t, const UpsertArgs& a,
                                             uint64_t clk, uint64_t warp,
                                             uint64_t nwarps) {
@@ -704,7 +706,7 @@ __device__ __forceinline__ void upsert_body(const TableView& t, const UpsertArgs
     for (int round = 0;; round++) {
       bool again = false;
       if (todo) {
-        res = upsert_round<Mode, S, VW, W>(t, tile, a, i, key, desired, l, head);
+        res = upsert_round<Mode, S, VW, W, kLocks>(t, tile, a, i, key, desired, l, head);
         if (res == kRetry) {
           if (retry_expired(t, tile, t0, 101)) {
             res = kTimedOut;
@@ -750,13 +752,15 @@ __device__ __forceinline__ void upsert_body(const TableView& t, const UpsertArgs
   }
 }
 
-template <int Mode, int S, int VW>
+// kLocks: launched while the caller may hold keys locked (lock_keys,
+// find_or_insert* with locked_key_ptrs); evictions then pass them by.
+template <int Mode, int S, int VW, bool kLocks = false>
 __global__ void __launch_bounds__(256, HKV_UPSERT_MIN_BLOCKS)
     upsert_kernel(TableView t, UpsertArgs a) {
   __shared__ uint64_t s_clock;
   if (threadIdx.x == 0) s_clock = global_timer_ns();
   __syncthreads();
-  upsert_body<Mode, S, VW>(t, a, s_clock,
+  upsert_body<Mode, S, VW, kLocks>(t, a, s_clock,
                            (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / 32,
                            (uint64_t)gridDim.x * (blockDim.x / 32));
 }

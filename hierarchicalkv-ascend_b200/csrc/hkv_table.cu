@@ -429,6 +429,15 @@ float TableImpl::load_factor(cudaStream_t s) {
 // ---------------------------------------------------------------------------
 // Upsert family
 // ---------------------------------------------------------------------------
+// The upsert kernel of MODE for the enclosing S and VW: the variant whose
+// evictions pass caller-held locks by while the caller may hold some.
+#define LAUNCH_UPSERT(MODE, VWIDTH, grid, s, v, a)                                   \
+  do {                                                                              \
+    if (maybe_locked_)                                                              \
+      upsert_kernel<MODE, S, VWIDTH, true><<<(grid), 256, 0, counted(s)>>>(v, a);   \
+    else                                                                            \
+      upsert_kernel<MODE, S, VWIDTH, false><<<(grid), 256, 0, counted(s)>>>(v, a);  \
+  } while (0)
 void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
                        const uint8_t* values_in, uint8_t* values_io,
                        const uint64_t* scores, uint64_t* ev_keys,
@@ -465,13 +474,13 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
     const int grid = upsert_grid(n);
     DISPATCH_STRATEGY(st, DISPATCH_VW(vw, {
       if (mode == kModeInsertOrAssign)
-        upsert_kernel<kModeInsertOrAssign, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
+        LAUNCH_UPSERT(kModeInsertOrAssign, VW, grid, s, v, a);
       else if (mode == kModeFindOrInsert)
-        upsert_kernel<kModeFindOrInsert, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
+        LAUNCH_UPSERT(kModeFindOrInsert, VW, grid, s, v, a);
       else if (mode == kModeFindOrInsertPtr)
-        upsert_kernel<kModeFindOrInsertPtr, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
+        LAUNCH_UPSERT(kModeFindOrInsertPtr, VW, grid, s, v, a);
       else
-        upsert_kernel<kModeInsertAndEvict, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
+        LAUNCH_UPSERT(kModeInsertAndEvict, VW, grid, s, v, a);
     }));
     CUDA_TRY(cudaGetLastError());
     return;
@@ -492,7 +501,7 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
     a.founds = ufound;
     const int grid = upsert_grid(n);
     DISPATCH_STRATEGY(st, {
-      upsert_kernel<kModeFindOrInsertPtr, S, 16><<<grid, 256, 0, counted(s)>>>(v, a);
+      LAUNCH_UPSERT(kModeFindOrInsertPtr, 16, grid, s, v, a);
     });
     CUDA_TRY(cudaGetLastError());
     scatter_ptrs_kernel<<<static_cast<int>(std::min<uint64_t>(ceil_div(n, 256),
@@ -528,11 +537,11 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
   const int grid = upsert_grid(n);
   DISPATCH_STRATEGY(st, DISPATCH_VW(vw, {
     if (mode == kModeInsertOrAssign)
-      upsert_kernel<kModeInsertOrAssign, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
+      LAUNCH_UPSERT(kModeInsertOrAssign, VW, grid, s, v, a);
     else if (mode == kModeFindOrInsert)
-      upsert_kernel<kModeFindOrInsert, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
+      LAUNCH_UPSERT(kModeFindOrInsert, VW, grid, s, v, a);
     else
-      upsert_kernel<kModeInsertAndEvict, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
+      LAUNCH_UPSERT(kModeInsertAndEvict, VW, grid, s, v, a);
   }));
   CUDA_TRY(cudaGetLastError());
   if (mode == kModeFindOrInsert) {
@@ -737,6 +746,7 @@ void TableImpl::find_or_insert_ptr(size_t n, const uint64_t* keys,
   if (!ignore) check_strategy(scores, false);
   HKV_REQUIRE(keys != nullptr && value_ptrs != nullptr && founds != nullptr,
               HKV_ERR_INVALID, "keys, values and founds must not be null");
+  if (locked_key_ptrs != nullptr) maybe_locked_ = true;
   upsert(kModeFindOrInsertPtr, n, keys, nullptr, nullptr, scores, nullptr,
          nullptr, nullptr, nullptr, s, unique, ignore, nullptr, nullptr, 1,
          value_ptrs, founds, locked_key_ptrs);
@@ -748,6 +758,7 @@ void TableImpl::lock_keys(size_t n, const uint64_t* keys, uint64_t** locked_key_
   // reference lock_keys_kernel.h:23-25: null keys or outputs -> nothing done
   if (keys == nullptr || locked_key_ptrs == nullptr) return;
   check_strategy(scores, false);
+  maybe_locked_ = true;
   const TableView v = view();
   DISPATCH_STRATEGY(strategy_, {
     lock_keys_kernel<S><<<tile_grid(n), 256, 0, counted(s)>>>(v, keys, locked_key_ptrs,
@@ -764,6 +775,9 @@ void TableImpl::unlock_keys(size_t n, uint64_t* const* locked_key_ptrs,
   unlock_keys_kernel<<<static_cast<int>(std::min<uint64_t>(ceil_div(n, 256), sm_count_ * 16ull)),
                        256, 0, counted(s)>>>(view(), n, locked_key_ptrs, keys, succeeded);
   CUDA_TRY(cudaGetLastError());
+  // the last lock released: later upserts go back to the kernels without the
+  // lock-passing scan (a recount, so this call synchronises the stream)
+  if (maybe_locked_) maybe_locked_ = sum_counts(num_buckets_, kLockShift, s) != 0;
 }
 
 void TableImpl::find_segments(const FindSegments& seg, uint32_t nseg,
@@ -820,6 +834,7 @@ void TableImpl::clear(cudaStream_t s) {
   init_buckets_kernel<<<warp_grid(num_buckets_), 256, 0, counted(s)>>>(
       view(), 0, num_buckets_, 0);
   CUDA_TRY(cudaGetLastError());
+  maybe_locked_ = false;  // every key word and lock count is reset
 }
 
 void TableImpl::export_batch(size_t n, size_t offset, uint64_t* d_counter,
@@ -1152,7 +1167,7 @@ void TableImpl::find_or_insert_in_scratch(size_t n, const uint64_t* keys,
   const int vw = value_width({values});
   const int grid = upsert_grid(n);
   DISPATCH_STRATEGY(st, DISPATCH_VW(vw, {
-    upsert_kernel<kModeFindOrInsert, S, VW><<<grid, 256, 0, counted(s)>>>(v, a);
+    LAUNCH_UPSERT(kModeFindOrInsert, VW, grid, s, v, a);
   }));
   DISPATCH_VW(vw, scatter_found_rows_kernel<VW><<<tile_grid(n), 256, 0, counted(s)>>>(
                       values, uid_of, rep_first, ustatus, n, value_bytes_));

@@ -273,6 +273,9 @@ class TableImpl {
   bool reach_max_ = false;
   bool pure_hbm_ = true;
   uint64_t epoch_ = kIgnoredEpoch;
+  // keys may be held locked by the caller (set by lock calls, cleared by an
+  // unlock that leaves none): upserts then use the lock-passing kernels
+  bool maybe_locked_ = false;
 };
 
 }  // namespace hkvb

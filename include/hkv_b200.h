@@ -191,7 +191,10 @@ int hkv_lock_keys(hkv_table* table, size_t n, const void* keys, void** locked_ke
 /* unlock_keys, hkv_hashtable.h:1788-1806: puts keys[i] back into the key
  * word at locked_key_ptrs[i] if that word is still locked by the caller;
  * succeededs[i] tells whether it was (false for NULL, for an address outside
- * this table's keys, or for a word that is not locked). */
+ * this table's keys, or for a word that is not locked). While keys may be
+ * locked, insert-like calls run kernels that pass locked slots by; to learn
+ * when none is left, this call recounts the locks and so synchronises the
+ * stream. */
 int hkv_unlock_keys(hkv_table* table, size_t n, void** locked_key_ptrs, const void* keys,
                     bool* succeededs, void* stream);
 
