@@ -138,6 +138,9 @@ __device__ __forceinline__ int find_probe(const TableView& t, const TileW<W>& ti
   const uint64_t* bk = t.keys + l.bkt * kBucket;
   const uint4* dl =
       reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) + tile.lane * kDV;
+  // the bucket's size word, read beside the digest line: a full bucket holds
+  // no EMPTY_KEY slot, so the stop rule below cannot apply to it
+  const int32_t bword = __ldg(t.sizes + l.bkt);
   M hits = 0, empt = 0;
 #pragma unroll
   for (uint32_t j = 0; j < kDV; j++) {
@@ -145,6 +148,7 @@ __device__ __forceinline__ int find_probe(const TableView& t, const TileW<W>& ti
     hits |= static_cast<M>(bytes_eq16(dv, l.d4)) << (16 * j);
     empt |= static_cast<M>(bytes_eq16(dv, kEmptyDigest * 0x01010101u)) << (16 * j);
   }
+  if ((bword & kSizeMask) >= static_cast<int32_t>(kBucket)) empt = 0;
   // digest hits holding the key, best = first in the reference's walk
   uint32_t best = 0xFFFFFFFFu;
   for (M h = hits; h; h &= h - 1) {
