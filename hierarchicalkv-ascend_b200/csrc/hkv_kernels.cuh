@@ -781,6 +781,8 @@ __device__ __forceinline__ int tile_locate_existing(const TableView& t,
   const uint64_t* bk = t.keys + l.bkt * kBucket;
   const uint4 dv = __ldcg(
       reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) + tile.lane);
+  // a full bucket holds no EMPTY_KEY slot: the stop rule cannot apply
+  const bool full = kStopRule && (__ldcg(t.sizes + l.bkt) & kSizeMask) >= int32_t{kBucket};
   const uint32_t lo = tile.lane * kDigestsPerLane;
   uint32_t hits = bytes_eq16(dv, l.d4);
   int mine = -1;
@@ -799,7 +801,7 @@ __device__ __forceinline__ int tile_locate_existing(const TableView& t,
   if (!fm) return tile.ballot(busy) ? -2 : -1;
   const uint32_t p = tile.shfl(static_cast<uint32_t>(mine), __ffs(fm) - 1);
   if constexpr (kStopRule) {
-    uint32_t empt = bytes_eq16(dv, kEmptyDigest * 0x01010101u);
+    uint32_t empt = full ? 0u : bytes_eq16(dv, kEmptyDigest * 0x01010101u);
     const uint32_t pr = hit_rank(p, l.pos);
     bool stop = false;
     while (empt) {
