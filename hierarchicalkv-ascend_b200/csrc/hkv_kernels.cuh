@@ -1354,6 +1354,24 @@ __device__ __forceinline__ void warp_copy_rows(const TableView& t, uint64_t sb, 
   }
 }
 
+// First clear bit of the 128-bit mask (m0: slots 0-63, m1: 64-127) at or
+// after `from`, cyclically; kBucket when every slot is set.
+__device__ __forceinline__ uint32_t first_free_from(uint64_t m0, uint64_t m1, uint32_t from) {
+  const uint64_t f0 = ~m0, f1 = ~m1;
+  if (from < 64) {
+    const uint64_t c = f0 & (~uint64_t{0} << from);
+    if (c) return __ffsll(static_cast<long long>(c)) - 1;
+    if (f1) return 64 + __ffsll(static_cast<long long>(f1)) - 1;
+    if (f0) return __ffsll(static_cast<long long>(f0)) - 1;
+    return kBucket;
+  }
+  const uint64_t c = f1 & (~uint64_t{0} << (from - 64));
+  if (c) return 64 + __ffsll(static_cast<long long>(c)) - 1;
+  if (f0) return __ffsll(static_cast<long long>(f0)) - 1;
+  if (f1) return 64 + __ffsll(static_cast<long long>(f1)) - 1;
+  return kBucket;
+}
+
 template <int VW>
 __global__ void __launch_bounds__(256)
     rehash_kernel(TableView t, uint64_t old_nb, uint8_t* __restrict__ scratch) {
@@ -1381,6 +1399,7 @@ __global__ void __launch_bounds__(256)
     __syncwarp();
     int32_t moved = 0, removed = 0;
     if (lane == 0) {
+      uint64_t nocc0 = 0, nocc1 = 0;  // occupied slots of the new bucket
       uint32_t kp = 0;
       while (kp < kBucket) {
         const uint64_t k = st.okeys[kp];
@@ -1395,17 +1414,19 @@ __global__ void __launch_bounds__(256)
           kp++;
           continue;
         }
-        // copy_key_to_new_bucket: first EMPTY slot from the new position
+        // copy_key_to_new_bucket: first EMPTY slot from the new position,
+        // cyclically (found in the occupancy mask instead of slot by slot)
         const uint32_t npos = static_cast<uint32_t>(g & (kBucket - 1));
-        for (uint32_t off = 0; off < kBucket; off++) {
-          const uint32_t p = (npos + off) & (kBucket - 1);
-          if (st.nkeys[p] == kEmptyKey) {
-            st.nkeys[p] = k;
-            st.nscores[p] = st.oscores[kp];
-            st.nsrc[p] = st.osrc[kp];
-            moved++;
-            break;
-          }
+        const uint32_t p = first_free_from(nocc0, nocc1, npos);
+        if (p < kBucket) {
+          st.nkeys[p] = k;
+          st.nscores[p] = st.oscores[kp];
+          st.nsrc[p] = st.osrc[kp];
+          if (p < 64)
+            nocc0 |= uint64_t{1} << p;
+          else
+            nocc1 |= uint64_t{1} << (p - 64);
+          moved++;
         }
         removed++;
         st.okeys[kp] = kEmptyKey;
