@@ -117,6 +117,32 @@ int main(int argc, char** argv) {
   CK(cudaMemcpy(found.data(), df, n * sizeof(bool), cudaMemcpyDeviceToHost));
   for (size_t i = 0; i < n; i++) EXPECT(found[i] && got[i] == 2 * hs[i]);
 
+  // lock_keys / unlock_keys (reference hkv_hashtable.h:1744-1806 and
+  // tests/test_lock_unlock_keys.cpp): locked keys are hidden from find until
+  // they are unlocked; a second unlock fails
+  constexpr size_t nl = 64;
+  K** lp;
+  bool* lok;
+  CK(cudaMalloc(&lp, nl * sizeof(K*)));
+  CK(cudaMalloc(&lok, nl * sizeof(bool)));
+  std::vector<char> ok(nl);
+  table.lock_keys(nl, dk, lp, lok, 0, ds);  // Lfu: the lock adds the score
+  CK(cudaMemcpy(ok.data(), lok, nl * sizeof(bool), cudaMemcpyDeviceToHost));
+  for (size_t i = 0; i < nl; i++) EXPECT(ok[i]);
+  table.find(n, dk, dv, df, out_s);
+  CK(cudaMemcpy(found.data(), df, n * sizeof(bool), cudaMemcpyDeviceToHost));
+  for (size_t i = 0; i < n; i++) EXPECT(static_cast<bool>(found[i]) == (i >= nl));
+  table.unlock_keys(nl, lp, dk, lok);
+  CK(cudaMemcpy(ok.data(), lok, nl * sizeof(bool), cudaMemcpyDeviceToHost));
+  for (size_t i = 0; i < nl; i++) EXPECT(ok[i]);
+  table.find(n, dk, dv, df, out_s);
+  CK(cudaMemcpy(got.data(), out_s, n * sizeof(S), cudaMemcpyDeviceToHost));
+  CK(cudaMemcpy(found.data(), df, n * sizeof(bool), cudaMemcpyDeviceToHost));
+  for (size_t i = 0; i < n; i++) EXPECT(found[i] && got[i] == (i < nl ? 3 : 2) * hs[i]);
+  table.unlock_keys(nl, lp, dk, lok);
+  CK(cudaMemcpy(ok.data(), lok, nl * sizeof(bool), cudaMemcpyDeviceToHost));
+  for (size_t i = 0; i < nl; i++) EXPECT(!ok[i]);
+
   table.erase(n / 2, dk);
   EXPECT(table.size() == n - n / 2);
   table.clear();
