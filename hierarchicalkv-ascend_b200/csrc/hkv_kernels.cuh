@@ -665,6 +665,17 @@ __device__ __forceinline__ bool retry_expired(const TableView& t, const Tl& tile
 #ifndef HKV_UPSERT_MIN_BLOCKS
 #define HKV_UPSERT_MIN_BLOCKS 5
 #endif
+// accum_or_assign: 5 blocks (48 registers) measured faster than 6 (40, more
+// spills) and 4 (64)
+#ifndef HKV_ACCUM_MIN_BLOCKS
+#define HKV_ACCUM_MIN_BLOCKS 5
+#endif
+// insert_and_evict keeps more state across its rounds (the victim and its
+// output): at 64 registers (4 blocks of 256 per SM) it spills nothing and
+// ran 4 % faster than at 48 with spills
+#ifndef HKV_EVICT_MIN_BLOCKS
+#define HKV_EVICT_MIN_BLOCKS 4
+#endif
 constexpr uint32_t kUpsertTile = HKV_UPSERT_TILE;
 
 // The upsert loop: keys [0, n) of `a`, warp `warp` of `nwarps` taking
@@ -759,7 +770,8 @@ __device__ __forceinline__ void upsert_body(const TableView& t, const UpsertArgs
 // kLocks: launched while the caller may hold keys locked (lock_keys,
 // find_or_insert* with locked_key_ptrs); evictions then pass them by.
 template <int Mode, int S, int VW, bool kLocks = false>
-__global__ void __launch_bounds__(256, HKV_UPSERT_MIN_BLOCKS)
+__global__ void __launch_bounds__(256, Mode == kModeInsertAndEvict ? HKV_EVICT_MIN_BLOCKS
+                                                                   : HKV_UPSERT_MIN_BLOCKS)
     upsert_kernel(TableView t, UpsertArgs a) {
   __shared__ uint64_t s_clock;
   if (threadIdx.x == 0) s_clock = global_timer_ns();
@@ -816,6 +828,56 @@ __device__ __forceinline__ int tile_locate_existing(const TableView& t,
   return static_cast<int>(p);
 }
 
+// tile_locate_existing for a tile of W lanes (kBucket / W digests per lane).
+template <bool kStopRule, uint32_t W>
+__device__ __forceinline__ int tile_locate_existing_w(const TableView& t,
+                                                      const TileW<W>& tile,
+                                                      const Locate& l, uint64_t key) {
+  constexpr uint32_t kD = TileW<W>::kDigests;
+  constexpr uint32_t kDV = kD / 16;
+  using M = typename std::conditional<(kD > 32), uint64_t, uint32_t>::type;
+  const uint64_t* bk = t.keys + l.bkt * kBucket;
+  const uint4* dl = reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) + tile.lane * kDV;
+  // a full bucket holds no EMPTY_KEY slot: the stop rule cannot apply
+  const bool full = kStopRule && (__ldcg(t.sizes + l.bkt) & kSizeMask) >= int32_t{kBucket};
+  const uint32_t lo = tile.lane * kD;
+  M hits = 0, empt = 0;
+#pragma unroll
+  for (uint32_t j = 0; j < kDV; j++) {
+    const uint4 dv = __ldcg(dl + j);
+    hits |= static_cast<M>(bytes_eq16(dv, l.d4)) << (16 * j);
+    if (kStopRule)
+      empt |= static_cast<M>(bytes_eq16(dv, kEmptyDigest * 0x01010101u)) << (16 * j);
+  }
+  int mine = -1;
+  bool busy = false;
+  while (hits) {
+    const uint32_t j = low_bit(hits);
+    hits &= hits - 1;
+    const uint64_t k = ld_relaxed_u64(bk + lo + j);
+    if (k == key) {
+      mine = static_cast<int>(lo + j);
+      break;
+    }
+    busy |= (k == kLockedKey);
+  }
+  const uint32_t fm = tile.ballot(mine >= 0);
+  if (!fm) return tile.ballot(busy) ? -2 : -1;
+  const uint32_t p = tile.shfl(static_cast<uint32_t>(mine), __ffs(fm) - 1);
+  if constexpr (kStopRule) {
+    if (full) empt = 0;
+    const uint32_t pr = hit_rank(p, l.pos);
+    bool stop = false;
+    while (empt) {
+      const uint32_t q = lo + low_bit(empt);
+      empt &= empt - 1;
+      if (empty_rank(q, l.pos) < pr && ld_relaxed_u64(bk + q) == kEmptyKey) stop = true;
+    }
+    if (tile.ballot(stop)) return -1;
+  }
+  return static_cast<int>(p);
+}
+
 // ============================================================================
 // accum_or_assign (reference accum_or_assign_kernel.h:55-155 with
 // find_and_lock, find_utils.h:94-228). A present key is found through its
@@ -831,6 +893,7 @@ struct AccumArgs {
   uint64_t n;
   uint64_t epoch;
   uint8_t* status;
+  uint32_t vec16;  // rows and inputs allow 16-byte vectors (float rows only)
 };
 
 template <class VT>
@@ -980,8 +1043,25 @@ __device__ __forceinline__ int accum_apply(const TableView& t, const AccumArgs& 
   const uint32_t ne = vb / sizeof(VT);
   VT* dst = reinterpret_cast<VT*>(value_ptr(t, l.bkt, slot));
   const VT* src = reinterpret_cast<const VT*>(a.values + i * vb);
-  for (uint32_t e = lane; e < ne; e += width)
-    dst[e] = is_accum ? AccumOps<VT>::add(src[e], dst[e]) : src[e];
+  if (std::is_same<VT, float>::value && a.vec16) {
+    // four elements per access, each added as in the scalar loop
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    for (uint32_t e = lane; e < vb / 16; e += width) {
+      float4 v = s4[e];
+      if (is_accum) {
+        const float4 o = d4[e];
+        v.x = v.x + o.x;
+        v.y = v.y + o.y;
+        v.z = v.z + o.z;
+        v.w = v.w + o.w;
+      }
+      d4[e] = v;
+    }
+  } else {
+    for (uint32_t e = lane; e < ne; e += width)
+      dst[e] = is_accum ? AccumOps<VT>::add(src[e], dst[e]) : src[e];
+  }
   if (lane == 0) {
     if (res == kOccupiedEmpty || res == kOccupiedReclaimed) atomicAdd(t.sizes + l.bkt, 1);
     const bool ins = res != kDuplicate;
@@ -1003,18 +1083,22 @@ __device__ __forceinline__ int accum_apply(const TableView& t, const AccumArgs& 
 // others (absent keys, keys whose slot another lane holds, keys being
 // inserted) then go one at a time through the whole warp's window scan,
 // which waits on locked slots, so repeats of a key serialise on its word.
+constexpr uint32_t kAccumTile = 4;
 template <int S, class VT>
-__global__ void __launch_bounds__(256) accum_kernel(TableView t, AccumArgs a) {
+__global__ void __launch_bounds__(256, HKV_ACCUM_MIN_BLOCKS)
+    accum_kernel(TableView t, AccumArgs a) {
+  constexpr uint32_t W = kAccumTile;
+  constexpr uint32_t KPW = 32 / W;  // keys per warp
   __shared__ uint64_t s_clock;
   if (threadIdx.x == 0) s_clock = global_timer_ns();
   __syncthreads();
   const uint64_t clk = s_clock;
-  const Tile tile;
+  const TileW<W> tile;
   const uint32_t wl = threadIdx.x & 31;
   const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x / 32);
   const uint64_t warp = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / 32;
-  for (uint64_t base = warp * 4; base < a.n; base += nwarps * 4) {
-    const uint64_t i = base + (wl >> 3);
+  for (uint64_t base = warp * KPW; base < a.n; base += nwarps * KPW) {
+    const uint64_t i = base + wl / W;
     const bool in = i < a.n;
     const uint64_t key = in ? a.keys[i] : 0;
     const bool valid = in && !is_reserved(key);
@@ -1030,13 +1114,13 @@ __global__ void __launch_bounds__(256) accum_kernel(TableView t, AccumArgs a) {
       desired = desired_when_missed<S>(a.scores, i, a.epoch, clk);
       is_accum = a.accum_or_assigns[i];
       l = locate(t, key);
-      const int p = tile_locate_existing<false>(t, tile, l, key);
+      const int p = tile_locate_existing_w<false>(t, tile, l, key);
       bool got = false;
       if (p >= 0 && tile.lane == 0)
         got = cas_acquire_u64(t.keys + l.bkt * kBucket + p, key, kLockedKey) == key;
       if (tile.shfl(got, 0))
         res = accum_apply<S, VT>(t, a, i, key, is_accum, desired, l,
-                                 static_cast<uint32_t>(p), key, kDuplicate, tile.lane, kTile,
+                                 static_cast<uint32_t>(p), key, kDuplicate, tile.lane, W,
                                  [&]() { tile.sync(); });
       else
         pending = true;
@@ -1062,7 +1146,7 @@ __global__ void __launch_bounds__(256) accum_kernel(TableView t, AccumArgs a) {
         r = accum_apply<S, VT>(t, a, wi, wk, wa, wd, wlc, slot, evk, r, wl, 32,
                                []() { __syncwarp(); });
       }
-      if ((wl >> 3) == (static_cast<uint32_t>(src) >> 3)) res = r;
+      if (wl / W == static_cast<uint32_t>(src) / W) res = r;
     }
     if (in && a.status != nullptr && tile.lane == 0) a.status[i] = res;
   }
@@ -1075,22 +1159,28 @@ __global__ void __launch_bounds__(256) accum_kernel(TableView t, AccumArgs a) {
 // Score update of existing keys (reference assign_scores_kernel_with_filter.h
 // :38-141, score rule update_without_missed) or erase (reference
 // remove_kernel.h:33-113: RECLAIM tombstone, score 0, reclaim digest, size
-// decrement), in the warp-uniform rounds of the upsert family.
+// decrement), in the warp-uniform rounds of the upsert family. One key per
+// kExistTile-lane tile; the next key is read one iteration ahead.
+constexpr uint32_t kExistTile = 4;
 template <int S, bool kErase>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 8)
     existing_key_kernel(TableView t, const uint64_t* __restrict__ keys,
                         const uint64_t* __restrict__ scores, uint64_t n,
                         uint64_t epoch) {
+  constexpr uint32_t W = kExistTile;
+  constexpr uint32_t KPW = 32 / W;  // keys per warp
   __shared__ uint64_t s_clock;
   if (threadIdx.x == 0) s_clock = global_timer_ns();
   __syncthreads();
   const uint64_t clk = s_clock;
-  const Tile tile;
+  const TileW<W> tile;
   const uint32_t wl = threadIdx.x & 31;
   const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x / 32);
   const uint64_t warp = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / 32;
-  for (uint64_t base = warp * 4; base < n; base += nwarps * 4) {
-    const uint64_t i = base + (wl >> 3);
+  const uint64_t stride = nwarps * KPW;
+  uint64_t next = warp * KPW + wl / W < n ? keys[warp * KPW + wl / W] : 0;
+  for (uint64_t base = warp * KPW; base < n; base += stride) {
+    const uint64_t i = base + wl / W;
     uint64_t key = 0, t0 = 0;
     bool todo = false;
     Locate l;
@@ -1098,7 +1188,8 @@ __global__ void __launch_bounds__(256)
     l.pos = 0;
     l.d4 = 0;
     if (i < n) {
-      key = keys[i];
+      key = next;
+      if (i + stride < n) next = keys[i + stride];
       if (!is_reserved(key)) {
         l = locate(t, key);
         todo = true;
@@ -1107,7 +1198,7 @@ __global__ void __launch_bounds__(256)
     for (int round = 0;; round++) {
       bool again = false;
       if (todo) {
-        const int p = tile_locate_existing<!kErase>(t, tile, l, key);
+        const int p = tile_locate_existing_w<!kErase>(t, tile, l, key);
         bool got = false;
         const uint64_t s = l.bkt * kBucket + (p < 0 ? 0 : p);
         if (p >= 0 && tile.lane == 0)

@@ -288,6 +288,13 @@ int TableImpl::tile_grid(size_t n) const {
   return static_cast<int>(std::min<uint64_t>(blocks, sm_count_ * 64ull));
 }
 
+// assign_scores / erase blocks: 256 / kExistTile keys per block pass, at most
+// the 8 blocks per SM that stay resident
+int TableImpl::existing_grid(size_t n) const {
+  const uint64_t blocks = ceil_div(std::max<size_t>(n, 1), 256 / kExistTile);
+  return static_cast<int>(std::min<uint64_t>(blocks, sm_count_ * 8ull));
+}
+
 // Find blocks; each tile walks its keys with the next key loaded ahead.
 int TableImpl::find_grid(size_t n) const {
   const uint64_t blocks = ceil_div(std::max<size_t>(n, 1), 256 / kFindTile);
@@ -297,10 +304,11 @@ int TableImpl::find_grid(size_t n) const {
 #ifndef HKV_UPSERT_BLOCKS_PER_SM
 #define HKV_UPSERT_BLOCKS_PER_SM HKV_UPSERT_MIN_BLOCKS
 #endif
-int TableImpl::upsert_grid(size_t n) const {
+int TableImpl::upsert_grid(size_t n, int mode) const {
   const uint64_t blocks = ceil_div(std::max<size_t>(n, 1), 256 / kUpsertTile);
-  return static_cast<int>(
-      std::min<uint64_t>(blocks, sm_count_ * uint64_t{HKV_UPSERT_BLOCKS_PER_SM}));
+  const uint64_t per_sm =
+      mode == kModeInsertAndEvict ? HKV_EVICT_MIN_BLOCKS : HKV_UPSERT_BLOCKS_PER_SM;
+  return static_cast<int>(std::min<uint64_t>(blocks, sm_count_ * per_sm));
 }
 
 int TableImpl::warp_grid(size_t nwarps) const {
@@ -471,7 +479,7 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
     a.n = n;
     a.dn = dn;
     const int vw = value_width({rows, ev_values});
-    const int grid = upsert_grid(n);
+    const int grid = upsert_grid(n, mode);
     DISPATCH_STRATEGY(st, DISPATCH_VW(vw, {
       if (mode == kModeInsertOrAssign)
         LAUNCH_UPSERT(kModeInsertOrAssign, VW, grid, s, v, a);
@@ -534,7 +542,7 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
   CUDA_TRY(cudaMemsetAsync(ustatus, kIllegal, n, s));
   const int vwr = value_width({rows});
   const int vw = value_width({rows, ev_values});
-  const int grid = upsert_grid(n);
+  const int grid = upsert_grid(n, mode);
   DISPATCH_STRATEGY(st, DISPATCH_VW(vw, {
     if (mode == kModeInsertOrAssign)
       LAUNCH_UPSERT(kModeInsertOrAssign, VW, grid, s, v, a);
@@ -685,8 +693,11 @@ void TableImpl::accum_or_assign(size_t n, const uint64_t* keys,
   if (keys == nullptr || values == nullptr || accum == nullptr) return;
   const int st = ignore ? kCustomized : strategy_;
   const TableView v = view();
-  AccumArgs a{keys, values, accum, scores, n, epoch_, nullptr};
-  const int grid = warp_grid(n);
+  AccumArgs a{keys, values, accum, scores, n, epoch_, nullptr,
+              value_type_ == HKV_VALUE_F32 && value_width({values}) == 16 ? 1u : 0u};
+  const uint64_t blocks = ceil_div(std::max<size_t>(n, 1), 256 / kAccumTile);
+  const int grid = static_cast<int>(
+      std::min<uint64_t>(blocks, sm_count_ * uint64_t{HKV_ACCUM_MIN_BLOCKS}));
   DISPATCH_STRATEGY(st, {
     if (value_type_ == HKV_VALUE_F32)
       accum_kernel<S, float><<<grid, 256, 0, counted(s)>>>(v, a);
@@ -704,8 +715,8 @@ void TableImpl::assign_scores(size_t n, const uint64_t* keys,
   check_strategy(scores, false);
   const TableView v = view();
   DISPATCH_STRATEGY(strategy_, {
-    existing_key_kernel<S, false><<<tile_grid(n), 256, 0, counted(s)>>>(v, keys, scores,
-                                                               n, epoch_);
+    existing_key_kernel<S, false><<<existing_grid(n), 256, 0, counted(s)>>>(v, keys, scores,
+                                                                   n, epoch_);
   });
   CUDA_TRY(cudaGetLastError());
 }
@@ -825,8 +836,8 @@ void TableImpl::contains(size_t n, const uint64_t* keys, bool* founds,
 
 void TableImpl::erase(size_t n, const uint64_t* keys, cudaStream_t s) {
   if (n == 0 || keys == nullptr) return;
-  existing_key_kernel<kLru, true><<<tile_grid(n), 256, 0, counted(s)>>>(view(), keys,
-                                                               nullptr, n, 0);
+  existing_key_kernel<kLru, true><<<existing_grid(n), 256, 0, counted(s)>>>(view(), keys,
+                                                                   nullptr, n, 0);
   CUDA_TRY(cudaGetLastError());
 }
 

@@ -211,8 +211,9 @@ class TableImpl {
 
   // grid size for kernels that use one 8-lane tile per key
   int tile_grid(size_t n) const;
+  int existing_grid(size_t n) const;
   int find_grid(size_t n) const;
-  int upsert_grid(size_t n) const;
+  int upsert_grid(size_t n, int mode = -1) const;
   int warp_grid(size_t nwarps) const;
 
   // find_or_insert for batches that may repeat keys, with every scratch

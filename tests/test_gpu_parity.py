@@ -191,9 +191,12 @@ def test_find_or_insert_exact(name):
     assert_same_state(g, o)
 
 
-def test_insert_and_evict_matches_oracle():
+# dim 8 rows fit the registers of a 4-lane tile and are written out after the
+# rounds; dim 64 rows are copied out while the victim's slot is held
+@pytest.mark.parametrize("dim", [8, 64])
+def test_insert_and_evict_matches_oracle(dim):
     rng = np.random.default_rng(51)
-    cap, dim = 128 * 32, 8
+    cap = 128 * 32
     g = GpuOps(make_table(cap, dim=dim), dim)
     pre = random_keys(rng, cap)
     g.insert_or_assign(pre, rng.random((cap, dim)).astype(np.float32),
@@ -212,12 +215,13 @@ def test_insert_and_evict_matches_oracle():
     assert_same_state(g, o)
 
 
-def test_insert_and_evict_every_key_accounted_lru():
+@pytest.mark.parametrize("dim", [4, 32, 64])
+def test_insert_and_evict_every_key_accounted_lru(dim):
     """tests/test_reserve.cpp:320-420 pattern under contention (LRU, LF -> 1):
     every inserted key is in the table with its value or was reported
     evicted with its value; size matches."""
     rng = np.random.default_rng(61)
-    cap, dim, batch = 128 * 256, 4, 8192
+    cap, batch = 128 * 256, 8192
     g = GpuOps(make_table(cap, dim=dim, strategy=H.EvictStrategy.kLru), dim)
     live = {}
     for step in range(12):
@@ -235,12 +239,15 @@ def test_insert_and_evict_every_key_accounted_lru():
     g.t.check_device_error()
 
 
-def test_accum_or_assign_exact():
+# dim 8 and 64: rows added four floats per 16-byte access; dim 5: one float
+# at a time. Random float rows: the sums must match the oracle's bit for bit.
+@pytest.mark.parametrize("dim", [8, 5, 64])
+def test_accum_or_assign_exact(dim):
     rng = np.random.default_rng(71)
-    cap, dim = 128 * 32, 8
+    cap = 128 * 32
     g = GpuOps(make_table(cap, dim=dim), dim)
     pre = random_keys(rng, cap // 2)
-    g.insert_or_assign(pre, rng.integers(0, 9, (len(pre), dim)).astype(np.float32),
+    g.insert_or_assign(pre, rng.standard_normal((len(pre), dim)).astype(np.float32),
                        rng.integers(1, 1 << 30, len(pre)).astype(np.uint64))
     o = oracle_from_gpu(g, cap, dim, O.CUSTOMIZED)
     nb = cap // 128
@@ -249,7 +256,7 @@ def test_accum_or_assign_exact():
                     np.uint64)
     fresh = one_key_per_bucket(rng, cap, np.arange(1, nb, 2))
     keys = np.concatenate([hits, fresh, hits[:5], fresh[:5]])
-    vals = rng.integers(0, 9, (len(keys), dim)).astype(np.float32)
+    vals = rng.standard_normal((len(keys), dim)).astype(np.float32)
     acc = np.concatenate([np.ones(len(hits)), np.zeros(len(fresh)),
                           np.zeros(5), np.ones(5)]).astype(np.uint8)
     # the trailing mismatched entries (assign on existing / accum on new)
