@@ -781,56 +781,13 @@ __global__ void __launch_bounds__(256, Mode == kModeInsertAndEvict ? HKV_EVICT_M
                            (uint64_t)gridDim.x * (blockDim.x / 32));
 }
 
-// Finds the slot holding `key` with plain loads (the reference's find rule
-// when kStopRule: a digest-empty EMPTY_KEY slot earlier in the walk hides
-// it). Returns the slot, -1 if absent, -2 if a locked digest-hit slot may
-// hold the key (the caller retries).
-template <bool kStopRule>
-__device__ __forceinline__ int tile_locate_existing(const TableView& t,
-                                                    const Tile& tile,
-                                                    const Locate& l,
-                                                    uint64_t key) {
-  const uint64_t* bk = t.keys + l.bkt * kBucket;
-  const uint4 dv = __ldcg(
-      reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) + tile.lane);
-  // a full bucket holds no EMPTY_KEY slot: the stop rule cannot apply
-  const bool full = kStopRule && (__ldcg(t.sizes + l.bkt) & kSizeMask) >= int32_t{kBucket};
-  const uint32_t lo = tile.lane * kDigestsPerLane;
-  uint32_t hits = bytes_eq16(dv, l.d4);
-  int mine = -1;
-  bool busy = false;
-  while (hits) {
-    const uint32_t j = __ffs(hits) - 1;
-    hits &= hits - 1;
-    const uint64_t k = ld_relaxed_u64(bk + lo + j);
-    if (k == key) {
-      mine = static_cast<int>(lo + j);
-      break;
-    }
-    busy |= (k == kLockedKey);
-  }
-  const uint32_t fm = tile.ballot(mine >= 0);
-  if (!fm) return tile.ballot(busy) ? -2 : -1;
-  const uint32_t p = tile.shfl(static_cast<uint32_t>(mine), __ffs(fm) - 1);
-  if constexpr (kStopRule) {
-    uint32_t empt = full ? 0u : bytes_eq16(dv, kEmptyDigest * 0x01010101u);
-    const uint32_t pr = hit_rank(p, l.pos);
-    bool stop = false;
-    while (empt) {
-      const uint32_t j = __ffs(empt) - 1;
-      empt &= empt - 1;
-      const uint32_t q = lo + j;
-      if (empty_rank(q, l.pos) < pr && ld_relaxed_u64(bk + q) == kEmptyKey)
-        stop = true;
-    }
-    if (tile.ballot(stop)) return -1;
-  }
-  return static_cast<int>(p);
-}
-
-// tile_locate_existing for a tile of W lanes (kBucket / W digests per lane).
+// A tile of W lanes (kBucket / W digests per lane) finds the slot holding
+// `key` with plain loads (the reference's find rule when kStopRule: a
+// digest-empty EMPTY_KEY slot earlier in the walk hides it). Returns the
+// slot, -1 if absent, -2 if a locked digest-hit slot may hold the key (the
+// caller retries).
 template <bool kStopRule, uint32_t W>
-__device__ __forceinline__ int tile_locate_existing_w(const TableView& t,
+__device__ __forceinline__ int tile_locate_existing(const TableView& t,
                                                       const TileW<W>& tile,
                                                       const Locate& l, uint64_t key) {
   constexpr uint32_t kD = TileW<W>::kDigests;
@@ -1114,7 +1071,7 @@ __global__ void __launch_bounds__(256, HKV_ACCUM_MIN_BLOCKS)
       desired = desired_when_missed<S>(a.scores, i, a.epoch, clk);
       is_accum = a.accum_or_assigns[i];
       l = locate(t, key);
-      const int p = tile_locate_existing_w<false>(t, tile, l, key);
+      const int p = tile_locate_existing<false>(t, tile, l, key);
       bool got = false;
       if (p >= 0 && tile.lane == 0)
         got = cas_acquire_u64(t.keys + l.bkt * kBucket + p, key, kLockedKey) == key;
@@ -1198,7 +1155,7 @@ __global__ void __launch_bounds__(256, 8)
     for (int round = 0;; round++) {
       bool again = false;
       if (todo) {
-        const int p = tile_locate_existing_w<!kErase>(t, tile, l, key);
+        const int p = tile_locate_existing<!kErase>(t, tile, l, key);
         bool got = false;
         const uint64_t s = l.bkt * kBucket + (p < 0 ? 0 : p);
         if (p >= 0 && tile.lane == 0)
@@ -1241,20 +1198,22 @@ __global__ void __launch_bounds__(256, 8)
 // caller-lock word; its key-word address goes to locked_key_ptrs[i]. Absent
 // keys get nullptr and false.
 template <int S>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 8)
     lock_keys_kernel(TableView t, const uint64_t* __restrict__ keys,
                      uint64_t** __restrict__ locked_key_ptrs, bool* __restrict__ succeeded,
                      const uint64_t* __restrict__ scores, uint64_t n, uint64_t epoch) {
+  constexpr uint32_t W = kExistTile;
+  constexpr uint32_t KPW = 32 / W;  // keys per warp
   __shared__ uint64_t s_clock;
   if (threadIdx.x == 0) s_clock = global_timer_ns();
   __syncthreads();
   const uint64_t clk = s_clock;
-  const Tile tile;
+  const TileW<W> tile;
   const uint32_t wl = threadIdx.x & 31;
   const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x / 32);
   const uint64_t warp = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / 32;
-  for (uint64_t base = warp * 4; base < n; base += nwarps * 4) {
-    const uint64_t i = base + (wl >> 3);
+  for (uint64_t base = warp * KPW; base < n; base += nwarps * KPW) {
+    const uint64_t i = base + wl / W;
     uint64_t key = 0, t0 = 0;
     bool todo = false, ok = false;
     uint64_t* addr = nullptr;

@@ -772,7 +772,7 @@ void TableImpl::lock_keys(size_t n, const uint64_t* keys, uint64_t** locked_key_
   maybe_locked_ = true;
   const TableView v = view();
   DISPATCH_STRATEGY(strategy_, {
-    lock_keys_kernel<S><<<tile_grid(n), 256, 0, counted(s)>>>(v, keys, locked_key_ptrs,
+    lock_keys_kernel<S><<<existing_grid(n), 256, 0, counted(s)>>>(v, keys, locked_key_ptrs,
                                                               succeeded, scores, n, epoch_);
   });
   CUDA_TRY(cudaGetLastError());
