@@ -14,10 +14,11 @@ accum_or_assign_kernel.h / remove_kernel.h walks) are compared with the
 oracle on that state."""
 import numpy as np
 import pytest
+import torch
 
 import hkv_b200 as H
 import hkv_oracle as O
-from hkv_gpu import GpuOps, make_table
+from hkv_gpu import GpuOps, dev, host, make_table
 from hkv_testutil import keys_for_bucket, murmur3_np
 
 pytestmark = pytest.mark.gpu
@@ -85,6 +86,14 @@ def test_lookups_stop_at_a_planted_empty_slot():
     np.testing.assert_array_equal(gv[gf], ov[of])
     np.testing.assert_array_equal(gs[gf], os_[of])
     np.testing.assert_array_equal(g.contains(rest), of)
+    # find* (reference find_ptr_with_digest_kernel.h) walks the same way
+    n = len(rest)
+    ptrs = torch.zeros(n, dtype=torch.int64, device="cuda")
+    pf = torch.zeros(n, dtype=torch.bool, device="cuda")
+    g.t.find_ptr(n, dev(rest), ptrs, pf)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(host(pf).astype(bool), of)
+    assert ((host(ptrs) != 0) == of).all()
 
 
 def test_assign_scores_applies_the_stop_rule():
@@ -107,9 +116,12 @@ def test_accum_and_erase_walk_the_whole_bucket():
     delta = rng.standard_normal((len(rest), dim)).astype(np.float32)
     acc = np.ones(len(rest), bool)
     sc = rng.integers(1, 1 << 30, len(rest)).astype(np.uint64)
+    before = g.t.get_state()
     g.accum_or_assign(rest, delta, acc, sc)
     o.accum_or_assign(rest, delta, acc.astype(np.uint8), sc)
     same_state(g, o)
+    slot = int(np.nonzero(before[0] == hidden)[0][0])
+    assert (g.t.get_state()[4][slot] != before[4][slot]).any()  # walked past the empty slot
     g.erase(rest[::2])
     o.erase(rest[::2])
     same_state(g, o)
