@@ -288,11 +288,17 @@ int TableImpl::tile_grid(size_t n) const {
   return static_cast<int>(std::min<uint64_t>(blocks, sm_count_ * 64ull));
 }
 
-// assign_scores / erase blocks: 256 / kExistTile keys per block pass, at most
-// the 8 blocks per SM that stay resident
+// assign_scores / erase / lock_keys blocks: 256 / kExistTile keys per block
+// pass, at most HKV_EXIST_BLOCKS_PER_SM blocks per SM. 8 stay resident; a
+// grid of many short blocks measured faster than one resident wave
+// (assign_scores 148 -> 129 us, erase 166 -> 156 us per 1 Mi keys)
+#ifndef HKV_EXIST_BLOCKS_PER_SM
+#define HKV_EXIST_BLOCKS_PER_SM 64
+#endif
 int TableImpl::existing_grid(size_t n) const {
   const uint64_t blocks = ceil_div(std::max<size_t>(n, 1), 256 / kExistTile);
-  return static_cast<int>(std::min<uint64_t>(blocks, sm_count_ * 8ull));
+  return static_cast<int>(
+      std::min<uint64_t>(blocks, sm_count_ * uint64_t{HKV_EXIST_BLOCKS_PER_SM}));
 }
 
 // Find blocks; each tile walks its keys with the next key loaded ahead.
@@ -304,10 +310,16 @@ int TableImpl::find_grid(size_t n) const {
 #ifndef HKV_UPSERT_BLOCKS_PER_SM
 #define HKV_UPSERT_BLOCKS_PER_SM HKV_UPSERT_MIN_BLOCKS
 #endif
+// insert_and_evict: many short blocks measured faster than one resident wave
+// (727 -> 652 us per 1 Mi keys); insert_or_assign / find_or_insert measured
+// the other way (359 -> 366, 378 -> 384 us) and keep the resident grid
+#ifndef HKV_EVICT_BLOCKS_PER_SM
+#define HKV_EVICT_BLOCKS_PER_SM 64
+#endif
 int TableImpl::upsert_grid(size_t n, int mode) const {
   const uint64_t blocks = ceil_div(std::max<size_t>(n, 1), 256 / kUpsertTile);
   const uint64_t per_sm =
-      mode == kModeInsertAndEvict ? HKV_EVICT_MIN_BLOCKS : HKV_UPSERT_BLOCKS_PER_SM;
+      mode == kModeInsertAndEvict ? HKV_EVICT_BLOCKS_PER_SM : HKV_UPSERT_BLOCKS_PER_SM;
   return static_cast<int>(std::min<uint64_t>(blocks, sm_count_ * per_sm));
 }
 
@@ -697,7 +709,7 @@ void TableImpl::accum_or_assign(size_t n, const uint64_t* keys,
               value_type_ == HKV_VALUE_F32 && value_width({values}) == 16 ? 1u : 0u};
   const uint64_t blocks = ceil_div(std::max<size_t>(n, 1), 256 / kAccumTile);
   const int grid = static_cast<int>(
-      std::min<uint64_t>(blocks, sm_count_ * uint64_t{HKV_ACCUM_MIN_BLOCKS}));
+      std::min<uint64_t>(blocks, sm_count_ * uint64_t{HKV_ACCUM_BLOCKS_PER_SM}));
   DISPATCH_STRATEGY(st, {
     if (value_type_ == HKV_VALUE_F32)
       accum_kernel<S, float><<<grid, 256, 0, counted(s)>>>(v, a);
