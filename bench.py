@@ -7,8 +7,10 @@ table filled to load factor 1.0. One step = find of 1 Mi keys (100% hits)
 the least recently used). value = keys of all steps on all GPUs / time.
 
 N = 1 runs the table directly. N > 1 runs the sharded table: every rank
-submits its own batches; keys travel to their owner GPU and results come
-back over NCCL all-to-all (weak scaling: per-GPU table and batch fixed).
+submits its own batches; keys and rows travel to their owner GPU and results
+come back over NVLink, by plain peer loads of the other ranks' memory in this
+library's own kernels (the peer transport), or by NCCL send/recv where peer
+mappings are unavailable (weak scaling: per-GPU table and batch fixed).
 
 `--impl reference` times the reference's algorithm on the host CPU instead
 (the reference needs an Ascend NPU and CANN, neither exists here, so its CPU
@@ -39,7 +41,9 @@ CAPACITY = 64 << 20          # slots per GPU
 BATCH = 1 << 20              # keys per call
 PREFILL_FACTOR = 1.6         # inserted keys / capacity to reach LF 1.0 under LRU
 HOT = 4 << 20                # most recent prefill keys, source of hits
-# algorithmic bytes per key (SURVEY 8d model, 128-byte digest line per bucket)
+# algorithmic bytes per key: the key, one 128-byte digest line per bucket
+# probe, the 8-byte key compare, the value row read and written, and for an
+# evicting insert the 1 KiB score scan
 FIND_HIT_BYTES = 145 + 2 * VALUE_BYTES                 # 401
 INSERT_HIT_BYTES = 160 + 2 * VALUE_BYTES               # 416
 INSERT_EVICT_BYTES = 1185 + 2 * VALUE_BYTES            # 1441

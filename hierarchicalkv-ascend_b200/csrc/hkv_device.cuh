@@ -338,6 +338,29 @@ __device__ __forceinline__ uint32_t linear_rank(uint32_t p, uint32_t pos) {
   return (p - pos) & (kBucket - 1);
 }
 
+// Bits j of the kD slots [lo, lo + kD) held by one lane whose slot lo + j
+// has linear rank from pos below L (0 <= L <= kBucket). The ranks of the
+// window rise by one per slot and wrap to 0 once, after w = kBucket - a
+// slots, a being the rank of slot lo.
+template <class M, uint32_t kD>
+__device__ __forceinline__ M linear_below(uint32_t lo, uint32_t pos, uint32_t L) {
+  auto low = [](uint32_t c) -> uint64_t { return c >= 64 ? ~0ull : ((1ull << c) - 1); };
+  const uint32_t a = (lo - pos) & (kBucket - 1);
+  const uint32_t w = kBucket - a;
+  const uint32_t c1 = L > a ? min(L - a, w) : 0u;
+  const uint64_t m = low(c1) | (low(min(w + L, kD)) & ~low(w));
+  return static_cast<M>(m & low(kD));
+}
+
+// Linear rank bound of the empty slots the group walk reaches before a digest
+// hit at p: the slots from pos up to p's group, none when p is in the start
+// group (hits of a group come before its empties, find_utils.h:40-84 and
+// insert_or_assign_kernel.h:105-183). empty_rank(q) < hit_rank(p) exactly
+// when q's linear rank is below this bound.
+__device__ __forceinline__ uint32_t walk_bound(uint32_t p, uint32_t pos) {
+  return group_index(p, pos) == 0 ? 0u : linear_rank(p & ~3u, pos);
+}
+
 // ---- score rules (reference score_functor.h) --------------------------------
 __device__ __forceinline__ uint64_t make_epoch(uint64_t e) { return e << 32; }
 __device__ __forceinline__ uint64_t make_nano(uint64_t c) {

@@ -160,13 +160,11 @@ __device__ __forceinline__ int find_probe(const TableView& t, const TileW<W>& ti
   if (best == 0xFFFFFFFFu) return -1;
   // an empty slot holding EMPTY_KEY ranked before the hit ends the walk
   // (find_utils.h:58-66)
-  const uint32_t prank = best >> 8;
+  const uint32_t p = best & 0xFF;
   bool stop = false;
-  for (M e = empt; e; e &= e - 1) {
-    const uint32_t q = lo + low_bit(e);
-    if (empty_rank(q, l.pos) < prank && __ldg(bk + q) == kEmptyKey) stop = true;
-  }
-  return tile.ballot(stop) ? -1 : static_cast<int>(best & 0xFF);
+  for (M e = empt & linear_below<M, kD>(lo, l.pos, walk_bound(p, l.pos)); e; e &= e - 1)
+    if (__ldg(bk + lo + low_bit(e)) == kEmptyKey) stop = true;
+  return tile.ballot(stop) ? -1 : static_cast<int>(p);
 }
 
 // Writes one find result at position o: flag, and for a hit the score and
@@ -534,38 +532,70 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const TileW<W>& 
   }
   const int32_t bword = __ldcg(t.sizes + l.bkt);  // size, caller locks above it
   // ---- 1. is the key here? (a digest hit that holds it is locked at once)
+  // Each lane locks its first digest hit holding the key in walk order (its
+  // slots from the start group on, then those before it), and the tile keeps
+  // the first in walk order: a key has one slot, except on layouts where a
+  // second copy was placed in front of it.
   int mine = -1;
   bool busy = false;
-  while (hits) {
-    const uint32_t j = low_bit(hits);
-    hits &= hits - 1;
-    const uint64_t k = cas_acquire_u64(bk + lo + j, key, kLockedKey);
-    if (k == key) {
-      mine = static_cast<int>(lo + j);
-      break;
+  auto try_hits = [&](M h) {
+    while (h && mine < 0) {
+      const uint32_t j = low_bit(h);
+      h &= h - 1;
+      const uint64_t k = cas_acquire_u64(bk + lo + j, key, kLockedKey);
+      if (k == key) mine = static_cast<int>(lo + j);
+      // an operation in flight may hold the key: retry. A caller's lock says
+      // nothing about which key it hides (a digest hit may belong to another
+      // key): like the reference, which compares the word with the key
+      // itself (insert_or_assign_kernel.h:128-140), such a slot is not it.
+      busy |= (k == kLockedKey);
     }
-    // an operation in flight may hold the key: retry. A caller's lock says
-    // nothing about which key it hides (a digest hit may belong to another
-    // key): like the reference, which compares the word with the key itself
-    // (insert_or_assign_kernel.h:128-140), such a slot is not the key.
-    busy |= (k == kLockedKey);
+  };
+  {
+    const uint32_t g0 = l.pos & ~3u;
+    const M from_g0 = ~static_cast<M>(0) << ((g0 >= lo && g0 < lo + kD) ? g0 - lo : 0);
+    try_hits(hits & from_g0);
+    try_hits(hits & ~from_g0);
   }
   int res = kRetry;
   bool got = false;
   uint32_t slot = 0;
   uint64_t vkey = 0, vscore = 0;
-  const uint32_t fm = tile.ballot(mine >= 0);
-  if (fm) {
-    const int src = __ffs(fm) - 1;
-    // a key lives in one slot; release any other lock defensively
-    if (mine >= 0 && static_cast<int>(tile.lane) != src)
-      store_release_u64(bk + mine, key);
-    slot = tile.shfl(static_cast<uint32_t>(mine), src);
-    got = true;
-    res = kDuplicate;
-  } else if (!tile.ballot(busy)) {
-    // ---- 2. first EMPTY slot in linear order from pos
-    if ((bword & kSizeMask) < static_cast<int32_t>(kBucket)) {
+  const bool not_full = (bword & kSizeMask) < static_cast<int32_t>(kBucket);
+  uint32_t first = mine >= 0 ? (hit_rank(mine, l.pos) << 8) | static_cast<uint32_t>(mine)
+                             : 0xFFFFFFFFu;
+#pragma unroll
+  for (int o = W / 2; o > 0; o >>= 1) first = min(first, tile.shfl_xor(first, o));
+  // the key is in the bucket, but the reference's group walk reaches an
+  // EMPTY slot first: it claims that slot instead
+  bool to_empty = false;
+  if (first != 0xFFFFFFFFu) {
+    slot = first & 0xFF;
+    const bool holder = mine == static_cast<int>(slot);
+    if (mine >= 0 && !holder) store_release_u64(bk + mine, key);
+    // The walk (insert_or_assign_kernel.h:105-183) examines a group's digest
+    // hits, then, below a full bucket, that group's EMPTY slots, group by
+    // group from pos: an EMPTY slot in a group before the key's takes the
+    // key (a second copy). Only a layout with a slot emptied in front of a
+    // placed key has one; the candidates are empty digests, rarely any.
+    bool before = false;
+    if (not_full) {
+      empt &= linear_below<M, kD>(lo, l.pos, walk_bound(slot, l.pos));
+      for (M e = empt; e; e &= e - 1)
+        if (ld_relaxed_u64(bk + lo + low_bit(e)) == kEmptyKey) before = true;
+    }
+    if (tile.ballot(before)) {
+      if (holder) store_release_u64(bk + slot, key);
+      to_empty = true;
+    } else {
+      got = true;
+      res = kDuplicate;
+    }
+  }
+  if (!got && (to_empty || !tile.ballot(busy))) {
+    // ---- 2. first EMPTY slot in linear order from pos (with to_empty, only
+    // those ahead of the key's group)
+    if (not_full) {
       const uint32_t sh = (l.pos >= lo && l.pos < lo + kD) ? l.pos - lo : 0;
       while (true) {
         uint32_t best = 0xFFFFFFFFu;
@@ -592,8 +622,9 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const TileW<W>& 
         }
       }
     }
-    // ---- 3. evict the minimum score
-    if (!got) {
+    // ---- 3. evict the minimum score (a key in the bucket whose EMPTY slots
+    // ahead were all taken meanwhile is retried: the walk then hits it)
+    if (!got && !to_empty) {
       uint64_t ms;
       uint32_t mp;
       // kernels launched while the caller may hold locks pass them by; the
@@ -786,12 +817,26 @@ __global__ void __launch_bounds__(256, Mode == kModeInsertAndEvict ? HKV_EVICT_M
                            (uint64_t)gridDim.x * (blockDim.x / 32));
 }
 
+// How a lookup of existing keys walks a bucket in the reference:
+//  kWalk      groups of 4 digests from the start group, first digest hit
+//             holding the key (lock_keys_kernel.h:78-124);
+//  kWalkStop  the same with find_without_lock's stop rule: an EMPTY_KEY slot
+//             with an empty digest reached before the key hides it
+//             (find_utils.h:31-86; assign_scores);
+//  kWindow    find_and_lock's 32-slot windows from pos (find_utils.h:94-147;
+//             accum_or_assign): the first slot holding the key in linear
+//             order, unless an earlier window holds an EMPTY_KEY slot, which
+//             find_and_lock would claim first.
+enum LocateRule : int { kWalk = 0, kWalkStop = 1, kWindow = 2 };
+
 // A tile of W lanes (kBucket / W digests per lane) finds the slot holding
-// `key` with plain loads (the reference's find rule when kStopRule: a
-// digest-empty EMPTY_KEY slot earlier in the walk hides it). Returns the
-// slot, -1 if absent, -2 if a locked digest-hit slot may hold the key (the
-// caller retries).
-template <bool kStopRule, uint32_t W>
+// `key` with plain loads, the first in the rule's order when a layout holds
+// two copies. Returns the slot, -1 if absent (or hidden by the stop rule),
+// -2 if a locked digest-hit slot may hold the key (the caller retries), and
+// for kWindow -3 when an EMPTY_KEY slot comes first (the caller takes
+// find_and_lock's full path). EMPTY_KEY slots are found through their empty
+// digests, which every slot this library empties carries.
+template <int Rule, uint32_t W>
 __device__ __forceinline__ int tile_locate_existing(const TableView& t,
                                                       const TileW<W>& tile,
                                                       const Locate& l, uint64_t key) {
@@ -800,44 +845,95 @@ __device__ __forceinline__ int tile_locate_existing(const TableView& t,
   using M = typename std::conditional<(kD > 32), uint64_t, uint32_t>::type;
   const uint64_t* bk = t.keys + l.bkt * kBucket;
   const uint4* dl = reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) + tile.lane * kDV;
-  // a full bucket holds no EMPTY_KEY slot: the stop rule cannot apply
-  const bool full = kStopRule && (__ldcg(t.sizes + l.bkt) & kSizeMask) >= int32_t{kBucket};
+  // a full bucket holds no EMPTY_KEY slot: no empty slot can come first
+  const bool full =
+      Rule != kWalk && (__ldcg(t.sizes + l.bkt) & kSizeMask) >= int32_t{kBucket};
   const uint32_t lo = tile.lane * kD;
   M hits = 0, empt = 0;
 #pragma unroll
   for (uint32_t j = 0; j < kDV; j++) {
     const uint4 dv = __ldcg(dl + j);
     hits |= static_cast<M>(bytes_eq16(dv, l.d4)) << (16 * j);
-    if (kStopRule)
+    if (Rule != kWalk)
       empt |= static_cast<M>(bytes_eq16(dv, kEmptyDigest * 0x01010101u)) << (16 * j);
   }
-  int mine = -1;
+  uint32_t best = 0xFFFFFFFFu;
   bool busy = false;
-  while (hits) {
-    const uint32_t j = low_bit(hits);
-    hits &= hits - 1;
-    const uint64_t k = ld_relaxed_u64(bk + lo + j);
+  for (M h = hits; h; h &= h - 1) {
+    const uint32_t q = lo + low_bit(h);
+    const uint64_t k = ld_relaxed_u64(bk + q);
     if (k == key) {
-      mine = static_cast<int>(lo + j);
-      break;
+      const uint32_t r = Rule == kWindow ? linear_rank(q, l.pos) : hit_rank(q, l.pos);
+      best = min(best, (r << 8) | q);
     }
     busy |= (k == kLockedKey);
   }
-  const uint32_t fm = tile.ballot(mine >= 0);
-  if (!fm) return tile.ballot(busy) ? -2 : -1;
-  const uint32_t p = tile.shfl(static_cast<uint32_t>(mine), __ffs(fm) - 1);
-  if constexpr (kStopRule) {
-    if (full) empt = 0;
-    const uint32_t pr = hit_rank(p, l.pos);
-    bool stop = false;
-    while (empt) {
-      const uint32_t q = lo + low_bit(empt);
-      empt &= empt - 1;
-      if (empty_rank(q, l.pos) < pr && ld_relaxed_u64(bk + q) == kEmptyKey) stop = true;
+#pragma unroll
+  for (int o = W / 2; o > 0; o >>= 1) best = min(best, tile.shfl_xor(best, o));
+  if (best == 0xFFFFFFFFu) return tile.ballot(busy) ? -2 : -1;
+  const uint32_t p = best & 0xFF;
+  if constexpr (Rule != kWalk) {
+    bool first = false;
+    if (!full) {
+      const uint32_t bound = Rule == kWindow ? linear_rank(p, l.pos) & ~31u : walk_bound(p, l.pos);
+      for (M e = empt & linear_below<M, kD>(lo, l.pos, bound); e; e &= e - 1)
+        if (ld_relaxed_u64(bk + lo + low_bit(e)) == kEmptyKey) first = true;
     }
-    if (tile.ballot(stop)) return -1;
+    if (tile.ballot(first)) return Rule == kWindow ? -3 : -1;
   }
   return static_cast<int>(p);
+}
+
+// erase (remove_kernel.h:79-110) visits the groups from the start group and
+// tombstones the first digest hit holding the key in each, visiting the
+// start group twice (offsets 0 and B): normally the key's one slot, on
+// layouts with two copies every copy it reaches. Each lane erases its own
+// slots; returns false when no slot held the key but a digest-hit slot was
+// locked (the caller retries).
+template <uint32_t W>
+__device__ __forceinline__ bool tile_erase(const TableView& t, const TileW<W>& tile,
+                                           const Locate& l, uint64_t key) {
+  constexpr uint32_t kD = TileW<W>::kDigests;
+  constexpr uint32_t kDV = kD / 16;
+  using M = typename std::conditional<(kD > 32), uint64_t, uint32_t>::type;
+  constexpr M kNib1 = static_cast<M>(0xEEEEEEEEEEEEEEEEull);  // bits 1-3 of each group
+  constexpr M kNib2 = static_cast<M>(0xCCCCCCCCCCCCCCCCull);  // bits 2-3 of each group
+  uint64_t* bk = t.keys + l.bkt * kBucket;
+  const uint4* dl = reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) + tile.lane * kDV;
+  const uint32_t lo = tile.lane * kD;
+  M hits = 0;
+#pragma unroll
+  for (uint32_t j = 0; j < kDV; j++)
+    hits |= static_cast<M>(bytes_eq16(__ldcg(dl + j), l.d4)) << (16 * j);
+  M held = 0;
+  bool busy = false;
+  for (M h = hits; h; h &= h - 1) {
+    const uint32_t j = low_bit(h);
+    const uint64_t k = ld_relaxed_u64(bk + lo + j);
+    if (k == key) held |= static_cast<M>(1) << j;
+    busy |= (k == kLockedKey);
+  }
+  // first holder of each group of 4 (groups start at multiples of 4 slots)
+  M upto = held;
+  upto |= (upto << 1) & kNib1;
+  upto |= (upto << 2) & kNib2;
+  M erase = held & ~((upto << 1) & kNib1);
+  const uint32_t g0 = l.pos & ~3u;
+  if (g0 >= lo && g0 < lo + kD) {
+    // the second visit of the start group takes its next holder
+    const M rest = held & ~erase & (static_cast<M>(0xF) << (g0 - lo));
+    erase |= rest & (~rest + 1);
+  }
+  for (M e = erase; e; e &= e - 1) {
+    const uint64_t s = l.bkt * kBucket + lo + low_bit(e);
+    if (cas_acquire_u64(t.keys + s, key, kLockedKey) == key) {
+      t.scores[s] = 0;
+      t.digests[s] = kReclaimDigest;
+      atomicSub(t.sizes + l.bkt, 1);
+      store_release_u64(t.keys + s, kReclaimKey);
+    }
+  }
+  return tile.ballot(held != 0) || !tile.ballot(busy);
 }
 
 // ============================================================================
@@ -1076,7 +1172,7 @@ __global__ void __launch_bounds__(256, HKV_ACCUM_MIN_BLOCKS)
       desired = desired_when_missed<S>(a.scores, i, a.epoch, clk);
       is_accum = a.accum_or_assigns[i];
       l = locate(t, key);
-      const int p = tile_locate_existing<false>(t, tile, l, key);
+      const int p = tile_locate_existing<kWindow>(t, tile, l, key);
       bool got = false;
       if (p >= 0 && tile.lane == 0)
         got = cas_acquire_u64(t.keys + l.bkt * kBucket + p, key, kLockedKey) == key;
@@ -1159,28 +1255,30 @@ __global__ void __launch_bounds__(256, 8)
     }
     for (int round = 0;; round++) {
       bool again = false;
-      if (todo) {
-        const int p = tile_locate_existing<!kErase>(t, tile, l, key);
+      if constexpr (kErase) {
+        if (todo) {
+          if (tile_erase(t, tile, l, key))
+            todo = false;
+          else if (retry_expired(t, tile, t0, 202))
+            todo = false;
+          else
+            again = true;
+        }
+      } else if (todo) {
+        const int p = tile_locate_existing<kWalkStop>(t, tile, l, key);
         bool got = false;
         const uint64_t s = l.bkt * kBucket + (p < 0 ? 0 : p);
         if (p >= 0 && tile.lane == 0)
           got = cas_acquire_u64(t.keys + s, key, kLockedKey) == key;
         if (tile.shfl(got, 0)) {
           if (tile.lane == 0) {
-            if constexpr (kErase) {
-              t.scores[s] = 0;
-              t.digests[s] = kReclaimDigest;
-              atomicSub(t.sizes + l.bkt, 1);
-              store_release_u64(t.keys + s, kReclaimKey);
-            } else {
-              uint64_t ns;
-              // only the Lfu rules read the stored score
-              const uint64_t old =
-                  (S == kLfu || S == kEpochLfu) ? ld_relaxed_u64(t.scores + s) : 0;
-              if (score_without_missed<S>(old, scores, i, epoch, clk, &ns))
-                t.scores[s] = ns;
-              store_release_u64(t.keys + s, key);
-            }
+            uint64_t ns;
+            // only the Lfu rules read the stored score
+            const uint64_t old =
+                (S == kLfu || S == kEpochLfu) ? ld_relaxed_u64(t.scores + s) : 0;
+            if (score_without_missed<S>(old, scores, i, epoch, clk, &ns))
+              t.scores[s] = ns;
+            store_release_u64(t.keys + s, key);
           }
           todo = false;
         } else if (p == -1) {
@@ -1236,7 +1334,7 @@ __global__ void __launch_bounds__(256, 8)
     for (int round = 0;; round++) {
       bool again = false;
       if (todo) {
-        const int p = tile_locate_existing<false>(t, tile, l, key);
+        const int p = tile_locate_existing<kWalk>(t, tile, l, key);
         bool got = false;
         const uint64_t s = l.bkt * kBucket + (p < 0 ? 0 : p);
         if (p >= 0 && tile.lane == 0)

@@ -1,6 +1,6 @@
 """CUDA table vs the CPU oracle on the same seeded inputs (GPU).
 
-Exactness rules (see DESIGN.md's parity section):
+Exactness rules:
 * find / contains / export: bit-exact (export as a set);
 * a batch whose keys touch distinct buckets: the whole raw table state
   (keys, scores, digests, bucket sizes, values) is bit-identical slot by slot

@@ -428,3 +428,180 @@ def test_multithreaded_oracle_equals_single_threaded():
     b.insert_or_assign(keys, vals, sc)
     for x, y in zip(a.get_state(), b.get_state()):
         assert (x == y).all()
+
+
+# ------------------------------------- erase, insert_or_assign, accum, assign
+def test_erase_in_full_bucket():
+    """tests/test_erase.cpp:73-150 (test_erase_in_full_bucket): one bucket
+    (capacity 128), Lru: keys 1..1024 in one call, then the last key again,
+    leave the bucket full with the last key in it; erasing it leaves 127;
+    inserting it again fills the bucket and changes no other key's
+    presence."""
+    t = O.OracleTable(128, 128, dim=8, strategy=O.LRU)
+    keys = np.arange(1, 1025, dtype=np.uint64)
+    vals = np.zeros((1024, 8), np.float32)
+    t.set_clock(100)
+    t.insert_or_assign(keys, vals)
+    t.set_clock(200)
+    t.insert_or_assign(keys[-1:], vals[:1])
+    assert t.size() == 128
+    before = t.contains(keys)
+    assert before[-1] and before.sum() == 128
+    t.erase(keys[-1:])
+    assert t.size() == 127
+    t.set_clock(300)
+    res = t.insert_or_assign(keys[-1:], vals[:1])
+    assert res[0] == O.R_OCCUPIED_RECLAIMED  # the tombstone (score 0) is the victim
+    assert t.size() == 128
+    assert (t.contains(keys) == before).all()
+
+
+def test_erase_then_insert_and_evict_reuses_tombstones():
+    """tests/test_erase.cpp:289-375 (test_erase_with_insert_and_evict): a full
+    one-bucket table (keys 1..128, Lru); erase 10 keys (size 118);
+    insert_and_evict of the same 10 keys reports nothing evicted (tombstones
+    are not reported), the size is back to 128 and the keys are found."""
+    t = O.OracleTable(128, 128, dim=8, strategy=O.LRU)
+    keys = np.arange(1, 129, dtype=np.uint64)
+    t.set_clock(10)
+    t.insert_or_assign(keys, np.zeros((128, 8), np.float32))
+    assert t.size() == 128
+    t.erase(keys[:10])
+    assert t.size() == 118
+    t.set_clock(20)
+    ek, _, _, _ = t.insert_and_evict(keys[:10], np.ones((10, 8), np.float32))
+    assert len(ek) == 0
+    assert t.size() == 128
+    assert t.contains(keys[:10]).all()
+
+
+def test_insert_or_assign_evict():
+    """tests/test_insert_or_assign.cpp:230-267 (test_evict): one bucket
+    (capacity 128), Lru, 1024 keys 0..1023 with values key*1e-5 in one call:
+    size 128, and every key found carries its own value."""
+    t = O.OracleTable(128, 128, dim=8, strategy=O.LRU)
+    keys = np.arange(0, 1024, dtype=np.uint64)
+    vals = (keys.astype(np.float64) * 1e-5).astype(np.float32)[:, None].repeat(8, 1)
+    t.set_clock(1)
+    t.insert_or_assign(keys, vals)
+    assert t.size() == 128
+    v, f, _ = t.find(keys)
+    assert f.sum() == 128
+    assert (v[f] == vals[f]).all()
+
+
+def test_insert_or_assign_repeated_keys():
+    """tests/test_insert_or_assign.cpp:454-560 (test_repeat_key_basic): keys
+    i // 10 for i < 1024 (103 distinct keys, 10 occurrences each, every
+    occurrence with its own value), unique_key = false: size 103, every key
+    found, its value one of its occurrences' values."""
+    dim, n, rep = 8, 1024, 10
+    t = O.OracleTable(128 * 1024, 128 * 1024, dim=dim, strategy=O.LRU)
+    keys = (np.arange(n) // rep).astype(np.uint64)
+    vals = ((np.arange(n) + 1).astype(np.float64) * 1e-5).astype(np.float32)[:, None].repeat(dim, 1)
+    t.insert_or_assign(keys, vals)
+    assert t.size() == (n + rep - 1) // rep
+    uniq = np.unique(keys)
+    v, f, _ = t.find(uniq)
+    assert f.all()
+    for k, row in zip(uniq, v):
+        occ = vals[keys == k]
+        assert any((row == o).all() for o in occ)
+
+
+def test_accum_or_assign_basic_when_full():
+    """tests/test_accum_or_assign.cpp:1659-1723 (test_basic_when_full),
+    Customized, as many random keys as slots, all assigns: erasing every key
+    empties the table, and assigning them again gives the same size."""
+    cap, dim = 128 * 64, 8
+    rng = np.random.default_rng(31)
+    keys = np.unique(rng.integers(0, 1 << 63, cap + 64, dtype=np.uint64))[:cap]
+    rng.shuffle(keys)
+    t = O.OracleTable(cap, cap, dim=dim, strategy=O.CUSTOMIZED)
+    vals = np.full((cap, dim), 1.0, np.float32)
+    acc = np.zeros(cap, np.uint8)
+    t.accum_or_assign(keys, vals, acc, keys.copy())
+    first = t.size()
+    assert 0 < first <= cap
+    t.erase(keys)
+    assert t.size() == 0
+    t.accum_or_assign(keys, vals, acc, keys.copy())
+    assert t.size() == first
+
+
+def test_accum_or_assign_values_check():
+    """tests/test_accum_or_assign.cpp:2204-2232 with CheckAccumOrAssignValues
+    :99-195, Lru, auto-grow from 1024 slots to U, batches of U + 13 random
+    keys from [0, 16 (U + 13)) with values key*1e-5, the accum flags taken
+    from a find of the batch: after each call every live key holds its old
+    value plus its delta (present and in the batch), its delta (new and in
+    the batch) or its old value (not in the batch); the size equals the
+    exported count."""
+    U, dim = 8192, 8
+    B = U + 13
+    t = O.OracleTable(1024, U, dim=dim, strategy=O.LRU)
+    rng = np.random.default_rng(32)
+    for rnd in range(6):
+        keys = np.unique(rng.integers(0, 16 * B, 2 * B, dtype=np.uint64))
+        rng.shuffle(keys)
+        keys = keys[:B]
+        vals = (keys.astype(np.float64) * 1e-5).astype(np.float32)[:, None].repeat(dim, 1)
+        _, found, _ = t.find(keys)
+        k0, v0, _ = t.export_batch(t.capacity())
+        assert len(k0) == t.size()
+        before = {int(k): v[0] for k, v in zip(k0, v0)}
+        t.set_clock(rnd + 1)
+        t.accum_or_assign(keys, vals, found.astype(np.uint8))
+        k1, v1, _ = t.export_batch(t.capacity())
+        assert len(k1) == t.size()
+        batch = {int(k): v[0] for k, v in zip(keys, vals)}
+        for k, row in zip(k1.tolist(), v1):
+            if k in before:
+                exp = np.float32(before[k] + batch[k]) if k in batch else before[k]
+            else:
+                assert k in batch
+                exp = batch[k]
+            assert (row == exp).all(), k
+
+
+def test_assign_scores_partial_keys():
+    """tests/test_assign_scores.cpp:301-394 (partial_keys_exist), Lfu: keys
+    1..500 inserted with scores = keys; assign_scores of keys 1..1000 with
+    scores 5000 + i keeps the size at 500, adds to the present keys' scores
+    (Lfu hit rule) and inserts nothing."""
+    t = O.OracleTable(128 * 1024, 128 * 1024, dim=8, strategy=O.LFU)
+    ins = np.arange(1, 501, dtype=np.uint64)
+    t.insert_or_assign(ins, np.zeros((500, 8), np.float32), ins.copy())
+    upd = np.arange(1, 1001, dtype=np.uint64)
+    sc = (5000 + np.arange(1000)).astype(np.uint64)
+    t.assign_scores(upd, sc)
+    assert t.size() == 500
+    _, f, s = t.find(upd)
+    assert f[:500].all() and not f[500:].any()
+    assert (s[:500] == ins + sc[:500]).all()
+
+
+def test_assign_scores_multiple_updates_and_lru():
+    """tests/test_assign_scores.cpp:681-751 (multiple_updates, Lfu: every key
+    stays found through repeated updates with scores (t+1)*1000 + i, the Lfu
+    rule adding each) and :1030-1108 (lru_strategy: assign_scores without
+    scores moves every Lru score forward)."""
+    n = 1024
+    keys = np.arange(1, n + 1, dtype=np.uint64)
+    t = O.OracleTable(128 * 1024, 128 * 1024, dim=8, strategy=O.LFU)
+    t.insert_or_assign(keys, np.zeros((n, 8), np.float32), keys.copy())
+    total = keys.copy()
+    for step in range(5):
+        sc = ((step + 1) * 1000 + np.arange(n)).astype(np.uint64)
+        t.assign_scores(keys, sc)
+        total += sc
+        _, f, s = t.find(keys)
+        assert f.all() and (s == total).all()
+    lru = O.OracleTable(128 * 1024, 128 * 1024, dim=8, strategy=O.LRU)
+    lru.set_clock(1000)
+    lru.insert_or_assign(keys, np.zeros((n, 8), np.float32))
+    _, _, s0 = lru.find(keys)
+    lru.set_clock(5000)
+    lru.assign_scores(keys)
+    _, f, s1 = lru.find(keys)
+    assert f.all() and (s1 >= s0).all() and (s1 > s0).any()
