@@ -510,12 +510,20 @@ __device__ __forceinline__ void upsert_locked(const TableView& t,
 //  3. otherwise the minimum-score slot (butterfly above); refuse iff
 //     desired < min; CAS(victim -> LOCKED) and re-check its score.
 // Returns the Occupy result, or kRetry.
+//
+// phase kPhaseProbe stops before step 3 when the bucket is full and returns
+// kDeferred; phase kPhaseEvict is step 3 alone, for a key such a probe
+// deferred (absent from a full bucket: a unique-key batch places a key only
+// through its own tile, and bucket sizes only grow during an upsert).
+enum UpsertPhase : int { kPhaseFull = 0, kPhaseProbe = 1, kPhaseEvict = 2 };
+constexpr int kDeferred = 8;  // a round's result: the key waits for an evict round
 template <int Mode, int S, int VW, uint32_t W, bool kLocks>
 __device__ __forceinline__ int upsert_round(const TableView& t, const TileW<W>& tile,
                                             const UpsertArgs& a, uint64_t i,
                                             uint64_t key, uint64_t desired,
                                             const Locate& l,
-                                            const RowHead<VW, W>& head) {
+                                            const RowHead<VW, W>& head,
+                                            int phase = kPhaseFull) {
   constexpr uint32_t kD = TileW<W>::kDigests;  // digests per lane
   constexpr uint32_t kDV = kD / 16;
   using M = typename std::conditional<(kD > 32), uint64_t, uint32_t>::type;
@@ -524,53 +532,74 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const TileW<W>& 
   const uint32_t lo = tile.lane * kD;
   const uint4* dl = reinterpret_cast<const uint4*>(t.digests + l.bkt * kBucket) + tile.lane * kDV;
   M hits = 0, empt = 0;
+  if (phase != kPhaseEvict) {
 #pragma unroll
-  for (uint32_t j = 0; j < kDV; j++) {
-    const uint4 dv = __ldcg(dl + j);
-    hits |= static_cast<M>(bytes_eq16(dv, l.d4)) << (16 * j);
-    empt |= static_cast<M>(bytes_eq16(dv, kEmptyDigest * 0x01010101u)) << (16 * j);
+    for (uint32_t j = 0; j < kDV; j++) {
+      const uint4 dv = __ldcg(dl + j);
+      hits |= static_cast<M>(bytes_eq16(dv, l.d4)) << (16 * j);
+      empt |= static_cast<M>(bytes_eq16(dv, kEmptyDigest * 0x01010101u)) << (16 * j);
+    }
   }
   const int32_t bword = __ldcg(t.sizes + l.bkt);  // size, caller locks above it
   // ---- 1. is the key here? (a digest hit that holds it is locked at once)
-  // Each lane locks its first digest hit holding the key in walk order (its
-  // slots from the start group on, then those before it), and the tile keeps
-  // the first in walk order: a key has one slot, except on layouts where a
-  // second copy was placed in front of it.
+  // Each lane locks its first digest hit holding the key in walk order, the
+  // tile keeps the first in walk order. A key has one slot, so normally one
+  // lane finds it and the index-order loop below is the walk order; only on
+  // layouts where a second copy was placed in front of the key do the two
+  // rare branches matter: a match in the start group's lane before the start
+  // group comes last in the walk (the lane keeps looking), and two lanes
+  // holding the key leave it to the walk rank.
   int mine = -1;
   bool busy = false;
-  auto try_hits = [&](M h) {
-    while (h && mine < 0) {
-      const uint32_t j = low_bit(h);
-      h &= h - 1;
+  {
+    const uint32_t g0 = l.pos & ~3u;
+    const uint32_t rot = (g0 >= lo && g0 < lo + kD) ? g0 - lo : 0;
+    int late = -1;  // a match before the start group, in that group's lane
+    while (hits) {
+      const uint32_t j = low_bit(hits);
+      hits &= hits - 1;
       const uint64_t k = cas_acquire_u64(bk + lo + j, key, kLockedKey);
-      if (k == key) mine = static_cast<int>(lo + j);
+      if (k == key) {
+        if (j >= rot) {
+          mine = static_cast<int>(lo + j);
+          break;
+        }
+        if (late < 0) late = static_cast<int>(lo + j);
+        else store_release_u64(bk + lo + j, key);
+        continue;
+      }
       // an operation in flight may hold the key: retry. A caller's lock says
       // nothing about which key it hides (a digest hit may belong to another
       // key): like the reference, which compares the word with the key
       // itself (insert_or_assign_kernel.h:128-140), such a slot is not it.
       busy |= (k == kLockedKey);
     }
-  };
-  {
-    const uint32_t g0 = l.pos & ~3u;
-    const M from_g0 = ~static_cast<M>(0) << ((g0 >= lo && g0 < lo + kD) ? g0 - lo : 0);
-    try_hits(hits & from_g0);
-    try_hits(hits & ~from_g0);
+    if (late >= 0) {
+      if (mine < 0)
+        mine = late;
+      else
+        store_release_u64(bk + late, key);
+    }
   }
   int res = kRetry;
   bool got = false;
   uint32_t slot = 0;
   uint64_t vkey = 0, vscore = 0;
-  const bool not_full = (bword & kSizeMask) < static_cast<int32_t>(kBucket);
-  uint32_t first = mine >= 0 ? (hit_rank(mine, l.pos) << 8) | static_cast<uint32_t>(mine)
-                             : 0xFFFFFFFFu;
-#pragma unroll
-  for (int o = W / 2; o > 0; o >>= 1) first = min(first, tile.shfl_xor(first, o));
+  const bool not_full =
+      phase != kPhaseEvict && (bword & kSizeMask) < static_cast<int32_t>(kBucket);
+  const uint32_t fm = tile.ballot(mine >= 0);
   // the key is in the bucket, but the reference's group walk reaches an
   // EMPTY slot first: it claims that slot instead
   bool to_empty = false;
-  if (first != 0xFFFFFFFFu) {
-    slot = first & 0xFF;
+  if (fm) {
+    slot = tile.shfl(static_cast<uint32_t>(mine), __ffs(fm) - 1);
+    if (__builtin_expect(__popc(fm) > 1, 0)) {
+      uint32_t first = mine >= 0 ? (hit_rank(mine, l.pos) << 8) | static_cast<uint32_t>(mine)
+                                 : 0xFFFFFFFFu;
+#pragma unroll
+      for (int o = W / 2; o > 0; o >>= 1) first = min(first, tile.shfl_xor(first, o));
+      slot = first & 0xFF;
+    }
     const bool holder = mine == static_cast<int>(slot);
     if (mine >= 0 && !holder) store_release_u64(bk + mine, key);
     // The walk (insert_or_assign_kernel.h:105-183) examines a group's digest
@@ -624,6 +653,7 @@ __device__ __forceinline__ int upsert_round(const TableView& t, const TileW<W>& 
     }
     // ---- 3. evict the minimum score (a key in the bucket whose EMPTY slots
     // ahead were all taken meanwhile is retried: the walk then hits it)
+    if (!got && !to_empty && phase == kPhaseProbe && !not_full) return kDeferred;
     if (!got && !to_empty) {
       uint64_t ms;
       uint32_t mp;
@@ -714,8 +744,61 @@ __device__ __forceinline__ bool retry_expired(const TableView& t, const Tl& tile
 #endif
 constexpr uint32_t kUpsertTile = HKV_UPSERT_TILE;
 
+// Outputs of key i once its result is final: the per-key status, no
+// address for find_or_insert* keys that got no slot, and insert_and_evict's
+// report of a refused input (reference insert_and_evict_kernel.h:553-557,
+// :675-683: the input with its desired score).
+template <int Mode, int VW, uint32_t W>
+__device__ __forceinline__ void upsert_finish(const TableView& t, const TileW<W>& tile,
+                                              const UpsertArgs& a, uint64_t i,
+                                              uint64_t key, uint64_t desired, int res,
+                                              const RowHead<VW, W>& head) {
+  if (a.status != nullptr && tile.lane == 0)
+    a.status[i * (a.status_stride ? a.status_stride : 1)] = res;
+  if constexpr (Mode == kModeFindOrInsertPtr) {
+    // refused, reserved or timed-out keys get no address
+    if (tile.lane == 0 && res != kDuplicate && res != kOccupiedEmpty &&
+        res != kOccupiedReclaimed && res != kEvict) {
+      a.value_ptrs[i] = nullptr;
+      if (a.founds != nullptr) a.founds[i] = false;
+      if (a.locked_key_ptrs != nullptr) a.locked_key_ptrs[i] = nullptr;
+    }
+  }
+  if constexpr (Mode == kModeInsertAndEvict) {
+    if (res == kRefused && a.report_refused) {
+      const uint32_t vb = t.value_bytes;
+      unsigned long long o = 0;
+      if (tile.lane == 0) {
+        o = warp_claim(a.ev_counter);
+        if (!HKV_BOUND(t, o < a.n, 4)) o = 0;
+        a.ev_keys[o] = key;
+        if (a.ev_scores) a.ev_scores[o] = desired;
+      }
+      o = tile.shfl(o, 0);
+      head.store(a.ev_values + o * vb, a.values_in + key_row(a, i) * vb, vb / VW, tile.lane);
+    }
+  }
+}
+
+// Keys a warp's probe rounds found absent from a full bucket wait here (per
+// warp, in shared memory) until the warp has a whole round of them.
+#ifndef HKV_UPSERT_SPLIT
+#define HKV_UPSERT_SPLIT 1
+#endif
+constexpr uint32_t kDeferCap = 16;
+
 // The upsert loop: keys [0, n) of `a`, warp `warp` of `nwarps` taking
 // keys warp * KPW, then every nwarps * KPW.
+//
+// A warp works on KPW keys at a time in warp-uniform rounds (the lock
+// discipline above), so a round lasts as long as its slowest key. At a high
+// load factor half of the keys are absent from full buckets and take the
+// eviction path (a 1 KiB score scan, the victim's exchange and re-check),
+// the others a short hit or empty-slot path. With HKV_UPSERT_SPLIT the
+// warp's probe rounds take new keys and finish every key that needs no
+// eviction; a key absent from a full bucket is deferred to the warp's queue,
+// and once KPW keys wait there an evict round runs them together, so the
+// short and the long paths no longer share rounds.
 template <int Mode, int S, int VW, bool kLocks>
 __device__ __forceinline__ void upsert_body(const TableView& t, const UpsertArgs& a,
                                             uint64_t clk, uint64_t warp,
@@ -732,6 +815,79 @@ __device__ __forceinline__ void upsert_body(const TableView& t, const UpsertArgs
   // probe, so neither waits behind the bucket's round trips
   const uint64_t stride = nwarps * KPW;
   uint64_t next = warp * KPW + wl / W < n ? a.keys[warp * KPW + wl / W] : 0;
+  if constexpr (HKV_UPSERT_SPLIT && Mode == kModeInsertAndEvict) {
+  static_assert(KPW <= kDeferCap / 2, "the queue takes one probe round on top of KPW - 1 keys");
+  __shared__ uint64_t s_defer[8][kDeferCap];  // blockDim.x == 256: 8 warps
+  uint64_t* dq = s_defer[threadIdx.x >> 5];
+  uint32_t qhead = 0, qcnt = 0;  // warp-uniform
+  uint64_t base = warp * KPW;
+  while (true) {
+    const bool evict = qcnt >= KPW || (base >= n && qcnt > 0);
+    if (!evict && base >= n) break;
+    uint64_t i = 0, key = 0;
+    bool have;
+    if (evict) {
+      const uint32_t take = min(qcnt, KPW);
+      have = wl / W < take;
+      if (have) {
+        i = dq[(qhead + wl / W) % kDeferCap];
+        key = a.keys[i];
+      }
+      qhead = (qhead + take) % kDeferCap;
+      qcnt -= take;
+    } else {
+      i = base + wl / W;
+      have = i < n;
+      if (have) {
+        key = next;
+        if (i + stride < n) next = a.keys[i + stride];
+      }
+      base += stride;
+    }
+    uint64_t desired = 0, t0 = 0;
+    int res = kIllegal;
+    bool todo = false;
+    RowHead<VW, W> head;
+    Locate l;
+    l.bkt = 0;
+    l.pos = 0;
+    l.d4 = 0;
+    if (have && !is_reserved(key)) {
+      if constexpr (Mode != kModeFindOrInsertPtr)
+        head.load(in_rows + key_row(a, i) * vb, nv, tile.lane);
+      desired = desired_when_missed<S>(a.scores, i, a.epoch, clk);
+      l = locate(t, key);
+      todo = true;
+    }
+    const int phase = evict ? kPhaseEvict : kPhaseProbe;
+    for (int round = 0;; round++) {
+      bool again = false;
+      if (todo) {
+        res = upsert_round<Mode, S, VW, W, kLocks>(t, tile, a, i, key, desired, l, head,
+                                                   phase);
+        if (res == kRetry) {
+          if (retry_expired(t, tile, t0, 101)) {
+            res = kTimedOut;
+            todo = false;
+          } else {
+            again = true;
+          }
+        } else {
+          todo = false;
+        }
+      }
+      if (!__any_sync(0xFFFFFFFFu, again)) break;
+      backoff(round);
+    }
+    const bool deferred = have && res == kDeferred;
+    const uint32_t dm = __ballot_sync(0xFFFFFFFFu, deferred && tile.lane == 0);
+    if (deferred && tile.lane == 0)
+      dq[(qhead + qcnt + __popc(dm & ((1u << wl) - 1))) % kDeferCap] = i;
+    qcnt += __popc(dm);
+    __syncwarp();  // the queue entries are read by other lanes of the warp
+    if (have && !deferred) upsert_finish<Mode, VW, W>(t, tile, a, i, key, desired, res, head);
+  }
+  } else {
   for (uint64_t base = warp * KPW; base < n; base += stride) {
     const uint64_t i = base + wl / W;
     uint64_t key = 0, desired = 0, t0 = 0;
@@ -772,34 +928,8 @@ __device__ __forceinline__ void upsert_body(const TableView& t, const UpsertArgs
       if (!__any_sync(0xFFFFFFFFu, again)) break;
       backoff(round);
     }
-    if (i < n) {
-      if (a.status != nullptr && tile.lane == 0)
-        a.status[i * (a.status_stride ? a.status_stride : 1)] = res;
-      if constexpr (Mode == kModeFindOrInsertPtr) {
-        // refused, reserved or timed-out keys get no address
-        if (tile.lane == 0 && res != kDuplicate && res != kOccupiedEmpty &&
-            res != kOccupiedReclaimed && res != kEvict) {
-          a.value_ptrs[i] = nullptr;
-          if (a.founds != nullptr) a.founds[i] = false;
-          if (a.locked_key_ptrs != nullptr) a.locked_key_ptrs[i] = nullptr;
-        }
-      }
-      if constexpr (Mode == kModeInsertAndEvict) {
-        if (res == kRefused && a.report_refused) {
-          // reference insert_and_evict_kernel.h:553-557, :675-683: the
-          // refused input is reported with its desired score
-          unsigned long long o = 0;
-          if (tile.lane == 0) {
-            o = warp_claim(a.ev_counter);
-            if (!HKV_BOUND(t, o < a.n, 4)) o = 0;
-            a.ev_keys[o] = key;
-            if (a.ev_scores) a.ev_scores[o] = desired;
-          }
-          o = tile.shfl(o, 0);
-          head.store(a.ev_values + o * vb, a.values_in + key_row(a, i) * vb, nv, tile.lane);
-        }
-      }
-    }
+    if (i < n) upsert_finish<Mode, VW, W>(t, tile, a, i, key, desired, res, head);
+  }
   }
 }
 

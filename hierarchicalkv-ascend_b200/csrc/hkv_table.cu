@@ -90,8 +90,8 @@ void magic_for(uint64_t d, uint64_t* magic, uint32_t* shift) {
 
 // ---------------------------------------------------------------------------
 TableImpl::TableImpl(const hkv_options& o, int key_type, int value_type,
-                     int strategy)
-    : opt_(o), key_type_(key_type), value_type_(value_type),
+                     int strategy, const hkv_allocator* allocator)
+    : opt_(o), mem_(allocator), key_type_(key_type), value_type_(value_type),
       strategy_(strategy) {
   // option checks, reference hkv_hashtable.h:962-1042
   HKV_REQUIRE(key_type == HKV_KEY_U64 || key_type == HKV_KEY_I64,
@@ -171,20 +171,27 @@ TableImpl::TableImpl(const hkv_options& o, int key_type, int value_type,
   slice_shift_ = std::min(log2_floor(rule), log2_floor(num_buckets_));
 
   const size_t slots = capacity_;
-  CUDA_TRY(cudaMalloc(&keys_, slots * 8));
-  CUDA_TRY(cudaMalloc(&scores_, slots * 8));
-  CUDA_TRY(cudaMalloc(&digests_, slots));
-  CUDA_TRY(cudaMalloc(&sizes_, num_buckets_ * 4));
-  CUDA_TRY(cudaMalloc(&d_error_, 2 * sizeof(int)));
-  CUDA_TRY(cudaMemset(d_error_, 0, 2 * sizeof(int)));
-  CUDA_TRY(cudaMalloc(&d_scratch_, 4 * sizeof(unsigned long long)));
-  CUDA_TRY(cudaHostAlloc(&h_scratch_, 4 * sizeof(unsigned long long),
-                         cudaHostAllocDefault));
-  const uint64_t max_buckets = std::max<uint64_t>(
-      num_buckets_, ceil_div(std::max<uint64_t>(max_size_, capacity_), kBucket));
-  d_slices_cap_ = ceil_div(max_buckets, 1ull << slice_shift_) + 1;
-  CUDA_TRY(cudaMalloc(&d_slices_, d_slices_cap_ * sizeof(uint8_t*)));
-  allocate_slices(0, num_buckets_);
+  // every allocation from mem_ (the caller's allocator, if any); a failure
+  // part way frees what was taken
+  try {
+    keys_ = static_cast<uint64_t*>(mem_.device(slots * 8));
+    scores_ = static_cast<uint64_t*>(mem_.device(slots * 8));
+    digests_ = static_cast<uint8_t*>(mem_.device(slots));
+    sizes_ = static_cast<int32_t*>(mem_.device(num_buckets_ * 4));
+    d_error_ = static_cast<int*>(mem_.device(2 * sizeof(int)));
+    CUDA_TRY(cudaMemset(d_error_, 0, 2 * sizeof(int)));
+    d_scratch_ = static_cast<unsigned long long*>(mem_.device(4 * sizeof(unsigned long long)));
+    h_scratch_ = static_cast<unsigned long long*>(
+        mem_.pinned(4 * sizeof(unsigned long long), cudaHostAllocDefault));
+    const uint64_t max_buckets = std::max<uint64_t>(
+        num_buckets_, ceil_div(std::max<uint64_t>(max_size_, capacity_), kBucket));
+    d_slices_cap_ = ceil_div(max_buckets, 1ull << slice_shift_) + 1;
+    d_slices_ = static_cast<uint8_t**>(mem_.device(d_slices_cap_ * sizeof(uint8_t*)));
+    allocate_slices(0, num_buckets_);
+  } catch (...) {
+    release();
+    throw;
+  }
   upload_slices();
   const TableView v = view();
   init_buckets_kernel<<<std::max(1, warp_grid(num_buckets_)), 256, 0, counted(0)>>>(
@@ -195,21 +202,33 @@ TableImpl::TableImpl(const hkv_options& o, int key_type, int value_type,
 
 TableImpl::~TableImpl() {
   cudaDeviceSynchronize();
+  release();
+}
+
+void TableImpl::release() noexcept {
   for (auto& s : slices_) {
     if (s.host)
-      cudaFreeHost(s.host);
+      mem_.free_pinned(s.host);
     else
-      cudaFree(s.dev);
+      mem_.free_device(s.dev);
   }
-  cudaFree(keys_);
-  cudaFree(scores_);
-  cudaFree(digests_);
-  cudaFree(sizes_);
-  cudaFree(d_error_);
-  cudaFree(d_scratch_);
+  slices_.clear();
+  mem_.free_device(keys_);
+  mem_.free_device(scores_);
+  mem_.free_device(digests_);
+  mem_.free_device(sizes_);
+  mem_.free_device(d_error_);
+  mem_.free_device(d_scratch_);
+  mem_.free_device(d_slices_);
+  mem_.free_pinned(h_scratch_);
+  keys_ = scores_ = nullptr;
+  digests_ = nullptr;
+  sizes_ = nullptr;
+  d_error_ = nullptr;
+  d_scratch_ = h_scratch_ = nullptr;
+  d_slices_ = nullptr;
   if (pool_) cudaMemPoolDestroy(pool_);
-  cudaFree(d_slices_);
-  cudaFreeHost(h_scratch_);
+  pool_ = nullptr;
 }
 
 // initialize_buckets slice placement, reference table.h:143-184: slices go to
@@ -223,14 +242,21 @@ void TableImpl::allocate_slices(uint64_t b0, uint64_t b1) {
     const size_t bytes = cnt * bucket_bytes;
     Slice s{nullptr, nullptr, bytes};
     if (remaining_hbm_ >= bytes) {
-      CUDA_TRY(cudaMalloc(&s.dev, bytes));
+      s.dev = static_cast<uint8_t*>(mem_.device(bytes));
       remaining_hbm_ -= bytes;
     } else {
       pure_hbm_ = false;
-      CUDA_TRY(cudaHostAlloc(&s.host, bytes,
-                             cudaHostAllocMapped | cudaHostAllocPortable));
-      CUDA_TRY(cudaHostGetDevicePointer(reinterpret_cast<void**>(&s.dev),
-                                        s.host, 0));
+      s.host = static_cast<uint8_t*>(
+          mem_.pinned(bytes, cudaHostAllocMapped | cudaHostAllocPortable));
+      const cudaError_t e =
+          cudaHostGetDevicePointer(reinterpret_cast<void**>(&s.dev), s.host, 0);
+      if (e != cudaSuccess) {
+        mem_.free_pinned(s.host);
+        throw HkvError{HKV_ERR_CUDA,
+                       std::string("a host value slice is not mapped into the device "
+                                   "address space (cudaHostGetDevicePointer: ") +
+                           cudaGetErrorString(e) + ")"};
+      }
     }
     slices_.push_back(s);
   }
@@ -509,7 +535,7 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
   if (mode == kModeFindOrInsertPtr) {
     // repeated keys: the representatives get addresses, every occurrence
     // then takes its representative's
-    Workspace ws(s, pool_);
+    Workspace ws(s, pool_, &mem_);
     const DedupResult d = dedup_batch(n, keys, scores, st, ws, s, sm_count_, d_error_);
     uint8_t** uptrs = ws.get<uint8_t*>(n);
     bool* ufound = ws.get<bool>(n);
@@ -533,7 +559,7 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
   }
 
   // ---- duplicate keys: merge to one representative per key ---------------
-  Workspace ws(s, pool_);
+  Workspace ws(s, pool_, &mem_);
   const DedupResult d =
       dedup_batch(n, keys, scores, st, ws, s, sm_count_, d_error_);
   uint8_t* ustatus = ws.get<uint8_t>(n);
@@ -882,12 +908,12 @@ void TableImpl::export_batch(size_t n, size_t offset, uint64_t* d_counter,
 namespace {
 // pinned host staging for one chunk of tuples: keys | scores | values
 struct HostChunk {
+  MemSource& mem;
   uint8_t* p = nullptr;
-  explicit HostChunk(size_t bytes) {
-    CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&p), std::max<size_t>(bytes, 1),
-                           cudaHostAllocDefault));
+  HostChunk(MemSource& m, size_t bytes) : mem(m) {
+    p = static_cast<uint8_t*>(mem.pinned(std::max<size_t>(bytes, 1), cudaHostAllocDefault));
   }
-  ~HostChunk() { cudaFreeHost(p); }
+  ~HostChunk() { mem.free_pinned(p); }
 };
 }  // namespace
 
@@ -899,11 +925,11 @@ size_t TableImpl::save(hkv_kv_write_fn write, void* user, size_t max_ws,
               "`key + score + value` tuple! Please set a larger value!");
   const size_t total = capacity_;
   const size_t n = std::min(max_ws / tuple, total);
-  HostChunk h(n * tuple);
+  HostChunk h(mem_, n * tuple);
   uint64_t* hk = reinterpret_cast<uint64_t*>(h.p);
   uint64_t* hs = hk + n;
   uint8_t* hv = reinterpret_cast<uint8_t*>(hs + n);
-  Workspace ws(s, pool_);
+  Workspace ws(s, pool_, &mem_);
   uint64_t* dcount = ws.get<uint64_t>(1);
   uint64_t* dk = ws.get<uint64_t>(n);
   uint64_t* dsc = ws.get<uint64_t>(n);
@@ -932,13 +958,13 @@ size_t TableImpl::load(hkv_kv_read_fn read, void* user, size_t max_ws,
               "[HierarchicalKV] max_workspace_size is smaller than a single "
               "`key + score + value` tuple! Please set a larger value!");
   const size_t n = max_ws / tuple;
-  HostChunk h(n * tuple);
+  HostChunk h(mem_, n * tuple);
   uint64_t* hk = reinterpret_cast<uint64_t*>(h.p);
   uint64_t* hs = hk + n;
   uint8_t* hv = reinterpret_cast<uint8_t*>(hs + n);
   size_t c = read(user, n, opt_.dim, hk, hv, hs);
   if (c == 0) return 0;
-  Workspace ws(s, pool_);
+  Workspace ws(s, pool_, &mem_);
   uint64_t* dk = ws.get<uint64_t>(n);
   uint64_t* dsc = ws.get<uint64_t>(n);
   uint8_t* dv = ws.get<uint8_t>(n * value_bytes_);
@@ -972,19 +998,27 @@ void TableImpl::double_capacity(cudaStream_t s) {
   uint64_t *nk = nullptr, *ns = nullptr;
   uint8_t* nd = nullptr;
   int32_t* nz = nullptr;
-  CUDA_TRY(cudaMalloc(&nk, new_slots * 8));
-  CUDA_TRY(cudaMalloc(&ns, new_slots * 8));
-  CUDA_TRY(cudaMalloc(&nd, new_slots));
-  CUDA_TRY(cudaMalloc(&nz, new_nb * 4));
+  try {
+    nk = static_cast<uint64_t*>(mem_.device(new_slots * 8));
+    ns = static_cast<uint64_t*>(mem_.device(new_slots * 8));
+    nd = static_cast<uint8_t*>(mem_.device(new_slots));
+    nz = static_cast<int32_t*>(mem_.device(new_nb * 4));
+  } catch (...) {
+    mem_.free_device(nk);
+    mem_.free_device(ns);
+    mem_.free_device(nd);
+    mem_.free_device(nz);
+    throw;
+  }
   CUDA_TRY(cudaMemcpyAsync(nk, keys_, old_slots * 8, cudaMemcpyDeviceToDevice, s));
   CUDA_TRY(cudaMemcpyAsync(ns, scores_, old_slots * 8, cudaMemcpyDeviceToDevice, s));
   CUDA_TRY(cudaMemcpyAsync(nd, digests_, old_slots, cudaMemcpyDeviceToDevice, s));
   CUDA_TRY(cudaMemcpyAsync(nz, sizes_, old_nb * 4, cudaMemcpyDeviceToDevice, s));
   CUDA_TRY(cudaStreamSynchronize(s));
-  cudaFree(keys_);
-  cudaFree(scores_);
-  cudaFree(digests_);
-  cudaFree(sizes_);
+  mem_.free_device(keys_);
+  mem_.free_device(scores_);
+  mem_.free_device(digests_);
+  mem_.free_device(sizes_);
   keys_ = nk;
   scores_ = ns;
   digests_ = nd;
@@ -1005,7 +1039,7 @@ void TableImpl::double_capacity(cudaStream_t s) {
   const int grid = static_cast<int>(
       std::max<uint64_t>(1, std::min<uint64_t>(ceil_div(old_nb, 8), max_warps / 8)));
   {
-    Workspace ws(s, pool_);
+    Workspace ws(s, pool_, &mem_);
     uint8_t* scratch = ws.get<uint8_t>(uint64_t{static_cast<uint32_t>(grid)} * 8 * row_block);
     DISPATCH_VW(vw, rehash_kernel<VW><<<grid, 256, 0, counted(s)>>>(v, old_nb, scratch));
     CUDA_TRY(cudaGetLastError());
@@ -1022,6 +1056,26 @@ void TableImpl::reserve(size_t new_capacity, cudaStream_t s) {
   while (capacity_ < new_capacity && capacity_ * 2 <= opt_.max_capacity)
     double_capacity(s);
   reach_max_ = capacity_ * 2 > opt_.max_capacity;
+}
+
+// set_max_capacity, reference hkv_hashtable.h:2955-2977.
+void TableImpl::set_max_capacity(size_t new_max) {
+  HKV_REQUIRE(is_pow2(new_max), HKV_ERR_INVALID,
+              "None power-of-2 new_max_capacity is not supported.");
+  if (new_max < capacity_) return;
+  // the slice table must hold the slices of the new maximum
+  const uint64_t need = ceil_div(ceil_div(new_max, kBucket), 1ull << slice_shift_) + 1;
+  if (need > d_slices_cap_) {
+    uint8_t** grown = static_cast<uint8_t**>(mem_.device(need * sizeof(uint8_t*)));
+    CUDA_TRY(cudaDeviceSynchronize());  // kernels in flight may read the old table
+    mem_.free_device(d_slices_);
+    d_slices_ = grown;
+    d_slices_cap_ = need;
+    upload_slices();
+  }
+  reach_max_ = false;
+  opt_.max_capacity = new_max;
+  max_size_ = std::max<uint64_t>(max_size_, new_max);
 }
 
 void TableImpl::check_device_error(cudaStream_t s) {
@@ -1296,18 +1350,33 @@ const char* hkv_last_error(void) { return hkvb::last_error(); }
 
 int hkv_table_create(const hkv_options* options, int key_type, int value_type,
                      int evict_strategy, hkv_table** out) {
+  return hkv_table_create_with_allocator(options, key_type, value_type, evict_strategy,
+                                         nullptr, out);
+}
+
+int hkv_table_create_with_allocator(const hkv_options* options, int key_type,
+                                    int value_type, int evict_strategy,
+                                    const hkv_allocator* allocator, hkv_table** out) {
   HKV_API_BEGIN
   HKV_REQUIRE(options != nullptr && out != nullptr, HKV_ERR_INVALID,
               "null argument");
   *out = nullptr;
   auto* t = new hkv_table;
   try {
-    t->impl = new TableImpl(*options, key_type, value_type, evict_strategy);
+    t->impl = new TableImpl(*options, key_type, value_type, evict_strategy, allocator);
   } catch (...) {
     delete t;
     throw;
   }
   *out = t;
+  HKV_API_END
+}
+
+int hkv_set_max_capacity(hkv_table* table, size_t new_max_capacity) {
+  HKV_API_BEGIN
+  HKV_TABLE(table);
+  HKV_LOCK(kUpdate, nullptr);
+  T->set_max_capacity(new_max_capacity);
   HKV_API_END
 }
 

@@ -47,19 +47,109 @@ struct Slice {
   size_t bytes;
 };
 
-// Stream-ordered scratch from the table's own memory pool. The pool keeps
-// freed blocks reserved, so a steady stream of same-sized calls maps device
-// memory once instead of at every call.
+// Where a table's memory comes from: the CUDA runtime, or the caller's
+// allocator (the reference's BaseAllocator, allocator.h:27-158, taken by
+// init, hkv_hashtable.h:962-978) through the callbacks of hkv_allocator.
+class MemSource {
+ public:
+  MemSource() = default;
+  explicit MemSource(const hkv_allocator* a) {
+    if (a == nullptr) return;
+    HKV_REQUIRE(a->alloc != nullptr && a->free != nullptr, HKV_ERR_INVALID,
+                "the allocator needs alloc and free");
+    a_ = *a;
+    custom_ = true;
+  }
+  bool custom() const { return custom_; }
+  void* device(size_t bytes) {
+    void* p = nullptr;
+    if (!custom_) {
+      CUDA_TRY(cudaMalloc(&p, bytes));
+      return p;
+    }
+    const int rc = a_.alloc(a_.user, HKV_MEMORY_DEVICE, &p, bytes, 0);
+    take(rc, p, bytes, "device");
+    return p;
+  }
+  void free_device(void* p) noexcept {
+    if (p == nullptr) return;
+    if (custom_)
+      a_.free(a_.user, HKV_MEMORY_DEVICE, p);
+    else
+      cudaFree(p);
+  }
+  void* pinned(size_t bytes, unsigned int flags) {
+    void* p = nullptr;
+    if (!custom_) {
+      CUDA_TRY(cudaHostAlloc(&p, bytes, flags));
+      return p;
+    }
+    const int rc = a_.alloc(a_.user, HKV_MEMORY_PINNED, &p, bytes, flags);
+    take(rc, p, bytes, "pinned");
+    return p;
+  }
+  void free_pinned(void* p) noexcept {
+    if (p == nullptr) return;
+    if (custom_)
+      a_.free(a_.user, HKV_MEMORY_PINNED, p);
+    else
+      cudaFreeHost(p);
+  }
+  // per-call scratch of a custom allocator (the pool otherwise)
+  void* device_async(size_t bytes, cudaStream_t s) {
+    void* p = nullptr;
+    // (the call completes before p is read: argument order is unspecified)
+    const int rc = a_.alloc_async != nullptr
+                       ? a_.alloc_async(a_.user, HKV_MEMORY_DEVICE, &p, bytes, s)
+                       : a_.alloc(a_.user, HKV_MEMORY_DEVICE, &p, bytes, 0);
+    take(rc, p, bytes, "device");
+    return p;
+  }
+  void free_device_async(void* p, cudaStream_t s) noexcept {
+    if (p == nullptr) return;
+    if (a_.free_async != nullptr) {
+      a_.free_async(a_.user, HKV_MEMORY_DEVICE, p, s);
+    } else {
+      cudaStreamSynchronize(s);  // the scratch may still be in use on s
+      a_.free(a_.user, HKV_MEMORY_DEVICE, p);
+    }
+  }
+
+ private:
+  static void take(int rc, void* p, size_t bytes, const char* what) {
+    if (rc != 0 || (p == nullptr && bytes != 0))
+      throw HkvError{HKV_ERR_CUDA, std::string("the caller's allocator failed to allocate ") +
+                                       std::to_string(bytes) + " bytes of " + what +
+                                       " memory"};
+  }
+  hkv_allocator a_{};
+  bool custom_ = false;
+};
+
+// Stream-ordered scratch for one call: from the table's own memory pool,
+// whose freed blocks stay reserved (a steady stream of same-sized calls maps
+// device memory once instead of at every call), or from the caller's
+// allocator when the table has one.
 class Workspace {
  public:
-  Workspace(cudaStream_t s, cudaMemPool_t pool) : stream_(s), pool_(pool) {}
+  Workspace(cudaStream_t s, cudaMemPool_t pool, MemSource* mem = nullptr)
+      : stream_(s), pool_(pool), mem_(mem != nullptr && mem->custom() ? mem : nullptr) {}
   ~Workspace() {
-    for (void* p : ptrs_) cudaFreeAsync(p, stream_);
+    for (void* p : ptrs_) {
+      if (mem_)
+        mem_->free_device_async(p, stream_);
+      else
+        cudaFreeAsync(p, stream_);
+    }
   }
   template <class T>
   T* get(size_t count) {
     void* p = nullptr;
-    CUDA_TRY(cudaMallocFromPoolAsync(&p, count * sizeof(T) + 16, pool_, stream_));
+    const size_t bytes = count * sizeof(T) + 16;
+    if (mem_)
+      p = mem_->device_async(bytes, stream_);
+    else
+      CUDA_TRY(cudaMallocFromPoolAsync(&p, bytes, pool_, stream_));
     ptrs_.push_back(p);
     return static_cast<T*>(p);
   }
@@ -67,6 +157,7 @@ class Workspace {
  private:
   cudaStream_t stream_;
   cudaMemPool_t pool_;
+  MemSource* mem_;
   std::vector<void*> ptrs_;
 };
 
@@ -129,7 +220,10 @@ class GroupMutex {
 
 class TableImpl {
  public:
-  TableImpl(const hkv_options& o, int key_type, int value_type, int strategy);
+  // allocator: the caller's (reference BaseAllocator), nullptr for the CUDA
+  // runtime; copied
+  TableImpl(const hkv_options& o, int key_type, int value_type, int strategy,
+            const hkv_allocator* allocator = nullptr);
   ~TableImpl();
 
   TableView view() const;
@@ -185,6 +279,7 @@ class TableImpl {
   size_t size(cudaStream_t s);
   float load_factor(cudaStream_t s);
   void reserve(size_t new_capacity, cudaStream_t s);
+  void set_max_capacity(size_t new_max_capacity);
   void check_device_error(cudaStream_t s);
   // save / load through BaseKVFile-style callbacks (synchronous)
   size_t save(hkv_kv_write_fn write, void* user, size_t max_ws, cudaStream_t s);
@@ -204,6 +299,9 @@ class TableImpl {
   int value_type() const { return value_type_; }
   int device() const { return device_; }
   cudaMemPool_t pool() const { return pool_; }
+  // scratch for one call on stream s (the caller's allocator, if any)
+  Workspace workspace(cudaStream_t s) { return Workspace(s, pool_, &mem_); }
+  MemSource& mem() { return mem_; }
   int* error_word() const { return d_error_; }
   int value_width(std::initializer_list<const void*> ptrs) const;
   void set_global_epoch(uint64_t e) { epoch_ = e; }
@@ -238,6 +336,8 @@ class TableImpl {
   // sum over buckets of (size word >> shift) & kSizeMask
   uint64_t sum_counts(uint64_t nb, int shift, cudaStream_t s);
   void allocate_slices(uint64_t b0, uint64_t b1);
+  // frees every table allocation (destructor, failed construction)
+  void release() noexcept;
   void upload_slices();
   void double_capacity(cudaStream_t s);
   void upsert(int mode, size_t n, const uint64_t* keys,
@@ -250,6 +350,7 @@ class TableImpl {
               uint64_t** locked_key_ptrs = nullptr);
 
   hkv_options opt_;
+  MemSource mem_;  // every table allocation goes through it
   int key_type_, value_type_, strategy_;
   uint32_t elem_bytes_, value_bytes_;
   int device_ = 0;

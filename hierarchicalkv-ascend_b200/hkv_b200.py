@@ -125,6 +125,26 @@ class HashTableOptions:
         return o
 
 
+# hkv_allocator (include/hkv_b200.h): the reference's BaseAllocator as
+# callbacks on a caller's object
+_ALLOC_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                             ctypes.POINTER(ctypes.c_void_p), ctypes.c_size_t, ctypes.c_uint)
+_ALLOC_ASYNC_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                   ctypes.POINTER(ctypes.c_void_p), ctypes.c_size_t,
+                                   ctypes.c_void_p)
+_FREE_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p)
+_FREE_ASYNC_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                  ctypes.c_void_p, ctypes.c_void_p)
+
+
+class _Allocator(ctypes.Structure):
+    _fields_ = [("user", ctypes.c_void_p), ("alloc", _ALLOC_FN),
+                ("alloc_async", _ALLOC_ASYNC_FN), ("free", _FREE_FN),
+                ("free_async", _FREE_ASYNC_FN)]
+
+
+MEMORY_DEVICE, MEMORY_PINNED, MEMORY_HOST = 0, 1, 2
+
 # C ABI symbols and their signatures (include/hkv_b200.h)
 _P = ctypes.c_void_p
 _SZ = ctypes.c_size_t
@@ -135,7 +155,12 @@ SIGNATURES = {
     "hkv_last_error": (ctypes.c_char_p, []),
     "hkv_table_create": (ctypes.c_int, [ctypes.POINTER(_Options), ctypes.c_int,
                                         ctypes.c_int, ctypes.c_int, ctypes.POINTER(_P)]),
+    "hkv_table_create_with_allocator": (ctypes.c_int, [ctypes.POINTER(_Options), ctypes.c_int,
+                                                       ctypes.c_int, ctypes.c_int,
+                                                       ctypes.POINTER(_Allocator),
+                                                       ctypes.POINTER(_P)]),
     "hkv_table_destroy": (ctypes.c_int, [_P]),
+    "hkv_set_max_capacity": (ctypes.c_int, [_P, _SZ]),
     "hkv_insert_or_assign": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _B, _B]),
     "hkv_insert_and_evict": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _P, _P, _P, _P, _B, _B]),
     "hkv_insert_and_evict_count": (ctypes.c_int, [_P, _SZ, _P, _P, _P, _P, _P, _P, _P,
@@ -196,7 +221,12 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     """Loads libhkv_b200.so and declares every C ABI signature."""
     lib = ctypes.CDLL(path)
     for name, (res, args) in SIGNATURES.items():
-        fn = getattr(lib, name)
+        # an older build (HKV_B200_LIB) may lack newer entry points: calling
+        # one then raises AttributeError; tests/test_abi.py checks that the
+        # in-tree library exports every declared symbol
+        fn = getattr(lib, name, None)
+        if fn is None:
+            continue
         fn.restype = res
         fn.argtypes = args
     return lib
@@ -225,6 +255,83 @@ def _check(status: int) -> None:
     if status == HKV_ERR_UNSUPPORTED:
         raise HkvUnsupported(msg)
     raise RuntimeError(msg)
+
+
+def _allocator_callbacks(allocator) -> _Allocator:
+    """hkv_allocator callbacks over a Python allocator object; an exception in
+    the object becomes a failed allocation (non-zero status)."""
+
+    def alloc(_u, mt, out, size, flags):
+        try:
+            out[0] = int(allocator.alloc(mt, int(size), int(flags)))
+            return 0
+        except Exception:
+            return 1
+
+    def free(_u, mt, ptr):
+        try:
+            allocator.free(mt, int(ptr or 0))
+            return 0
+        except Exception:
+            return 1
+
+    a = _Allocator()
+    a.user = None
+    a.alloc = _ALLOC_FN(alloc)
+    a.free = _FREE_FN(free)
+    if hasattr(allocator, "alloc_async") and hasattr(allocator, "free_async"):
+        def alloc_async(_u, mt, out, size, stream):
+            try:
+                out[0] = int(allocator.alloc_async(mt, int(size), stream or 0))
+                return 0
+            except Exception:
+                return 1
+
+        def free_async(_u, mt, ptr, stream):
+            try:
+                allocator.free_async(mt, int(ptr or 0), stream or 0)
+                return 0
+            except Exception:
+                return 1
+
+        a.alloc_async = _ALLOC_ASYNC_FN(alloc_async)
+        a.free_async = _FREE_ASYNC_FN(free_async)
+    else:
+        a.alloc_async = ctypes.cast(None, _ALLOC_ASYNC_FN)
+        a.free_async = ctypes.cast(None, _FREE_ASYNC_FN)
+    a._keep = (alloc, free)  # the Python functions behind the callbacks
+    return a
+
+
+class TorchAllocator:
+    """A BaseAllocator over PyTorch's CUDA caching allocator for device
+    memory (so a table embedded in a PyTorch program shares torch's memory
+    pool and shows in torch.cuda.memory_allocated) and pinned host memory
+    from torch (pinned tensors, mapped into the device address space on
+    this platform). Blocks are kept by address until freed."""
+
+    def __init__(self, device=None):
+        import torch
+
+        self._torch = torch
+        self.device = torch.cuda.current_device() if device is None else device
+        self.blocks = {}
+
+    def alloc(self, memory_type, size, flags=0):
+        t = self._torch
+        n = max(int(size), 1)
+        if memory_type == MEMORY_DEVICE:
+            buf = t.empty(n, dtype=t.uint8, device=f"cuda:{self.device}")
+        elif memory_type == MEMORY_PINNED:
+            buf = t.empty(n, dtype=t.uint8, pin_memory=True)
+        else:
+            buf = t.empty(n, dtype=t.uint8)
+        addr = buf.data_ptr()
+        self.blocks[addr] = buf
+        return addr
+
+    def free(self, memory_type, addr):
+        self.blocks.pop(addr, None)
 
 
 def kernel_launches() -> int:
@@ -278,16 +385,28 @@ class HashTable:
         return t
 
     # -- lifecycle ---------------------------------------------------------
-    def init(self, options: HashTableOptions) -> None:
-        """HashTable::init, reference hkv_hashtable.h:962-1042."""
+    def init(self, options: HashTableOptions, allocator=None) -> None:
+        """HashTable::init(options, allocator), reference hkv_hashtable.h
+        :962-1042. `allocator` (the reference's BaseAllocator) provides
+        alloc(memory_type, size, pinned_flags) -> address and
+        free(memory_type, address), and optionally alloc_async(memory_type,
+        size, stream) and free_async(memory_type, address, stream); every
+        allocation of the table comes from it (MEMORY_DEVICE / MEMORY_PINNED,
+        see hkv_allocator in include/hkv_b200.h). It must outlive the
+        table."""
         if self._h is not None:
             return
         h = ctypes.c_void_p()
         o = options._c()
-        _check(lib().hkv_table_create(ctypes.byref(o),
-                                      KEY_I64 if self.key_dtype == "int64" else KEY_U64,
-                                      VALUE_TYPES[self.value_dtype],
-                                      self.evict_strategy, ctypes.byref(h)))
+        kt = KEY_I64 if self.key_dtype == "int64" else KEY_U64
+        if allocator is None:
+            _check(lib().hkv_table_create(ctypes.byref(o), kt, VALUE_TYPES[self.value_dtype],
+                                          self.evict_strategy, ctypes.byref(h)))
+        else:
+            self._alloc_cbs = _allocator_callbacks(allocator)  # kept alive with the table
+            _check(lib().hkv_table_create_with_allocator(
+                ctypes.byref(o), kt, VALUE_TYPES[self.value_dtype], self.evict_strategy,
+                ctypes.byref(self._alloc_cbs), ctypes.byref(h)))
         self._h = h.value
         self._options = options
 
@@ -500,6 +619,26 @@ class HashTable:
 
     def reserve(self, new_capacity, stream=None):
         _check(lib().hkv_reserve(self._h, new_capacity, _stream(stream)))
+
+    def set_max_capacity(self, new_max_capacity):
+        """set_max_capacity, reference hkv_hashtable.h:2955-2977."""
+        _check(lib().hkv_set_max_capacity(self._h, new_max_capacity))
+
+    def raw_view(self):
+        """Addresses of the raw table arrays (hkv_table_view): keys, scores,
+        digests, sizes, slices (device array of slice addresses), capacity,
+        num_buckets, slice_shift, value_bytes."""
+
+        class _View(ctypes.Structure):
+            _fields_ = [("keys", _P), ("scores", _P), ("digests", _P), ("sizes", _P),
+                        ("slices", _P), ("capacity", _U64), ("num_buckets", _U64),
+                        ("bucket_size", ctypes.c_uint32), ("slice_shift", ctypes.c_uint32),
+                        ("value_bytes", ctypes.c_uint32), ("dim", ctypes.c_uint32),
+                        ("reclaim_digest", ctypes.c_uint8)]
+
+        v = _View()
+        _check(lib().hkv_table_get_view(self._h, ctypes.byref(v)))
+        return {f: getattr(v, f) for f, _ in _View._fields_}
 
     def set_global_epoch(self, epoch: int):
         _check(lib().hkv_set_global_epoch(self._h, epoch))

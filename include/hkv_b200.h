@@ -100,8 +100,60 @@ const char* hkv_last_error(void);
 int hkv_table_create(const hkv_options* options, int key_type, int value_type,
                      int evict_strategy, hkv_table** out);
 
+/* ---- caller-provided allocator ----------------------------------------------
+ * init(options, BaseAllocator*) (hkv_hashtable.h:962-978) takes every
+ * allocation of the table from the caller's allocator, whose interface is
+ * allocator.h:27-158: alloc / alloc_async / free / free_async of a
+ * MemoryType (Device = HBM, Pinned = page-locked host memory, Host). Here the
+ * allocator is a struct of callbacks on the caller's `user` object; each
+ * returns 0 on success and non-zero on failure (the call then fails with
+ * HKV_ERR_CUDA). The table takes from it:
+ *  - Device: its bucket arrays (keys, scores, digests, sizes), the value
+ *    slices that fit max_hbm_for_vectors, the slice table and its counters,
+ *    at creation and at each doubling (reserve, auto-grow), the old arrays
+ *    freed after the rehash;
+ *  - Pinned, pinned_flags = cudaHostAllocMapped | cudaHostAllocPortable (3):
+ *    the value slices beyond max_hbm_for_vectors; the memory must be mapped
+ *    into the device address space (cudaHostGetDevicePointer must accept it);
+ *  - Pinned, pinned_flags = 0: host staging for size() and save / load;
+ *  - Device through alloc_async / free_async on the call's stream: per-call
+ *    scratch (the duplicate-key merge, rehash rows, save / load chunks). When
+ *    alloc_async / free_async are NULL, alloc is used, and free after the
+ *    stream has drained.
+ * Everything is freed through the same allocator by hkv_table_destroy. The
+ * allocator must outlive the table. */
+typedef enum {
+  HKV_MEMORY_DEVICE = 0,
+  HKV_MEMORY_PINNED = 1,
+  HKV_MEMORY_HOST = 2
+} hkv_memory_type;
+
+typedef struct {
+  void* user;
+  int (*alloc)(void* user, int memory_type, void** ptr, size_t size,
+               unsigned int pinned_flags);
+  int (*alloc_async)(void* user, int memory_type, void** ptr, size_t size,
+                     void* stream);
+  int (*free)(void* user, int memory_type, void* ptr);
+  int (*free_async)(void* user, int memory_type, void* ptr, void* stream);
+} hkv_allocator;
+
+/* HashTable::init(options, allocator), hkv_hashtable.h:962-978: as
+ * hkv_table_create, with every allocation from `allocator` (copied; NULL
+ * means the CUDA runtime, as hkv_table_create). */
+int hkv_table_create_with_allocator(const hkv_options* options, int key_type,
+                                    int value_type, int evict_strategy,
+                                    const hkv_allocator* allocator,
+                                    hkv_table** out);
+
 /* HashTable::~HashTable, hkv_hashtable.h:944-960. */
 int hkv_table_destroy(hkv_table* table);
+
+/* set_max_capacity, hkv_hashtable.h:2955-2977: a power of two (else
+ * HKV_ERR_INVALID) below the current capacity is ignored; otherwise it
+ * becomes the capacity reserve and auto-grow may reach, and the table may
+ * grow again. */
+int hkv_set_max_capacity(hkv_table* table, size_t new_max_capacity);
 
 /* insert_or_assign, hkv_hashtable.h:1077-1215. */
 int hkv_insert_or_assign(hkv_table* table, size_t n, const void* keys,
@@ -339,9 +391,13 @@ int hkv_load_files(hkv_table* table, const char* keys_path,
  * scratch, so a call takes at most 16384 keys; larger calls fail with
  * HKV_ERR_INVALID. The table
  * never grows in this call: a batch that would trigger auto-grow fails with
- * HKV_ERR_RUNTIME (call hkv_reserve first). The first call on a device looks
- * up the array's device address, so make that first call before any stream
- * capture. Every call in the process shares the array and finds the last
+ * HKV_ERR_RUNTIME (call hkv_reserve first); to tell, a call on a table that
+ * has not reached its maximum capacity reads the sampled bucket sizes back
+ * and so synchronises `stream`, as the reference's auto-grow check does. The
+ * first call on a device looks up the array's device address, so make that
+ * first call before any stream capture; the address is kept for the life of
+ * the process, so after cudaDeviceReset on that device this entry point must
+ * not be called again. Every call in the process shares the array and finds the last
  * call's contents in it (what must start empty is cleared at the start of
  * each call); calls that overlap on the GPU race on it and must be ordered
  * by the caller. Results are those of hkv_find_or_insert with

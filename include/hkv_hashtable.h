@@ -24,6 +24,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 #include <type_traits>
@@ -111,6 +112,134 @@ constexpr int value_code() {
 inline void* st(cudaStream_t s) { return reinterpret_cast<void*>(s); }
 }  // namespace detail
 
+/* MemoryType and BaseAllocator, reference allocator.h:27-84: the interface
+ * of a caller's allocator, from which HashTable::init(options, allocator)
+ * takes every allocation of the table (see hkv_allocator in hkv_b200.h for
+ * which memory comes from where). Pinned memory given for value rows must be
+ * mapped into the device address space (pinned_flags carries
+ * cudaHostAllocMapped). The allocator must outlive the table. */
+enum MemoryType {
+  Device,  // HBM
+  Pinned,  // page-locked host memory
+  Host,    // host memory
+};
+
+class BaseAllocator {
+ public:
+  BaseAllocator(const BaseAllocator&) = delete;
+  BaseAllocator(BaseAllocator&&) = delete;
+  BaseAllocator& operator=(const BaseAllocator&) = delete;
+  BaseAllocator& operator=(BaseAllocator&&) = delete;
+  BaseAllocator() = default;
+  virtual ~BaseAllocator() = default;
+
+  virtual void alloc(const MemoryType type, void** ptr, size_t size,
+                     unsigned int pinned_flags = 0) = 0;
+  virtual void alloc_async(const MemoryType type, void** ptr, size_t size,
+                           cudaStream_t stream) = 0;
+  virtual void free(const MemoryType type, void* ptr) = 0;
+  virtual void free_async(const MemoryType type, void* ptr, cudaStream_t stream) = 0;
+
+  template <typename T>
+  void alloc(const MemoryType type, T** ptr, size_t size, unsigned int pinned_flags = 0) {
+    void* p = nullptr;
+    alloc(type, &p, size, pinned_flags);
+    *ptr = static_cast<T*>(p);
+  }
+  template <typename T>
+  void alloc_async(const MemoryType type, T** ptr, size_t size, cudaStream_t stream) {
+    void* p = nullptr;
+    alloc_async(type, &p, size, stream);
+    *ptr = static_cast<T*>(p);
+  }
+};
+
+/* DefaultAllocator, reference allocator.h:86-158, on the CUDA runtime. */
+class DefaultAllocator : public virtual BaseAllocator {
+ public:
+  using BaseAllocator::alloc;
+  using BaseAllocator::alloc_async;
+  void alloc(const MemoryType type, void** ptr, size_t size,
+             unsigned int pinned_flags = 0) override {
+    switch (type) {
+      case Device:
+        detail::cuda(cudaMalloc(ptr, size));
+        break;
+      case Pinned:
+        detail::cuda(cudaHostAlloc(ptr, size, pinned_flags));
+        break;
+      case Host:
+        *ptr = std::malloc(size);
+        break;
+    }
+  }
+  void alloc_async(const MemoryType type, void** ptr, size_t size,
+                   cudaStream_t stream) override {
+    if (type != Device)
+      throw HkvException("[DefaultAllocator] alloc_async is only support for MemoryType::Device!");
+    detail::cuda(cudaMallocAsync(ptr, size, stream));
+  }
+  void free(const MemoryType type, void* ptr) override {
+    if (ptr == nullptr) return;
+    switch (type) {
+      case Device:
+        detail::cuda(cudaFree(ptr));
+        break;
+      case Pinned:
+        detail::cuda(cudaFreeHost(ptr));
+        break;
+      case Host:
+        std::free(ptr);
+        break;
+    }
+  }
+  void free_async(const MemoryType type, void* ptr, cudaStream_t stream) override {
+    if (ptr == nullptr) return;
+    if (type != Device)
+      throw HkvException("[DefaultAllocator] free_async is only support for MemoryType::Device!");
+    detail::cuda(cudaFreeAsync(ptr, stream));
+  }
+};
+
+namespace detail {
+/* hkv_allocator callbacks over a BaseAllocator: exceptions stay on this side
+ * of the C ABI and become a non-zero status. */
+inline int alloc_cb(void* u, int type, void** ptr, size_t size, unsigned int flags) {
+  try {
+    static_cast<BaseAllocator*>(u)->alloc(static_cast<MemoryType>(type), ptr, size, flags);
+    return 0;
+  } catch (...) {
+    return 1;
+  }
+}
+inline int alloc_async_cb(void* u, int type, void** ptr, size_t size, void* stream) {
+  try {
+    static_cast<BaseAllocator*>(u)->alloc_async(static_cast<MemoryType>(type), ptr, size,
+                                                static_cast<cudaStream_t>(stream));
+    return 0;
+  } catch (...) {
+    return 1;
+  }
+}
+inline int free_cb(void* u, int type, void* ptr) {
+  try {
+    static_cast<BaseAllocator*>(u)->free(static_cast<MemoryType>(type), ptr);
+    return 0;
+  } catch (...) {
+    return 1;
+  }
+}
+inline int free_async_cb(void* u, int type, void* ptr, void* stream) {
+  try {
+    static_cast<BaseAllocator*>(u)->free_async(static_cast<MemoryType>(type), ptr,
+                                               static_cast<cudaStream_t>(stream));
+    return 0;
+  } catch (...) {
+    return 1;
+  }
+}
+}  // namespace detail
+
 /* BaseKVFile / LocalKVFile, reference types.h:291-464: save() and load()
  * move (key, vector, score) tuples between the table and a file through
  * these. LocalKVFile keeps the reference's on-disk format: three files of
@@ -165,6 +294,109 @@ class LocalKVFile : public BaseKVFile<K, V, S> {
   std::FILE* fp_[3] = {nullptr, nullptr, nullptr};
 };
 
+/* HashTableBase<K, V, S>, reference hkv_hashtable.h:171-871: the abstract
+ * interface a caller may hold the table through. HashTable implements every
+ * method; assign with values, assign_values, find with missed keys and
+ * find_and_update are outside this build's scope and throw HkvException. */
+template <typename K, typename V, typename S = uint64_t>
+class HashTableBase {
+ public:
+  using size_type = size_t;
+  using key_type = K;
+  using value_type = V;
+  using score_type = S;
+  using allocator_type = BaseAllocator;
+
+  virtual ~HashTableBase() {}
+  virtual void init(const HashTableOptions& options, allocator_type* allocator = nullptr) = 0;
+  virtual void insert_or_assign(const size_type n, const key_type* keys,
+                                const value_type* values, const score_type* scores = nullptr,
+                                cudaStream_t stream = 0, bool unique_key = true,
+                                bool ignore_evict_strategy = false) = 0;
+  virtual void insert_and_evict(const size_type n, const key_type* keys,
+                                const value_type* values, const score_type* scores,
+                                key_type* evicted_keys, value_type* evicted_values,
+                                score_type* evicted_scores, size_type* d_evicted_counter,
+                                cudaStream_t stream = 0, bool unique_key = true,
+                                bool ignore_evict_strategy = false) = 0;
+  virtual size_type insert_and_evict(const size_type n, const key_type* keys,
+                                     const value_type* values, const score_type* scores,
+                                     key_type* evicted_keys, value_type* evicted_values,
+                                     score_type* evicted_scores, cudaStream_t stream = 0,
+                                     bool unique_key = true,
+                                     bool ignore_evict_strategy = false) = 0;
+  virtual void accum_or_assign(const size_type n, const key_type* keys,
+                               const value_type* value_or_deltas, const bool* accum_or_assigns,
+                               const score_type* scores = nullptr, cudaStream_t stream = 0,
+                               bool ignore_evict_strategy = false) = 0;
+  virtual void find_or_insert(const size_type n, const key_type* keys, value_type* values,
+                              score_type* scores = nullptr, cudaStream_t stream = 0,
+                              bool unique_key = true, bool ignore_evict_strategy = false) = 0;
+  virtual void find_or_insert(const size_type n, const key_type* keys, value_type** values,
+                              bool* founds, score_type* scores = nullptr,
+                              cudaStream_t stream = 0, bool unique_key = true,
+                              bool ignore_evict_strategy = false,
+                              key_type** locked_key_ptrs = nullptr) = 0;
+  virtual void lock_keys(const size_type n, key_type const* keys, key_type** locked_key_ptrs,
+                         bool* succeededs = nullptr, cudaStream_t stream = 0,
+                         score_type const* scores = nullptr) = 0;
+  virtual void unlock_keys(const size_type n, key_type** locked_key_ptrs,
+                           const key_type* keys, bool* succeededs = nullptr,
+                           cudaStream_t stream = 0) = 0;
+  virtual void assign(const size_type n, const key_type* keys, const value_type* values,
+                      const score_type* scores = nullptr, cudaStream_t stream = 0,
+                      bool unique_key = true) = 0;
+  virtual void assign_scores(const size_type n, const key_type* keys,
+                             const score_type* scores = nullptr, cudaStream_t stream = 0,
+                             bool unique_key = true) = 0;
+  virtual void assign(const size_type n, const key_type* keys,
+                      const score_type* scores = nullptr, cudaStream_t stream = 0,
+                      bool unique_key = true) = 0;
+  virtual void assign_values(const size_type n, const key_type* keys,
+                             const value_type* values, cudaStream_t stream = 0,
+                             bool unique_key = true) = 0;
+  virtual void find(const size_type n, const key_type* keys, value_type* values,
+                    bool* founds, score_type* scores = nullptr,
+                    cudaStream_t stream = 0) const = 0;
+  virtual void find(const size_type n, const key_type* keys, value_type* values,
+                    key_type* missed_keys, int* missed_indices, int* missed_size,
+                    score_type* scores = nullptr, cudaStream_t stream = 0) const = 0;
+  virtual void find(const size_type n, const key_type* keys, value_type** values,
+                    bool* founds, score_type* scores = nullptr, cudaStream_t stream = 0,
+                    bool unique_key = true) const = 0;
+  virtual void find_and_update(const size_type n, const key_type* keys, value_type** values,
+                               bool* founds, score_type* scores = nullptr,
+                               cudaStream_t stream = 0, bool unique_key = true) = 0;
+  virtual void contains(const size_type n, const key_type* keys, bool* founds,
+                        cudaStream_t stream = 0) const = 0;
+  virtual void erase(const size_type n, const key_type* keys, cudaStream_t stream = 0) = 0;
+  virtual void clear(cudaStream_t stream = 0) = 0;
+  virtual void export_batch(size_type n, const size_type offset, size_type* d_counter,
+                            key_type* keys, value_type* values,
+                            score_type* scores = nullptr,
+                            cudaStream_t stream = 0) const = 0;
+  virtual size_type export_batch(const size_type n, const size_type offset, key_type* keys,
+                                 value_type* values, score_type* scores = nullptr,
+                                 cudaStream_t stream = 0) const = 0;
+  virtual bool empty(cudaStream_t stream = 0) const = 0;
+  virtual size_type size(cudaStream_t stream = 0) const = 0;
+  virtual size_type capacity() const = 0;
+  virtual void reserve(const size_type new_capacity, cudaStream_t stream = 0) = 0;
+  virtual float load_factor(cudaStream_t stream = 0) const = 0;
+  virtual void set_max_capacity(size_type new_max_capacity) = 0;
+  virtual size_type dim() const noexcept = 0;
+  virtual size_type max_bucket_size() const noexcept = 0;
+  virtual size_type bucket_count() const noexcept = 0;
+  virtual bool is_pure_hbm_mode() const noexcept = 0;
+  virtual size_type save(BaseKVFile<K, V, S>* file,
+                         const size_t max_workspace_size = 1L * 1024 * 1024,
+                         cudaStream_t stream = 0) const = 0;
+  virtual size_type load(BaseKVFile<K, V, S>* file,
+                         const size_t max_workspace_size = 1L * 1024 * 1024,
+                         cudaStream_t stream = 0) = 0;
+  virtual void set_global_epoch(const uint64_t epoch) = 0;
+};
+
 /* HashTable<K, V, S, Strategy>, reference hkv_hashtable.h:895-3485.
  * K: uint64_t or int64_t; S: uint64_t; V: the element type of the vectors
  * (float, double, uint32_t, uint64_t, int8_t, or a 2-byte half type; for a
@@ -172,12 +404,13 @@ class LocalKVFile : public BaseKVFile<K, V, S> {
  * select bfloat16 arithmetic in accum_or_assign). */
 template <typename K, typename V, typename S = uint64_t,
           int Strategy = EvictStrategy::kLru>
-class HashTable {
+class HashTable : public HashTableBase<K, V, S> {
  public:
   using size_type = size_t;
   using key_type = K;
   using value_type = V;
   using score_type = S;
+  using allocator_type = BaseAllocator;
   static constexpr int evict_strategy = Strategy;
 
   HashTable() {
@@ -185,7 +418,7 @@ class HashTable {
                   "The key_type must be int64_t or uint64_t.");
     static_assert(std::is_same<S, uint64_t>::value, "The score_type must be uint64_t.");
   }
-  ~HashTable() {
+  ~HashTable() override {
     if (t_) hkv_table_destroy(t_);
   }
   HashTable(const HashTable&) = delete;
@@ -193,11 +426,10 @@ class HashTable {
   HashTable(HashTable&&) = delete;
   HashTable& operator=(HashTable&&) = delete;
 
-  /* init, reference hkv_hashtable.h:962-1042. An allocator argument is
-   * accepted for signature compatibility; memory is always cudaMalloc /
-   * cudaHostAlloc(Mapped). */
-  void init(const HashTableOptions& options, void* allocator = nullptr) {
-    (void)allocator;
+  /* init, reference hkv_hashtable.h:962-1042: every allocation of the table
+   * comes from `allocator` (the CUDA runtime when it is null), which must
+   * outlive the table. */
+  void init(const HashTableOptions& options, allocator_type* allocator = nullptr) override {
     if (t_) return;
     hkv_options o;
     hkv_options_init(&o);
@@ -220,9 +452,11 @@ class HashTable {
     if (sizeof(V) == 2) vc = HKV_VALUE_BF16;
 #endif
     if (vc < 0) throw HkvException("unsupported value_type");
-    detail::check(hkv_table_create(
+    hkv_allocator a{allocator, &detail::alloc_cb, &detail::alloc_async_cb, &detail::free_cb,
+                    &detail::free_async_cb};
+    detail::check(hkv_table_create_with_allocator(
         &o, std::is_same<K, int64_t>::value ? HKV_KEY_I64 : HKV_KEY_U64, vc,
-        Strategy, &t_));
+        Strategy, allocator != nullptr ? &a : nullptr, &t_));
     options_ = options;
   }
 
@@ -399,15 +633,37 @@ class HashTable {
 
   size_type dim() const noexcept { return options_.dim; }
   size_type max_bucket_size() const noexcept { return options_.max_bucket_size; }
-  size_type bucket_count() const {
+  size_type bucket_count() const noexcept override {
     size_t c = 0;
-    detail::check(hkv_bucket_count(t_, &c));
-    return c;
+    return hkv_bucket_count(t_, &c) == HKV_OK ? c : 0;
   }
-  bool is_pure_hbm_mode() const {
+  bool is_pure_hbm_mode() const noexcept override {
     bool b = true;
-    detail::check(hkv_is_pure_hbm_mode(t_, &b));
-    return b;
+    return hkv_is_pure_hbm_mode(t_, &b) == HKV_OK ? b : true;
+  }
+
+  /* set_max_capacity, reference hkv_hashtable.h:2955-2977. */
+  void set_max_capacity(size_type new_max_capacity) override {
+    detail::check(hkv_set_max_capacity(t_, new_max_capacity));
+    if (new_max_capacity >= capacity()) options_.max_capacity = new_max_capacity;
+  }
+
+  /* Outside this build's scope (HashTableBase declares them): each throws. */
+  void assign(const size_type, const key_type*, const value_type*,
+              const score_type* = nullptr, cudaStream_t = 0, bool = true) override {
+    throw HkvException("assign with values is not supported by this build");
+  }
+  void assign_values(const size_type, const key_type*, const value_type*,
+                     cudaStream_t = 0, bool = true) override {
+    throw HkvException("assign_values is not supported by this build");
+  }
+  void find(const size_type, const key_type*, value_type*, key_type*, int*, int*,
+            score_type* = nullptr, cudaStream_t = 0) const override {
+    throw HkvException("find with missed keys is not supported by this build");
+  }
+  void find_and_update(const size_type, const key_type*, value_type**, bool*,
+                       score_type* = nullptr, cudaStream_t = 0, bool = true) override {
+    throw HkvException("find_and_update is not supported by this build");
   }
 
 #ifdef __CUDACC__

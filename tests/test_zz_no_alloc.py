@@ -76,3 +76,31 @@ def test_noalloc_rejects_batches_beyond_its_scratch():
     assert wide.size() == 3
     # the repeated key reads back its first occurrence's row
     assert torch.equal(vals[2], first[0]) and torch.equal(vals[[0, 1, 3]], first[[0, 1, 3]])
+
+
+def test_noalloc_refuses_a_batch_that_would_grow_the_table_and_takes_no_memory():
+    """A table that can still grow: a batch that would trigger auto-grow fails
+    (growing allocates) and leaves the capacity alone; calls that fit take no
+    device memory (free device memory is the same before and after, once the
+    first call has looked up the array's address)."""
+    cap, dim = 128 * 64, 32
+    t = make_table(cap, dim=dim, strategy=H.EvictStrategy.kLfu, max_capacity=4 * cap)
+    rng = np.random.default_rng(77)
+    base = np.unique(rng.integers(1, 1 << 62, 4200, dtype=np.uint64))[:4000]
+    k0, v0, s0 = dev(base), dev(rng.standard_normal((4000, dim)).astype(np.float32)), \
+        dev(np.ones(4000, np.uint64))
+    t.find_or_insert_noalloc(2000, k0[:2000], v0[:2000], s0[:2000])
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    t.find_or_insert_noalloc(1800, k0[2000:3800], v0[2000:3800], s0[2000:3800])
+    t.find_or_insert_noalloc(200, k0[:200], v0[:200], s0[:200])  # hits (the load
+    # factor check counts them as if new: 3800 + 200 of 8192 slots)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
+    assert t.size() == 3800 and t.capacity() == cap
+    # 3800 / 8192 + 1000 / 8192 > max_load_factor 0.5: the reference would grow
+    more = dev(np.unique(rng.integers(1 << 62, 1 << 63, 1100, dtype=np.uint64))[:1000])
+    with pytest.raises(RuntimeError):
+        t.find_or_insert_noalloc(1000, more, v0[:1000], s0[:1000])
+    assert t.capacity() == cap and t.size() == 3800
+    t.check_device_error()
