@@ -324,6 +324,15 @@ def run_gpu(args):
     e2e_line = e2e(table, finds, inserts, vals, warm + steps, n_e2e, dist, device)
     log("e2e done")
     local.check_device_error()  # a lock or peer wait that ran out fails the run
+    # the headline table goes before config 5's leg (its shard takes ~70 GB)
+    if world > 1:
+        table.close()
+    del table, local, finds, inserts, vals, founds, out_vals
+    torch.cuda.empty_cache()
+    cfg5 = None
+    if not args.no_config5:
+        cfg5 = config5_leg(rank, world, dist, device)
+        log("config 5 leg done")
     keys_total = 2 * BATCH * steps * world
     value = keys_total / (ms * 1e-3) / 1e9
 
@@ -369,6 +378,8 @@ def run_gpu(args):
         result["clocks"] = clocks
         result["gpu_launches"] = launches
         result["e2e"] = e2e_line
+        if cfg5 is not None:
+            result["config5"] = cfg5
         if world == 1 and args.save_load:
             result["save_load"] = save_load_times(device)
             log("save/load done")
@@ -378,7 +389,6 @@ def run_gpu(args):
                 log("cpu baseline done")
         print(json.dumps(result), flush=True)
     if world > 1:
-        table.close()
         dist.barrier()
         dist.destroy_process_group()
 
@@ -461,9 +471,56 @@ def e2e(table, finds, inserts, vals, first, steps, dist=None, device=None):
         ms = float(tt.item())
     h2d = BATCH * 8 * 2 + BATCH * VALUE_BYTES
     d2h = BATCH * VALUE_BYTES + BATCH
+    peak = pinned_copy_peaks()
+    up = h2d * steps / (ms * 1e-3) / 1e9
+    down = d2h * steps / (ms * 1e-3) / 1e9
     return {"value": round(2 * BATCH * steps * world / (ms * 1e-3) / 1e9, 4), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
-            "pipelined": "H2D / table calls / D2H on three streams, two buffer sets"}
+            "pipelined": "H2D / table calls / D2H on three streams, two buffer sets",
+            # the step's copies against the host link's measured peak (both
+            # directions at once, as the pipeline runs them)
+            "host_link": {"h2d_gbs": round(up, 1), "d2h_gbs": round(down, 1),
+                          "peak_h2d_gbs": peak["h2d_duplex"], "peak_d2h_gbs": peak["d2h_duplex"],
+                          "frac": round(max(up / peak["h2d_duplex"], down / peak["d2h_duplex"]), 4),
+                          "peak_kind": "measured pinned cudaMemcpyAsync, 256 MiB each way "
+                                       "concurrently on two streams"}}
+
+
+def pinned_copy_peaks(nbytes=256 << 20, reps=3):
+    """Pinned host <-> device cudaMemcpyAsync bandwidth on this GPU (best of
+    `reps`): each direction alone, and both at once on two streams."""
+    import torch
+
+    hb = [torch.empty(nbytes, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+    db = [torch.empty(nbytes, dtype=torch.uint8, device="cuda") for _ in range(2)]
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    out = {"h2d": 0.0, "d2h": 0.0, "h2d_duplex": 0.0, "d2h_duplex": 0.0}
+    for _ in range(reps):
+        for name, dst, src in (("h2d", db[0], hb[0]), ("d2h", hb[1], db[1])):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            a.record()
+            dst.copy_(src, non_blocking=True)
+            b.record()
+            torch.cuda.synchronize()
+            out[name] = max(out[name], nbytes / (a.elapsed_time(b) * 1e-3) / 1e9)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        torch.cuda.synchronize()
+        ev[0].record(s1)
+        ev[2].record(s2)
+        with torch.cuda.stream(s1):
+            db[0].copy_(hb[0], non_blocking=True)
+        with torch.cuda.stream(s2):
+            hb[1].copy_(db[1], non_blocking=True)
+        ev[1].record(s1)
+        ev[3].record(s2)
+        torch.cuda.synchronize()
+        out["h2d_duplex"] = max(out["h2d_duplex"],
+                                nbytes / (ev[0].elapsed_time(ev[1]) * 1e-3) / 1e9)
+        out["d2h_duplex"] = max(out["d2h_duplex"],
+                                nbytes / (ev[2].elapsed_time(ev[3]) * 1e-3) / 1e9)
+    return {k: round(v, 1) for k, v in out.items()}
 
 
 def save_load_times(device, capacity=8 << 20):
@@ -716,6 +773,10 @@ def run_hybrid(args):
     founds = torch.zeros(n, dtype=torch.bool, device=dev)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    # the host link's own peak (pinned cudaMemcpyAsync each way): the
+    # roofline denominator for rows in host memory
+    link = pinned_copy_peaks()
+    log(f"pinned copy peak: {link} GB/s")
     res = {}
     for name in ("find", "insert_or_assign"):
         def call(i):
@@ -735,11 +796,18 @@ def run_hybrid(args):
         # rows that cross the host link per call: found rows of host buckets
         # (find), inserted rows of host buckets (insert, 1 - 1/16 of uniform keys)
         host_frac = (n - nh) / n if name == "find" else 1 - hbm_buckets / view.num_buckets
-        link = n * host_frac * vb
+        link_bytes = n * host_frac * vb
+        gbs = link_bytes / (ms * 1e-3) / 1e9
+        peak = link["h2d"] if name == "find" else link["d2h"]  # rows read / written
         res[name] = {"ms_per_call": round(ms, 4), "bkvs": round(n / (ms * 1e-3) / 1e9, 4),
                      "host_rows_fraction": round(host_frac, 4),
-                     "host_link_bytes_per_call": int(link),
-                     "host_link_gbs": round(link / (ms * 1e-3) / 1e9, 1)}
+                     "host_link_bytes_per_call": int(link_bytes),
+                     "host_link_gbs": round(gbs, 1),
+                     "roofline": {"bound": "host link", "achieved": round(gbs, 1),
+                                  "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
+                                  "peak_kind": "measured pinned cudaMemcpyAsync, " +
+                                               ("host to device" if name == "find"
+                                                else "device to host")}}
         log(f"hybrid {name}: {ms * 1000:.1f} us per call, {res[name]['host_link_gbs']} GB/s "
             f"over the host link")
     hit = float(founds.float().mean().item())
@@ -748,7 +816,8 @@ def run_hybrid(args):
                       "capacity": cap, "max_hbm_for_vectors": hbm,
                       "hbm_bucket_fraction": round(hbm_buckets / view.num_buckets, 4),
                       "load_factor": 0.75, "batch": n, "steps": steps, "warmup": warm,
-                      "find_hit_rate_last_call": round(hit, 4), "ops": res}), flush=True)
+                      "find_hit_rate_last_call": round(hit, 4), "pinned_copy_gbs": link,
+                      "ops": res}), flush=True)
 
 
 # --------------------------------------------------------------------------
@@ -766,6 +835,113 @@ def zipf_ids(n, s, universe, gen, device):
     a = 1.0 - s
     x = ((universe ** a - 1.0) * u + 1.0) ** (1.0 / a)
     return (x.floor().to(torch.int64) - 1).clamp_(0, universe - 1)
+
+
+def config5_leg(rank, world, dist, device, steps=5, warm=2):
+    """BASELINE config 5 on this run's GPUs: one table shard of 256 Mi slots
+    per GPU (dim 64, kLfu, scores 1..16), prefilled with as many keys as
+    slots; each step every GPU submits 8 Mi power-law keys (a seeded
+    Zipf(1.1) stand-in over 2^30 ids, repeats merged: unique_key = false) to
+    find_or_insert, routed to their owner GPUs; then every shard is dumped
+    with export_batch. Times are device times (CUDA events, max over
+    ranks)."""
+    import torch
+
+    import hkv_b200 as H
+
+    cap, dim, batch, s_exp = 256 << 20, 64, 8 << 20, 1.1
+    strat = H.EvictStrategy.kLfu
+    opts = H.HashTableOptions(init_capacity=cap, max_capacity=cap,
+                              max_hbm_for_vectors=cap * dim * 8, dim=dim, max_load_factor=1.0)
+    if world == 1:
+        table = local = H.HashTable(strat)
+        table.init(opts)
+    else:
+        uid = [H.ShardedHashTable.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        opts.device_id = torch.cuda.current_device()
+        table = H.ShardedHashTable(opts, rank, world, uid[0], strat, max_batch=batch)
+        local = H.HashTable.borrow(H.lib().hkv_sharded_local(table._h), strat)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(5150 + rank)
+    chunk = 4 << 20
+    pv = torch.randn((chunk, dim), device=device)
+    for st in range(0, cap * world, chunk):  # each shard keeps the keys it owns
+        k = keys_from_counters((1 << 44) + st, chunk, device)
+        if world > 1:
+            k = k[owner_t(k, world) == rank]
+        sc = torch.randint(1, 17, (k.numel(),), generator=gen, device=device)
+        local.insert_or_assign(k.numel(), k, pv[:k.numel()], sc)
+    del pv
+    torch.cuda.synchronize()
+    lf = local.load_factor()
+    nb = 3  # batches cycled through the steps
+    batches = []
+    for _ in range(nb):
+        k = key_of(zipf_ids(batch, s_exp, 1 << 30, gen, device))
+        batches.append((k, torch.randn((batch, dim), generator=gen, device=device),
+                        torch.randint(1, 17, (batch,), generator=gen, device=device)))
+    uniq = sum(int(torch.unique(b[0]).numel()) for b in batches) / (nb * batch)
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        k, v, sc = batches[i % nb]
+        table.find_or_insert(batch, k, v, sc, unique_key=False)
+
+    for i in range(warm):
+        step(i)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        step(warm + i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    local.check_device_error()
+    del batches
+    # dump every shard: export_batch over all of its slots in 16 Mi pieces
+    piece = 16 << 20
+    ek = torch.empty(piece, dtype=torch.int64, device=device)
+    ev = torch.empty((piece, dim), device=device)
+    es = torch.empty(piece, dtype=torch.int64, device=device)
+    cnt = torch.zeros(1, dtype=torch.int64, device=device)
+    live = local.size()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0.record(stream)
+    for off in range(0, cap, piece):
+        local.export_batch(piece, off, ek, ev, es, d_counter=cnt)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ems = e0.elapsed_time(e1)
+    tt = torch.tensor([ms, ems], device=device)
+    lt = torch.tensor([live], dtype=torch.int64, device=device)
+    if dist:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        dist.all_reduce(lt)
+    ms, ems = (float(x) for x in tt.tolist())
+    if world > 1:
+        table.close()
+    del table, local, ek, ev, es
+    torch.cuda.empty_cache()
+    keys = batch * steps * world
+    return {"workload": "BASELINE config 5: 256 Mi slots per GPU, dim 64, kLfu (scores "
+                        "1..16), 8 Mi keys per GPU per step (seeded Zipf(1.1) stand-in over "
+                        "2^30 ids, repeats merged), find_or_insert routed to the owner "
+                        "shard; then export_batch of every shard",
+            "n_gpus": world, "load_factor_before": round(lf, 4),
+            "distinct_fraction": round(uniq, 4), "steps": steps, "warmup": warm,
+            "batches_cycled": nb,
+            "find_or_insert_bkvs": round(keys / (ms * 1e-3) / 1e9, 4),
+            "find_or_insert_bkvs_per_gpu": round(keys / world / (ms * 1e-3) / 1e9, 4),
+            "ms_per_step": round(ms / steps, 4),
+            "export_ms": round(ems, 3), "exported_keys": int(lt.item()),
+            "export_slots_per_ns": round(cap * world / (ems * 1e-3) / 1e9, 3)}
 
 
 def run_zipf(args):
@@ -848,6 +1024,55 @@ def run_zipf(args):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms = float(tt.item())
     local.check_device_error()
+    ie = None
+    if world == 1:
+        # BASELINE config 3's second leg: insert_and_evict of the same batches
+        # (repeats merged), the epoch still advancing every 10 steps, the
+        # evicted and refused tuples collected each step
+        ek = torch.empty(batch, dtype=torch.int64, device=device)
+        ev = torch.empty((batch, dim), device=device)
+        es = torch.empty(batch, dtype=torch.int64, device=device)
+        cnt = torch.zeros(1, dtype=torch.int64, device=device)
+        outs = []
+        # fresh batches from the same power law: the hot keys are resident,
+        # the tail brings keys that must evict (or be refused)
+        for b in range(nb):
+            ids = zipf_ids(batch, s_exp, 1 << 30, gen, device)
+            batches[b] = (key_of(ids), torch.randn((batch, dim), generator=gen, device=device),
+                          torch.randint(1, 17, (batch,), generator=gen, device=device))
+
+        def evict_step(i):
+            nonlocal epoch
+            k, v, sc = batches[i % nb]
+            cnt.zero_()
+            table.insert_and_evict(batch, k, v, sc, ek, ev, es, cnt, unique_key=False)
+            if strat == H.EvictStrategy.kEpochLfu and (i + 1) % 10 == 0:
+                epoch += 1
+                local.set_global_epoch(epoch)
+
+        for i in range(warm):
+            evict_step(i)
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for i in range(steps):
+            evict_step(warm + i)
+            outs.append(cnt.clone())
+        t1.record(stream)
+        torch.cuda.synchronize()
+        ie_ms = t0.elapsed_time(t1)
+        # the last step: every input key is in the table or among its outputs
+        k = batches[(warm + steps - 1) % nb][0]
+        found = torch.zeros(batch, dtype=torch.bool, device=device)
+        table.contains(batch, k, found)
+        c = int(outs[-1].item())
+        reported = torch.isin(k, ek[:c])
+        ok = bool((found | reported).all().item())
+        local.check_device_error()
+        ie = {"bkvs": round(batch * steps / (ie_ms * 1e-3) / 1e9, 4),
+              "ms_per_step": round(ie_ms / steps, 4),
+              "outputs_per_step": round(sum(int(o.item()) for o in outs) / steps, 1),
+              "every_input_present_or_reported": ok}
+        log(f"insert_and_evict leg: {ie}")
     if rank == 0:
         print(json.dumps({
             "metric": "B-KV/s for find_or_insert of Zipf keys with repeats (unique_key=false)",
@@ -863,7 +1088,8 @@ def run_zipf(args):
                         "per GPU per step, Zipf(1.1) stand-in, sharded peer transport"),
                        "capacity_per_gpu": cap, "dim": dim, "batch_per_gpu": batch,
                        "distinct_fraction": round(uniq, 4),
-                       "batches_cycled": nb}}), flush=True)
+                       "batches_cycled": nb},
+            "insert_and_evict": ie}), flush=True)
     if world > 1:
         table.close()
         dist.barrier()
@@ -987,6 +1213,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-config5", action="store_true",
+                    help="skip BASELINE config 5's leg (sharded find_or_insert of "
+                         "power-law keys, then a dump of every shard)")
     ap.add_argument("--save-load", action="store_true",
                     help="also time save/load (LocalKVFile files in a temporary "
                          "directory) of an 8 Mi-slot table; adds a save_load key")

@@ -1054,13 +1054,16 @@ __device__ __forceinline__ bool tile_erase(const TableView& t, const TileW<W>& t
     const M rest = held & ~erase & (static_cast<M>(0xF) << (g0 - lo));
     erase |= rest & (~rest + 1);
   }
+  // The key word turns into the tombstone in one CAS; score, digest and size
+  // follow with plain writes, as the reference's erase writes them
+  // (remove_kernel.h:96-101, no lock): no other operation of this launch
+  // touches the slot, and the next launch sees every write.
   for (M e = erase; e; e &= e - 1) {
     const uint64_t s = l.bkt * kBucket + lo + low_bit(e);
-    if (cas_acquire_u64(t.keys + s, key, kLockedKey) == key) {
+    if (cas_u64(t.keys + s, key, kReclaimKey) == key) {
       t.scores[s] = 0;
       t.digests[s] = kReclaimDigest;
       atomicSub(t.sizes + l.bkt, 1);
-      store_release_u64(t.keys + s, kReclaimKey);
     }
   }
   return tile.ballot(held != 0) || !tile.ballot(busy);
@@ -1396,19 +1399,28 @@ __global__ void __launch_bounds__(256, 8)
         }
       } else if (todo) {
         const int p = tile_locate_existing<kWalkStop>(t, tile, l, key);
-        bool got = false;
-        const uint64_t s = l.bkt * kBucket + (p < 0 ? 0 : p);
-        if (p >= 0 && tile.lane == 0)
-          got = cas_acquire_u64(t.keys + s, key, kLockedKey) == key;
-        if (tile.shfl(got, 0)) {
+        if (p >= 0) {
+          // The score of the slot found, as the reference updates it
+          // (assign_scores_kernel_with_filter.h:65-140, no lock): no other
+          // operation of this launch moves the key. The Lfu rules add, so a
+          // key repeated in the batch takes every addition: an atomic add,
+          // or for EpochLfu's saturating low half a CAS loop.
           if (tile.lane == 0) {
+            uint64_t* sp = t.scores + l.bkt * kBucket + p;
             uint64_t ns;
-            // only the Lfu rules read the stored score
-            const uint64_t old =
-                (S == kLfu || S == kEpochLfu) ? ld_relaxed_u64(t.scores + s) : 0;
-            if (score_without_missed<S>(old, scores, i, epoch, clk, &ns))
-              t.scores[s] = ns;
-            store_release_u64(t.keys + s, key);
+            if constexpr (S == kLfu) {
+              if (scores != nullptr)
+                atomicAdd(reinterpret_cast<unsigned long long*>(sp), scores[i]);
+            } else if constexpr (S == kEpochLfu) {
+              uint64_t old = ld_relaxed_u64(sp);
+              while (score_without_missed<S>(old, scores, i, epoch, clk, &ns)) {
+                const uint64_t prev = cas_u64(sp, old, ns);
+                if (prev == old) break;
+                old = prev;
+              }
+            } else if (score_without_missed<S>(0, scores, i, epoch, clk, &ns)) {
+              *sp = ns;
+            }
           }
           todo = false;
         } else if (p == -1) {

@@ -380,6 +380,43 @@ def test_reserve_exact_layout():
     assert g.contains(present).all()
 
 
+def test_reserve_into_host_slices():
+    """BASELINE config 4's reserve, scaled down: max_hbm_for_vectors holds
+    exactly the first value slice, so the slices a doubling appends go to
+    mapped pinned host memory (table.h:143-184, :360-377;
+    hkv_hashtable.h:2873-2935), low bucket indices keep HBM. The layout after
+    reserve equals the oracle's slot for slot, values included, and every
+    key reads back its row through find."""
+    rng = np.random.default_rng(133)
+    cap, dim = 128 * 64, 4
+    bucket_bytes = 128 * dim * 4
+    g = GpuOps(make_table(cap, dim=dim, max_capacity=cap * 8, max_load_factor=1.0,
+                          max_hbm=bucket_bytes * 64), dim)
+    assert g.t.is_pure_hbm_mode()  # the initial buckets fit
+    pre = random_keys(rng, int(cap * 0.95))
+    vals = rng.random((len(pre), dim)).astype(np.float32)
+    g.insert_or_assign(pre, vals, rng.integers(1, 1 << 30, len(pre)).astype(np.uint64))
+    o = oracle_from_gpu(g, cap, dim, O.CUSTOMIZED, max_capacity=cap * 8, lf=1.0)
+    present = pre[g.contains(pre)]
+    g.t.reserve(cap * 4)
+    o.reserve(cap * 4)
+    assert g.t.capacity() == o.capacity() == cap * 4
+    assert not g.t.is_pure_hbm_mode()  # the appended slices are host memory
+    assert_same_state(g, o)
+    got, f, _ = g.find(present)
+    ov, of, _ = o.find(present)
+    assert f.all() and of.all() and (got == ov).all()
+    # rows in host slices are written through too
+    newk = random_keys(rng, 2000, lo=1 << 62)
+    nv = rng.random((2000, dim)).astype(np.float32)
+    g.insert_or_assign(newk, nv, np.full(2000, 1 << 31, np.uint64))
+    o.insert_or_assign(newk, nv, np.full(2000, 1 << 31, np.uint64))
+    gk, gs, _, gz, gvals = g.t.get_state()
+    ok, os_, _, oz, ovals = o.get_state()
+    assert (gz == oz).all()  # several keys per bucket: compare the live set, not slots
+    assert live_set(gk, gs, gvals) == live_set(ok, os_, ovals)
+
+
 def test_reserve_full_table():
     """tests/test_reserve.cpp:193-300: a full table doubles to LF 0.5 with
     every key still found."""
