@@ -162,8 +162,10 @@ __device__ __forceinline__ int find_probe(const TableView& t, const TileW<W>& ti
   // (find_utils.h:58-66)
   const uint32_t p = best & 0xFF;
   bool stop = false;
-  for (M e = empt & linear_below<M, kD>(lo, l.pos, walk_bound(p, l.pos)); e; e &= e - 1)
-    if (__ldg(bk + lo + low_bit(e)) == kEmptyKey) stop = true;
+  if (empt) {  // none at all in a full bucket
+    for (M e = empt & linear_below<M, kD>(lo, l.pos, walk_bound(p, l.pos)); e; e &= e - 1)
+      if (__ldg(bk + lo + low_bit(e)) == kEmptyKey) stop = true;
+  }
   return tile.ballot(stop) ? -1 : static_cast<int>(p);
 }
 
