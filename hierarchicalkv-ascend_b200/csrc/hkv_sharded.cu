@@ -438,11 +438,15 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// finish in owner order (find, and find_or_insert of a batch without merged
-// duplicates): block b reads owner b % world's result region for this rank
-// front to back, so the tiles of a warp read consecutive rows and tails over
-// NVLink; inv (written by route) maps each position back to its input.
-// sent[o] is the number of keys this rank routed to owner o.
+// finish in owner order: block b reads owner b % world's result region for
+// this rank front to back, so the tiles of a warp read consecutive rows and
+// tails over NVLink; inv (written by route) maps each position back to its
+// input (find, and find_or_insert of a batch without merged duplicates) or
+// to its representative u (find_or_insert of a merged batch: the row goes to
+// the representative's first occurrence row_of[u] and the status to
+// ustatus[u], so each distinct key crosses NVLink once and its later
+// occurrences copy it locally afterwards). sent[o] is the number of keys
+// this rank routed to owner o.
 template <int VW>
 __global__ void __launch_bounds__(256)
     p2p_finish_ordered_kernel(int mode, PeerBases peers, WinLayout lay, uint32_t world,
@@ -450,7 +454,9 @@ __global__ void __launch_bounds__(256)
                               const uint32_t* __restrict__ sent,
                               const uint32_t* __restrict__ inv,
                               uint8_t* __restrict__ values, bool* __restrict__ founds,
-                              uint64_t* __restrict__ scores) {
+                              uint64_t* __restrict__ scores,
+                              const uint32_t* __restrict__ row_of,
+                              uint8_t* __restrict__ ustatus) {
   wait_flags(peers.base[self], lay.done, world, epoch, false, nullptr, err, 302);
   __syncthreads();
   using V = typename VecOf<VW>::T;
@@ -478,13 +484,15 @@ __global__ void __launch_bounds__(256)
     uint4 tail = make_uint4(0, 0, 0, 0);
     if (tile.lane == 0)
       tail = __ldcg(reinterpret_cast<const uint4*>(ob + lay.res_tail) + slot);
-    const uint64_t i = invo[pos];
+    const uint32_t u = invo[pos];
+    const uint64_t i = row_of != nullptr ? row_of[u] : u;
     const uint32_t f = tile.shfl(tail.z & 0xFFu, 0);
     const bool ok = mode == 0 ? f != 0 : (f != kRefused && f != kIllegal && f != kTimedOut);
     const uint64_t sc = (uint64_t{tail.y} << 32) | tail.x;
     if (tile.lane == 0) {
       if (founds != nullptr) founds[i] = ok;
       if (ok && scores != nullptr) scores[i] = sc;
+      if (ustatus != nullptr) ustatus[u] = static_cast<uint8_t>(f);
     }
     if (ok && values != nullptr) {
       V* dp = reinterpret_cast<V*>(values + i * vb);
@@ -865,16 +873,28 @@ class ShardedImpl {
     const int vwf = (kind == 2 || values == nullptr)
                         ? 16
                         : local_->value_width({values, win_ + lay_.res_rows});
-    if (kind == 0 || (kind == 1 && uid_of == nullptr)) {
+    if (kind == 0 || kind == 1) {
       // a multiple of world blocks: block b reads owner b % world's results
       const uint64_t per_owner = std::max<uint64_t>(
           1, std::min<uint64_t>(ceil_div(std::max<uint64_t>(n, 1) * 4, 256),
                                 sm_count_ * 16ull / world_));
       const int gf = static_cast<int>(per_owner * world_);
+      // a merged find_or_insert batch: representatives first, then their
+      // later occurrences from the local copies (kIllegal until an owner's
+      // status arrives: an overflowed representative is skipped)
+      uint8_t* ustatus = nullptr;
+      if (uid_of != nullptr) {
+        ustatus = ws.get<uint8_t>(std::max<size_t>(n, 1));
+        CUDA_TRY(cudaMemsetAsync(ustatus, kIllegal, n, s));
+      }
       SHARD_DISPATCH_VW(vwf, p2p_finish_ordered_kernel<VW><<<gf, 256, 0, counted(s)>>>(
                                  kind, peers_, lay_, world_, me, epoch_, err, d_sent_,
                                  d_inv_, values, kind == 0 ? founds : nullptr,
-                                 kind == 0 ? scores : nullptr));
+                                 kind == 0 ? scores : nullptr, row_of, ustatus));
+      if (uid_of != nullptr) {
+        CUDA_TRY(cudaGetLastError());
+        local_->scatter_found_rows(values, uid_of, row_of, ustatus, n, s);
+      }
     } else {
       const int gf = static_cast<int>(std::max<uint64_t>(
           1, std::min<uint64_t>(ceil_div(std::max<uint64_t>(n, 1) * 4, 256),

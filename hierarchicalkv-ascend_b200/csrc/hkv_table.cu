@@ -862,6 +862,16 @@ void TableImpl::upsert_counted(int mode, size_t n_bound, const uint32_t* dn,
          nullptr, nullptr, s, true, false, status, dn, status_stride);
 }
 
+void TableImpl::scatter_found_rows(uint8_t* values, const uint32_t* uid_of,
+                                   const uint32_t* rep_first, const uint8_t* ustatus,
+                                   size_t n, cudaStream_t s) {
+  if (n == 0 || values == nullptr) return;
+  const int vw = value_width({values});
+  DISPATCH_VW(vw, scatter_found_rows_kernel<VW><<<tile_grid(n), 256, 0, counted(s)>>>(
+                      values, uid_of, rep_first, ustatus, n, value_bytes_));
+  CUDA_TRY(cudaGetLastError());
+}
+
 void TableImpl::contains(size_t n, const uint64_t* keys, bool* founds,
                          cudaStream_t s) {
   if (n == 0) return;
@@ -1828,8 +1838,7 @@ int hkv_dim(hkv_table* table, size_t* out) {
 int hkv_max_bucket_size(hkv_table* table, size_t* out) {
   HKV_API_BEGIN
   HKV_TABLE(table);
-  (void)T;
-  *out = hkvb::kBucket;
+  *out = T->bucket_count() > 0 ? hkvb::kBucket : 0;
   HKV_API_END
 }
 

@@ -258,6 +258,12 @@ class TableImpl {
                       const uint64_t* keys, const uint8_t* values_in,
                       uint8_t* values_io, const uint64_t* scores,
                       uint8_t* status, uint32_t status_stride, cudaStream_t s);
+  // find_or_insert of a merged batch, last step: every later occurrence of
+  // a key copies the row its representative left at rep_first[uid_of[i]]
+  // (skipped where ustatus says the key was refused)
+  void scatter_found_rows(uint8_t* values, const uint32_t* uid_of,
+                          const uint32_t* rep_first, const uint8_t* ustatus, size_t n,
+                          cudaStream_t s);
   // find* / find_or_insert*: addresses of the value rows instead of copies
   void find_ptr(size_t n, const uint64_t* keys, uint8_t** value_ptrs, bool* founds,
                 uint64_t* scores, cudaStream_t s);
