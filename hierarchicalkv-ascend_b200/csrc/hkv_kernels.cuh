@@ -279,8 +279,10 @@ __global__ void __launch_bounds__(256, HKV_FIND_MIN_BLOCKS)
 
 struct UpsertArgs {
   const uint64_t* keys;
-  const uint8_t* values_in;  // insert_or_assign / insert_and_evict input rows
-  uint8_t* values_io;        // find_or_insert rows (in on a miss, out on a hit)
+  const uint8_t* values_in;  // insert_or_assign / insert_and_evict input rows;
+                             // find_or_insert: input rows apart (optional)
+  uint8_t* values_io;        // find_or_insert rows (in on a miss, out on a hit;
+                             // out on a hit only when values_in is set)
   const uint64_t* scores;    // input scores (nullable per strategy)
   uint64_t n;
   uint64_t epoch;
@@ -482,6 +484,8 @@ __device__ __forceinline__ void upsert_locked(const TableView& t,
   if constexpr (Mode == kModeFindOrInsert) {
     if (res == kDuplicate)
       copy_row<VW>(a.values_io + key_row(a, i) * vb, row, vb, tile.lane, W);
+    else if (a.values_in != nullptr)  // input rows apart, read only here
+      copy_row<VW>(row, a.values_in + key_row(a, i) * vb, vb, tile.lane, W);
     else
       head.store(row, a.values_io + key_row(a, i) * vb, nv, tile.lane);
   } else if constexpr (Mode != kModeFindOrInsertPtr) {
@@ -812,7 +816,12 @@ __device__ __forceinline__ void upsert_body(const TableView& t, const UpsertArgs
   const uint64_t n = a.dn != nullptr ? *a.dn : a.n;
   const uint32_t vb = t.value_bytes;
   const uint32_t nv = vb / VW;
-  const uint8_t* in_rows = Mode == kModeFindOrInsert ? a.values_io : a.values_in;
+  // find_or_insert with values_in set (the sharded owner: input rows in a
+  // peer's memory) reads an input row only for a key it inserts, and writes
+  // values_io only for a key it finds
+  const uint8_t* in_rows = Mode == kModeFindOrInsert
+                               ? (a.values_in != nullptr ? nullptr : a.values_io)
+                               : a.values_in;
   // keys are read one iteration ahead, the head of the input row before the
   // probe, so neither waits behind the bucket's round trips
   const uint64_t stride = nwarps * KPW;
@@ -855,7 +864,7 @@ __device__ __forceinline__ void upsert_body(const TableView& t, const UpsertArgs
     l.pos = 0;
     l.d4 = 0;
     if (have && !is_reserved(key)) {
-      if constexpr (Mode != kModeFindOrInsertPtr)
+      if (Mode != kModeFindOrInsertPtr && in_rows != nullptr)
         head.load(in_rows + key_row(a, i) * vb, nv, tile.lane);
       desired = desired_when_missed<S>(a.scores, i, a.epoch, clk);
       l = locate(t, key);
@@ -904,7 +913,7 @@ __device__ __forceinline__ void upsert_body(const TableView& t, const UpsertArgs
       key = next;
       if (i + stride < n) next = a.keys[i + stride];
       if (!is_reserved(key)) {
-        if constexpr (Mode != kModeFindOrInsertPtr)
+        if (Mode != kModeFindOrInsertPtr && in_rows != nullptr)
           head.load(in_rows + key_row(a, i) * vb, nv, tile.lane);
         desired = desired_when_missed<S>(a.scores, i, a.epoch, clk);
         l = locate(t, key);

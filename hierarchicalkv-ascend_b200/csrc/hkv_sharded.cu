@@ -226,7 +226,7 @@ __device__ __forceinline__ uint64_t* flag_at(uint8_t* base, uint64_t off,
 
 // route: sort this rank's keys by owner into its own send area. `keys` are
 // the batch keys (find, or distinct keys) or the merged representatives
-// (count *dm). where[u] = owner << 32 | position.
+// (count *dm); inv maps each send position back to its key.
 template <int VW>
 __global__ void __launch_bounds__(256)
     p2p_route_kernel(const uint64_t* __restrict__ keys,
@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(256)
                      const uint32_t* __restrict__ dm, uint64_t n,
                      uint32_t world, uint32_t self, PeerBases peers,
                      WinLayout lay, uint32_t* __restrict__ counters,
-                     uint64_t* __restrict__ where, uint32_t* __restrict__ inv,
+                     uint32_t* __restrict__ inv,
                      uint32_t* __restrict__ sent, uint64_t epoch,
                      int* __restrict__ err) {
   __shared__ uint32_t cnt[kMaxWorld];
@@ -272,11 +272,9 @@ __global__ void __launch_bounds__(256)
         slot = uint64_t{d} * lay.M + pos;
         skeys[slot] = key;
         if (scores != nullptr) sscores[slot] = scores[u];
-        where[u] = (uint64_t{d} << 32) | pos;
         inv[slot] = static_cast<uint32_t>(u);
       } else {
         atomicOr(err, kErrPeerOverflow);
-        where[u] = ~uint64_t{0};
       }
     }
     if (rows != nullptr) {
@@ -347,26 +345,6 @@ __global__ void p2p_wait_arrive_kernel(uint8_t* self_base, WinLayout lay,
   wait_flags(self_base, lay.arrive, world, epoch, true, counts, err, 301);
 }
 
-// serve, find_or_insert: bring each requester's input rows into the local
-// result area, where the table kernel then leaves found rows in place
-template <int VW>
-__global__ void __launch_bounds__(256)
-    p2p_pull_rows_kernel(PeerBases peers, WinLayout lay, uint32_t world,
-                         uint32_t self, const uint32_t* __restrict__ counts) {
-  const Tile tile;
-  const uint32_t vb = lay.vb;
-  const uint64_t ntiles = uint64_t{gridDim.x} * (blockDim.x / kTile);
-  const uint64_t t0 = (uint64_t{blockIdx.x} * blockDim.x + threadIdx.x) / kTile;
-  uint8_t* res = peers.base[self] + lay.res_rows;
-  for (uint32_t src = 0; src < world; src++) {
-    const uint64_t c = min(static_cast<uint64_t>(counts[src]), lay.M);
-    const uint8_t* in = peers.base[src] + lay.snd_rows + uint64_t{self} * lay.M * vb;
-    uint8_t* out = res + uint64_t{src} * lay.M * vb;
-    for (uint64_t j = t0; j < c; j += ntiles)
-      copy_row<VW>(out + j * vb, in + j * vb, vb, tile.lane, kTile);
-  }
-}
-
 // serve: every result of this epoch is in place (written by the kernels
 // before this one in stream order); tell each requester with a system-scope
 // release
@@ -377,76 +355,26 @@ __global__ void p2p_signal_done_kernel(PeerBases peers, WinLayout lay,
     st_release_sys_u64(flag_at(peers.base[w], lay.done, self), epoch);
 }
 
-// finish: wait for every owner, then read the results from the owners'
-// result areas. mode 0: find (rows, flags, scores of found keys, per
-// input); mode 1: find_or_insert (rows of found or inserted representatives,
-// to every occurrence through uid_of); mode 2: insert_or_assign (wait only).
-// A 4-lane tile per key issues the flag, score and row loads together, so a
-// key costs one NVLink round trip; rows longer than the registers hold (16
-// vectors) finish with a second pass.
-template <int VW>
-__global__ void __launch_bounds__(256)
-    p2p_finish_kernel(int mode, PeerBases peers, WinLayout lay, uint32_t world,
-                      uint32_t self, uint64_t epoch, int* err, uint64_t n,
-                      const uint64_t* __restrict__ where,
-                      const uint32_t* __restrict__ uid_of,
-                      uint8_t* __restrict__ values, bool* __restrict__ founds,
-                      uint64_t* __restrict__ scores) {
-  wait_flags(peers.base[self], lay.done, world, epoch, false, nullptr, err, 302);
-  __syncthreads();
-  if (mode == 2) return;
-  using V = typename VecOf<VW>::T;
-  constexpr uint32_t W = 4;
-  constexpr uint32_t kHead = 4;  // row vectors per lane held in registers
-  const TileW<W> tile;
-  const uint32_t vb = lay.vb;
-  const uint32_t nv = vb / VW;
-  const uint64_t ntiles = uint64_t{gridDim.x} * (blockDim.x / W);
-  for (uint64_t i = (uint64_t{blockIdx.x} * blockDim.x + threadIdx.x) / W; i < n;
-       i += ntiles) {
-    const uint32_t u = uid_of != nullptr ? uid_of[i] : static_cast<uint32_t>(i);
-    const uint64_t w = u != 0xFFFFFFFFu ? where[u] : ~uint64_t{0};
-    if (w == ~uint64_t{0}) {
-      if (tile.lane == 0 && founds != nullptr) founds[i] = false;
-      continue;
-    }
-    const uint8_t* ob = peers.base[static_cast<uint32_t>(w >> 32)];
-    const uint64_t slot = uint64_t{self} * lay.M + (w & 0xFFFFFFFFu);
-    const V* sp = reinterpret_cast<const V*>(ob + lay.res_rows + slot * vb);
-    V head[kHead];
-#pragma unroll
-    for (uint32_t h = 0; h < kHead; h++)
-      if (values != nullptr && tile.lane + h * W < nv) head[h] = __ldcg(sp + tile.lane + h * W);
-    // tail: find -> score (8 bytes) | found flag; find_or_insert -> status
-    uint4 tail = make_uint4(0, 0, 0, 0);
-    if (tile.lane == 0)
-      tail = __ldcg(reinterpret_cast<const uint4*>(ob + lay.res_tail) + slot);
-    const uint32_t f = tile.shfl(tail.z & 0xFFu, 0);
-    const bool ok = mode == 0 ? f != 0 : (f != kRefused && f != kIllegal && f != kTimedOut);
-    const uint64_t sc = (uint64_t{tail.y} << 32) | tail.x;
-    if (tile.lane == 0) {
-      if (founds != nullptr) founds[i] = ok;
-      if (ok && scores != nullptr) scores[i] = sc;
-    }
-    if (ok && values != nullptr) {
-      V* dp = reinterpret_cast<V*>(values + i * vb);
-#pragma unroll
-      for (uint32_t h = 0; h < kHead; h++)
-        if (tile.lane + h * W < nv) dp[tile.lane + h * W] = head[h];
-      for (uint32_t v = tile.lane + kHead * W; v < nv; v += W) dp[v] = __ldcg(sp + v);
-    }
-  }
+// finish of insert_or_assign: nothing comes back but the owners' done flags
+__global__ void p2p_wait_done_kernel(uint8_t* self_base, WinLayout lay, uint32_t world,
+                                     uint64_t epoch, int* err) {
+  wait_flags(self_base, lay.done, world, epoch, false, nullptr, err, 302);
 }
 
-// finish in owner order: block b reads owner b % world's result region for
-// this rank front to back, so the tiles of a warp read consecutive rows and
-// tails over NVLink; inv (written by route) maps each position back to its
-// input (find, and find_or_insert of a batch without merged duplicates) or
-// to its representative u (find_or_insert of a merged batch: the row goes to
-// the representative's first occurrence row_of[u] and the status to
-// ustatus[u], so each distinct key crosses NVLink once and its later
-// occurrences copy it locally afterwards). sent[o] is the number of keys
-// this rank routed to owner o.
+// finish: wait for every owner, then read the results in owner order. Block
+// b reads owner b % world's result region for this rank front to back, so
+// the tiles of a warp read consecutive rows and tails over NVLink; inv
+// (written by route) maps each position back to its input (find, and
+// find_or_insert of a batch without merged duplicates) or to its
+// representative u (find_or_insert of a merged batch: the row goes to the
+// representative's first occurrence row_of[u] and the status to ustatus[u],
+// so each distinct key crosses NVLink once and its later occurrences copy it
+// locally afterwards). A 4-lane tile per key issues the flag, score and row
+// loads together, so a key costs one NVLink round trip. mode 0: find (rows,
+// flags and scores of found keys); mode 1: find_or_insert, rows of the keys
+// the owner found (an inserted key's row is the caller's own input row,
+// already in place). sent[o] is the number of keys this rank routed to
+// owner o.
 template <int VW>
 __global__ void __launch_bounds__(256)
     p2p_finish_ordered_kernel(int mode, PeerBases peers, WinLayout lay, uint32_t world,
@@ -494,7 +422,7 @@ __global__ void __launch_bounds__(256)
       if (ok && scores != nullptr) scores[i] = sc;
       if (ustatus != nullptr) ustatus[u] = static_cast<uint8_t>(f);
     }
-    if (ok && values != nullptr) {
+    if ((mode == 0 ? ok : f == kDuplicate) && values != nullptr) {
       V* dp = reinterpret_cast<V*>(values + i * vb);
 #pragma unroll
       for (uint32_t h = 0; h < kHead; h++)
@@ -539,7 +467,6 @@ class ShardedImpl {
         if (p != rank_ && peers_.base[p]) cudaIpcCloseMemHandle(peers_.base[p]);
       cudaFree(win_);
       cudaFree(d_route_counters_);
-      cudaFree(d_where_);
       cudaFree(d_inv_);
       cudaFree(d_sent_);
     }
@@ -736,7 +663,6 @@ class ShardedImpl {
                cudaSuccess &&
            cudaMemset(d_route_counters_, 0, (kMaxWorld + 1) * sizeof(uint32_t)) ==
                cudaSuccess &&
-           cudaMalloc(&d_where_, max_batch * sizeof(uint64_t)) == cudaSuccess &&
            cudaMalloc(&d_inv_, world_ * max_batch * sizeof(uint32_t)) == cudaSuccess &&
            cudaMalloc(&d_sent_, kMaxWorld * sizeof(uint32_t)) == cudaSuccess;
       cudaGetLastError();
@@ -750,12 +676,10 @@ class ShardedImpl {
       std::memset(&peers_, 0, sizeof peers_);
       cudaFree(win_);
       cudaFree(d_route_counters_);
-      cudaFree(d_where_);
       cudaFree(d_inv_);
       cudaFree(d_sent_);
       win_ = nullptr;
       d_route_counters_ = nullptr;
-      d_where_ = nullptr;
       d_inv_ = nullptr;
       d_sent_ = nullptr;
       return;
@@ -816,7 +740,7 @@ class ShardedImpl {
     SHARD_DISPATCH_VW(vw, p2p_route_kernel<VW><<<gr, 256, 0, counted(s)>>>(
                               rkeys, rscores, kind == 0 ? nullptr : values, row_of,
                               dm, n, world_, me, peers_, lay_, d_route_counters_,
-                              d_where_, d_inv_, d_sent_, epoch_, err));
+                              d_inv_, d_sent_, epoch_, err));
     CUDA_TRY(cudaGetLastError());
     // 2. serve what the requesters sorted for this rank
     uint32_t* counts = d_counts_;  // kMaxWorld entries, device
@@ -838,14 +762,6 @@ class ShardedImpl {
       }
       local_->find_segments(seg, static_cast<uint32_t>(world_), counts, M, s);
     } else {
-      if (kind == 1) {
-        const int vwr = local_->value_width({win_ + lay_.snd_rows});
-        const int g = static_cast<int>(std::min<uint64_t>(
-            ceil_div(M * kTile, 256), sm_count_ * 16ull));
-        SHARD_DISPATCH_VW(vwr, p2p_pull_rows_kernel<VW><<<g, 256, 0, counted(s)>>>(
-                                   peers_, lay_, world_, me, counts));
-        CUDA_TRY(cudaGetLastError());
-      }
       // one launch per requester, in rank order: a key sent by several
       // requesters is applied once per requester, in rank order (concurrent
       // inserts of one new key could both claim an empty slot)
@@ -856,8 +772,11 @@ class ShardedImpl {
         const uint64_t* sc =
             send_scores ? reinterpret_cast<const uint64_t*>(pb + lay_.snd_scores) + mine
                         : nullptr;
+        // find_or_insert reads a requester's input row only for a key it
+        // inserts, and leaves only found rows in the result area
         if (kind == 1)
-          local_->upsert_counted(kModeFindOrInsert, M, counts + src, k, nullptr,
+          local_->upsert_counted(kModeFindOrInsert, M, counts + src, k,
+                                 pb + lay_.snd_rows + mine * vb,
                                  win_ + lay_.res_rows + o * vb, sc,
                                  win_ + lay_.res_tail + o * 16 + 8, 16, s);
         else
@@ -896,13 +815,7 @@ class ShardedImpl {
         local_->scatter_found_rows(values, uid_of, row_of, ustatus, n, s);
       }
     } else {
-      const int gf = static_cast<int>(std::max<uint64_t>(
-          1, std::min<uint64_t>(ceil_div(std::max<uint64_t>(n, 1) * 4, 256),
-                                sm_count_ * 16ull)));
-      SHARD_DISPATCH_VW(vwf, p2p_finish_kernel<VW><<<gf, 256, 0, counted(s)>>>(
-                                 kind, peers_, lay_, world_, me, epoch_, err, n, d_where_,
-                                 kind == 1 ? uid_of : nullptr,
-                                 kind == 2 ? nullptr : values, nullptr, nullptr));
+      p2p_wait_done_kernel<<<1, kMaxWorld, 0, counted(s)>>>(win_, lay_, world_, epoch_, err);
     }
     CUDA_TRY(cudaGetLastError());
   }
@@ -935,7 +848,6 @@ class ShardedImpl {
   uint8_t* win_ = nullptr;
   PeerBases peers_{};
   uint32_t* d_route_counters_ = nullptr;
-  uint64_t* d_where_ = nullptr;  // owner << 32 | position of each routed key
   uint32_t* d_inv_ = nullptr;    // [world][max_batch] input of each routed position
   uint32_t* d_sent_ = nullptr;   // [kMaxWorld] keys routed to each owner
 };

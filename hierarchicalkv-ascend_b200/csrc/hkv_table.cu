@@ -516,7 +516,7 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
     a.scores = scores;
     a.n = n;
     a.dn = dn;
-    const int vw = value_width({rows, ev_values});
+    const int vw = value_width({rows, values_in, ev_values});
     const int grid = upsert_grid(n, mode);
     DISPATCH_STRATEGY(st, DISPATCH_VW(vw, {
       if (mode == kModeInsertOrAssign)
@@ -1242,7 +1242,6 @@ void TableImpl::find_or_insert_in_scratch(size_t n, const uint64_t* keys,
   UpsertArgs a;
   std::memset(&a, 0, sizeof a);
   a.keys = ukeys;
-  a.values_in = values;
   a.values_io = values;
   a.row_index = rep_first;
   a.scores = uscores;

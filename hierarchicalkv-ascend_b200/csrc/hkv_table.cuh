@@ -253,7 +253,8 @@ class TableImpl {
                      uint64_t bound, cudaStream_t s);
   // unique-key insert_or_assign / find_or_insert of up to n_bound keys
   // (device count *dn), per-key Occupy result at status[i * status_stride];
-  // no auto-grow
+  // no auto-grow. find_or_insert given values_in reads an input row there
+  // only for a key it inserts and writes values_io only for a key it finds.
   void upsert_counted(int mode, size_t n_bound, const uint32_t* dn,
                       const uint64_t* keys, const uint8_t* values_in,
                       uint8_t* values_io, const uint64_t* scores,

@@ -24,8 +24,8 @@ def _free_port():
     return p
 
 
-def _unique_batch(world, rank):
-    rng = np.random.default_rng(500)
+def _unique_batch(world, rank, seed=500):
+    rng = np.random.default_rng(seed)
     pool = np.unique(rng.integers(1, 1 << 62, 2500, dtype=np.uint64))
     out = []
     for r in range(world):
@@ -73,6 +73,16 @@ def _rank(rank, world, port, outdir, max_batch):
                        torch.from_numpy(uv).cuda(), torch.from_numpy(us.view(np.int64)).cuda(),
                        unique_key=True)
     torch.cuda.synchronize()
+    # unique-key find_or_insert: some keys new, some inserted just above; a
+    # key several ranks send is inserted by the lowest rank and found by the
+    # others
+    fk, fvals, fsc = _unique_batch(world, rank, seed=501)
+    fk[: len(fk) // 2] = uk[: len(fk) // 2]
+    fdv = torch.from_numpy(fvals).cuda()
+    t.find_or_insert(len(fk), torch.from_numpy(fk.view(np.int64)).cuda(), fdv,
+                     torch.from_numpy(fsc.view(np.int64)).cuda(), unique_key=True)
+    torch.cuda.synchronize()
+    fio = fdv.cpu().numpy()
     # collective find of every rank's first batch
     k0, _, _ = _batches(world, 0)[rank]
     fv = torch.zeros((len(k0), 4), device="cuda")
@@ -87,7 +97,7 @@ def _rank(rank, world, port, outdir, max_batch):
     np.savez(os.path.join(outdir, f"r{rank}.npz"), *results, keys=keys[live],
              scores=scores[live], fv=fv.cpu().numpy(), ff=ff.cpu().numpy(),
              fs=fs.cpu().numpy().view(np.uint64), total=np.array([total]),
-             own_ok=np.array([own_ok]), transport=np.array([transport]))
+             own_ok=np.array([own_ok]), transport=np.array([transport]), fio=fio)
     dist.barrier()
     t.close()
     dist.destroy_process_group()
@@ -110,7 +120,8 @@ def test_sharded_gpus_match_one_table(tmp_path, transport, max_batch):
     res = [np.load(tmp_path / f"r{r}.npz") for r in range(world)]
     assert all(str(r["transport"][0]) == transport for r in res)
     assert all(bool(r["own_ok"][0]) for r in res)
-    one = O.OracleTable(128 * 128, 128 * 128, dim=4, strategy=O.LFU)
+    # as many slots as the shards together: no bucket of either overflows
+    one = O.OracleTable(world * 128 * 64, world * 128 * 64, dim=4, strategy=O.LFU)
     for step in range(3):
         bs = _batches(world, step)
         out, _ = one.find_or_insert(np.concatenate([b[0] for b in bs]),
@@ -124,6 +135,19 @@ def test_sharded_gpus_match_one_table(tmp_path, transport, max_batch):
     ub = [_unique_batch(world, r) for r in range(world)]
     one.insert_or_assign(np.concatenate([b[0] for b in ub]), np.concatenate([b[1] for b in ub]),
                          np.concatenate([b[2] for b in ub]))
+    fb = []
+    for r in range(world):
+        fk, fvals, fsc = _unique_batch(world, r, seed=501)
+        fk[: len(fk) // 2] = ub[r][0][: len(fk) // 2]
+        fb.append((fk, fvals, fsc))
+    out, _ = one.find_or_insert(np.concatenate([b[0] for b in fb]),
+                                np.concatenate([b[1] for b in fb]),
+                                np.concatenate([b[2] for b in fb]))
+    off = 0
+    for r in range(world):
+        n = len(fb[r][0])
+        assert (res[r]["fio"] == out[off:off + n]).all(), ("unique find_or_insert", r)
+        off += n
     gk = np.concatenate([r["keys"] for r in res])
     gs = np.concatenate([r["scores"] for r in res])
     _, f, s = one.find(gk)
