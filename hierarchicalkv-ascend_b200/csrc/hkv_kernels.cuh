@@ -1610,30 +1610,31 @@ __global__ void __launch_bounds__(256)
 
 // ============================================================================
 // Rehash after the bucket count doubles (reference rehash_kernel.h:30-207).
-// One warp per old bucket. The bucket's keys and scores and its new
-// sibling's are staged in shared memory, where lane 0 runs the reference's
-// sequential algorithm (copy_key_to_new_bucket :30-67, then
-// defragmentation_for_rehash :77-135, then the scan starts again) on
-// metadata only, recording for every final slot which original slot its
-// entry came from. The reference restarts the scan at slot 0 after each
-// moved key. Entries the scan has passed stay in the bucket wherever the
-// back-shifts put them, so the scan resumes instead at the lowest slot that
-// received an entry not yet passed (a flag per slot travels with its entry)
-// -- the same decisions, without the quadratic rescan. The
-// value rows then move in parallel: rows bound for the new bucket straight
-// from their old slots, rows that change slot inside the old bucket through
-// the warp's scratch rows. The final layout is the reference's, slot for
-// slot.
+// One warp per old bucket. The reference scans the bucket from slot 0, moves
+// the first key whose new bucket differs (copy_key_to_new_bucket :30-67:
+// first EMPTY slot of the new bucket from the key's start position,
+// cyclically), back-shifts the entries behind the hole
+// (defragmentation_for_rehash :77-135: the first entry before the next
+// EMPTY_KEY that may move into the hole moves, and the hole follows it), and
+// restarts at slot 0. Every restart finds the lowest slot holding a key that
+// must move, so that is the order here. The warp replays it on metadata:
+// slot s belongs to lane s % 32, which keeps the slot's start position, its
+// EMPTY_KEY flag and its must-move flag in registers; each step is a warp
+// minimum (redux) over the lanes' candidates -- the next key to move, the
+// distance to the next EMPTY_KEY after the hole, the nearest entry that may
+// fill it -- and lane 0 moves the key, score and original slot in shared
+// memory. The value rows then move in parallel: rows bound for the new
+// bucket straight from their old slots, rows that change slot inside the old
+// bucket through the warp's scratch rows. The final layout is the
+// reference's, slot for slot.
 // ============================================================================
 struct RehashStage {
   uint64_t okeys[kBucket];
   uint64_t oscores[kBucket];
   uint64_t nkeys[kBucket];
   uint64_t nscores[kBucket];
-  uint8_t ohome[kBucket];
   uint8_t osrc[kBucket];  // original slot of the entry now at q (old bucket)
   uint8_t nsrc[kBucket];  // original slot of the entry now at q (new bucket)
-  uint8_t seen[kBucket];  // the entry now at q was passed by the scan
 };
 
 // Copies, for every q < kBucket with pick(q), the row of slot src(q) of
@@ -1678,6 +1679,21 @@ __device__ __forceinline__ uint32_t first_free_from(uint64_t m0, uint64_t m1, ui
   return kBucket;
 }
 
+// Slot entry of one lane's four slots (lane + 32 j): start position in the
+// bucket (7 bits), EMPTY_KEY flag, must-move flag.
+struct RehashSlots {
+  uint32_t home[4];
+  bool emp[4], mv[4];
+};
+
+// May the entry at cur (start position `start`) fill the hole at rm? The
+// reference's condition (rehash_kernel.h:101-103): start lies outside the
+// cyclic interval (rm, cur].
+__device__ __forceinline__ bool may_fill(uint32_t start, uint32_t rm, uint32_t cur) {
+  return (start <= rm && rm < cur) || (cur < start && start <= rm) ||
+         (rm < cur && cur < start);
+}
+
 template <int VW>
 __global__ void __launch_bounds__(256)
     rehash_kernel(TableView t, uint64_t old_nb, uint8_t* __restrict__ scratch) {
@@ -1689,77 +1705,117 @@ __global__ void __launch_bounds__(256)
   const uint64_t gw = blockIdx.x * (uint64_t)(blockDim.x / 32) + wi;
   uint8_t* rows = scratch + gw * kBucket * t.value_bytes;  // this warp's scratch rows
   const uint64_t new_cap = t.capacity;  // power of two after doubling
+  constexpr uint32_t kNone = 0xFFu;
   for (uint64_t b = gw; b < old_nb; b += nwarps) {
     const uint64_t nbk = b + old_nb;
-    for (uint32_t q = lane; q < kBucket; q += 32) {
+    RehashSlots r;
+#pragma unroll
+    for (uint32_t j = 0; j < 4; j++) {
+      const uint32_t q = lane + 32 * j;
       const uint64_t k = t.keys[b * kBucket + q];
       st.okeys[q] = k;
       st.oscores[q] = t.scores[b * kBucket + q];
       st.nkeys[q] = kEmptyKey;
       st.nscores[q] = 0;
-      st.ohome[q] = static_cast<uint8_t>(murmur3(k) & (kBucket - 1));
       st.osrc[q] = static_cast<uint8_t>(q);
       st.nsrc[q] = static_cast<uint8_t>(q);
-      st.seen[q] = 0;
+      const uint64_t h = murmur3(k);
+      r.home[j] = static_cast<uint32_t>(h & (kBucket - 1));
+      r.emp[j] = k == kEmptyKey;
+      r.mv[j] = k != kEmptyKey && k != kReclaimKey && ((h & (new_cap - 1)) >> kBucketShift) != b;
     }
     __syncwarp();
     int32_t moved = 0, removed = 0;
-    if (lane == 0) {
-      uint64_t nocc0 = 0, nocc1 = 0;  // occupied slots of the new bucket
-      uint32_t kp = 0;
-      while (kp < kBucket) {
-        const uint64_t k = st.okeys[kp];
-        if (k == kEmptyKey || k == kReclaimKey) {
-          st.seen[kp] = 1;
-          kp++;
-          continue;
+    uint64_t nocc0 = 0, nocc1 = 0;  // occupied slots of the new bucket (warp-uniform)
+    while (true) {
+      // the lowest slot holding a key that must move
+      uint32_t mine = kNone;
+#pragma unroll
+      for (uint32_t j = 0; j < 4; j++)
+        if (r.mv[j]) mine = min(mine, lane + 32 * j);
+      const uint32_t q = __reduce_min_sync(0xFFFFFFFFu, mine);
+      if (q == kNone) break;
+      const uint32_t qj = q >> 5;
+      uint32_t hsel = 0;
+#pragma unroll
+      for (uint32_t j = 0; j < 4; j++)
+        if (j == qj) hsel = r.home[j];
+      // the new start position: new capacity >= kBucket, so the key's low
+      // hash bits are its start position in either bucket
+      const uint32_t npos = __shfl_sync(0xFFFFFFFFu, hsel, q & 31);
+      const uint32_t p = first_free_from(nocc0, nocc1, npos);
+      if (p < kBucket) {
+        if (p < 64)
+          nocc0 |= uint64_t{1} << p;
+        else
+          nocc1 |= uint64_t{1} << (p - 64);
+        if (lane == 0) {
+          st.nkeys[p] = st.okeys[q];
+          st.nscores[p] = st.oscores[q];
+          st.nsrc[p] = st.osrc[q];
         }
-        const uint64_t g = murmur3(k) & (new_cap - 1);
-        if ((g >> kBucketShift) == b) {
-          st.seen[kp] = 1;
-          kp++;
-          continue;
-        }
-        // copy_key_to_new_bucket: first EMPTY slot from the new position,
-        // cyclically (found in the occupancy mask instead of slot by slot)
-        const uint32_t npos = static_cast<uint32_t>(g & (kBucket - 1));
-        const uint32_t p = first_free_from(nocc0, nocc1, npos);
-        if (p < kBucket) {
-          st.nkeys[p] = k;
-          st.nscores[p] = st.oscores[kp];
-          st.nsrc[p] = st.osrc[kp];
-          if (p < 64)
-            nocc0 |= uint64_t{1} << p;
-          else
-            nocc1 |= uint64_t{1} << (p - 64);
-          moved++;
-        }
-        removed++;
-        st.okeys[kp] = kEmptyKey;
-        // defragmentation_for_rehash: shift later entries back into the hole
-        uint32_t resume = kp;
-        uint32_t rm = kp, off = 1;
-        while (off < kBucket) {
-          const uint32_t cur = (rm + off) & (kBucket - 1);
-          const uint64_t ck = st.okeys[cur];
-          if (ck == kEmptyKey) break;
-          const uint32_t start = st.ohome[cur];
-          if ((start <= rm && rm < cur) || (cur < start && start <= rm) ||
-              (rm < cur && cur < start)) {
-            st.okeys[rm] = ck;
-            st.oscores[rm] = st.oscores[cur];
-            st.ohome[rm] = st.ohome[cur];
-            st.osrc[rm] = st.osrc[cur];
-            st.seen[rm] = st.seen[cur];
-            st.okeys[cur] = kEmptyKey;
-            if (!st.seen[rm]) resume = min(resume, rm);  // not yet scanned: rescan from rm
-            rm = cur;
-            off = 1;
-          } else {
-            off++;
+        moved++;
+      }
+      removed++;
+      if (lane == 0) st.okeys[q] = kEmptyKey;
+      if (lane == (q & 31)) {
+#pragma unroll
+        for (uint32_t j = 0; j < 4; j++)
+          if (j == qj) {
+            r.emp[j] = true;
+            r.mv[j] = false;
           }
+      }
+      // back-shift behind the hole
+      uint32_t rm = q;
+      while (true) {
+        uint32_t e_l = kBucket;
+#pragma unroll
+        for (uint32_t j = 0; j < 4; j++) {
+          const uint32_t d = (lane + 32 * j - rm) & (kBucket - 1);
+          if (r.emp[j] && d != 0) e_l = min(e_l, d);
         }
-        kp = resume;
+        const uint32_t e = __reduce_min_sync(0xFFFFFFFFu, e_l);
+        uint32_t c_l = kNone;
+#pragma unroll
+        for (uint32_t j = 0; j < 4; j++) {
+          const uint32_t s = lane + 32 * j;
+          const uint32_t d = (s - rm) & (kBucket - 1);
+          if (!r.emp[j] && d != 0 && d < e && may_fill(r.home[j], rm, s)) c_l = min(c_l, d);
+        }
+        const uint32_t c = __reduce_min_sync(0xFFFFFFFFu, c_l);
+        if (c == kNone) break;
+        const uint32_t cur = (rm + c) & (kBucket - 1);
+        const uint32_t cj = cur >> 5, rj = rm >> 5;
+        uint32_t pk = 0;
+#pragma unroll
+        for (uint32_t j = 0; j < 4; j++)
+          if (j == cj) pk = r.home[j] | (r.mv[j] ? 0x100u : 0u);
+        pk = __shfl_sync(0xFFFFFFFFu, pk, cur & 31);
+        if (lane == (rm & 31)) {
+#pragma unroll
+          for (uint32_t j = 0; j < 4; j++)
+            if (j == rj) {
+              r.home[j] = pk & 0xFFu;
+              r.mv[j] = (pk & 0x100u) != 0;
+              r.emp[j] = false;
+            }
+        }
+        if (lane == (cur & 31)) {
+#pragma unroll
+          for (uint32_t j = 0; j < 4; j++)
+            if (j == cj) {
+              r.emp[j] = true;
+              r.mv[j] = false;
+            }
+        }
+        if (lane == 0) {
+          st.okeys[rm] = st.okeys[cur];
+          st.oscores[rm] = st.oscores[cur];
+          st.osrc[rm] = st.osrc[cur];
+          st.okeys[cur] = kEmptyKey;
+        }
+        rm = cur;
       }
     }
     __syncwarp();

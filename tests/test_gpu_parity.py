@@ -360,17 +360,19 @@ def test_export_batch_offsets_and_counter():
     assert int(d.item()) == 5000
 
 
-def test_reserve_exact_layout():
+@pytest.mark.parametrize("nb,erased", [(64, 300), (4096, 20000)])
+def test_reserve_exact_layout(nb, erased):
     """reserve doubles the buckets and rehashes with the reference's
     algorithm (rehash_kernel.h:30-207): the GPU layout after reserve equals
-    the oracle's slot for slot, from the same starting state."""
-    rng = np.random.default_rng(121)
-    cap, dim = 128 * 64, 4
+    the oracle's slot for slot, from the same starting state (reclaimed
+    slots of erased keys included)."""
+    rng = np.random.default_rng(121 + nb)
+    cap, dim = 128 * nb, 4
     g = GpuOps(make_table(cap, dim=dim, max_capacity=cap * 8, max_load_factor=1.0), dim)
     pre = random_keys(rng, int(cap * 0.9))
     g.insert_or_assign(pre, rng.random((len(pre), dim)).astype(np.float32),
                        rng.integers(1, 1 << 30, len(pre)).astype(np.uint64))
-    g.erase(pre[:300])
+    g.erase(pre[:erased])
     o = oracle_from_gpu(g, cap, dim, O.CUSTOMIZED, max_capacity=cap * 8, lf=1.0)
     present = pre[g.contains(pre)]  # the batch overfilled some buckets
     g.t.reserve(cap * 4)
