@@ -6,9 +6,11 @@ For them the library offers a find_or_insert for batches that may repeat
 keys whose scratch is one fixed device array instead of per-call
 allocations. This test calls it through the C ABI and checks that two calls
 in a row give exactly what the allocating entry point (hkv_find_or_insert
-with unique_key=false) gives on a twin table: the same returned values and
-the same table contents (every live key with its score and value, and every
-bucket's size; integer and byte work, so the comparison is exact). Slot
+with unique_key=false) gives on a twin table, and what the CPU oracle's
+find_or_insert (oracle/hkv_oracle.c, one key after another as the reference
+processes a batch) gives: the same returned values and the same table
+contents (every live key with its score and value, and every bucket's size;
+integer and byte work, so the comparison is exact). Slot
 positions inside a bucket are not compared: when several keys of a batch
 land in one bucket, which of them takes which free slot depends on thread
 timing in either entry point. It lives in its own file, collected last, and
@@ -19,6 +21,7 @@ import pytest
 import torch
 
 import hkv_b200 as H
+import hkv_oracle as O
 from hkv_gpu import dev, host, make_table
 from hkv_testutil import live_set
 
@@ -37,6 +40,7 @@ def test_noalloc_matches_allocating_entry_point_on_two_calls():
     cap, dim = 128 * 512, 32
     ref = make_table(cap, dim=dim, strategy=H.EvictStrategy.kLfu)
     nal = make_table(cap, dim=dim, strategy=H.EvictStrategy.kLfu)
+    ora = O.OracleTable(cap, cap, dim=dim, strategy=O.LFU)
     pool = np.unique(rng.integers(1, 1 << 62, 9000, dtype=np.uint64))
     for call in range(2):
         # call 0 inserts; call 1 mixes hits on call 0's keys with new keys
@@ -48,11 +52,17 @@ def test_noalloc_matches_allocating_entry_point_on_two_calls():
         nal.find_or_insert_noalloc(len(keys), dev(keys), out_nal, dev(scores))
         torch.cuda.synchronize()
         assert torch.equal(out_ref, out_nal), f"returned values differ on call {call}"
+        out_ora, _ = ora.find_or_insert(keys, vals, scores)
+        assert (host(out_nal) == out_ora).all(), f"values differ from the oracle on call {call}"
         rk, rs, _, rz, rv = ref.get_state()
         nk, ns, _, nz, nv = nal.get_state()
         assert (rz == nz).all(), f"bucket sizes differ on call {call}"
         assert live_set(rk, rs, rv) == live_set(nk, ns, nv), \
             f"table contents differ on call {call}"
+        ok, os_, _, oz, ov = ora.get_state()
+        assert (oz == nz).all(), f"bucket sizes differ from the oracle on call {call}"
+        assert live_set(ok, os_, ov) == live_set(nk, ns, nv), \
+            f"table contents differ from the oracle on call {call}"
         nal.check_device_error()
     assert ref.size() == nal.size() > 0
 
