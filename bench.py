@@ -250,6 +250,40 @@ def prepare_batches(steps, rank, world, total_prefill, device, seed, capacity):
     return finds, inserts, vals
 
 
+def kernel_timeline(step, n, dist, rank, world, label):
+    """Per-kernel device time of n calls of step(i) on this rank (torch
+    profiler, CUPTI activity records), printed by every rank in rank order as
+    one JSON line each. Diagnostics only: a profiled run is never a bench
+    value."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for i in range(n):
+            step(i)
+        torch.cuda.synchronize()
+    acc = {}
+    for e in prof.events():
+        if e.device_type.name != "CUDA":
+            continue
+        name = e.name.replace("void ", "").replace("hkvb::", "")
+        name = name.replace("(anonymous namespace)::", "").split("(")[0][:80]
+        c, t = acc.get(name, (0, 0.0))
+        acc[name] = (c + 1, t + e.device_time_total)
+    rows = sorted(acc.items(), key=lambda kv: -kv[1][1])
+    line = {"timeline": label, "rank": rank, "world": world, "calls": n,
+            "us_per_call": {k: round(t / n, 1) for k, (c, t) in rows},
+            "launches_per_call": {k: round(c / n, 2) for k, (c, t) in rows}}
+    for r in range(world):
+        if r == rank:
+            print(json.dumps(line), flush=True)
+        if dist:
+            dist.barrier()
+
+
 def run_gpu(args):
     import numpy as np
     import torch
@@ -288,6 +322,23 @@ def run_gpu(args):
         step(i)
     torch.cuda.synchronize()
     log("warmup done")
+    if args.timeline:
+        kernel_timeline(lambda i: table.find(BATCH, finds[warm + i], out_vals,
+                                             founds[warm + i]),
+                        steps, dist, rank, world, "config 2 find")
+        kernel_timeline(lambda i: table.insert_or_assign(BATCH, inserts[warm + i],
+                                                         vals[warm + i], unique_key=True),
+                        steps, dist, rank, world, "config 2 insert_or_assign")
+        if world > 1:
+            table.close()
+        del table, local, finds, inserts, vals, founds, out_vals
+        torch.cuda.empty_cache()
+        if not args.no_config5:
+            config5_leg(rank, world, dist, device, timeline=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if dist:
         dist.barrier()
     sampler = ClockSampler(local_rank)
@@ -837,7 +888,7 @@ def zipf_ids(n, s, universe, gen, device):
     return (x.floor().to(torch.int64) - 1).clamp_(0, universe - 1)
 
 
-def config5_leg(rank, world, dist, device, steps=5, warm=2):
+def config5_leg(rank, world, dist, device, steps=5, warm=2, timeline=False):
     """BASELINE config 5 on this run's GPUs: one table shard of 256 Mi slots
     per GPU (dim 64, kLfu, scores 1..16), prefilled with as many keys as
     slots; each step every GPU submits 8 Mi power-law keys (a seeded
@@ -891,6 +942,12 @@ def config5_leg(rank, world, dist, device, steps=5, warm=2):
     for i in range(warm):
         step(i)
     torch.cuda.synchronize()
+    if timeline:
+        kernel_timeline(lambda i: step(warm + i), steps, dist, rank, world,
+                        "config 5 find_or_insert")
+        if world > 1:
+            table.close()
+        return None
     if dist:
         dist.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
@@ -1219,6 +1276,11 @@ def main():
     ap.add_argument("--save-load", action="store_true",
                     help="also time save/load (LocalKVFile files in a temporary "
                          "directory) of an 8 Mi-slot table; adds a save_load key")
+    ap.add_argument("--timeline", action="store_true",
+                    help="diagnostics, not the bench line: per-kernel device times of "
+                         "the headline's find and insert_or_assign calls and of config "
+                         "5's find_or_insert (torch profiler), one JSON line per rank "
+                         "and leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--capacity", type=int, default=CAPACITY,
                     help="slots per GPU (diagnostics; the metric uses the default)")
