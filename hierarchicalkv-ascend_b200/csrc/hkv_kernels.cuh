@@ -1609,32 +1609,218 @@ __global__ void __launch_bounds__(256)
 }
 
 // ============================================================================
-// Rehash after the bucket count doubles (reference rehash_kernel.h:30-207).
-// One warp per old bucket. The reference scans the bucket from slot 0, moves
-// the first key whose new bucket differs (copy_key_to_new_bucket :30-67:
-// first EMPTY slot of the new bucket from the key's start position,
-// cyclically), back-shifts the entries behind the hole
-// (defragmentation_for_rehash :77-135: the first entry before the next
-// EMPTY_KEY that may move into the hole moves, and the hole follows it), and
-// restarts at slot 0. Every restart finds the lowest slot holding a key that
-// must move, so that is the order here. The warp replays it on metadata:
-// slot s belongs to lane s % 32, which keeps the slot's start position, its
-// EMPTY_KEY flag and its must-move flag in registers; each step is a warp
-// minimum (redux) over the lanes' candidates -- the next key to move, the
-// distance to the next EMPTY_KEY after the hole, the nearest entry that may
-// fill it -- and lane 0 moves the key, score and original slot in shared
-// memory. The value rows then move in parallel: rows bound for the new
-// bucket straight from their old slots, rows that change slot inside the old
+// Rehash after the bucket count doubles (reference rehash_kernel.h:30-207),
+// in two passes.
+//
+// The reference scans an old bucket from slot 0, moves the first key whose
+// new bucket differs (copy_key_to_new_bucket :30-67: first EMPTY slot of the
+// new bucket from the key's start position, cyclically), back-shifts the
+// entries behind the hole (defragmentation_for_rehash :77-135: the first
+// entry before the next EMPTY_KEY that may move into the hole moves there,
+// and the hole follows it) and restarts at slot 0, so every restart finds
+// the lowest slot that holds a key to move.
+//
+// Pass 1, rehash_replay_kernel: one thread per old bucket replays exactly
+// that on a packed copy of the bucket in shared memory (per slot: start
+// position, EMPTY_KEY flag, must-move flag, original slot: 16 bits), its
+// must-move and EMPTY_KEY flags also held as 128-bit register masks (the
+// next key to move is the lowest must-move bit; a back-shift stops at the
+// next EMPTY_KEY bit). The chain of shift steps is inherently sequential, so
+// a bucket gets one thread and an SM replays 512 buckets at once. Thread c
+// keeps slots q and q + 1 in the two halves of word (q / 2) of column c, so
+// the 32 threads of a warp always touch 32 different banks. Output per old
+// bucket: the original slot of the entry that ends in each slot of the old
+// and of the new bucket (one byte each, 0xFF: empty), and both buckets'
+// sizes.
+//
+// Both passes read the old key and score arrays; pass 2 writes every slot of
+// both buckets into the new (doubled) arrays, so the old metadata is neither
+// copied nor the new buckets cleared first.
+//
+// Pass 2, rehash_apply_kernel: one warp per old bucket moves keys, scores,
+// digests and value rows by those maps: rows bound for the new bucket
+// straight from their old slots, rows that change slot inside the old
 // bucket through the warp's scratch rows. The final layout is the
 // reference's, slot for slot.
 // ============================================================================
+constexpr uint32_t kReplayBuckets = 256;  // buckets (threads) per replay block
+// packed slot: start position (bits 0-6), EMPTY_KEY (7), bound for the new
+// bucket (8), original slot (9-15)
+constexpr uint32_t kEntEmpty = 0x80u;
+constexpr uint32_t kEntMove = 0x100u;
+constexpr uint32_t kEntSrcShift = 9;
+// packed slots (2 bytes, [slot / 2][bucket][2]), the new bucket's original
+// slots ([slot / 4][bucket][4] bytes), per bucket the must-move / EMPTY_KEY
+// masks and the new bucket's occupancy
+constexpr size_t kReplaySmem = size_t{kBucket} * kReplayBuckets * 2 +
+                               size_t{kBucket} * kReplayBuckets +
+                               size_t{kReplayBuckets} * 6 * 8;
+
+__device__ __forceinline__ uint32_t ent_index(uint32_t q, uint32_t c) {
+  return ((q >> 1) * kReplayBuckets + c) * 2 + (q & 1);
+}
+__device__ __forceinline__ uint32_t nsrc_index(uint32_t q, uint32_t c) {
+  return ((q >> 2) * kReplayBuckets + c) * 4 + (q & 3);
+}
+
+__device__ __forceinline__ void bit_set(uint64_t& m0, uint64_t& m1, uint32_t x) {
+  if (x < 64)
+    m0 |= uint64_t{1} << x;
+  else
+    m1 |= uint64_t{1} << (x - 64);
+}
+__device__ __forceinline__ void bit_clear(uint64_t& m0, uint64_t& m1, uint32_t x) {
+  if (x < 64)
+    m0 &= ~(uint64_t{1} << x);
+  else
+    m1 &= ~(uint64_t{1} << (x - 64));
+}
+__device__ __forceinline__ bool bit_test(uint64_t m0, uint64_t m1, uint32_t x) {
+  return ((x < 64 ? m0 >> x : m1 >> (x - 64)) & 1) != 0;
+}
+
+// First clear bit of the 128-bit mask (m0: slots 0-63, m1: 64-127) at or
+// after `from`, cyclically; kBucket when every slot is set.
+__device__ __forceinline__ uint32_t first_free_from(uint64_t m0, uint64_t m1, uint32_t from) {
+  const uint64_t f0 = ~m0, f1 = ~m1;
+  if (from < 64) {
+    const uint64_t c = f0 & (~uint64_t{0} << from);
+    if (c) return __ffsll(static_cast<long long>(c)) - 1;
+    if (f1) return 64 + __ffsll(static_cast<long long>(f1)) - 1;
+    if (f0) return __ffsll(static_cast<long long>(f0)) - 1;
+    return kBucket;
+  }
+  const uint64_t c = f1 & (~uint64_t{0} << (from - 64));
+  if (c) return 64 + __ffsll(static_cast<long long>(c)) - 1;
+  if (f0) return __ffsll(static_cast<long long>(f0)) - 1;
+  if (f1) return 64 + __ffsll(static_cast<long long>(f1)) - 1;
+  return kBucket;
+}
+
+// May the entry at cur (start position `start`) fill the hole at rm? The
+// reference's condition (rehash_kernel.h:101-103): start lies outside the
+// cyclic interval (rm, cur].
+__device__ __forceinline__ bool may_fill(uint32_t start, uint32_t rm, uint32_t cur) {
+  return (start <= rm && rm < cur) || (cur < start && start <= rm) ||
+         (rm < cur && cur < start);
+}
+
+__global__ void __launch_bounds__(kReplayBuckets)
+    rehash_replay_kernel(TableView t, uint64_t old_nb, const uint64_t* __restrict__ old_keys,
+                         uint8_t* __restrict__ maps) {
+  extern __shared__ uint64_t replay_smem[];
+  uint64_t* mask = replay_smem;  // [6][kReplayBuckets]: mv0 mv1 em0 em1 nocc0 nocc1
+  uint16_t* E = reinterpret_cast<uint16_t*>(replay_smem + 6 * kReplayBuckets);
+  uint8_t* N = reinterpret_cast<uint8_t*>(E + kBucket * kReplayBuckets);
+  constexpr uint32_t kWarps = kReplayBuckets / 32;
+  const uint32_t lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
+  const uint32_t c = threadIdx.x;  // this thread's bucket column
+  const uint64_t new_cap = t.capacity;  // power of two after doubling
+  for (uint64_t b0 = uint64_t{blockIdx.x} * kReplayBuckets; b0 < old_nb;
+       b0 += uint64_t{gridDim.x} * kReplayBuckets) {
+    // pack: warp wi reads buckets wi, wi + kWarps, ... with coalesced loads
+    for (uint32_t i = wi; i < kReplayBuckets && b0 + i < old_nb; i += kWarps) {
+      const uint64_t b = b0 + i;
+      uint32_t mv[4], em[4];
+#pragma unroll
+      for (uint32_t j = 0; j < 4; j++) {
+        const uint32_t q = lane + 32 * j;
+        const uint64_t k = old_keys[b * kBucket + q];
+        const uint64_t h = murmur3(k);
+        uint32_t e = static_cast<uint32_t>(h & (kBucket - 1)) | (q << kEntSrcShift);
+        if (k == kEmptyKey)
+          e |= kEntEmpty;
+        else if (k != kReclaimKey && ((h & (new_cap - 1)) >> kBucketShift) != b)
+          e |= kEntMove;
+        E[ent_index(q, i)] = static_cast<uint16_t>(e);
+        mv[j] = __ballot_sync(0xFFFFFFFFu, (e & kEntMove) != 0);
+        em[j] = __ballot_sync(0xFFFFFFFFu, (e & kEntEmpty) != 0);
+      }
+      if (lane == 0) {
+        mask[0 * kReplayBuckets + i] = mv[0] | (uint64_t{mv[1]} << 32);
+        mask[1 * kReplayBuckets + i] = mv[2] | (uint64_t{mv[3]} << 32);
+        mask[2 * kReplayBuckets + i] = em[0] | (uint64_t{em[1]} << 32);
+        mask[3 * kReplayBuckets + i] = em[2] | (uint64_t{em[3]} << 32);
+      }
+    }
+    __syncthreads();
+    const uint64_t b = b0 + c;
+    if (b < old_nb) {
+      uint64_t mv0 = mask[0 * kReplayBuckets + c], mv1 = mask[1 * kReplayBuckets + c];
+      uint64_t em0 = mask[2 * kReplayBuckets + c], em1 = mask[3 * kReplayBuckets + c];
+      uint64_t nocc0 = 0, nocc1 = 0;
+      int32_t moved = 0, removed = 0;
+      while (mv0 | mv1) {
+        const uint32_t q = mv0 ? __ffsll(static_cast<long long>(mv0)) - 1
+                               : 64 + __ffsll(static_cast<long long>(mv1)) - 1;
+        const uint32_t e = E[ent_index(q, c)];
+        // the new start position: new capacity >= kBucket, so the key's low
+        // hash bits are its start position in either bucket
+        const uint32_t p = first_free_from(nocc0, nocc1, e & (kBucket - 1));
+        if (p < kBucket) {
+          N[nsrc_index(p, c)] = static_cast<uint8_t>(e >> kEntSrcShift);
+          bit_set(nocc0, nocc1, p);
+          moved++;
+        }
+        removed++;
+        E[ent_index(q, c)] = kEntEmpty;
+        bit_clear(mv0, mv1, q);
+        bit_set(em0, em1, q);
+        // back-shift behind the hole
+        uint32_t rm = q;
+        for (uint32_t off = 1; off < kBucket;) {
+          const uint32_t cur = (rm + off) & (kBucket - 1);
+          if (bit_test(em0, em1, cur)) break;
+          const uint32_t ce = E[ent_index(cur, c)];
+          if (may_fill(ce & (kBucket - 1), rm, cur)) {
+            E[ent_index(rm, c)] = static_cast<uint16_t>(ce);
+            E[ent_index(cur, c)] = kEntEmpty;
+            bit_clear(em0, em1, rm);
+            bit_set(em0, em1, cur);
+            if (ce & kEntMove) {
+              bit_clear(mv0, mv1, cur);
+              bit_set(mv0, mv1, rm);
+            }
+            rm = cur;
+            off = 1;
+          } else {
+            off++;
+          }
+        }
+      }
+      mask[4 * kReplayBuckets + c] = nocc0;
+      mask[5 * kReplayBuckets + c] = nocc1;
+      t.sizes[b] -= removed;
+      t.sizes[b + old_nb] = moved;
+    }
+    __syncthreads();
+    // maps: bytes [0, kBucket) the original slot of each final old-bucket
+    // slot, [kBucket, 2 kBucket) of each new-bucket slot; 0xFF: empty
+    for (uint32_t i = wi; i < kReplayBuckets && b0 + i < old_nb; i += kWarps) {
+      const uint64_t nocc0 = mask[4 * kReplayBuckets + i], nocc1 = mask[5 * kReplayBuckets + i];
+      uint32_t ow = 0, nw = 0;
+#pragma unroll
+      for (uint32_t k = 0; k < 4; k++) {
+        const uint32_t q = lane * 4 + k;
+        const uint32_t e = E[ent_index(q, i)];
+        const uint32_t os = (e & kEntEmpty) ? 0xFFu : (e >> kEntSrcShift) & 0x7Fu;
+        const uint32_t ns = bit_test(nocc0, nocc1, q) ? N[nsrc_index(q, i)] : 0xFFu;
+        ow |= os << (8 * k);
+        nw |= ns << (8 * k);
+      }
+      uint32_t* mw = reinterpret_cast<uint32_t*>(maps + (b0 + i) * 2 * kBucket);
+      mw[lane] = ow;
+      mw[32 + lane] = nw;
+    }
+    __syncthreads();
+  }
+}
+
 struct RehashStage {
-  uint64_t okeys[kBucket];
+  uint64_t okeys[kBucket];    // the old bucket's keys and scores before the rehash
   uint64_t oscores[kBucket];
-  uint64_t nkeys[kBucket];
-  uint64_t nscores[kBucket];
-  uint8_t osrc[kBucket];  // original slot of the entry now at q (old bucket)
-  uint8_t nsrc[kBucket];  // original slot of the entry now at q (new bucket)
+  uint8_t osrc[kBucket];      // original slot of the entry ending at q (old bucket)
+  uint8_t nsrc[kBucket];      // original slot of the entry ending at q (new bucket)
 };
 
 // Copies, for every q < kBucket with pick(q), the row of slot src(q) of
@@ -1661,42 +1847,11 @@ __device__ __forceinline__ void warp_copy_rows(const TableView& t, uint64_t sb, 
   }
 }
 
-// First clear bit of the 128-bit mask (m0: slots 0-63, m1: 64-127) at or
-// after `from`, cyclically; kBucket when every slot is set.
-__device__ __forceinline__ uint32_t first_free_from(uint64_t m0, uint64_t m1, uint32_t from) {
-  const uint64_t f0 = ~m0, f1 = ~m1;
-  if (from < 64) {
-    const uint64_t c = f0 & (~uint64_t{0} << from);
-    if (c) return __ffsll(static_cast<long long>(c)) - 1;
-    if (f1) return 64 + __ffsll(static_cast<long long>(f1)) - 1;
-    if (f0) return __ffsll(static_cast<long long>(f0)) - 1;
-    return kBucket;
-  }
-  const uint64_t c = f1 & (~uint64_t{0} << (from - 64));
-  if (c) return 64 + __ffsll(static_cast<long long>(c)) - 1;
-  if (f0) return __ffsll(static_cast<long long>(f0)) - 1;
-  if (f1) return 64 + __ffsll(static_cast<long long>(f1)) - 1;
-  return kBucket;
-}
-
-// Slot entry of one lane's four slots (lane + 32 j): start position in the
-// bucket (7 bits), EMPTY_KEY flag, must-move flag.
-struct RehashSlots {
-  uint32_t home[4];
-  bool emp[4], mv[4];
-};
-
-// May the entry at cur (start position `start`) fill the hole at rm? The
-// reference's condition (rehash_kernel.h:101-103): start lies outside the
-// cyclic interval (rm, cur].
-__device__ __forceinline__ bool may_fill(uint32_t start, uint32_t rm, uint32_t cur) {
-  return (start <= rm && rm < cur) || (cur < start && start <= rm) ||
-         (rm < cur && cur < start);
-}
-
 template <int VW>
 __global__ void __launch_bounds__(256)
-    rehash_kernel(TableView t, uint64_t old_nb, uint8_t* __restrict__ scratch) {
+    rehash_apply_kernel(TableView t, uint64_t old_nb, const uint64_t* __restrict__ old_keys,
+                        const uint64_t* __restrict__ old_scores,
+                        const uint8_t* __restrict__ maps, uint8_t* __restrict__ scratch) {
   __shared__ RehashStage stage[8];
   const uint32_t lane = threadIdx.x & 31;
   const uint32_t wi = threadIdx.x >> 5;
@@ -1704,148 +1859,47 @@ __global__ void __launch_bounds__(256)
   const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x / 32);
   const uint64_t gw = blockIdx.x * (uint64_t)(blockDim.x / 32) + wi;
   uint8_t* rows = scratch + gw * kBucket * t.value_bytes;  // this warp's scratch rows
-  const uint64_t new_cap = t.capacity;  // power of two after doubling
   constexpr uint32_t kNone = 0xFFu;
   for (uint64_t b = gw; b < old_nb; b += nwarps) {
     const uint64_t nbk = b + old_nb;
-    RehashSlots r;
 #pragma unroll
     for (uint32_t j = 0; j < 4; j++) {
       const uint32_t q = lane + 32 * j;
-      const uint64_t k = t.keys[b * kBucket + q];
-      st.okeys[q] = k;
-      st.oscores[q] = t.scores[b * kBucket + q];
-      st.nkeys[q] = kEmptyKey;
-      st.nscores[q] = 0;
-      st.osrc[q] = static_cast<uint8_t>(q);
-      st.nsrc[q] = static_cast<uint8_t>(q);
-      const uint64_t h = murmur3(k);
-      r.home[j] = static_cast<uint32_t>(h & (kBucket - 1));
-      r.emp[j] = k == kEmptyKey;
-      r.mv[j] = k != kEmptyKey && k != kReclaimKey && ((h & (new_cap - 1)) >> kBucketShift) != b;
+      st.okeys[q] = old_keys[b * kBucket + q];
+      st.oscores[q] = old_scores[b * kBucket + q];
     }
-    __syncwarp();
-    int32_t moved = 0, removed = 0;
-    uint64_t nocc0 = 0, nocc1 = 0;  // occupied slots of the new bucket (warp-uniform)
-    while (true) {
-      // the lowest slot holding a key that must move
-      uint32_t mine = kNone;
-#pragma unroll
-      for (uint32_t j = 0; j < 4; j++)
-        if (r.mv[j]) mine = min(mine, lane + 32 * j);
-      const uint32_t q = __reduce_min_sync(0xFFFFFFFFu, mine);
-      if (q == kNone) break;
-      const uint32_t qj = q >> 5;
-      uint32_t hsel = 0;
-#pragma unroll
-      for (uint32_t j = 0; j < 4; j++)
-        if (j == qj) hsel = r.home[j];
-      // the new start position: new capacity >= kBucket, so the key's low
-      // hash bits are its start position in either bucket
-      const uint32_t npos = __shfl_sync(0xFFFFFFFFu, hsel, q & 31);
-      const uint32_t p = first_free_from(nocc0, nocc1, npos);
-      if (p < kBucket) {
-        if (p < 64)
-          nocc0 |= uint64_t{1} << p;
-        else
-          nocc1 |= uint64_t{1} << (p - 64);
-        if (lane == 0) {
-          st.nkeys[p] = st.okeys[q];
-          st.nscores[p] = st.oscores[q];
-          st.nsrc[p] = st.osrc[q];
-        }
-        moved++;
-      }
-      removed++;
-      if (lane == 0) st.okeys[q] = kEmptyKey;
-      if (lane == (q & 31)) {
-#pragma unroll
-        for (uint32_t j = 0; j < 4; j++)
-          if (j == qj) {
-            r.emp[j] = true;
-            r.mv[j] = false;
-          }
-      }
-      // back-shift behind the hole
-      uint32_t rm = q;
-      while (true) {
-        uint32_t e_l = kBucket;
-#pragma unroll
-        for (uint32_t j = 0; j < 4; j++) {
-          const uint32_t d = (lane + 32 * j - rm) & (kBucket - 1);
-          if (r.emp[j] && d != 0) e_l = min(e_l, d);
-        }
-        const uint32_t e = __reduce_min_sync(0xFFFFFFFFu, e_l);
-        uint32_t c_l = kNone;
-#pragma unroll
-        for (uint32_t j = 0; j < 4; j++) {
-          const uint32_t s = lane + 32 * j;
-          const uint32_t d = (s - rm) & (kBucket - 1);
-          if (!r.emp[j] && d != 0 && d < e && may_fill(r.home[j], rm, s)) c_l = min(c_l, d);
-        }
-        const uint32_t c = __reduce_min_sync(0xFFFFFFFFu, c_l);
-        if (c == kNone) break;
-        const uint32_t cur = (rm + c) & (kBucket - 1);
-        const uint32_t cj = cur >> 5, rj = rm >> 5;
-        uint32_t pk = 0;
-#pragma unroll
-        for (uint32_t j = 0; j < 4; j++)
-          if (j == cj) pk = r.home[j] | (r.mv[j] ? 0x100u : 0u);
-        pk = __shfl_sync(0xFFFFFFFFu, pk, cur & 31);
-        if (lane == (rm & 31)) {
-#pragma unroll
-          for (uint32_t j = 0; j < 4; j++)
-            if (j == rj) {
-              r.home[j] = pk & 0xFFu;
-              r.mv[j] = (pk & 0x100u) != 0;
-              r.emp[j] = false;
-            }
-        }
-        if (lane == (cur & 31)) {
-#pragma unroll
-          for (uint32_t j = 0; j < 4; j++)
-            if (j == cj) {
-              r.emp[j] = true;
-              r.mv[j] = false;
-            }
-        }
-        if (lane == 0) {
-          st.okeys[rm] = st.okeys[cur];
-          st.oscores[rm] = st.oscores[cur];
-          st.osrc[rm] = st.osrc[cur];
-          st.okeys[cur] = kEmptyKey;
-        }
-        rm = cur;
-      }
-    }
+    const uint32_t* mw = reinterpret_cast<const uint32_t*>(maps + b * 2 * kBucket);
+    reinterpret_cast<uint32_t*>(st.osrc)[lane] = mw[lane];
+    reinterpret_cast<uint32_t*>(st.nsrc)[lane] = mw[32 + lane];
     __syncwarp();
     // rows: new bucket from the old slots, and the old bucket's moving rows
     // into scratch, before any old row is overwritten
     warp_copy_rows<VW>(
-        t, b, nbk, rows, false, false, [&](uint32_t q) { return st.nkeys[q] != kEmptyKey; },
+        t, b, nbk, rows, false, false, [&](uint32_t q) { return st.nsrc[q] != kNone; },
         [&](uint32_t q) { return static_cast<uint32_t>(st.nsrc[q]); }, lane);
     auto stays_moved = [&](uint32_t q) {
-      return st.okeys[q] != kEmptyKey && st.okeys[q] != kReclaimKey && st.osrc[q] != q;
+      const uint32_t o = st.osrc[q];
+      return o != kNone && o != q && st.okeys[o] != kReclaimKey;
     };
     warp_copy_rows<VW>(t, b, b, rows, false, true, stays_moved,
                        [&](uint32_t q) { return static_cast<uint32_t>(st.osrc[q]); }, lane);
     __syncwarp();
     warp_copy_rows<VW>(t, b, b, rows, true, false, stays_moved,
                        [&](uint32_t q) { return q; }, lane);
-    for (uint32_t q = lane; q < kBucket; q += 32) {
-      const uint64_t ok = st.okeys[q], nk = st.nkeys[q];
+#pragma unroll
+    for (uint32_t j = 0; j < 4; j++) {
+      const uint32_t q = lane + 32 * j;
+      const uint32_t o = st.osrc[q], n = st.nsrc[q];
+      const uint64_t ok = o == kNone ? kEmptyKey : st.okeys[o];
+      const uint64_t nk = n == kNone ? kEmptyKey : st.okeys[n];
       t.keys[b * kBucket + q] = ok;
-      t.scores[b * kBucket + q] = st.oscores[q];
+      t.scores[b * kBucket + q] = o == kNone ? 0 : st.oscores[o];
       t.digests[b * kBucket + q] =
           ok == kEmptyKey ? kEmptyDigest : digest_of_hash(murmur3(ok));
       t.keys[nbk * kBucket + q] = nk;
-      t.scores[nbk * kBucket + q] = st.nscores[q];
+      t.scores[nbk * kBucket + q] = n == kNone ? 0 : st.oscores[n];
       t.digests[nbk * kBucket + q] =
           nk == kEmptyKey ? kEmptyDigest : digest_of_hash(murmur3(nk));
-    }
-    if (lane == 0) {
-      t.sizes[b] -= removed;
-      t.sizes[nbk] = moved;
     }
     __syncwarp();
   }

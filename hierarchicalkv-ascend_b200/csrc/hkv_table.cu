@@ -9,13 +9,13 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <string>
 
 #include "hkv_dedup.cuh"
 #include "hkv_kernels.cuh"
-#include <cstdio>
 
 #include "../../include/hkv_scan.cuh"
 #include "hkv_table.cuh"
@@ -1004,15 +1004,28 @@ void TableImpl::double_capacity(cudaStream_t s) {
               "the table cannot grow while keys are locked (lock_keys or "
               "find_or_insert with locked_key_ptrs): unlock them first");
   const uint64_t old_nb = num_buckets_, new_nb = old_nb * 2;
-  const size_t old_slots = old_nb * kBucket, new_slots = new_nb * kBucket;
+  const size_t new_slots = new_nb * kBucket;
+  // pass 2 runs one warp per old bucket, each with kBucket scratch rows for
+  // the rows that change slot inside their bucket (at most 512 MB of scratch)
+  const uint64_t row_block = uint64_t{kBucket} * value_bytes_;
+  const uint64_t max_warps = std::max<uint64_t>(
+      8, std::min<uint64_t>(sm_count_ * 64ull, (512ull << 20) / row_block));
+  const int grid = static_cast<int>(
+      std::max<uint64_t>(1, std::min<uint64_t>(ceil_div(old_nb, 8), max_warps / 8)));
+  // every allocation first: a failure leaves the table as it was
+  Workspace ws(s, pool_, &mem_);
   uint64_t *nk = nullptr, *ns = nullptr;
   uint8_t* nd = nullptr;
   int32_t* nz = nullptr;
+  uint8_t *maps = nullptr, *scratch = nullptr;
   try {
     nk = static_cast<uint64_t*>(mem_.device(new_slots * 8));
     ns = static_cast<uint64_t*>(mem_.device(new_slots * 8));
     nd = static_cast<uint8_t*>(mem_.device(new_slots));
     nz = static_cast<int32_t*>(mem_.device(new_nb * 4));
+    // 2 x kBucket bytes of slot maps per old bucket (pass 1 -> pass 2)
+    maps = ws.get<uint8_t>(old_nb * 2 * kBucket);
+    scratch = ws.get<uint8_t>(uint64_t{static_cast<uint32_t>(grid)} * 8 * row_block);
   } catch (...) {
     mem_.free_device(nk);
     mem_.free_device(ns);
@@ -1020,41 +1033,42 @@ void TableImpl::double_capacity(cudaStream_t s) {
     mem_.free_device(nz);
     throw;
   }
-  CUDA_TRY(cudaMemcpyAsync(nk, keys_, old_slots * 8, cudaMemcpyDeviceToDevice, s));
-  CUDA_TRY(cudaMemcpyAsync(ns, scores_, old_slots * 8, cudaMemcpyDeviceToDevice, s));
-  CUDA_TRY(cudaMemcpyAsync(nd, digests_, old_slots, cudaMemcpyDeviceToDevice, s));
+  allocate_slices(old_nb, new_nb);
+  upload_slices();
+  // The two passes read the old key and score arrays and write every slot
+  // of both halves of the new ones (keys, scores, digests), so neither a
+  // copy of the old metadata nor a clear of the new buckets is needed; the
+  // sizes start from the old ones.
   CUDA_TRY(cudaMemcpyAsync(nz, sizes_, old_nb * 4, cudaMemcpyDeviceToDevice, s));
-  CUDA_TRY(cudaStreamSynchronize(s));
-  mem_.free_device(keys_);
-  mem_.free_device(scores_);
-  mem_.free_device(digests_);
-  mem_.free_device(sizes_);
+  uint64_t* const ok = keys_;
+  uint64_t* const os = scores_;
+  uint8_t* const od = digests_;
+  int32_t* const oz = sizes_;
   keys_ = nk;
   scores_ = ns;
   digests_ = nd;
   sizes_ = nz;
-  allocate_slices(old_nb, new_nb);
-  upload_slices();
   num_buckets_ = new_nb;
   capacity_ = new_slots;
   magic_for(capacity_, &div_magic_, &div_shift_);
   const TableView v = view();
-  init_buckets_kernel<<<warp_grid(old_nb), 256, 0, counted(s)>>>(v, old_nb, new_nb, 1);
+  CUDA_TRY(cudaFuncSetAttribute(rehash_replay_kernel,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(kReplaySmem)));
+  const int rgrid = static_cast<int>(std::max<uint64_t>(
+      1, std::min<uint64_t>(ceil_div(old_nb, kReplayBuckets), sm_count_ * 64ull)));
+  rehash_replay_kernel<<<rgrid, kReplayBuckets, kReplaySmem, counted(s)>>>(v, old_nb, ok,
+                                                                          maps);
+  CUDA_TRY(cudaGetLastError());
   const int vw = value_width({});
-  // one warp per old bucket, each with kBucket scratch rows for the rows that
-  // change slot inside their bucket (at most 512 MB of scratch)
-  const uint64_t row_block = uint64_t{kBucket} * value_bytes_;
-  const uint64_t max_warps = std::max<uint64_t>(
-      8, std::min<uint64_t>(sm_count_ * 64ull, (512ull << 20) / row_block));
-  const int grid = static_cast<int>(
-      std::max<uint64_t>(1, std::min<uint64_t>(ceil_div(old_nb, 8), max_warps / 8)));
-  {
-    Workspace ws(s, pool_, &mem_);
-    uint8_t* scratch = ws.get<uint8_t>(uint64_t{static_cast<uint32_t>(grid)} * 8 * row_block);
-    DISPATCH_VW(vw, rehash_kernel<VW><<<grid, 256, 0, counted(s)>>>(v, old_nb, scratch));
-    CUDA_TRY(cudaGetLastError());
-    CUDA_TRY(cudaStreamSynchronize(s));
-  }
+  DISPATCH_VW(vw, rehash_apply_kernel<VW><<<grid, 256, 0, counted(s)>>>(v, old_nb, ok, os,
+                                                                        maps, scratch));
+  CUDA_TRY(cudaGetLastError());
+  CUDA_TRY(cudaStreamSynchronize(s));
+  mem_.free_device(ok);
+  mem_.free_device(os);
+  mem_.free_device(od);
+  mem_.free_device(oz);
 }
 
 void TableImpl::reserve(size_t new_capacity, cudaStream_t s) {
