@@ -1623,10 +1623,14 @@ __global__ void __launch_bounds__(256)
 // Pass 1, rehash_replay_kernel: one thread per old bucket replays exactly
 // that on a packed copy of the bucket in shared memory (per slot: start
 // position, EMPTY_KEY flag, must-move flag, original slot: 16 bits), its
-// must-move and EMPTY_KEY flags also held as 128-bit register masks (the
+// must-move flags also held as a 128-bit register mask (the
 // next key to move is the lowest must-move bit; a back-shift stops at the
-// next EMPTY_KEY bit). The chain of shift steps is inherently sequential, so
-// a bucket gets one thread and an SM replays 512 buckets at once. Thread c
+// next EMPTY_KEY slot). An entry may fill a hole d slots behind it only if it
+// sits at least d slots past its start position, and moves only bring
+// entries closer to theirs, so the search for a filler also stops at the
+// bucket's largest displacement. The chain of shift steps is inherently
+// sequential, so a bucket gets one thread and an SM replays 512 buckets at
+// once. Thread c
 // keeps slots q and q + 1 in the two halves of word (q / 2) of column c, so
 // the 32 threads of a warp always touch 32 different banks. Output per old
 // bucket: the original slot of the entry that ends in each slot of the old
@@ -1654,7 +1658,7 @@ constexpr uint32_t kEntSrcShift = 9;
 // masks and the new bucket's occupancy
 constexpr size_t kReplaySmem = size_t{kBucket} * kReplayBuckets * 2 +
                                size_t{kBucket} * kReplayBuckets +
-                               size_t{kReplayBuckets} * 6 * 8;
+                               size_t{kReplayBuckets} * 5 * 8;
 
 __device__ __forceinline__ uint32_t ent_index(uint32_t q, uint32_t c) {
   return ((q >> 1) * kReplayBuckets + c) * 2 + (q & 1);
@@ -1697,20 +1701,14 @@ __device__ __forceinline__ uint32_t first_free_from(uint64_t m0, uint64_t m1, ui
   return kBucket;
 }
 
-// May the entry at cur (start position `start`) fill the hole at rm? The
-// reference's condition (rehash_kernel.h:101-103): start lies outside the
-// cyclic interval (rm, cur].
-__device__ __forceinline__ bool may_fill(uint32_t start, uint32_t rm, uint32_t cur) {
-  return (start <= rm && rm < cur) || (cur < start && start <= rm) ||
-         (rm < cur && cur < start);
-}
-
 __global__ void __launch_bounds__(kReplayBuckets)
     rehash_replay_kernel(TableView t, uint64_t old_nb, const uint64_t* __restrict__ old_keys,
                          uint8_t* __restrict__ maps) {
   extern __shared__ uint64_t replay_smem[];
-  uint64_t* mask = replay_smem;  // [6][kReplayBuckets]: mv0 mv1 em0 em1 nocc0 nocc1
-  uint16_t* E = reinterpret_cast<uint16_t*>(replay_smem + 6 * kReplayBuckets);
+  // [5][kReplayBuckets]: must-move mask (2 words), new bucket's occupancy
+  // (2 words), largest displacement
+  uint64_t* mask = replay_smem;
+  uint16_t* E = reinterpret_cast<uint16_t*>(replay_smem + 5 * kReplayBuckets);
   uint8_t* N = reinterpret_cast<uint8_t*>(E + kBucket * kReplayBuckets);
   constexpr uint32_t kWarps = kReplayBuckets / 32;
   const uint32_t lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
@@ -1719,13 +1717,26 @@ __global__ void __launch_bounds__(kReplayBuckets)
   for (uint64_t b0 = uint64_t{blockIdx.x} * kReplayBuckets; b0 < old_nb;
        b0 += uint64_t{gridDim.x} * kReplayBuckets) {
     // pack: warp wi reads buckets wi, wi + kWarps, ... with coalesced loads
-    for (uint32_t i = wi; i < kReplayBuckets && b0 + i < old_nb; i += kWarps) {
+    for (uint32_t i0 = wi; i0 < kReplayBuckets; i0 += 4 * kWarps) {
+      // four buckets' keys in flight per warp
+      uint64_t kk[4][4];
+#pragma unroll
+      for (uint32_t u = 0; u < 4; u++)
+#pragma unroll
+        for (uint32_t j = 0; j < 4; j++) {
+          const uint64_t bu = b0 + i0 + u * kWarps;
+          kk[u][j] = bu < old_nb ? old_keys[bu * kBucket + lane + 32 * j] : kEmptyKey;
+        }
+#pragma unroll
+      for (uint32_t u = 0; u < 4; u++) {
+      const uint32_t i = i0 + u * kWarps;
+      if (b0 + i >= old_nb) break;
       const uint64_t b = b0 + i;
-      uint32_t mv[4], em[4];
+      uint32_t mv[4], dmax = 0;
 #pragma unroll
       for (uint32_t j = 0; j < 4; j++) {
         const uint32_t q = lane + 32 * j;
-        const uint64_t k = old_keys[b * kBucket + q];
+        const uint64_t k = kk[u][j];
         const uint64_t h = murmur3(k);
         uint32_t e = static_cast<uint32_t>(h & (kBucket - 1)) | (q << kEntSrcShift);
         if (k == kEmptyKey)
@@ -1733,27 +1744,31 @@ __global__ void __launch_bounds__(kReplayBuckets)
         else if (k != kReclaimKey && ((h & (new_cap - 1)) >> kBucketShift) != b)
           e |= kEntMove;
         E[ent_index(q, i)] = static_cast<uint16_t>(e);
+        if (!(e & kEntEmpty)) dmax = max(dmax, (q - static_cast<uint32_t>(h)) & (kBucket - 1));
         mv[j] = __ballot_sync(0xFFFFFFFFu, (e & kEntMove) != 0);
-        em[j] = __ballot_sync(0xFFFFFFFFu, (e & kEntEmpty) != 0);
       }
+      dmax = __reduce_max_sync(0xFFFFFFFFu, dmax);
       if (lane == 0) {
+        mask[4 * kReplayBuckets + i] = dmax;
         mask[0 * kReplayBuckets + i] = mv[0] | (uint64_t{mv[1]} << 32);
         mask[1 * kReplayBuckets + i] = mv[2] | (uint64_t{mv[3]} << 32);
-        mask[2 * kReplayBuckets + i] = em[0] | (uint64_t{em[1]} << 32);
-        mask[3 * kReplayBuckets + i] = em[2] | (uint64_t{em[3]} << 32);
+      }
       }
     }
     __syncthreads();
     const uint64_t b = b0 + c;
     if (b < old_nb) {
       uint64_t mv0 = mask[0 * kReplayBuckets + c], mv1 = mask[1 * kReplayBuckets + c];
-      uint64_t em0 = mask[2 * kReplayBuckets + c], em1 = mask[3 * kReplayBuckets + c];
+      // slot q of this column: col[(q / 2) * 2 kReplayBuckets + q % 2]
+      uint16_t* col = E + 2 * c;
+      // no entry can fill a hole farther behind it than this
+      const uint32_t reach = static_cast<uint32_t>(mask[4 * kReplayBuckets + c]) + 1;
       uint64_t nocc0 = 0, nocc1 = 0;
       int32_t moved = 0, removed = 0;
       while (mv0 | mv1) {
         const uint32_t q = mv0 ? __ffsll(static_cast<long long>(mv0)) - 1
                                : 64 + __ffsll(static_cast<long long>(mv1)) - 1;
-        const uint32_t e = E[ent_index(q, c)];
+        const uint32_t e = col[(q >> 1) * 2 * kReplayBuckets + (q & 1)];
         // the new start position: new capacity >= kBucket, so the key's low
         // hash bits are its start position in either bucket
         const uint32_t p = first_free_from(nocc0, nocc1, e & (kBucket - 1));
@@ -1763,20 +1778,20 @@ __global__ void __launch_bounds__(kReplayBuckets)
           moved++;
         }
         removed++;
-        E[ent_index(q, c)] = kEntEmpty;
+        col[(q >> 1) * 2 * kReplayBuckets + (q & 1)] = kEntEmpty;
         bit_clear(mv0, mv1, q);
-        bit_set(em0, em1, q);
-        // back-shift behind the hole
+        // back-shift behind the hole. The reference lets the entry at cur
+        // fill the hole at rm when its start position lies outside the
+        // cyclic interval (rm, cur] (rehash_kernel.h:101-103): the same as
+        // sitting at least `off` = cur - rm slots past its start position.
         uint32_t rm = q;
-        for (uint32_t off = 1; off < kBucket;) {
+        for (uint32_t off = 1; off < reach;) {
           const uint32_t cur = (rm + off) & (kBucket - 1);
-          if (bit_test(em0, em1, cur)) break;
-          const uint32_t ce = E[ent_index(cur, c)];
-          if (may_fill(ce & (kBucket - 1), rm, cur)) {
-            E[ent_index(rm, c)] = static_cast<uint16_t>(ce);
-            E[ent_index(cur, c)] = kEntEmpty;
-            bit_clear(em0, em1, rm);
-            bit_set(em0, em1, cur);
+          const uint32_t ce = col[(cur >> 1) * 2 * kReplayBuckets + (cur & 1)];
+          if (ce & kEntEmpty) break;
+          if (((cur - ce) & (kBucket - 1)) >= off) {
+            col[(rm >> 1) * 2 * kReplayBuckets + (rm & 1)] = static_cast<uint16_t>(ce);
+            col[(cur >> 1) * 2 * kReplayBuckets + (cur & 1)] = kEntEmpty;
             if (ce & kEntMove) {
               bit_clear(mv0, mv1, cur);
               bit_set(mv0, mv1, rm);
@@ -1788,8 +1803,8 @@ __global__ void __launch_bounds__(kReplayBuckets)
           }
         }
       }
-      mask[4 * kReplayBuckets + c] = nocc0;
-      mask[5 * kReplayBuckets + c] = nocc1;
+      mask[2 * kReplayBuckets + c] = nocc0;
+      mask[3 * kReplayBuckets + c] = nocc1;
       t.sizes[b] -= removed;
       t.sizes[b + old_nb] = moved;
     }
@@ -1797,7 +1812,7 @@ __global__ void __launch_bounds__(kReplayBuckets)
     // maps: bytes [0, kBucket) the original slot of each final old-bucket
     // slot, [kBucket, 2 kBucket) of each new-bucket slot; 0xFF: empty
     for (uint32_t i = wi; i < kReplayBuckets && b0 + i < old_nb; i += kWarps) {
-      const uint64_t nocc0 = mask[4 * kReplayBuckets + i], nocc1 = mask[5 * kReplayBuckets + i];
+      const uint64_t nocc0 = mask[2 * kReplayBuckets + i], nocc1 = mask[3 * kReplayBuckets + i];
       uint32_t ow = 0, nw = 0;
 #pragma unroll
       for (uint32_t k = 0; k < 4; k++) {
@@ -1821,29 +1836,48 @@ struct RehashStage {
   uint64_t oscores[kBucket];
   uint8_t osrc[kBucket];      // original slot of the entry ending at q (old bucket)
   uint8_t nsrc[kBucket];      // original slot of the entry ending at q (new bucket)
+  uint8_t lsrc[2][kBucket];   // rows to copy: [0] into the new bucket,
+  uint8_t ldst[2][kBucket];   // [1] to another slot of the old bucket
 };
 
-// Copies, for every q < kBucket with pick(q), the row of slot src(q) of
-// bucket sb to slot q of bucket db (or scratch rows when dst_scratch / from
-// scratch rows when src_scratch); the warp's lanes split the row vectors.
-template <int VW, class Pick, class Src>
-__device__ __forceinline__ void warp_copy_rows(const TableView& t, uint64_t sb, uint64_t db,
+// Copies the rows lsrc[k] -> ldst[k], k < cnt (slots of bucket sb / db, or
+// the warp's scratch rows). Rows of nv <= 32 vectors: the lanes form 32 / nv
+// groups of nv, each group one row, four rows' loads in flight; longer rows:
+// the warp walks each row 32 vectors at a time.
+template <int VW>
+__device__ __forceinline__ void warp_copy_list(const TableView& t, uint64_t sb, uint64_t db,
                                                uint8_t* scratch, bool src_scratch,
-                                               bool dst_scratch, Pick pick, Src src,
+                                               bool dst_scratch, const uint8_t* lsrc,
+                                               const uint8_t* ldst, uint32_t cnt,
                                                uint32_t lane) {
   using V = typename VecOf<VW>::T;
   const uint32_t vb = t.value_bytes;
   const uint32_t nv = vb / VW;
-  for (uint32_t x = lane; x < kBucket * nv; x += 32) {
-    const uint32_t q = x / nv;
-    const uint32_t v = x - q * nv;
-    if (!pick(q)) continue;
-    const uint32_t sq = src(q);
-    const V* sp = reinterpret_cast<const V*>(
-        src_scratch ? scratch + uint64_t{sq} * vb : value_ptr(t, sb, sq));
-    V* dp = reinterpret_cast<V*>(dst_scratch ? scratch + uint64_t{q} * vb
-                                             : value_ptr(t, db, q));
-    dp[v] = sp[v];
+  auto sptr = [&](uint32_t q) {
+    return reinterpret_cast<const V*>(src_scratch ? scratch + uint64_t{q} * vb
+                                                  : value_ptr(t, sb, q));
+  };
+  auto dptr = [&](uint32_t q) {
+    return reinterpret_cast<V*>(dst_scratch ? scratch + uint64_t{q} * vb : value_ptr(t, db, q));
+  };
+  if (nv <= 32) {
+    const uint32_t rpi = 32 / nv, lq = lane / nv, lv = lane - lq * nv;
+    if (lq >= rpi) return;
+    uint32_t k = lq;
+    for (; k + 3 * rpi < cnt; k += 4 * rpi) {
+      V x[4];
+#pragma unroll
+      for (uint32_t u = 0; u < 4; u++) x[u] = sptr(lsrc[k + u * rpi])[lv];
+#pragma unroll
+      for (uint32_t u = 0; u < 4; u++) dptr(ldst[k + u * rpi])[lv] = x[u];
+    }
+    for (; k < cnt; k += rpi) dptr(ldst[k])[lv] = sptr(lsrc[k])[lv];
+  } else {
+    for (uint32_t k = 0; k < cnt; k++) {
+      const V* sp = sptr(lsrc[k]);
+      V* dp = dptr(ldst[k]);
+      for (uint32_t v = lane; v < nv; v += 32) dp[v] = sp[v];
+    }
   }
 }
 
@@ -1860,6 +1894,7 @@ __global__ void __launch_bounds__(256)
   const uint64_t gw = blockIdx.x * (uint64_t)(blockDim.x / 32) + wi;
   uint8_t* rows = scratch + gw * kBucket * t.value_bytes;  // this warp's scratch rows
   constexpr uint32_t kNone = 0xFFu;
+  const uint32_t lt = (1u << lane) - 1;
   for (uint64_t b = gw; b < old_nb; b += nwarps) {
     const uint64_t nbk = b + old_nb;
 #pragma unroll
@@ -1872,20 +1907,37 @@ __global__ void __launch_bounds__(256)
     reinterpret_cast<uint32_t*>(st.osrc)[lane] = mw[lane];
     reinterpret_cast<uint32_t*>(st.nsrc)[lane] = mw[32 + lane];
     __syncwarp();
-    // rows: new bucket from the old slots, and the old bucket's moving rows
-    // into scratch, before any old row is overwritten
-    warp_copy_rows<VW>(
-        t, b, nbk, rows, false, false, [&](uint32_t q) { return st.nsrc[q] != kNone; },
-        [&](uint32_t q) { return static_cast<uint32_t>(st.nsrc[q]); }, lane);
-    auto stays_moved = [&](uint32_t q) {
-      const uint32_t o = st.osrc[q];
-      return o != kNone && o != q && st.okeys[o] != kReclaimKey;
-    };
-    warp_copy_rows<VW>(t, b, b, rows, false, true, stays_moved,
-                       [&](uint32_t q) { return static_cast<uint32_t>(st.osrc[q]); }, lane);
+    // the rows that move: into the new bucket, and to another slot of the
+    // old bucket (reclaimed slots carry no row)
+    uint32_t c0 = 0, c1 = 0;
+#pragma unroll
+    for (uint32_t j = 0; j < 4; j++) {
+      const uint32_t q = lane + 32 * j;
+      const uint32_t n = st.nsrc[q], o = st.osrc[q];
+      const bool p0 = n != kNone;
+      const bool p1 = o != kNone && o != q && st.okeys[o] != kReclaimKey;
+      const uint32_t m0 = __ballot_sync(0xFFFFFFFFu, p0);
+      const uint32_t m1 = __ballot_sync(0xFFFFFFFFu, p1);
+      if (p0) {
+        const uint32_t at = c0 + __popc(m0 & lt);
+        st.lsrc[0][at] = static_cast<uint8_t>(n);
+        st.ldst[0][at] = static_cast<uint8_t>(q);
+      }
+      if (p1) {
+        const uint32_t at = c1 + __popc(m1 & lt);
+        st.lsrc[1][at] = static_cast<uint8_t>(o);
+        st.ldst[1][at] = static_cast<uint8_t>(q);
+      }
+      c0 += __popc(m0);
+      c1 += __popc(m1);
+    }
     __syncwarp();
-    warp_copy_rows<VW>(t, b, b, rows, true, false, stays_moved,
-                       [&](uint32_t q) { return q; }, lane);
+    // new bucket rows from the old slots, and the old bucket's moving rows
+    // into scratch, before any old row is overwritten
+    warp_copy_list<VW>(t, b, nbk, rows, false, false, st.lsrc[0], st.ldst[0], c0, lane);
+    warp_copy_list<VW>(t, b, b, rows, false, true, st.lsrc[1], st.ldst[1], c1, lane);
+    __syncwarp();
+    warp_copy_list<VW>(t, b, b, rows, true, false, st.ldst[1], st.ldst[1], c1, lane);
 #pragma unroll
     for (uint32_t j = 0; j < 4; j++) {
       const uint32_t q = lane + 32 * j;
