@@ -1623,19 +1623,18 @@ __global__ void __launch_bounds__(256)
 // Pass 1, rehash_replay_kernel: one thread per old bucket replays exactly
 // that on a packed copy of the bucket in shared memory (per slot: start
 // position, EMPTY_KEY flag, must-move flag, original slot: 16 bits), its
-// must-move flags also held as a 128-bit register mask (the
-// next key to move is the lowest must-move bit; a back-shift stops at the
-// next EMPTY_KEY slot). An entry may fill a hole d slots behind it only if it
+// must-move flags also held as a 128-bit register mask (the next key to
+// move is the lowest must-move bit; a back-shift stops at the next
+// EMPTY_KEY slot). An entry may fill a hole d slots behind it only if it
 // sits at least d slots past its start position, and moves only bring
 // entries closer to theirs, so the search for a filler also stops at the
 // bucket's largest displacement. The chain of shift steps is inherently
-// sequential, so a bucket gets one thread and an SM replays 512 buckets at
-// once. Thread c
-// keeps slots q and q + 1 in the two halves of word (q / 2) of column c, so
-// the 32 threads of a warp always touch 32 different banks. Output per old
-// bucket: the original slot of the entry that ends in each slot of the old
-// and of the new bucket (one byte each, 0xFF: empty), and both buckets'
-// sizes.
+// sequential, so a bucket gets one thread and an SM replays 768 buckets at
+// once. Thread c keeps slots q and q + 1 in the two halves of word (q / 2)
+// of column c, so the 32 threads of a warp always touch 32 different banks.
+// Output per old bucket: the original slot of the entry that ends in each
+// slot of the old and of the new bucket (one byte each, 0xFF: empty; the
+// new bucket's bytes written as keys move), and both buckets' sizes.
 //
 // Both passes read the old key and score arrays; pass 2 writes every slot of
 // both buckets into the new (doubled) arrays, so the old metadata is neither
@@ -1653,19 +1652,15 @@ constexpr uint32_t kReplayBuckets = 256;  // buckets (threads) per replay block
 constexpr uint32_t kEntEmpty = 0x80u;
 constexpr uint32_t kEntMove = 0x100u;
 constexpr uint32_t kEntSrcShift = 9;
-// packed slots (2 bytes, [slot / 2][bucket][2]), the new bucket's original
-// slots ([slot / 4][bucket][4] bytes), per bucket the must-move / EMPTY_KEY
-// masks and the new bucket's occupancy
+// packed slots (2 bytes, [slot / 2][bucket][2]) and per bucket the
+// must-move mask and the largest displacement: 70 KiB, three blocks per SM
 constexpr size_t kReplaySmem = size_t{kBucket} * kReplayBuckets * 2 +
-                               size_t{kBucket} * kReplayBuckets +
-                               size_t{kReplayBuckets} * 5 * 8;
+                               size_t{kReplayBuckets} * 3 * 8;
 
 __device__ __forceinline__ uint32_t ent_index(uint32_t q, uint32_t c) {
   return ((q >> 1) * kReplayBuckets + c) * 2 + (q & 1);
 }
-__device__ __forceinline__ uint32_t nsrc_index(uint32_t q, uint32_t c) {
-  return ((q >> 2) * kReplayBuckets + c) * 4 + (q & 3);
-}
+
 
 __device__ __forceinline__ void bit_set(uint64_t& m0, uint64_t& m1, uint32_t x) {
   if (x < 64)
@@ -1678,9 +1673,6 @@ __device__ __forceinline__ void bit_clear(uint64_t& m0, uint64_t& m1, uint32_t x
     m0 &= ~(uint64_t{1} << x);
   else
     m1 &= ~(uint64_t{1} << (x - 64));
-}
-__device__ __forceinline__ bool bit_test(uint64_t m0, uint64_t m1, uint32_t x) {
-  return ((x < 64 ? m0 >> x : m1 >> (x - 64)) & 1) != 0;
 }
 
 // First clear bit of the 128-bit mask (m0: slots 0-63, m1: 64-127) at or
@@ -1705,11 +1697,9 @@ __global__ void __launch_bounds__(kReplayBuckets)
     rehash_replay_kernel(TableView t, uint64_t old_nb, const uint64_t* __restrict__ old_keys,
                          uint8_t* __restrict__ maps) {
   extern __shared__ uint64_t replay_smem[];
-  // [5][kReplayBuckets]: must-move mask (2 words), new bucket's occupancy
-  // (2 words), largest displacement
+  // [3][kReplayBuckets]: must-move mask (2 words), largest displacement
   uint64_t* mask = replay_smem;
-  uint16_t* E = reinterpret_cast<uint16_t*>(replay_smem + 5 * kReplayBuckets);
-  uint8_t* N = reinterpret_cast<uint8_t*>(E + kBucket * kReplayBuckets);
+  uint16_t* E = reinterpret_cast<uint16_t*>(replay_smem + 3 * kReplayBuckets);
   constexpr uint32_t kWarps = kReplayBuckets / 32;
   const uint32_t lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
   const uint32_t c = threadIdx.x;  // this thread's bucket column
@@ -1748,8 +1738,10 @@ __global__ void __launch_bounds__(kReplayBuckets)
         mv[j] = __ballot_sync(0xFFFFFFFFu, (e & kEntMove) != 0);
       }
       dmax = __reduce_max_sync(0xFFFFFFFFu, dmax);
+      // the new bucket's map row starts empty; the replay fills what it moves
+      reinterpret_cast<uint32_t*>(maps + b * 2 * kBucket + kBucket)[lane] = 0xFFFFFFFFu;
       if (lane == 0) {
-        mask[4 * kReplayBuckets + i] = dmax;
+        mask[2 * kReplayBuckets + i] = dmax;
         mask[0 * kReplayBuckets + i] = mv[0] | (uint64_t{mv[1]} << 32);
         mask[1 * kReplayBuckets + i] = mv[2] | (uint64_t{mv[3]} << 32);
       }
@@ -1762,7 +1754,8 @@ __global__ void __launch_bounds__(kReplayBuckets)
       // slot q of this column: col[(q / 2) * 2 kReplayBuckets + q % 2]
       uint16_t* col = E + 2 * c;
       // no entry can fill a hole farther behind it than this
-      const uint32_t reach = static_cast<uint32_t>(mask[4 * kReplayBuckets + c]) + 1;
+      const uint32_t reach = static_cast<uint32_t>(mask[2 * kReplayBuckets + c]) + 1;
+      uint8_t* nmap = maps + b * 2 * kBucket + kBucket;
       uint64_t nocc0 = 0, nocc1 = 0;
       int32_t moved = 0, removed = 0;
       while (mv0 | mv1) {
@@ -1773,7 +1766,7 @@ __global__ void __launch_bounds__(kReplayBuckets)
         // hash bits are its start position in either bucket
         const uint32_t p = first_free_from(nocc0, nocc1, e & (kBucket - 1));
         if (p < kBucket) {
-          N[nsrc_index(p, c)] = static_cast<uint8_t>(e >> kEntSrcShift);
+          nmap[p] = static_cast<uint8_t>(e >> kEntSrcShift);
           bit_set(nocc0, nocc1, p);
           moved++;
         }
@@ -1803,29 +1796,23 @@ __global__ void __launch_bounds__(kReplayBuckets)
           }
         }
       }
-      mask[2 * kReplayBuckets + c] = nocc0;
-      mask[3 * kReplayBuckets + c] = nocc1;
       t.sizes[b] -= removed;
       t.sizes[b + old_nb] = moved;
     }
     __syncthreads();
     // maps: bytes [0, kBucket) the original slot of each final old-bucket
-    // slot, [kBucket, 2 kBucket) of each new-bucket slot; 0xFF: empty
+    // slot (written here), [kBucket, 2 kBucket) of each new-bucket slot
+    // (written by the replay); 0xFF: empty
     for (uint32_t i = wi; i < kReplayBuckets && b0 + i < old_nb; i += kWarps) {
-      const uint64_t nocc0 = mask[2 * kReplayBuckets + i], nocc1 = mask[3 * kReplayBuckets + i];
-      uint32_t ow = 0, nw = 0;
+      uint32_t ow = 0;
 #pragma unroll
       for (uint32_t k = 0; k < 4; k++) {
         const uint32_t q = lane * 4 + k;
         const uint32_t e = E[ent_index(q, i)];
         const uint32_t os = (e & kEntEmpty) ? 0xFFu : (e >> kEntSrcShift) & 0x7Fu;
-        const uint32_t ns = bit_test(nocc0, nocc1, q) ? N[nsrc_index(q, i)] : 0xFFu;
         ow |= os << (8 * k);
-        nw |= ns << (8 * k);
       }
-      uint32_t* mw = reinterpret_cast<uint32_t*>(maps + (b0 + i) * 2 * kBucket);
-      mw[lane] = ow;
-      mw[32 + lane] = nw;
+      reinterpret_cast<uint32_t*>(maps + (b0 + i) * 2 * kBucket)[lane] = ow;
     }
     __syncthreads();
   }
