@@ -987,6 +987,14 @@ def config5_leg(rank, world, dist, device, steps=5, warm=2, timeline=False):
     del table, local, ek, ev, es
     torch.cuda.empty_cache()
     keys = batch * steps * world
+    # per GPU and step, the same merged-batch model as --workload zipf: merge
+    # reads of keys and scores, each distinct key's find or insert (hit
+    # model, 160 + 2 Vb), one output row per later occurrence; the NVLink
+    # bytes of N > 1 are not counted
+    peak, peak_kind = peaks()
+    vb = dim * 4
+    step_bytes = 16 * batch + uniq * batch * (160 + 2 * vb) + (1 - uniq) * batch * vb
+    ach = step_bytes / (ms / steps * 1e-3) / 1e9
     return {"workload": "BASELINE config 5: 256 Mi slots per GPU, dim 64, kLfu (scores "
                         "1..16), 8 Mi keys per GPU per step (seeded Zipf(1.1) stand-in over "
                         "2^30 ids, repeats merged), find_or_insert routed to the owner "
@@ -998,7 +1006,11 @@ def config5_leg(rank, world, dist, device, steps=5, warm=2, timeline=False):
             "find_or_insert_bkvs_per_gpu": round(keys / world / (ms * 1e-3) / 1e9, 4),
             "ms_per_step": round(ms / steps, 4),
             "export_ms": round(ems, 3), "exported_keys": int(lt.item()),
-            "export_slots_per_ns": round(cap * world / (ems * 1e-3) / 1e9, 3)}
+            "export_slots_per_ns": round(cap * world / (ems * 1e-3) / 1e9, 3),
+            "roofline_per_gpu": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak,
+                                 "unit": "GB/s", "frac": round(ach / peak, 4),
+                                 "algorithmic_bytes_per_step": int(step_bytes),
+                                 "peak_kind": peak_kind}}
 
 
 def run_zipf(args):
@@ -1050,6 +1062,14 @@ def run_zipf(args):
         batches.append((k, torch.randn((batch, dim), generator=gen, device=device),
                         torch.randint(1, 17, (batch,), generator=gen, device=device)))
     uniq = sum(int(torch.unique(b[0]).numel()) for b in batches) / (nb * batch)
+    peak, peak_kind = peaks()
+    vb = dim * 4
+
+    def merged_roofline(ms_step, per_step_bytes):
+        ach = per_step_bytes / (ms_step * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(ach / peak, 4), "algorithmic_bytes_per_step": int(per_step_bytes),
+                "peak_kind": peak_kind}
 
     def step(i):
         # values are in/out: a found key's row overwrites its input row, a
@@ -1125,10 +1145,18 @@ def run_zipf(args):
         reported = torch.isin(k, ek[:c])
         ok = bool((found | reported).all().item())
         local.check_device_error()
+        outs_step = sum(int(o.item()) for o in outs) / steps
+        u_ie = sum(int(torch.unique(b[0]).numel()) for b in batches) / nb
+        # merge reads of keys and scores, each distinct key's upsert (hit
+        # model, 160 + 2 Vb), and per reported tuple the eviction's score scan
+        # (1025 more) and the output key, score and row
+        ie_bytes = 16 * batch + u_ie * (160 + 2 * vb) + outs_step * (1025 + 16 + vb)
         ie = {"bkvs": round(batch * steps / (ie_ms * 1e-3) / 1e9, 4),
               "ms_per_step": round(ie_ms / steps, 4),
-              "outputs_per_step": round(sum(int(o.item()) for o in outs) / steps, 1),
-              "every_input_present_or_reported": ok}
+              "outputs_per_step": round(outs_step, 1),
+              "distinct_fraction": round(u_ie / batch, 4),
+              "every_input_present_or_reported": ok,
+              "roofline": merged_roofline(ie_ms / steps, ie_bytes)}
         log(f"insert_and_evict leg: {ie}")
     if rank == 0:
         print(json.dumps({
@@ -1146,6 +1174,12 @@ def run_zipf(args):
                        "capacity_per_gpu": cap, "dim": dim, "batch_per_gpu": batch,
                        "distinct_fraction": round(uniq, 4),
                        "batches_cycled": nb},
+            # merge reads of keys and scores, each distinct key's find or
+            # insert (hit model, 160 + 2 Vb), one output row per later
+            # occurrence
+            "roofline": merged_roofline(
+                ms / steps, 16 * batch + uniq * batch * (160 + 2 * vb)
+                + (1 - uniq) * batch * vb),
             "insert_and_evict": ie}), flush=True)
     if world > 1:
         table.close()
