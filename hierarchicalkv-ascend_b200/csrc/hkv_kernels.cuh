@@ -816,7 +816,8 @@ __device__ __forceinline__ void upsert_body(const TableView& t, const UpsertArgs
   const uint64_t n = a.dn != nullptr ? *a.dn : a.n;
   const uint32_t vb = t.value_bytes;
   const uint32_t nv = vb / VW;
-  // find_or_insert with values_in set (the sharded owner: input rows in a
+  // find_or_insert with values_in set (the table's own calls, with the
+  // caller's rows in both; the sharded owner, with the input rows in a
   // peer's memory) reads an input row only for a key it inserts, and writes
   // values_io only for a key it finds
   const uint8_t* in_rows = Mode == kModeFindOrInsert

@@ -707,7 +707,10 @@ void TableImpl::find_or_insert(size_t n, const uint64_t* keys, uint8_t* values,
   check_strategy(scores, ignore);
   HKV_REQUIRE(keys != nullptr && values != nullptr, HKV_ERR_INVALID,
               "keys and values must not be null");
-  upsert(kModeFindOrInsert, n, keys, nullptr, values, scores, nullptr, nullptr,
+  // the input rows are passed as values_in too: the kernel then reads a
+  // key's input row only when it inserts the key, instead of loading every
+  // row before the probe (a found key's row replaces it)
+  upsert(kModeFindOrInsert, n, keys, values, values, scores, nullptr, nullptr,
          nullptr, nullptr, s, unique, ignore, status);
 }
 
@@ -1256,6 +1259,7 @@ void TableImpl::find_or_insert_in_scratch(size_t n, const uint64_t* keys,
   UpsertArgs a;
   std::memset(&a, 0, sizeof a);
   a.keys = ukeys;
+  a.values_in = values;  // input rows read only for inserted keys
   a.values_io = values;
   a.row_index = rep_first;
   a.scores = uscores;
