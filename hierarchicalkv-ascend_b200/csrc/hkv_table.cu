@@ -1000,34 +1000,35 @@ size_t TableImpl::load(hkv_kv_read_fn read, void* user, size_t max_ws,
 // ---------------------------------------------------------------------------
 // reserve, reference hkv_hashtable.h:2873-2935 and table.h:360-377
 // ---------------------------------------------------------------------------
-void TableImpl::double_capacity(cudaStream_t s) {
+void TableImpl::grow(uint64_t final_nb, cudaStream_t s) {
   // a rehash would move a key a caller holds locked away from the address
   // the caller was given
   HKV_REQUIRE(sum_counts(num_buckets_, kLockShift, s) == 0, HKV_ERR_RUNTIME,
               "the table cannot grow while keys are locked (lock_keys or "
               "find_or_insert with locked_key_ptrs): unlock them first");
-  const uint64_t old_nb = num_buckets_, new_nb = old_nb * 2;
-  const size_t new_slots = new_nb * kBucket;
+  const uint64_t start_nb = num_buckets_;
+  const size_t final_slots = final_nb * kBucket;
   // pass 2 runs one warp per old bucket, each with kBucket scratch rows for
   // the rows that change slot inside their bucket (at most 512 MB of scratch)
   const uint64_t row_block = uint64_t{kBucket} * value_bytes_;
   const uint64_t max_warps = std::max<uint64_t>(
       8, std::min<uint64_t>(sm_count_ * 64ull, (512ull << 20) / row_block));
-  const int grid = static_cast<int>(
-      std::max<uint64_t>(1, std::min<uint64_t>(ceil_div(old_nb, 8), max_warps / 8)));
-  // every allocation first: a failure leaves the table as it was
+  const int grid = static_cast<int>(std::max<uint64_t>(
+      1, std::min<uint64_t>(ceil_div(final_nb / 2, 8), max_warps / 8)));
+  // every allocation first, once for all the doublings: a failure leaves the
+  // table as it was
   Workspace ws(s, pool_, &mem_);
   uint64_t *nk = nullptr, *ns = nullptr;
   uint8_t* nd = nullptr;
   int32_t* nz = nullptr;
   uint8_t *maps = nullptr, *scratch = nullptr;
   try {
-    nk = static_cast<uint64_t*>(mem_.device(new_slots * 8));
-    ns = static_cast<uint64_t*>(mem_.device(new_slots * 8));
-    nd = static_cast<uint8_t*>(mem_.device(new_slots));
-    nz = static_cast<int32_t*>(mem_.device(new_nb * 4));
-    // 2 x kBucket bytes of slot maps per old bucket (pass 1 -> pass 2)
-    maps = ws.get<uint8_t>(old_nb * 2 * kBucket);
+    nk = static_cast<uint64_t*>(mem_.device(final_slots * 8));
+    ns = static_cast<uint64_t*>(mem_.device(final_slots * 8));
+    nd = static_cast<uint8_t*>(mem_.device(final_slots));
+    nz = static_cast<int32_t*>(mem_.device(final_nb * 4));
+    // 2 x kBucket bytes of slot maps per old bucket of the last doubling
+    maps = ws.get<uint8_t>(final_nb / 2 * 2 * kBucket);
     scratch = ws.get<uint8_t>(uint64_t{static_cast<uint32_t>(grid)} * 8 * row_block);
   } catch (...) {
     mem_.free_device(nk);
@@ -1036,13 +1037,15 @@ void TableImpl::double_capacity(cudaStream_t s) {
     mem_.free_device(nz);
     throw;
   }
-  allocate_slices(old_nb, new_nb);
+  allocate_slices(start_nb, final_nb);
   upload_slices();
-  // The two passes read the old key and score arrays and write every slot
-  // of both halves of the new ones (keys, scores, digests), so neither a
-  // copy of the old metadata nor a clear of the new buckets is needed; the
-  // sizes start from the old ones.
-  CUDA_TRY(cudaMemcpyAsync(nz, sizes_, old_nb * 4, cudaMemcpyDeviceToDevice, s));
+  // The two passes read the key and score arrays of the previous size and
+  // write every slot of both halves of the doubled size (keys, scores,
+  // digests), so neither a copy of the old metadata nor a clear of the new
+  // buckets is needed; the sizes start from the old ones. The first doubling
+  // reads the old arrays, each later one the new arrays in place (pass 2
+  // stages an old bucket in shared memory before it rewrites it).
+  CUDA_TRY(cudaMemcpyAsync(nz, sizes_, start_nb * 4, cudaMemcpyDeviceToDevice, s));
   uint64_t* const ok = keys_;
   uint64_t* const os = scores_;
   uint8_t* const od = digests_;
@@ -1051,22 +1054,28 @@ void TableImpl::double_capacity(cudaStream_t s) {
   scores_ = ns;
   digests_ = nd;
   sizes_ = nz;
-  num_buckets_ = new_nb;
-  capacity_ = new_slots;
-  magic_for(capacity_, &div_magic_, &div_shift_);
-  const TableView v = view();
   CUDA_TRY(cudaFuncSetAttribute(rehash_replay_kernel,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(kReplaySmem)));
-  const int rgrid = static_cast<int>(std::max<uint64_t>(
-      1, std::min<uint64_t>(ceil_div(old_nb, kReplayBuckets), sm_count_ * 64ull)));
-  rehash_replay_kernel<<<rgrid, kReplayBuckets, kReplaySmem, counted(s)>>>(v, old_nb, ok,
-                                                                          maps);
-  CUDA_TRY(cudaGetLastError());
   const int vw = value_width({});
-  DISPATCH_VW(vw, rehash_apply_kernel<VW><<<grid, 256, 0, counted(s)>>>(v, old_nb, ok, os,
-                                                                        maps, scratch));
-  CUDA_TRY(cudaGetLastError());
+  const uint64_t* src_keys = ok;
+  const uint64_t* src_scores = os;
+  for (uint64_t old_nb = start_nb; old_nb < final_nb; old_nb *= 2) {
+    num_buckets_ = old_nb * 2;
+    capacity_ = num_buckets_ * kBucket;
+    magic_for(capacity_, &div_magic_, &div_shift_);
+    const TableView v = view();
+    const int rgrid = static_cast<int>(std::max<uint64_t>(
+        1, std::min<uint64_t>(ceil_div(old_nb, kReplayBuckets), sm_count_ * 64ull)));
+    rehash_replay_kernel<<<rgrid, kReplayBuckets, kReplaySmem, counted(s)>>>(v, old_nb,
+                                                                            src_keys, maps);
+    CUDA_TRY(cudaGetLastError());
+    DISPATCH_VW(vw, rehash_apply_kernel<VW><<<grid, 256, 0, counted(s)>>>(
+                        v, old_nb, src_keys, src_scores, maps, scratch));
+    CUDA_TRY(cudaGetLastError());
+    src_keys = keys_;
+    src_scores = scores_;
+  }
   CUDA_TRY(cudaStreamSynchronize(s));
   mem_.free_device(ok);
   mem_.free_device(os);
@@ -1080,8 +1089,12 @@ void TableImpl::reserve(size_t new_capacity, cudaStream_t s) {
     return;
   }
   CUDA_TRY(cudaStreamSynchronize(s));
-  while (capacity_ < new_capacity && capacity_ * 2 <= opt_.max_capacity)
-    double_capacity(s);
+  // the reference doubles until the capacity covers the request
+  // (hkv_hashtable.h:2873-2935); here the arrays grow once to the final size
+  // and the doublings' rehashes run one after another
+  uint64_t target = capacity_;
+  while (target < new_capacity && target * 2 <= opt_.max_capacity) target *= 2;
+  if (target > capacity_) grow(target / kBucket, s);
   reach_max_ = capacity_ * 2 > opt_.max_capacity;
 }
 

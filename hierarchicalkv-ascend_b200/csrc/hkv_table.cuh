@@ -346,7 +346,9 @@ class TableImpl {
   // frees every table allocation (destructor, failed construction)
   void release() noexcept;
   void upload_slices();
-  void double_capacity(cudaStream_t s);
+  // doubles the bucket count until it reaches final_nb (a power of two
+  // times the current count), rehashing after each doubling
+  void grow(uint64_t final_nb, cudaStream_t s);
   void upsert(int mode, size_t n, const uint64_t* keys,
               const uint8_t* values_in, uint8_t* values_io,
               const uint64_t* scores, uint64_t* ev_keys, uint8_t* ev_values,
