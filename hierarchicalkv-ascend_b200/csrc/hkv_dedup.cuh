@@ -265,25 +265,66 @@ __global__ void dedup_inverse_kernel(DedupView d,
 
 // find_or_insert scatter: the representatives found or inserted their keys
 // in place (at their first occurrence's row); every later occurrence reads
-// its representative's row. values is both source and destination.
+// its representative's row. values is both source and destination (a source
+// row is a first occurrence, never a destination). A warp resolves 32
+// consecutive occurrences at once, lists the ones that copy, and moves their
+// rows 32 / nv at a time (nv vectors per row), four rows in flight per lane.
 template <int VW>
-__global__ void scatter_found_rows_kernel(uint8_t* values,
-                                          const uint32_t* __restrict__ uid_of,
-                                          const uint32_t* __restrict__ rep_first,
-                                          const uint8_t* __restrict__ ustatus,
-                                          uint64_t n, uint32_t vb) {
-  const Tile tile;
-  const uint64_t ntiles = (uint64_t)gridDim.x * (blockDim.x / kTile);
-  for (uint64_t i = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / kTile;
-       i < n; i += ntiles) {
-    const uint32_t u = uid_of[i];
-    if (u == kNoIndex) continue;
-    const uint32_t f = rep_first[u];
-    if (f == static_cast<uint32_t>(i)) continue;
-    const uint8_t st = ustatus[u];
-    if (st == kRefused || st == kIllegal || st == kTimedOut) continue;
-    copy_row<VW>(values + i * vb, values + static_cast<uint64_t>(f) * vb, vb, tile.lane,
-                 kTile);
+__global__ void __launch_bounds__(256)
+    scatter_found_rows_kernel(uint8_t* values, const uint32_t* __restrict__ uid_of,
+                              const uint32_t* __restrict__ rep_first,
+                              const uint8_t* __restrict__ ustatus, uint64_t n, uint32_t vb) {
+  using V = typename VecOf<VW>::T;
+  __shared__ uint8_t lst[8][32];  // blockDim.x == 256: 8 warps
+  const uint32_t nv = vb / VW;
+  const uint32_t lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
+  const uint64_t warp = (blockIdx.x * uint64_t{blockDim.x} + threadIdx.x) >> 5;
+  const uint64_t nwarps = uint64_t{gridDim.x} * (blockDim.x >> 5);
+  for (uint64_t base = warp * 32; base < n; base += nwarps * 32) {
+    const uint64_t i = base + lane;
+    uint32_t src = kNoIndex;
+    if (i < n) {
+      const uint32_t u = uid_of[i];
+      if (u != kNoIndex) {
+        const uint32_t f = rep_first[u];
+        const uint8_t st = ustatus[u];
+        if (f != static_cast<uint32_t>(i) && st != kRefused && st != kIllegal &&
+            st != kTimedOut)
+          src = f;
+      }
+    }
+    const uint32_t todo = __ballot_sync(0xFFFFFFFFu, src != kNoIndex);
+    if (src != kNoIndex) lst[wi][__popc(todo & ((1u << lane) - 1))] = static_cast<uint8_t>(lane);
+    __syncwarp();
+    const uint32_t cnt = __popc(todo);
+    if (nv <= 32) {
+      const uint32_t rpi = 32 / nv, lq = lane / nv, lv = lane - lq * nv;
+      for (uint32_t k0 = 0; k0 < cnt; k0 += 4 * rpi) {
+        V x[4];
+        uint32_t rr[4];
+        bool ok[4];
+#pragma unroll
+        for (uint32_t u = 0; u < 4; u++) {
+          const uint32_t k = k0 + u * rpi + lq;
+          ok[u] = lq < rpi && k < cnt;
+          rr[u] = ok[u] ? lst[wi][k] : 0u;
+          const uint32_t sr = __shfl_sync(0xFFFFFFFFu, src, rr[u]);
+          if (ok[u]) x[u] = reinterpret_cast<const V*>(values + uint64_t{sr} * vb)[lv];
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < 4; u++)
+          if (ok[u]) reinterpret_cast<V*>(values + (base + rr[u]) * vb)[lv] = x[u];
+      }
+    } else {
+      for (uint32_t k = 0; k < cnt; k++) {
+        const uint32_t r = lst[wi][k];
+        const uint32_t sr = __shfl_sync(0xFFFFFFFFu, src, r);
+        const V* sp = reinterpret_cast<const V*>(values + uint64_t{sr} * vb);
+        V* dp = reinterpret_cast<V*>(values + (base + r) * vb);
+        for (uint32_t v = lane; v < nv; v += 32) dp[v] = sp[v];
+      }
+    }
+    __syncwarp();  // the next pass rewrites the list
   }
 }
 
