@@ -1037,8 +1037,29 @@ void TableImpl::grow(uint64_t final_nb, cudaStream_t s) {
     mem_.free_device(nz);
     throw;
   }
-  allocate_slices(start_nb, final_nb);
-  upload_slices();
+  const size_t had_slices = slices_.size();
+  const size_t had_hbm = remaining_hbm_;
+  const bool was_pure = pure_hbm_;
+  try {
+    allocate_slices(start_nb, final_nb);
+    upload_slices();
+  } catch (...) {
+    // give back the slices this call added, then the new arrays
+    for (size_t i = had_slices; i < slices_.size(); i++) {
+      if (slices_[i].host != nullptr)
+        mem_.free_pinned(slices_[i].host);
+      else
+        mem_.free_device(slices_[i].dev);
+    }
+    slices_.resize(had_slices);
+    remaining_hbm_ = had_hbm;
+    pure_hbm_ = was_pure;
+    mem_.free_device(nk);
+    mem_.free_device(ns);
+    mem_.free_device(nd);
+    mem_.free_device(nz);
+    throw;
+  }
   // The two passes read the key and score arrays of the previous size and
   // write every slot of both halves of the doubled size (keys, scores,
   // digests), so neither a copy of the old metadata nor a clear of the new

@@ -155,3 +155,48 @@ def test_a_failing_allocator_fails_the_call():
     with pytest.raises(H.CudaException):
         table_with(a, 128 * 4096, 128 * 4096, dim=64)
     assert not a.blocks  # what was taken before the failure went back
+
+
+def test_a_reserve_that_fails_leaves_the_table_as_it_was():
+    """The second new value slice is refused: reserve raises, every block it
+    took goes back, and the table keeps its capacity, size and contents."""
+
+    class RefusesSecondSlice(Counting):
+        armed = False
+        seen = 0
+
+        def alloc(self, mt, size, flags=0):
+            if self.armed and size == 64 * 128 * 16 * 4:  # one 64-bucket value slice
+                self.seen += 1
+                if self.seen == 2:
+                    raise MemoryError("no")
+            return Counting.alloc(self, mt, size, flags)
+
+    a = RefusesSecondSlice()
+    cap, dim = 128 * 64, 16
+    t = table_with(a, cap, 128 * 256, dim=dim)
+    rng = np.random.default_rng(77)
+    keys = np.unique(rng.integers(1, 1 << 62, 6000, dtype=np.uint64))[:5000]
+    vals = rng.standard_normal((len(keys), dim)).astype(np.float32)
+    t.insert_or_assign(len(keys), torch.from_numpy(keys.view(np.int64)).cuda(),
+                       torch.from_numpy(vals).cuda())
+    torch.cuda.synchronize()
+    size_before = t.size()
+    held = set(a.blocks)
+    a.armed = True
+    with pytest.raises(H.CudaException):
+        t.reserve(128 * 256)
+    a.armed = False
+    assert set(a.blocks) == held  # the call's new arrays and slices went back
+    assert t.capacity() == cap and t.size() == size_before
+    got = torch.zeros((len(keys), dim), device="cuda")
+    f = torch.zeros(len(keys), dtype=torch.bool, device="cuda")
+    t.find(len(keys), torch.from_numpy(keys.view(np.int64)).cuda(), got, f)
+    torch.cuda.synchronize()
+    ok = f.cpu().numpy()
+    assert ok.sum() == size_before
+    assert (got.cpu().numpy()[ok] == vals[ok]).all()
+    # and it can still grow
+    t.reserve(128 * 256)
+    assert t.capacity() == 128 * 256 and t.size() == size_before
+    t.close()
