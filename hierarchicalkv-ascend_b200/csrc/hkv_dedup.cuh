@@ -17,7 +17,6 @@ struct DedupView {
   uint64_t* set_keys;   // [cap] EMPTY_KEY when free
   uint32_t* set_first;  // [cap] smallest input index holding that key
   uint32_t* set_last;   // [cap] largest input index holding that key
-  uint32_t* set_uid;    // [cap] representative number of that key
   unsigned long long* set_sum;  // [cap] summed scores (score_mode kScoreSum*)
   uint64_t cap;         // power of two
 };
@@ -220,9 +219,12 @@ __global__ void __launch_bounds__(kScanThreads)
     if (base + j < n) data[base + j] += add;
 }
 
-// Stage 3: representatives. For first occurrence i with rank u:
-// ukeys[u] = key, set_uid[slot] = u, rep_first[u] = i, rep_last[u] = the
-// key's last index, uscores[u] = its merged score (score_mode).
+// Stage 3: representatives and the inverse map. Every input i gets
+// uid_of[i] = the representative number of its key, which is the scanned
+// rank of the key's first occurrence (kNoIndex for reserved inputs); for a
+// first occurrence i with rank u: ukeys[u] = key, rep_first[u] = i,
+// rep_last[u] = the key's last index, uscores[u] = its merged score
+// (score_mode).
 __global__ void dedup_emit_kernel(DedupView d, const uint64_t* __restrict__ keys,
                                   const uint32_t* __restrict__ slot_of,
                                   const uint32_t* __restrict__ rank, uint64_t n,
@@ -230,15 +232,21 @@ __global__ void dedup_emit_kernel(DedupView d, const uint64_t* __restrict__ keys
                                   uint32_t* __restrict__ rep_first,
                                   uint32_t* __restrict__ rep_last,
                                   const uint64_t* __restrict__ scores, int score_mode,
-                                  uint64_t* __restrict__ uscores) {
+                                  uint64_t* __restrict__ uscores,
+                                  uint32_t* __restrict__ uid_of) {
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
        i += (uint64_t)gridDim.x * blockDim.x) {
     const uint32_t s = slot_of[i];
-    if (s == kNoIndex || d.set_first[s] != static_cast<uint32_t>(i)) continue;
-    const uint32_t u = rank[i];
+    if (s == kNoIndex) {
+      uid_of[i] = kNoIndex;
+      continue;
+    }
+    const uint32_t f = d.set_first[s];
+    const uint32_t u = rank[f];
+    uid_of[i] = u;
+    if (f != static_cast<uint32_t>(i)) continue;
     const uint32_t last = d.set_last[s];
     ukeys[u] = keys[i];
-    d.set_uid[s] = u;
     rep_first[u] = static_cast<uint32_t>(i);
     if (rep_last) rep_last[u] = last;
     if (score_mode == kScoreLast) {
@@ -249,17 +257,6 @@ __global__ void dedup_emit_kernel(DedupView d, const uint64_t* __restrict__ keys
       const uint64_t t = d.set_sum[s];
       uscores[u] = t > 0xFFFFFFFFull ? 0xFFFFFFFFull : t;
     }
-  }
-}
-
-// Stage 4: inverse map uid_of[i] (kNoIndex for reserved inputs).
-__global__ void dedup_inverse_kernel(DedupView d,
-                                     const uint32_t* __restrict__ slot_of,
-                                     uint64_t n, uint32_t* __restrict__ uid_of) {
-  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
-       i += (uint64_t)gridDim.x * blockDim.x) {
-    const uint32_t s = slot_of[i];
-    uid_of[i] = s == kNoIndex ? kNoIndex : d.set_uid[s];
   }
 }
 

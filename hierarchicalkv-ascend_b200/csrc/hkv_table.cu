@@ -635,8 +635,7 @@ void dedup_stages(const DedupView& d, size_t n, const uint64_t* keys,
   scan_add_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, counted(s)>>>(rank, n,
                                                                              sums);
   dedup_emit_kernel<<<g1, 256, 0, counted(s)>>>(d, keys, slot_of, rank, n, ukeys, rep_first,
-                                                rep_last, scores, score_mode, uscores);
-  dedup_inverse_kernel<<<g1, 256, 0, counted(s)>>>(d, slot_of, n, uid_of);
+                                                rep_last, scores, score_mode, uscores, uid_of);
   CUDA_TRY(cudaGetLastError());
 }
 
@@ -651,7 +650,6 @@ DedupResult dedup_batch(size_t n, const uint64_t* keys, const uint64_t* scores,
   d.set_keys = ws.get<uint64_t>(cap);
   d.set_first = ws.get<uint32_t>(cap);
   d.set_last = ws.get<uint32_t>(cap);
-  d.set_uid = ws.get<uint32_t>(cap);
   d.set_sum = score_mode >= kScoreSum ? ws.get<unsigned long long>(cap) : nullptr;
   DedupResult r;
   uint32_t* slot_of = ws.get<uint32_t>(n);
@@ -1273,7 +1271,6 @@ void TableImpl::find_or_insert_in_scratch(size_t n, const uint64_t* keys,
   d.set_keys = ws.get<uint64_t>(d.cap);
   d.set_first = ws.get<uint32_t>(d.cap);
   d.set_last = ws.get<uint32_t>(d.cap);
-  d.set_uid = ws.get<uint32_t>(d.cap);
   d.set_sum = ws.get<unsigned long long>(d.cap);
   uint32_t* slot_of = ws.get<uint32_t>(n);
   uint32_t* rank = ws.get<uint32_t>(n);
