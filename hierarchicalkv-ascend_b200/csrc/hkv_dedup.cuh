@@ -16,7 +16,8 @@ constexpr uint32_t kNoIndex = 0xFFFFFFFFu;
 struct DedupView {
   uint64_t* set_keys;   // [cap] EMPTY_KEY when free
   uint32_t* set_first;  // [cap] smallest input index holding that key
-  uint32_t* set_last;   // [cap] largest input index holding that key
+  uint32_t* set_last;   // [cap] largest input index holding that key (nullptr:
+                        // not needed, the last occurrence is never used)
   unsigned long long* set_sum;  // [cap] summed scores (score_mode kScoreSum*)
   uint64_t cap;         // power of two
 };
@@ -114,7 +115,7 @@ dedup_insert_kernel(DedupView d, const uint64_t* __restrict__ keys, uint64_t n,
         atomicOr(error, kErrSpinTimeout);  // set full: cannot happen at 2x
       } else {
         atomicMin(d.set_first + res, lfirst[l]);
-        atomicMax(d.set_last + res, llast[l]);
+        if (d.set_last != nullptr) atomicMax(d.set_last + res, llast[l]);
         if (sum) atomicAdd(d.set_sum + res, lsum[l]);
       }
       lfirst[l] = res;
@@ -245,7 +246,7 @@ __global__ void dedup_emit_kernel(DedupView d, const uint64_t* __restrict__ keys
     const uint32_t u = rank[f];
     uid_of[i] = u;
     if (f != static_cast<uint32_t>(i)) continue;
-    const uint32_t last = d.set_last[s];
+    const uint32_t last = d.set_last != nullptr ? d.set_last[s] : 0u;
     ukeys[u] = keys[i];
     rep_first[u] = static_cast<uint32_t>(i);
     if (rep_last) rep_last[u] = last;

@@ -503,7 +503,7 @@ class ShardedImpl {
       d.dm = nullptr;
     } else if (n > 0) {
       d = dedup_batch(n, keys, in_scores, st, ws, s, sm_count_,
-                      local_->error_word());
+                      local_->error_word(), kind != 1);
     } else {
       d.ukeys = ws.get<uint64_t>(1);
       d.rep_first = d.rep_last = d.uid_of = ws.get<uint32_t>(1);
@@ -724,7 +724,7 @@ class ShardedImpl {
       rscores = send_scores ? scores : nullptr;
     } else if (kind != 0 && n > 0) {
       const DedupResult d = dedup_batch(n, keys, send_scores ? scores : nullptr,
-                                        st, ws, s, sm_count_, err);
+                                        st, ws, s, sm_count_, err, kind != 1);
       rkeys = d.ukeys;
       rscores = d.uscores;
       row_of = kind == 1 ? d.rep_first : d.rep_last;

@@ -536,7 +536,8 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
     // repeated keys: the representatives get addresses, every occurrence
     // then takes its representative's
     Workspace ws(s, pool_, &mem_);
-    const DedupResult d = dedup_batch(n, keys, scores, st, ws, s, sm_count_, d_error_);
+    const DedupResult d =
+        dedup_batch(n, keys, scores, st, ws, s, sm_count_, d_error_, false);
     uint8_t** uptrs = ws.get<uint8_t*>(n);
     bool* ufound = ws.get<bool>(n);
     a.keys = d.ukeys;
@@ -560,8 +561,8 @@ void TableImpl::upsert(int mode, size_t n, const uint64_t* keys,
 
   // ---- duplicate keys: merge to one representative per key ---------------
   Workspace ws(s, pool_, &mem_);
-  const DedupResult d =
-      dedup_batch(n, keys, scores, st, ws, s, sm_count_, d_error_);
+  const DedupResult d = dedup_batch(n, keys, scores, st, ws, s, sm_count_, d_error_,
+                                    mode != kModeFindOrInsert);
   uint8_t* ustatus = ws.get<uint8_t>(n);
   const uint32_t* uid_of = d.uid_of;
   // Each representative works on the caller's row of one of its
@@ -619,7 +620,7 @@ void dedup_stages(const DedupView& d, size_t n, const uint64_t* keys,
                   uint64_t* uscores, cudaStream_t s, int sm_count, int* d_error) {
   CUDA_TRY(cudaMemsetAsync(d.set_keys, 0xFF, d.cap * 8, s));
   CUDA_TRY(cudaMemsetAsync(d.set_first, 0xFF, d.cap * 4, s));
-  CUDA_TRY(cudaMemsetAsync(d.set_last, 0, d.cap * 4, s));
+  if (d.set_last != nullptr) CUDA_TRY(cudaMemsetAsync(d.set_last, 0, d.cap * 4, s));
   if (score_mode >= kScoreSum) CUDA_TRY(cudaMemsetAsync(d.set_sum, 0, d.cap * 8, s));
   const uint64_t ntiles = ceil_div(n, kScanTile);
   const int g1 = static_cast<int>(
@@ -641,15 +642,18 @@ void dedup_stages(const DedupView& d, size_t n, const uint64_t* keys,
 
 DedupResult dedup_batch(size_t n, const uint64_t* keys, const uint64_t* scores,
                         int strategy, Workspace& ws, cudaStream_t s,
-                        int sm_count, int* d_error) {
+                        int sm_count, int* d_error, bool need_last) {
   uint64_t cap = 1024;
   while (cap < 2 * static_cast<uint64_t>(n)) cap <<= 1;
   const int score_mode = dedup_score_mode(strategy, scores != nullptr);
+  // the last occurrence: its row (insert_or_assign, insert_and_evict) or its
+  // score (score_mode kScoreLast)
+  need_last = need_last || score_mode == kScoreLast;
   DedupView d;
   d.cap = cap;
   d.set_keys = ws.get<uint64_t>(cap);
   d.set_first = ws.get<uint32_t>(cap);
-  d.set_last = ws.get<uint32_t>(cap);
+  d.set_last = need_last ? ws.get<uint32_t>(cap) : nullptr;
   d.set_sum = score_mode >= kScoreSum ? ws.get<unsigned long long>(cap) : nullptr;
   DedupResult r;
   uint32_t* slot_of = ws.get<uint32_t>(n);
@@ -659,7 +663,7 @@ DedupResult dedup_batch(size_t n, const uint64_t* keys, const uint64_t* scores,
   r.dm = ws.get<uint32_t>(1);
   r.ukeys = ws.get<uint64_t>(n);
   r.rep_first = ws.get<uint32_t>(n);
-  r.rep_last = ws.get<uint32_t>(n);
+  r.rep_last = need_last ? ws.get<uint32_t>(n) : nullptr;
   r.uscores = scores ? ws.get<uint64_t>(n) : nullptr;
   dedup_stages(d, n, keys, scores, score_mode, slot_of, rank, sums, r.dm, r.ukeys,
                r.rep_first, r.rep_last, r.uid_of, r.uscores, s, sm_count, d_error);
@@ -1270,7 +1274,9 @@ void TableImpl::find_or_insert_in_scratch(size_t n, const uint64_t* keys,
   d.cap = kNoAllocSetSlots;
   d.set_keys = ws.get<uint64_t>(d.cap);
   d.set_first = ws.get<uint32_t>(d.cap);
-  d.set_last = ws.get<uint32_t>(d.cap);
+  // find_or_insert takes the first occurrence's row; the last matters only
+  // for its score under score_mode kScoreLast
+  d.set_last = score_mode == kScoreLast ? ws.get<uint32_t>(d.cap) : nullptr;
   d.set_sum = ws.get<unsigned long long>(d.cap);
   uint32_t* slot_of = ws.get<uint32_t>(n);
   uint32_t* rank = ws.get<uint32_t>(n);
@@ -1279,7 +1285,7 @@ void TableImpl::find_or_insert_in_scratch(size_t n, const uint64_t* keys,
   uint32_t* dm = ws.get<uint32_t>(1);
   uint64_t* ukeys = ws.get<uint64_t>(n);
   uint32_t* rep_first = ws.get<uint32_t>(n);
-  uint32_t* rep_last = ws.get<uint32_t>(n);
+  uint32_t* rep_last = d.set_last != nullptr ? ws.get<uint32_t>(n) : nullptr;
   uint64_t* uscores = scores ? ws.get<uint64_t>(n) : nullptr;
   uint8_t* ustatus = ws.get<uint8_t>(n);
   // the array keeps the previous call's contents: reset what starts empty

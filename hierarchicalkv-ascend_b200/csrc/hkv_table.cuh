@@ -171,9 +171,11 @@ struct DedupResult {
   uint64_t* uscores;  // merged scores, nullptr when scores == nullptr
   uint32_t* dm;
 };
+// need_last: the caller uses rep_last (rows from each key's last
+// occurrence); without it rep_last is nullptr unless the scores need it
 DedupResult dedup_batch(size_t n, const uint64_t* keys, const uint64_t* scores,
                         int strategy, Workspace& ws, cudaStream_t s,
-                        int sm_count, int* d_error);
+                        int sm_count, int* d_error, bool need_last = true);
 
 // The reference's api_lock (group_lock.h:45-406): readers share it
 // (find, contains, export, size), updaters share it (assign_scores), and
