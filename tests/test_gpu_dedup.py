@@ -79,3 +79,35 @@ def test_repeated_keys_across_merge_blocks(strategy, op):
     np.testing.assert_array_equal(gv, rv)
     # the hot keys did repeat across merge blocks of 1024 inputs
     assert np.bincount(np.searchsorted(np.sort(distinct), keys)).max() > 2000
+
+
+@pytest.mark.parametrize("dim", [5, 33, 136])
+def test_repeated_keys_rows_of_any_width(dim):
+    """The merge's row copies at row widths that take each copy path: 20-byte
+    rows (4-byte vectors, several rows per warp), 132-byte rows (33 vectors,
+    a warp per row) and 544-byte rows (34 16-byte vectors, a warp per row);
+    results against the oracle, as above."""
+    rng = np.random.default_rng(500 + dim)
+    cap, universe, n = 128 * 256, 3000, 12000
+    t = make_table(cap, dim=dim, strategy=H.EvictStrategy.kLfu)
+    o = O.OracleTable(cap, cap, dim=dim, strategy=O.LFU)
+    g = GpuOps(t, dim)
+    key_of = rng.permutation(np.unique(rng.integers(1, 1 << 62, 2 * universe,
+                                                    dtype=np.uint64)))[:universe]
+    pre = key_of[1::2]
+    pv = rng.standard_normal((len(pre), dim)).astype(np.float32)
+    ps = rng.integers(1, 50, len(pre)).astype(np.uint64)
+    g.insert_or_assign(pre, pv, ps)
+    o.insert_or_assign(pre, pv, ps)
+    keys = key_of[power_law_batch(rng, universe, n)]
+    vals = rng.standard_normal((n, dim)).astype(np.float32)
+    sc = rng.integers(1, 50, n).astype(np.uint64)
+    got = g.find_or_insert(keys, vals, sc, unique=False)
+    ref, _ = o.find_or_insert(keys, vals, sc)
+    np.testing.assert_array_equal(got, ref)
+    assert live(t.get_state()) == live(o.get_state())
+    distinct = np.unique(keys)
+    gv, gf, _ = g.find(distinct)
+    rv, rf = o.find(distinct)[:2]
+    assert gf.all() and rf.all()
+    np.testing.assert_array_equal(gv, rv)

@@ -382,6 +382,27 @@ def test_reserve_exact_layout(nb, erased):
     assert g.contains(present).all()
 
 
+@pytest.mark.parametrize("dim", [5, 33, 136])
+def test_reserve_rows_of_any_width(dim):
+    """reserve's row moves at row widths that take each copy path of the
+    rehash: 20-byte rows (4-byte vectors, several rows per warp pass),
+    132-byte rows (33 vectors) and 544-byte rows (34 16-byte vectors), the
+    latter two a warp per row; two doublings, the second in place; layout
+    and values equal the oracle's slot for slot."""
+    rng = np.random.default_rng(700 + dim)
+    cap = 128 * 32
+    g = GpuOps(make_table(cap, dim=dim, max_capacity=cap * 4, max_load_factor=1.0), dim)
+    pre = random_keys(rng, int(cap * 0.9))
+    g.insert_or_assign(pre, rng.standard_normal((len(pre), dim)).astype(np.float32),
+                       rng.integers(1, 1 << 30, len(pre)).astype(np.uint64))
+    g.erase(pre[:200])
+    o = oracle_from_gpu(g, cap, dim, O.CUSTOMIZED, max_capacity=cap * 4, lf=1.0)
+    g.t.reserve(cap * 4)
+    o.reserve(cap * 4)
+    assert g.t.capacity() == o.capacity() == cap * 4
+    assert_same_state(g, o)
+
+
 def test_reserve_into_host_slices():
     """BASELINE config 4's reserve, scaled down: max_hbm_for_vectors holds
     exactly the first value slice, so the slices a doubling appends go to
