@@ -130,17 +130,7 @@ dedup_insert_kernel(DedupView d, const uint64_t* __restrict__ keys, uint64_t n,
   }
 }
 
-// Stage 2: flag[i] = 1 iff input i is the first occurrence of its key.
-__global__ void dedup_flag_kernel(DedupView d, const uint32_t* __restrict__ slot_of,
-                                  uint64_t n, uint32_t* __restrict__ flag) {
-  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
-       i += (uint64_t)gridDim.x * blockDim.x) {
-    const uint32_t s = slot_of[i];
-    flag[i] = (s != kNoIndex && d.set_first[s] == static_cast<uint32_t>(i)) ? 1u : 0u;
-  }
-}
-
-// ---- exclusive prefix sum of uint32 (three passes) -------------------------
+// ---- Stage 2: exclusive prefix count of first occurrences (three passes) ---
 constexpr int kScanThreads = 256;
 constexpr int kScanItems = 8;
 constexpr int kScanTile = kScanThreads * kScanItems;
@@ -173,22 +163,30 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v,
   return before;
 }
 
-// pass 1: per-tile exclusive scan in place, tile totals to sums[]
+// pass 1 of the merge's scan with the flags computed in place: input i
+// counts 1 iff it is its key's first occurrence (the set holds the key's
+// smallest index); rank[i] = the exclusive count before i within the tile
 __global__ void __launch_bounds__(kScanThreads)
-    scan_tiles_kernel(uint32_t* __restrict__ data, uint64_t n,
-                      uint32_t* __restrict__ sums) {
+    scan_first_tiles_kernel(DedupView d, const uint32_t* __restrict__ slot_of, uint64_t n,
+                            uint32_t* __restrict__ rank, uint32_t* __restrict__ sums) {
   const uint64_t base = blockIdx.x * (uint64_t)kScanTile + threadIdx.x * kScanItems;
   uint32_t v[kScanItems], acc = 0;
 #pragma unroll
   for (int j = 0; j < kScanItems; j++) {
-    v[j] = (base + j < n) ? data[base + j] : 0u;
-    acc += v[j];
+    const uint64_t i = base + j;
+    uint32_t f = 0;
+    if (i < n) {
+      const uint32_t s = slot_of[i];
+      f = (s != kNoIndex && d.set_first[s] == static_cast<uint32_t>(i)) ? 1u : 0u;
+    }
+    v[j] = f;
+    acc += f;
   }
   uint32_t total;
   uint32_t run = block_exclusive_scan(acc, &total);
 #pragma unroll
   for (int j = 0; j < kScanItems; j++) {
-    if (base + j < n) data[base + j] = run;
+    if (base + j < n) rank[base + j] = run;
     run += v[j];
   }
   if (threadIdx.x == 0) sums[blockIdx.x] = total;

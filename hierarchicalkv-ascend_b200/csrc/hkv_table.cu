@@ -629,9 +629,8 @@ void dedup_stages(const DedupView& d, size_t n, const uint64_t* keys,
       std::min<uint64_t>(ceil_div(n, kDedupChunk), sm_count * 4ull));
   dedup_insert_kernel<<<gi, kDedupThreads, 0, counted(s)>>>(d, keys, n, scores, score_mode,
                                                             slot_of, d_error);
-  dedup_flag_kernel<<<g1, 256, 0, counted(s)>>>(d, slot_of, n, rank);
-  scan_tiles_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, counted(s)>>>(rank, n,
-                                                                               sums);
+  scan_first_tiles_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, counted(s)>>>(
+      d, slot_of, n, rank, sums);
   scan_sums_kernel<<<1, kScanThreads, 0, counted(s)>>>(sums, ntiles, dm);
   scan_add_kernel<<<static_cast<int>(ntiles), kScanThreads, 0, counted(s)>>>(rank, n,
                                                                              sums);
