@@ -416,7 +416,9 @@ struct RowHead {
     for (uint32_t k = 0; k < kHead; k++)
       v[k] = lane + k * W < nv ? sp[lane + k * W] : V{};
   }
-  // the whole row: head from registers, the rest from src
+  // the whole row: head from registers, the rest from src. Streaming
+  // (evict-first) stores: the kernel never reads the row back, and its
+  // write-back then happens inside this launch instead of the next one's
   __device__ __forceinline__ void store(uint8_t* __restrict__ dst,
                                         const uint8_t* __restrict__ src,
                                         uint32_t nv, uint32_t lane) const {
@@ -424,8 +426,8 @@ struct RowHead {
     const V* sp = reinterpret_cast<const V*>(src);
 #pragma unroll
     for (uint32_t k = 0; k < kHead; k++)
-      if (lane + k * W < nv) d[lane + k * W] = v[k];
-    for (uint32_t x = lane + kHead * W; x < nv; x += W) d[x] = sp[x];
+      if (lane + k * W < nv) __stcs(d + lane + k * W, v[k]);
+    for (uint32_t x = lane + kHead * W; x < nv; x += W) __stcs(d + x, sp[x]);
   }
 };
 
